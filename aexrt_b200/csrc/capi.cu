@@ -1,0 +1,640 @@
+// C ABI of the B200 W8A8 backend (declared in include/aexrt_b200.h).
+//
+// Host side of the hot path: layout-8 weight quantization and repack into the
+// K-slot layout the tcgen05 kernel streams, the reference's int8 shape guard,
+// TMA descriptor encoding, tile / pipeline selection and the launches.  All
+// launches are asynchronous and allocate nothing; only plan creation allocates
+// (the packed weights, scales, bias and a status word).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/aexrt_b200.h"
+#include "conv_tc.cuh"
+#include "quant.cuh"
+
+using namespace aexrt;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return 0;
+}
+
+bool cuda_ok(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return true;
+  fail("%s: %s", what, cudaGetErrorString(e));
+  return false;
+}
+
+// cuTensorMapEncodeTiled, fetched through the runtime so the library does not
+// link libcuda directly (it must load on machines without a GPU driver).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail("cuTensorMapEncodeTiled unavailable (no CUDA driver)") != 0;
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail("TMA base address must be 16-byte aligned") != 0;
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i > 0) s[i - 1] = strides_bytes[i - 1];
+  }
+  const CUresult r = fn(map, dt, rank, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r)) != 0;
+  return true;
+}
+
+// Output tile (tw x th <= 128 pixels) maximising the useful fraction of the
+// 128-row MMA tile; ties prefer fewer, wider tiles.
+void pick_tile(int oh, int ow, int& tw, int& th) {
+  double best = -1.0;
+  tw = th = 1;
+  for (int w = 1; w <= std::min(ow, 128); ++w) {
+    const int h = std::min(oh, 128 / w);
+    const long tiles = static_cast<long>((oh + h - 1) / h) * ((ow + w - 1) / w);
+    const double util = static_cast<double>(oh) * ow / (static_cast<double>(tiles) * 128.0);
+    if (util > best + 1e-9) {
+      best = util;
+      tw = w;
+      th = h;
+    }
+  }
+}
+
+}  // namespace
+
+struct AexrtB200ConvPlan {
+  AexrtConv2DDesc desc{};
+  uint32_t kind = 0, kernel_id = 0, flags = 0;
+  bool f16 = false, pg = false;
+  int k = 1, stride = 1, pad = 0;
+  int slabs = 0;         // input slabs (16 ch int8, 8 ch fp16)
+  int in_hp = 0, in_wp = 0;
+  int tw = 0, th = 0, tiles_w = 0, tiles_h = 0;
+  int bn = 0, n_tiles = 0, oc_alloc = 0;
+  int q_total = 0, kk_p = 0, sps = 0, stages = 0, smem = 0;
+  void* d_w = nullptr;
+  float* d_scale = nullptr;
+  float* d_bias = nullptr;
+  uint32_t* d_status = nullptr;
+  CUtensorMap w_map;
+  int device = 0;
+};
+
+namespace {
+
+using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const ConvTcParams);
+constexpr int kMaxConvSmem = 200 * 1024;
+
+template <bool F16, bool PG>
+KernelFn kernel_for_bn(int bn) {
+  switch (bn) {
+    case 16: return conv_tc_kernel<F16, PG, 16>;
+    case 32: return conv_tc_kernel<F16, PG, 32>;
+    case 64: return conv_tc_kernel<F16, PG, 64>;
+    case 128: return conv_tc_kernel<F16, PG, 128>;
+    case 256:
+      if constexpr (!PG) return conv_tc_kernel<F16, PG, 256>;
+      return nullptr;
+    default: return nullptr;
+  }
+}
+
+KernelFn kernel_for(bool f16, bool pg, int bn) {
+  if (f16) return kernel_for_bn<true, false>(bn);
+  return pg ? kernel_for_bn<false, true>(bn) : kernel_for_bn<false, false>(bn);
+}
+
+int choose_bn(int oc, bool pg, uint32_t requested) {
+  if (requested) return static_cast<int>(requested);
+  const int cands[] = {256, 128, 64, 32, 16};
+  int best = 16;
+  long best_waste = 1L << 40;
+  for (int c : cands) {
+    if (pg && c > 128) continue;
+    const int tiles = (oc + c - 1) / c;
+    const long waste = static_cast<long>(tiles) * c - oc;
+    if (waste < best_waste) {  // first (largest) tile with the least padding
+      best_waste = waste;
+      best = c;
+    }
+  }
+  return best;
+}
+
+bool check_desc_int8(const AexrtConv2DDesc& d, uint32_t kernel_id, bool pg) {
+  // can_use_conv_int8 (native/aexrt_d3d12_runtime.cpp:9398-9422)
+  if (d.groups != 1 || d.in_channels % 4 || d.out_channels % 4)
+    return fail("int8 conv needs groups == 1, in_channels %% 4 == 0, out_channels %% 4 == 0") != 0;
+  if (d.dilation_h != 1 || d.dilation_w != 1) return fail("int8 conv needs dilation 1") != 0;
+  if (kernel_id == 51) {
+    if (d.kernel_h != 1 || d.kernel_w != 1 || d.stride_h != 1 || d.stride_w != 1 || d.pad_top || d.pad_left)
+      return fail("kernel 51 needs a 1x1 stride-1 conv without padding") != 0;
+    if (d.out_channels % 8 || d.in_h != d.out_h || d.in_w != d.out_w)
+      return fail("kernel 51 needs out_channels %% 8 == 0 and same spatial size") != 0;
+  } else if (kernel_id == 52 || kernel_id == 53) {
+    if (d.kernel_h != 3 || d.kernel_w != 3 || d.pad_top != 1 || d.pad_left != 1)
+      return fail("kernels 52/53 need a 3x3 conv with padding 1") != 0;
+    if (kernel_id == 52) {
+      if (d.stride_h != 1 || d.stride_w != 1 || d.in_h != d.out_h || d.in_w != d.out_w)
+        return fail("kernel 52 needs stride 1 and same spatial size") != 0;
+    } else {
+      if (d.stride_h != 2 || d.stride_w != 2 || d.in_h < d.out_h * 2 - 1 || d.in_w < d.out_w * 2 - 1)
+        return fail("kernel 53 needs stride 2 and in >= 2*out-1") != 0;
+      if (d.out_h != (d.in_h + 1) / 2 || d.out_w != (d.in_w + 1) / 2)
+        return fail("kernel 53 output size must be ceil(in/2)") != 0;
+    }
+  } else {
+    return fail("unknown int8 kernel id %u (expected 51, 52 or 53)", kernel_id) != 0;
+  }
+  if (pg && d.in_channels % 16) return fail("pg16 scaling needs in_channels %% 16 == 0") != 0;
+  if (d.batch == 0 || d.out_h == 0 || d.out_w == 0) return fail("empty conv") != 0;
+  return true;
+}
+
+AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t kernel_id, uint32_t flags, bool f16,
+                              const void* host_w, const float* scale, const float* bias, uint32_t block_n) {
+  if (kind != AEXRT_B200_KIND_CONV && kind != AEXRT_B200_KIND_CONV_SILU) {
+    fail("kind must be CONV (1) or CONV_SILU (2)");
+    return nullptr;
+  }
+  if (!host_w || !bias || (!f16 && !scale)) {
+    fail("null weight/scale/bias pointer");
+    return nullptr;
+  }
+  auto* p = new AexrtB200ConvPlan();
+  p->desc = d;
+  p->kind = kind;
+  p->kernel_id = kernel_id;
+  p->flags = flags;
+  p->f16 = f16;
+  p->pg = !f16 && (flags & AEXRT_B200_PLAN_FLAG_INT8_PERGROUP);
+  p->k = static_cast<int>(d.kernel_h);
+  p->stride = static_cast<int>(d.stride_h);
+  p->pad = static_cast<int>(d.pad_top);
+  const int cps = f16 ? 8 : 16;  // channels per slot
+  const int ic = static_cast<int>(d.in_channels), oc = static_cast<int>(d.out_channels);
+  const int kk = p->k * p->k;
+  p->slabs = (ic + cps - 1) / cps;
+  p->in_hp = static_cast<int>(d.in_h) + (p->stride == 2 ? (d.in_h & 1) : 0);
+  p->in_wp = static_cast<int>(d.in_w) + (p->stride == 2 ? (d.in_w & 1) : 0);
+  pick_tile(static_cast<int>(d.out_h), static_cast<int>(d.out_w), p->tw, p->th);
+  p->tiles_w = (static_cast<int>(d.out_w) + p->tw - 1) / p->tw;
+  p->tiles_h = (static_cast<int>(d.out_h) + p->th - 1) / p->th;
+  p->bn = choose_bn(oc, p->pg, block_n);
+  if (!kernel_for(f16, p->pg, p->bn)) {
+    fail("unsupported block_n %d", p->bn);
+    delete p;
+    return nullptr;
+  }
+  p->n_tiles = (oc + p->bn - 1) / p->bn;
+  p->oc_alloc = p->n_tiles * p->bn;
+  if (p->pg) {
+    p->kk_p = (kk + 1) & ~1;
+    p->q_total = p->slabs * p->kk_p;
+  } else {
+    p->kk_p = 0;
+    p->q_total = (kk * p->slabs + 1) & ~1;
+  }
+  p->sps = std::min(8, p->q_total);
+  {
+    const ConvSmemPlan one = conv_smem_plan(p->tw, p->th, p->sps, 1, p->bn);
+    const int budget = 110 * 1024;
+    int st = (budget - 2048 - 128) / one.stage_bytes;
+    const int stage_iters = (p->q_total + p->sps - 1) / p->sps;
+    st = std::max(2, std::min({st, 6, std::max(2, stage_iters)}));
+    p->stages = st;
+    p->smem = conv_smem_plan(p->tw, p->th, p->sps, st, p->bn).total_bytes;
+  }
+
+  // ---- weight repack into [slot][oc_alloc][16 bytes]
+  const size_t slot_row = 16;
+  std::vector<uint8_t> packed(static_cast<size_t>(p->q_total) * p->oc_alloc * slot_row, 0);
+  for (int q = 0; q < p->q_total; ++q) {
+    int tap, slab;
+    if (p->pg) {
+      slab = q / p->kk_p;
+      tap = q - slab * p->kk_p;
+      if (tap >= kk || slab >= p->slabs) tap = -1;
+    } else {
+      tap = q / p->slabs;
+      slab = q - tap * p->slabs;
+      if (tap >= kk) tap = -1;
+    }
+    if (tap < 0) continue;
+    for (int o = 0; o < oc; ++o) {
+      uint8_t* dst = packed.data() + (static_cast<size_t>(q) * p->oc_alloc + o) * slot_row;
+      for (int c = 0; c < cps; ++c) {
+        const int ci = slab * cps + c;
+        if (ci >= ic) continue;
+        const size_t src = (static_cast<size_t>(o) * ic + ci) * kk + tap;
+        if (f16) {
+          const __half h = __float2half_rn(static_cast<const float*>(host_w)[src]);
+          std::memcpy(dst + 2 * c, &h, 2);
+        } else {
+          dst[c] = static_cast<uint8_t>(static_cast<const int8_t*>(host_w)[src]);
+        }
+      }
+    }
+  }
+  bool ok = cuda_ok(cudaGetDevice(&p->device), "cudaGetDevice") &&
+            cuda_ok(cudaMalloc(&p->d_w, packed.size()), "cudaMalloc(weights)") &&
+            cuda_ok(cudaMemcpy(p->d_w, packed.data(), packed.size(), cudaMemcpyHostToDevice), "copy weights") &&
+            cuda_ok(cudaMalloc(reinterpret_cast<void**>(&p->d_bias), sizeof(float) * oc), "cudaMalloc(bias)") &&
+            cuda_ok(cudaMemcpy(p->d_bias, bias, sizeof(float) * oc, cudaMemcpyHostToDevice), "copy bias") &&
+            cuda_ok(cudaMalloc(reinterpret_cast<void**>(&p->d_status), sizeof(uint32_t)), "cudaMalloc(status)") &&
+            cuda_ok(cudaMemset(p->d_status, 0, sizeof(uint32_t)), "memset(status)");
+  if (ok && !f16) {
+    ok = cuda_ok(cudaMalloc(reinterpret_cast<void**>(&p->d_scale), sizeof(float) * oc), "cudaMalloc(scale)") &&
+         cuda_ok(cudaMemcpy(p->d_scale, scale, sizeof(float) * oc, cudaMemcpyHostToDevice), "copy scale");
+  }
+  if (ok) {
+    const uint64_t dims[3] = {static_cast<uint64_t>(f16 ? 8 : 16), static_cast<uint64_t>(p->oc_alloc),
+                              static_cast<uint64_t>(p->q_total)};
+    const uint64_t strides[2] = {16, 16ull * p->oc_alloc};
+    const uint32_t box[3] = {static_cast<uint32_t>(f16 ? 8 : 16), static_cast<uint32_t>(p->bn),
+                             static_cast<uint32_t>(p->sps)};
+    ok = encode_map(&p->w_map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, p->d_w, dims,
+                    strides, box);
+  }
+  if (ok) {
+    // the attribute is a per-kernel cap shared by every plan of this instance: set it to the
+    // largest dynamic shared memory any plan may request, never to this plan's size
+    ok = p->smem <= kMaxConvSmem &&
+         cuda_ok(cudaFuncSetAttribute(kernel_for(f16, p->pg, p->bn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kMaxConvSmem),
+                 "cudaFuncSetAttribute");
+    if (p->smem > kMaxConvSmem) fail("conv plan needs %d bytes of shared memory", p->smem);
+  }
+  if (!ok) {
+    aexrt_b200_conv_plan_destroy(p);
+    return nullptr;
+  }
+  return p;
+}
+
+bool encode_act_map(const AexrtB200ConvPlan* p, const void* x, CUtensorMap* map) {
+  const uint64_t hp = p->in_hp, wp = p->in_wp;
+  const uint64_t sn = static_cast<uint64_t>(p->slabs) * p->desc.batch;
+  const uint32_t ce = p->f16 ? 8 : 16;  // elements per 16-byte slot
+  const CUtensorMapDataType dt = p->f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  if (p->stride == 1) {
+    const uint64_t dims[4] = {ce, wp, hp, sn};
+    const uint64_t strides[3] = {16, 16 * wp, 16 * wp * hp};
+    const uint32_t box[4] = {ce, static_cast<uint32_t>(p->tw), static_cast<uint32_t>(p->th), 1};
+    return encode_map(map, dt, 4, x, dims, strides, box);
+  }
+  const uint64_t dims[5] = {2ull * ce, wp / 2, 2, hp / 2, sn};
+  const uint64_t strides[4] = {32, 16 * wp, 32 * wp, 16 * wp * hp};
+  const uint32_t box[5] = {ce, static_cast<uint32_t>(p->tw), 1, static_cast<uint32_t>(p->th), 1};
+  return encode_map(map, dt, 5, x, dims, strides, box);
+}
+
+int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_rec, const void* res, uint32_t res_ldc,
+                uint32_t res_coff, void* out, uint32_t out_ldc, uint32_t out_coff, uint32_t* amax_out,
+                uint32_t amax_stride, uint32_t amax_goff, int32_t* acc_dump, void* stream) {
+  if (!p) return fail("null plan");
+  if (!x || !out) return fail("null input/output pointer");
+  if (!p->f16 && !scale_rec) return fail("null scale record");
+  const uint32_t oc = p->desc.out_channels;
+  if (out_ldc < out_coff + oc || reinterpret_cast<uintptr_t>(out) % 2)
+    return fail("output slice out of range (need coff + oc <= ldc)");
+  if (res && (res_ldc < res_coff + oc || reinterpret_cast<uintptr_t>(res) % 2))
+    return fail("residual slice out of range (need coff + oc <= ldc)");
+  if (amax_out && (amax_goff * 16 + oc > amax_stride * 16 || out_coff % 16))
+    return fail("amax_out slots out of range (need amax_goff + ceil(oc/16) <= amax_stride, coff %% 16 == 0)");
+  if (reinterpret_cast<uintptr_t>(x) % 16) return fail("packed input must be 16-byte aligned");
+  CUtensorMap act_map;
+  if (!encode_act_map(p, x, &act_map)) return 0;
+  ConvTcParams prm{};
+  prm.n_img = static_cast<int>(p->desc.batch);
+  prm.slabs = p->slabs;
+  prm.in_h = p->in_hp;
+  prm.in_w = p->in_wp;
+  prm.oc = static_cast<int>(oc);
+  prm.oh = static_cast<int>(p->desc.out_h);
+  prm.ow = static_cast<int>(p->desc.out_w);
+  prm.ksize = p->k;
+  prm.stride = p->stride;
+  prm.pad = p->pad;
+  prm.tw = p->tw;
+  prm.th = p->th;
+  prm.tiles_w = p->tiles_w;
+  prm.tiles_h = p->tiles_h;
+  prm.q_total = p->q_total;
+  prm.sps = p->sps;
+  prm.stages = p->stages;
+  prm.kk_p = p->kk_p;
+  prm.silu = p->kind == AEXRT_B200_KIND_CONV_SILU;
+  prm.scale_rec = scale_rec;
+  prm.w_scale = p->d_scale;
+  prm.bias = p->d_bias;
+  prm.res = static_cast<const __half*>(res);
+  prm.res_ldc = static_cast<int>(res_ldc);
+  prm.res_coff = static_cast<int>(res_coff);
+  prm.out = static_cast<__half*>(out);
+  prm.out_ldc = static_cast<int>(out_ldc);
+  prm.out_coff = static_cast<int>(out_coff);
+  prm.out_vec = (out_ldc % 8 == 0 && out_coff % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) ? 1 : 0;
+  prm.res_vec = (res && res_ldc % 8 == 0 && res_coff % 8 == 0 && reinterpret_cast<uintptr_t>(res) % 16 == 0) ? 1 : 0;
+  prm.amax_out = amax_out;
+  prm.amax_stride = static_cast<int>(amax_stride);
+  prm.amax_goff = static_cast<int>(amax_goff);
+  prm.acc_dump = acc_dump;
+  prm.status = p->d_status;
+  const dim3 grid(static_cast<unsigned>(p->desc.batch * p->tiles_h * p->tiles_w), static_cast<unsigned>(p->n_tiles));
+  KernelFn fn = kernel_for(p->f16, p->pg, p->bn);
+  fn<<<grid, kConvThreads, p->smem, static_cast<cudaStream_t>(stream)>>>(act_map, p->w_map, prm);
+  return cuda_ok(cudaGetLastError(), "conv launch") ? 1 : 0;
+}
+
+void quant_params_common(QuantParams& q, const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w,
+                         uint32_t layout, uint32_t ldc, uint32_t coff, const uint32_t* amax_groups,
+                         uint32_t groups_total, uint32_t group_offset) {
+  std::memset(&q, 0, sizeof(q));
+  q.nsrc = 1;
+  QuantSrc& s = q.src[0];
+  s.ptr = x;
+  s.layout = static_cast<int>(layout);
+  s.ldc = static_cast<int>(layout == AEXRT_B200_LAYOUT_NHWC_F16 ? ldc : c);
+  s.coff = static_cast<int>(layout == AEXRT_B200_LAYOUT_NHWC_F16 ? coff : 0);
+  s.ch = static_cast<int>(c);
+  s.up = 1;
+  s.src_h = static_cast<int>(h);
+  s.src_w = static_cast<int>(w);
+  s.amax_g = amax_groups;
+  s.amax_stride = static_cast<int>(groups_total);
+  s.amax_goff = static_cast<int>(group_offset);
+  q.n = static_cast<int>(n);
+  q.h = static_cast<int>(h);
+  q.w = static_cast<int>(w);
+  q.c_total = static_cast<int>(c);
+}
+
+}  // namespace
+
+extern "C" {
+
+uint32_t aexrt_b200_abi_version(void) { return AEXRT_B200_ABI_VERSION; }
+
+const char* aexrt_b200_get_last_error(void) { return g_last_error.c_str(); }
+
+int aexrt_b200_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+int aexrt_b200_quantize_conv_weight_int8(const float* weight, uint32_t out_channels, uint32_t in_channels,
+                                         uint32_t kernel_elems, uint32_t fp16_engine, int8_t* codes_out,
+                                         float* scale_out) {
+  if (!weight || !codes_out || !scale_out) return fail("null pointer");
+  const size_t row = static_cast<size_t>(in_channels) * kernel_elems;
+  std::vector<float> src(row);
+  for (uint32_t o = 0; o < out_channels; ++o) {
+    float amax = 0.0f;
+    for (size_t i = 0; i < row; ++i) {
+      float v = weight[o * row + i];
+      if (fp16_engine) v = __half2float(__float2half_rn(v));
+      src[i] = v;
+      amax = std::max(amax, std::fabs(v));
+    }
+    // engine.py:2450-2457 — every operation rounds to fp32
+    volatile float scale = amax > 0.0f ? amax / 127.0f : 1.0f;
+    volatile float inv = 1.0f / scale;
+    for (size_t i = 0; i < row; ++i) {
+      volatile float prod = src[i] * inv;
+      volatile float mag = std::fabs(prod) + 0.5f;
+      float q = std::floor(mag);
+      if (prod < 0.0f) q = -q;
+      if (prod == 0.0f) q = 0.0f;
+      q = std::min(127.0f, std::max(-127.0f, q));
+      codes_out[o * row + i] = static_cast<int8_t>(q);
+    }
+    scale_out[o] = scale;
+  }
+  return 1;
+}
+
+int aexrt_b200_act_amax_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t layout,
+                            uint32_t ldc, uint32_t coff, uint32_t* amax_groups, uint32_t groups_total,
+                            uint32_t group_offset, uint32_t zero_first, void* stream) {
+  if (!x || !amax_groups) return fail("null pointer");
+  const uint32_t groups = (c + 15) / 16;
+  if (group_offset + groups > groups_total) return fail("amax group range exceeds groups_total");
+  if (n == 0 || c == 0 || h == 0 || w == 0) return 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (zero_first) {
+    if (!cuda_ok(cudaMemset2DAsync(amax_groups + group_offset, groups_total * 4, 0, groups * 4, n, st), "memset amax"))
+      return 0;
+  }
+  const int hw = static_cast<int>(h * w);
+  if (reinterpret_cast<uintptr_t>(x) % 16) return fail("x must be 16-byte aligned");
+  if (layout == AEXRT_B200_LAYOUT_NCHW_F16) {
+    const int chunk = 8192;
+    const int blocks = static_cast<int>((16ull * hw + chunk - 1) / chunk);
+    amax_nchw_f16_kernel<<<dim3(blocks, groups, n), 256, 0, st>>>(static_cast<const __half*>(x), static_cast<int>(c),
+                                                                   hw, static_cast<int>(groups_total), chunk,
+                                                                   amax_groups + group_offset);
+  } else if (layout == AEXRT_B200_LAYOUT_NHWC_F16) {
+    if (ldc < coff + c || ldc % 8 || coff % 8 || reinterpret_cast<uintptr_t>(x) % 16)
+      return fail("NHWC slice must be 16-byte aligned (ldc, coff multiples of 8)");
+    const int vec = static_cast<int>((c + 7) / 8);
+    const int ppb = std::max(1, 2048 / vec);
+    const int blocks = (hw + ppb - 1) / ppb;
+    amax_nhwc_f16_kernel<<<dim3(blocks, n), 256, groups * 4, st>>>(
+        static_cast<const __half*>(x), hw, static_cast<int>(c), static_cast<int>(ldc), static_cast<int>(coff),
+        static_cast<int>(groups), ppb, amax_groups + group_offset, static_cast<int>(groups_total));
+  } else {
+    return fail("amax supports fp16 NCHW or NHWC input");
+  }
+  return cuda_ok(cudaGetLastError(), "amax launch") ? 1 : 0;
+}
+
+uint64_t aexrt_b200_packed_act_bytes(uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t stride) {
+  const uint64_t hp = h + (stride == 2 ? (h & 1) : 0), wp = w + (stride == 2 ? (w & 1) : 0);
+  return static_cast<uint64_t>(n) * ((c + 15) / 16) * hp * wp * 16;
+}
+
+uint64_t aexrt_b200_packed_f16_bytes(uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t stride) {
+  const uint64_t hp = h + (stride == 2 ? (h & 1) : 0), wp = w + (stride == 2 ? (w & 1) : 0);
+  return static_cast<uint64_t>(n) * ((c + 7) / 8) * hp * wp * 16;
+}
+
+int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t layout,
+                                uint32_t ldc, uint32_t coff, const uint32_t* amax_groups, uint32_t groups_total,
+                                uint32_t group_offset, uint32_t mode, uint32_t consumer_stride, void* q_out,
+                                float* scale_rec, void* stream) {
+  if (!x || !amax_groups || !q_out) return fail("null pointer");
+  if (layout > AEXRT_B200_LAYOUT_NCHW_F16) return fail("quantize supports fp16 NHWC or NCHW input");
+  if (mode > 1) return fail("mode must be 0 (per tensor) or 1 (pg16)");
+  if (mode == 1 && c % 16) return fail("pg16 needs c %% 16 == 0");
+  if (layout == AEXRT_B200_LAYOUT_NHWC_F16 && (ldc < coff + c || ldc % 8 || coff % 8))
+    return fail("NHWC slice must be 16-byte aligned (ldc, coff multiples of 8)");
+  if (group_offset + (c + 15) / 16 > groups_total) return fail("amax group range exceeds groups_total");
+  if (reinterpret_cast<uintptr_t>(q_out) % 16) return fail("q_out must be 16-byte aligned");
+  if (n == 0 || c == 0 || h == 0 || w == 0) return 1;
+  QuantParams q;
+  quant_params_common(q, x, n, c, h, w, layout, ldc, coff, amax_groups, groups_total, group_offset);
+  q.slabs = static_cast<int>((c + 15) / 16);
+  q.hp = static_cast<int>(h + (consumer_stride == 2 ? (h & 1) : 0));
+  q.wp = static_cast<int>(w + (consumer_stride == 2 ? (w & 1) : 0));
+  q.mode = static_cast<int>(mode);
+  q.out = q_out;
+  q.rec = scale_rec;
+  const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, n);
+  quantize_i8_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(q);
+  return cuda_ok(cudaGetLastError(), "quantize launch") ? 1 : 0;
+}
+
+int aexrt_b200_pack_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t layout, uint32_t ldc,
+                        uint32_t coff, uint32_t consumer_stride, void* out, void* stream) {
+  if (!x || !out) return fail("null pointer");
+  if (layout > AEXRT_B200_LAYOUT_NCHW_F32) return fail("unknown layout");
+  if (layout == AEXRT_B200_LAYOUT_NHWC_F16 && (ldc < coff + c || ldc % 8 || coff % 8))
+    return fail("NHWC slice must be 16-byte aligned (ldc, coff multiples of 8)");
+  if (reinterpret_cast<uintptr_t>(out) % 16) return fail("out must be 16-byte aligned");
+  if (n == 0 || c == 0 || h == 0 || w == 0) return 1;
+  QuantParams q;
+  quant_params_common(q, x, n, c, h, w, layout, ldc, coff, nullptr, 0, 0);
+  q.slabs = static_cast<int>((c + 7) / 8);
+  q.hp = static_cast<int>(h + (consumer_stride == 2 ? (h & 1) : 0));
+  q.wp = static_cast<int>(w + (consumer_stride == 2 ? (w & 1) : 0));
+  q.out = out;
+  const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, n);
+  pack_f16_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(q);
+  return cuda_ok(cudaGetLastError(), "pack launch") ? 1 : 0;
+}
+
+AexrtB200ConvPlan* aexrt_b200_conv_plan_create(const AexrtConv2DDesc* desc, uint32_t kind, uint32_t kernel_id,
+                                               uint32_t flags, const int8_t* codes, const float* w_scale,
+                                               const float* bias, uint32_t block_n) {
+  if (!desc) {
+    fail("null desc");
+    return nullptr;
+  }
+  const bool pg = flags & AEXRT_B200_PLAN_FLAG_INT8_PERGROUP;
+  if (!check_desc_int8(*desc, kernel_id, pg)) return nullptr;
+  return build_plan(*desc, kind, kernel_id, flags, false, codes, w_scale, bias, block_n);
+}
+
+AexrtB200ConvPlan* aexrt_b200_conv_plan_create_f16(const AexrtConv2DDesc* desc, uint32_t kind, const float* weight,
+                                                   const float* bias, uint32_t block_n) {
+  if (!desc) {
+    fail("null desc");
+    return nullptr;
+  }
+  const AexrtConv2DDesc& d = *desc;
+  const bool k_ok = (d.kernel_h == 1 && d.kernel_w == 1 && d.pad_top == 0 && d.pad_left == 0) ||
+                    (d.kernel_h == 3 && d.kernel_w == 3 && d.pad_top == 1 && d.pad_left == 1);
+  const bool s_ok = (d.stride_h == 1 && d.stride_w == 1) || (d.stride_h == 2 && d.stride_w == 2 && d.kernel_h == 3);
+  if (!k_ok || !s_ok || d.groups != 1 || d.dilation_h != 1 || d.dilation_w != 1) {
+    fail("fp16 conv supports 1x1 s1 p0 and 3x3 s1/s2 p1, groups 1");
+    return nullptr;
+  }
+  const uint32_t oh = (d.in_h + 2 * d.pad_top - d.kernel_h) / d.stride_h + 1;
+  const uint32_t ow = (d.in_w + 2 * d.pad_left - d.kernel_w) / d.stride_w + 1;
+  if (d.out_h != oh || d.out_w != ow || d.batch == 0) {
+    fail("fp16 conv output size mismatch");
+    return nullptr;
+  }
+  return build_plan(d, kind, 0, 0, true, weight, nullptr, bias, block_n);
+}
+
+int aexrt_b200_conv_plan_info(const AexrtB200ConvPlan* p, AexrtB200ConvPlanInfo* info) {
+  if (!p || !info) return fail("null pointer");
+  AexrtB200ConvPlanInfo i{};
+  i.struct_size = sizeof(i);
+  i.kernel_id = p->kernel_id;
+  i.flags = p->flags;
+  i.kind = p->kind;
+  i.is_f16 = p->f16;
+  i.tile_w = p->tw;
+  i.tile_h = p->th;
+  i.block_n = p->bn;
+  i.k_slots = p->q_total;
+  i.stages = p->stages;
+  i.smem_bytes = p->smem;
+  i.grid_m = p->desc.batch * p->tiles_h * p->tiles_w;
+  i.grid_n = p->n_tiles;
+  i.in_hp = p->in_hp;
+  i.in_wp = p->in_wp;
+  *info = i;
+  return 1;
+}
+
+void aexrt_b200_conv_plan_destroy(AexrtB200ConvPlan* p) {
+  if (!p) return;
+  if (p->d_w) cudaFree(p->d_w);
+  if (p->d_scale) cudaFree(p->d_scale);
+  if (p->d_bias) cudaFree(p->d_bias);
+  if (p->d_status) cudaFree(p->d_status);
+  delete p;
+}
+
+int aexrt_b200_conv_w8a8(const AexrtB200ConvPlan* plan, const void* q_act, const float* scale_rec,
+                         const void* residual, uint32_t res_ldc, uint32_t res_coff, void* out, uint32_t out_ldc,
+                         uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride, uint32_t amax_goff,
+                         int32_t* acc_dump, void* stream) {
+  if (plan && plan->f16) return fail("plan is fp16; use aexrt_b200_conv_f16");
+  return launch_conv(plan, q_act, scale_rec, residual, res_ldc, res_coff, out, out_ldc, out_coff, amax_out,
+                     amax_stride, amax_goff, acc_dump, stream);
+}
+
+int aexrt_b200_conv_f16(const AexrtB200ConvPlan* plan, const void* x_slab8, const void* residual, uint32_t res_ldc,
+                        uint32_t res_coff, void* out, uint32_t out_ldc, uint32_t out_coff, uint32_t* amax_out,
+                        uint32_t amax_stride, uint32_t amax_goff, void* stream) {
+  if (plan && !plan->f16) return fail("plan is int8; use aexrt_b200_conv_w8a8");
+  return launch_conv(plan, x_slab8, nullptr, residual, res_ldc, res_coff, out, out_ldc, out_coff, amax_out,
+                     amax_stride, amax_goff, nullptr, stream);
+}
+
+int aexrt_b200_conv_status(const AexrtB200ConvPlan* plan, uint32_t* status) {
+  if (!plan || !status) return fail("null pointer");
+  if (!cuda_ok(cudaMemcpy(status, plan->d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost), "read status")) return 0;
+  return cuda_ok(cudaMemset(plan->d_status, 0, sizeof(uint32_t)), "clear status") ? 1 : 0;
+}
+
+}  // extern "C"

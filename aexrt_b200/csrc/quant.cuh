@@ -1,0 +1,243 @@
+// Activation amax and int8 quantize kernels (reference a3/a4:
+// native/aexrt_d3d12_runtime.cpp:3212-3361), plus the fp16 slab repack used by
+// the fp16 convs.  All of them are HBM-bound byte/element passes: 16-byte
+// vector loads/stores, one atomic per block and group, grids sized over the
+// whole tensor (never one block per channel group, which is the reference's
+// "grid collapse" the block-split amax fixed, runtime.cpp:3226-3231).
+#pragma once
+#include <cuda_fp16.h>
+
+#include <cstdint>
+
+namespace aexrt {
+
+// ----------------------------------------------------------------------------
+// amax
+// ----------------------------------------------------------------------------
+
+// Per (image, 16-channel group) amax of an NCHW fp16 tensor.  The 16 channel
+// planes of one group are one contiguous strip of 16*H*W halves; grid.x splits
+// each strip into chunks so small-channel / large-plane tensors still fill the
+// GPU.  Result: float bits, atomically max-ed into amax_g[n * G + g].
+__global__ void amax_nchw_f16_kernel(const __half* __restrict__ x, int c, int hw, int groups, int chunk,
+                                     uint32_t* __restrict__ amax_g) {
+  const int g = blockIdx.y;
+  const int n = blockIdx.z;
+  const int c0 = g * 16;
+  const int gch = min(16, c - c0);
+  const size_t strip_len = static_cast<size_t>(gch) * hw;
+  const size_t base = (static_cast<size_t>(n) * c + c0) * hw;
+  const size_t begin = static_cast<size_t>(blockIdx.x) * chunk;
+  const size_t end = min(strip_len, begin + chunk);
+  float m = 0.0f;
+  if (begin < end) {
+    const __half* s = x + base;
+    // 16-byte vector loads when the strip start is 16-byte aligned (c*h*w a multiple of 8)
+    const bool vec = ((base & 7) == 0) && ((begin & 7) == 0);
+    if (vec) {
+      const size_t vend = begin + ((end - begin) / 8) * 8;
+      for (size_t i = begin + static_cast<size_t>(threadIdx.x) * 8; i < vend; i += static_cast<size_t>(blockDim.x) * 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(s + i);
+        const __half2* h2 = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __half22float2(h2[k]);
+          m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      }
+      for (size_t t = vend + threadIdx.x; t < end; t += blockDim.x) m = fmaxf(m, fabsf(__half2float(s[t])));
+    } else {
+      for (size_t t = begin + threadIdx.x; t < end; t += blockDim.x) m = fmaxf(m, fabsf(__half2float(s[t])));
+    }
+  }
+  uint32_t bits = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+  __shared__ uint32_t warp_max[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) warp_max[warp] = bits;
+  __syncthreads();
+  if (warp == 0) {
+    bits = lane < (blockDim.x >> 5) ? warp_max[lane] : 0u;
+    bits = __reduce_max_sync(0xffffffffu, bits);
+    if (lane == 0 && begin < end) atomicMax(&amax_g[static_cast<size_t>(n) * groups + g], bits);
+  }
+}
+
+// Per (image, 16-channel group) amax of an NHWC fp16 slice (ldc, coff).  Each
+// thread handles 8 channels of one pixel; block-level maxima go through shared
+// memory so each block issues one global atomic per group it touched.
+__global__ void amax_nhwc_f16_kernel(const __half* __restrict__ x, int hw, int c, int ldc, int coff, int groups,
+                                     int pix_per_block, uint32_t* __restrict__ amax_g, int amax_stride) {
+  extern __shared__ uint32_t gmax[];
+  const int n = blockIdx.y;
+  for (int i = threadIdx.x; i < groups; i += blockDim.x) gmax[i] = 0u;
+  __syncthreads();
+  const int vec_per_pix = (c + 7) / 8;
+  const int p0 = blockIdx.x * pix_per_block;
+  const int p1 = min(hw, p0 + pix_per_block);
+  const int total = (p1 - p0) * vec_per_pix;
+  for (int t = threadIdx.x; t < total; t += blockDim.x) {
+    const int pp = p0 + t / vec_per_pix;
+    const int cv = (t % vec_per_pix) * 8;
+    const __half* s = x + (static_cast<size_t>(n) * hw + pp) * ldc + coff + cv;
+    float m = 0.0f;
+    if (cv + 8 <= c) {
+      const uint4 v = *reinterpret_cast<const uint4*>(s);
+      const __half2* h2 = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(h2[k]);
+        m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    } else {
+      for (int k = 0; cv + k < c; ++k) m = fmaxf(m, fabsf(__half2float(s[k])));
+    }
+    atomicMax(&gmax[cv / 16], __float_as_uint(m));
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < groups; i += blockDim.x) {
+    if (gmax[i] != 0u) atomicMax(&amax_g[static_cast<size_t>(n) * amax_stride + i], gmax[i]);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// quantize / repack
+// ----------------------------------------------------------------------------
+
+constexpr int kMaxQuantSrc = 4;
+
+// One channel range of the (virtually concatenated) input of a conv.
+struct QuantSrc {
+  const void* ptr;        // fp16 NHWC slice, fp16 NCHW, or fp32 NCHW (see layout)
+  int layout;             // 0 = NHWC fp16, 1 = NCHW fp16, 2 = NCHW fp32
+  int ldc, coff;          // NHWC: channel stride and offset of the slice
+  int ch;                 // channels contributed (multiple of 16 except for the last source)
+  int up;                 // nearest-neighbour upsample factor (1 or 2) applied on read
+  int src_h, src_w;       // spatial dims of the source tensor
+  const uint32_t* amax_g; // per (image, group) amax bits of the source tensor (int8 only)
+  int amax_stride, amax_goff;
+};
+
+struct QuantParams {
+  QuantSrc src[kMaxQuantSrc];
+  int nsrc;
+  int n, h, w;        // logical dims of the consumer input
+  int c_total;        // channels of the consumer input
+  int slabs;          // ceil(c_total / channels per slab)
+  int hp, wp;         // dims of the packed output buffer (>= h, w; the extra rows/cols are zero)
+  int mode;           // int8: 0 = per-tensor scale, 1 = pg16 scale
+  void* out;          // int8 [n][slabs][hp][wp][16] or fp16 [n][slabs][hp][wp][8]
+  float* rec;         // int8: per image record [1 + slabs] of fp32 amax (slot 0 = tensor)
+};
+
+__device__ __forceinline__ float load_src(const QuantSrc& s, int n, int h, int w, int c) {
+  const int sh = h / s.up, sw = w / s.up;
+  if (s.layout == 0) {
+    return __half2float(static_cast<const __half*>(s.ptr)[(static_cast<size_t>(n) * s.src_h * s.src_w + static_cast<size_t>(sh) * s.src_w + sw) * s.ldc + s.coff + c]);
+  } else if (s.layout == 1) {
+    return __half2float(static_cast<const __half*>(s.ptr)[((static_cast<size_t>(n) * s.ch + c) * s.src_h + sh) * s.src_w + sw]);
+  }
+  return static_cast<const float*>(s.ptr)[((static_cast<size_t>(n) * s.ch + c) * s.src_h + sh) * s.src_w + sw];
+}
+
+// int8 codes of one 16-channel slab per thread: q = round_half_even(x * (127/amax)),
+// low byte kept with no clamp, zero when amax <= 0 (runtime.cpp:3333-3344).
+__global__ void quantize_i8_kernel(const QuantParams p) {
+  const int slab = blockIdx.y;
+  const int n = blockIdx.z;
+  __shared__ float s_mult;
+  __shared__ int s_src, s_cin;
+  if (threadIdx.x == 0) {
+    // locate the source holding this slab and the scale it is quantized with
+    int base = 0, k = 0;
+    while (k < p.nsrc - 1 && slab * 16 >= base + p.src[k].ch) {
+      base += p.src[k].ch;
+      ++k;
+    }
+    const int cin = slab * 16 - base;
+    const QuantSrc& s = p.src[k];
+    const float ag = __uint_as_float(s.amax_g[static_cast<size_t>(n) * s.amax_stride + s.amax_goff + cin / 16]);
+    float at = 0.0f;
+    for (int kk = 0; kk < p.nsrc; ++kk) {
+      const QuantSrc& t = p.src[kk];
+      for (int g = 0; g < (t.ch + 15) / 16; ++g)
+        at = fmaxf(at, __uint_as_float(t.amax_g[static_cast<size_t>(n) * t.amax_stride + t.amax_goff + g]));
+    }
+    const float a = p.mode == 1 ? ag : at;
+    s_mult = a > 0.0f ? __fdiv_rn(127.0f, a) : 0.0f;
+    s_src = k;
+    s_cin = cin;
+    if (blockIdx.x == 0 && p.rec != nullptr) {
+      float* r = p.rec + static_cast<size_t>(n) * (1 + p.slabs);
+      r[1 + slab] = ag;
+      if (slab == 0) r[0] = at;
+    }
+  }
+  __syncthreads();
+  const int pix = blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= p.hp * p.wp) return;
+  const int h = pix / p.wp, w = pix - (pix / p.wp) * p.wp;
+  uint32_t packed[4] = {0u, 0u, 0u, 0u};
+  if (h < p.h && w < p.w && s_mult != 0.0f) {
+    const QuantSrc& s = p.src[s_src];
+    const int nch = min(16, s.ch - s_cin);
+    float v[16];
+    if (s.layout == 0 && nch == 16) {
+      const __half* src = static_cast<const __half*>(s.ptr) +
+                          (static_cast<size_t>(n) * s.src_h * s.src_w + static_cast<size_t>(h / s.up) * s.src_w + w / s.up) * s.ldc +
+                          s.coff + s_cin;
+      const uint4 a = *reinterpret_cast<const uint4*>(src);
+      const uint4 b = *reinterpret_cast<const uint4*>(src + 8);
+      const __half* ha = reinterpret_cast<const __half*>(&a);
+      const __half* hb = reinterpret_cast<const __half*>(&b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[i] = __half2float(ha[i]);
+        v[8 + i] = __half2float(hb[i]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = i < nch ? load_src(s, n, h, w, s_cin + i) : 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int q = __float2int_rn(__fmul_rn(v[i], s_mult));
+      packed[i >> 2] |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * (i & 3));
+    }
+  }
+  int8_t* out = static_cast<int8_t*>(p.out) + ((static_cast<size_t>(n) * p.slabs + slab) * p.hp * p.wp + pix) * 16;
+  *reinterpret_cast<uint4*>(out) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+}
+
+// fp16 repack into 8-channel slabs for the fp16 convs (no scaling).
+__global__ void pack_f16_kernel(const QuantParams p) {
+  const int slab = blockIdx.y;
+  const int n = blockIdx.z;
+  const int pix = blockIdx.x * blockDim.x + threadIdx.x;
+  if (pix >= p.hp * p.wp) return;
+  const int h = pix / p.wp, w = pix - (pix / p.wp) * p.wp;
+  __align__(16) __half hv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) hv[i] = __float2half_rn(0.0f);
+  if (h < p.h && w < p.w) {
+    int base = 0, k = 0;
+    while (k < p.nsrc - 1 && slab * 8 >= base + p.src[k].ch) {
+      base += p.src[k].ch;
+      ++k;
+    }
+    const QuantSrc& s = p.src[k];
+    const int cin = slab * 8 - base;
+    const int nch = min(8, s.ch - cin);
+    if (s.layout == 0 && nch == 8) {
+      const __half* src = static_cast<const __half*>(s.ptr) +
+                          (static_cast<size_t>(n) * s.src_h * s.src_w + static_cast<size_t>(h / s.up) * s.src_w + w / s.up) * s.ldc +
+                          s.coff + cin;
+      *reinterpret_cast<uint4*>(hv) = *reinterpret_cast<const uint4*>(src);
+    } else {
+      for (int i = 0; i < nch; ++i) hv[i] = __float2half_rn(load_src(s, n, h, w, cin + i));
+    }
+  }
+  __half* out = static_cast<__half*>(p.out) + ((static_cast<size_t>(n) * p.slabs + slab) * p.hp * p.wp + pix) * 8;
+  *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(hv);
+}
+
+}  // namespace aexrt

@@ -1,0 +1,196 @@
+/*
+ * aexrt_b200 — C ABI of the B200 (sm_100a) W8A8 convolution backend.
+ *
+ * Conventions follow the reference runtime's C ABI (native/aexrt.h):
+ *   - every entry point returns int 1 on success and 0 on failure, never aborts,
+ *     and records a message retrievable with aexrt_b200_get_last_error()
+ *     (reference: aexrt_yolo_get_last_error, aexrt.h:406);
+ *   - opaque handles are owned by the library until their destroy call;
+ *   - device pointers are plain `void*`/typed pointers into the current CUDA
+ *     device's memory and `stream` is a cudaStream_t (NULL = legacy default);
+ *   - launches are asynchronous on `stream`; none of them allocates memory.
+ *
+ * Data layouts used on the device:
+ *   fp16 activations: NHWC slices (channel stride `ldc`, channel offset `coff`);
+ *   int8 codes:       [image][ceil(C/16)][Hp][Wp][16]   ("slab16");
+ *   fp16 conv input:  [image][ceil(C/8)][Hp][Wp][8]     ("slab8");
+ *   amax groups:      uint32 float bits, [image][groups_total] (one per 16 channels);
+ *   scale record:     float [image][1 + ceil(C/16)]: slot 0 = per-tensor amax,
+ *                     slot 1+g = amax of 16-channel group g (the reference's
+ *                     amax buffer layout, runtime.cpp:3241-3258, one per image).
+ */
+#ifndef AEXRT_B200_H
+#define AEXRT_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with -fvisibility=hidden; everything declared here is exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define AEXRT_B200_ABI_VERSION 1u
+
+/* Layout-identical to the reference's AexrtConv2DDesc (native/aexrt.h:98-115). */
+typedef struct AexrtConv2DDesc {
+    uint32_t batch;
+    uint32_t in_channels;
+    uint32_t in_h;
+    uint32_t in_w;
+    uint32_t out_channels;
+    uint32_t out_h;
+    uint32_t out_w;
+    uint32_t kernel_h;
+    uint32_t kernel_w;
+    uint32_t stride_h;
+    uint32_t stride_w;
+    uint32_t pad_top;
+    uint32_t pad_left;
+    uint32_t dilation_h;
+    uint32_t dilation_w;
+    uint32_t groups;
+} AexrtConv2DDesc;
+
+/* Command kinds and plan flags, same values as the reference compiler
+ * (src/aexrt/engine.py:85-96, 103-118). */
+#define AEXRT_B200_KIND_CONV 1u
+#define AEXRT_B200_KIND_CONV_SILU 2u
+#define AEXRT_B200_PLAN_FLAG_INT8_PERGROUP (1u << 4)
+
+/* Activation layouts accepted by the amax / quantize entry points. */
+#define AEXRT_B200_LAYOUT_NHWC_F16 0u
+#define AEXRT_B200_LAYOUT_NCHW_F16 1u
+#define AEXRT_B200_LAYOUT_NCHW_F32 2u
+
+/* Activation scale modes (the INT8_PERGROUP plan flag selects pg16). */
+#define AEXRT_B200_SCALE_PER_TENSOR 0u
+#define AEXRT_B200_SCALE_PG16 1u
+
+typedef struct AexrtB200ConvPlan AexrtB200ConvPlan;
+
+/* Read-only description of a conv plan (the analogue of AexrtConvPlanInfo,
+ * native/aexrt.h:435-445, for one command). */
+typedef struct AexrtB200ConvPlanInfo {
+    uint32_t struct_size;
+    uint32_t kernel_id;        /* 51 = 1x1, 52 = 3x3 s1, 53 = 3x3 s2 (0 for fp16 plans) */
+    uint32_t flags;            /* plan flags (bit 4 = INT8_PERGROUP) */
+    uint32_t kind;             /* AEXRT_B200_KIND_CONV or _CONV_SILU */
+    uint32_t is_f16;
+    uint32_t tile_w, tile_h;   /* spatial output tile (M = tile_w*tile_h <= 128) */
+    uint32_t block_n;          /* output channels per CTA */
+    uint32_t k_slots;          /* 16-byte K slots incl. padding */
+    uint32_t stages;           /* TMA/MMA pipeline depth */
+    uint32_t smem_bytes;
+    uint32_t grid_m, grid_n;
+    uint32_t in_hp, in_wp;     /* packed input buffer dims expected by the launch */
+    uint32_t reserved[4];
+} AexrtB200ConvPlanInfo;
+
+/* ---------------------------------------------------------------- library */
+uint32_t aexrt_b200_abi_version(void);
+/* Thread-local message of the last failed call on this thread ("" if none). */
+const char* aexrt_b200_get_last_error(void);
+/* Number of visible CUDA devices (0 when no driver or GPU is present). */
+int aexrt_b200_device_count(void);
+
+/* ---------------------------------------------------------------- a1: weights
+ * Per-output-channel symmetric int8 quantization of a conv weight
+ * [out_channels][in_channels][kernel_elems] (fp32): the layout-8 payload.
+ * Replaces src/aexrt/engine.py:2418-2465 (_add_packed_conv_int8) and its C++
+ * twin ensure_conv_int8_weight (native/aexrt_d3d12_runtime.cpp:21716-21742);
+ * host-side, bit-identical.  fp16_engine=1 rounds the weights through fp16 first. */
+int aexrt_b200_quantize_conv_weight_int8(const float* weight, uint32_t out_channels, uint32_t in_channels,
+                                         uint32_t kernel_elems, uint32_t fp16_engine, int8_t* codes_out,
+                                         float* scale_out);
+
+/* ---------------------------------------------------------------- a3: amax
+ * Per-image amax of |x| per 16-channel group (float bits), atomically max-ed
+ * into amax_groups[image * groups_total + group_offset + g].  zero_first=1
+ * clears this call's slots first.  Replaces aexrt_int8_quant_zero +
+ * aexrt_int8_quant_amax (native/aexrt_d3d12_runtime.cpp:3159-3275, recorded by
+ * record_int8_prequant_activation :21622-21644); per image instead of over
+ * the [C][N*H*W] view, which is the reference's batch-1 behaviour. */
+int aexrt_b200_act_amax_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t layout,
+                            uint32_t ldc, uint32_t coff, uint32_t* amax_groups, uint32_t groups_total,
+                            uint32_t group_offset, uint32_t zero_first, void* stream);
+
+/* ---------------------------------------------------------------- a4: quantize
+ * Bytes of the slab16 int8 buffer a conv with the given stride reads
+ * (stride 2 pads H and W up to even). */
+uint64_t aexrt_b200_packed_act_bytes(uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t stride);
+
+/* int8 codes q = round_half_even(x * 127/amax) (no clamp, 0 when amax <= 0)
+ * into the slab16 layout, plus the per-image scale record the conv reads.
+ * mode = AEXRT_B200_SCALE_PER_TENSOR uses max over all groups, PG16 each
+ * group's own amax.  Replaces aexrt_int8_quant_pack[_pg]
+ * (native/aexrt_d3d12_runtime.cpp:3277-3361, recorder :21646-21659). */
+int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t layout,
+                                uint32_t ldc, uint32_t coff, const uint32_t* amax_groups, uint32_t groups_total,
+                                uint32_t group_offset, uint32_t mode, uint32_t consumer_stride, void* q_out,
+                                float* scale_rec, void* stream);
+
+/* ---------------------------------------------------------------- a2/a9: plans
+ * Builds a device-resident W8A8 conv plan from layout-8 weights (codes in
+ * [oc][ic][kh][kw] order + per-oc fp32 scale) and fp32 bias.  kernel_id is the
+ * reference's planned kernel (51 1x1, 52 3x3 s1, 53 3x3 s2) and must pass the
+ * reference's guard can_use_conv_int8 (native/aexrt_d3d12_runtime.cpp:9398-9422)
+ * plus IC % 16 == 0 when flags has INT8_PERGROUP; the weight repack replaces
+ * ensure_conv_int8_weight's uint32 repack (runtime.cpp:21744-21775).
+ * block_n = 0 picks the output-channel tile automatically.  Allocates device
+ * memory (set-up time only).  Returns NULL on error. */
+AexrtB200ConvPlan* aexrt_b200_conv_plan_create(const AexrtConv2DDesc* desc, uint32_t kind, uint32_t kernel_id,
+                                               uint32_t flags, const int8_t* codes, const float* w_scale,
+                                               const float* bias, uint32_t block_n);
+
+/* fp16 conv plan (stem / detect head of the model): fp32 weights are rounded
+ * to fp16, accumulation is fp32.  Any k in {1,3}, stride in {1,2}, pad k/2. */
+AexrtB200ConvPlan* aexrt_b200_conv_plan_create_f16(const AexrtConv2DDesc* desc, uint32_t kind, const float* weight,
+                                                   const float* bias, uint32_t block_n);
+
+int aexrt_b200_conv_plan_info(const AexrtB200ConvPlan* plan, AexrtB200ConvPlanInfo* info);
+void aexrt_b200_conv_plan_destroy(AexrtB200ConvPlan* plan);
+
+/* ---------------------------------------------------------------- a6/a7/a10: conv
+ * One W8A8 conv launch (per-tensor or pg16 per the plan flags):
+ *   y = (sum_k q_a*q_w) * amax/127 * w_scale[oc] + bias[oc]      (per tensor)
+ *   y = (sum_g fl32(S_g) * amax_g/127) * w_scale[oc] + bias[oc]  (pg16)
+ * then SiLU (CONV_SILU), then + residual (C2f tail, optional), stored as fp16
+ * into out[pixel*out_ldc + out_coff + oc].  When amax_out is non-NULL the
+ * epilogue also max-es |y| per (image, 16-channel group) into
+ * amax_out[image*amax_stride + amax_goff + oc/16] for the next layer.
+ * acc_dump (optional, debugging) receives the int32 accumulators:
+ * [pixel][oc] per tensor, [group][pixel][oc] for pg16.
+ * Replaces the prequant conv kernels 51/52/53 (runtime.cpp:4614-4923), the LTS
+ * variants (:3371-3812) and the unfused CONCAT / BINARY Add neighbours. */
+int aexrt_b200_conv_w8a8(const AexrtB200ConvPlan* plan, const void* q_act, const float* scale_rec,
+                         const void* residual, uint32_t res_ldc, uint32_t res_coff, void* out, uint32_t out_ldc,
+                         uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride, uint32_t amax_goff,
+                         int32_t* acc_dump, void* stream);
+
+/* fp16 conv launch on slab8 input (see aexrt_b200_pack_f16). */
+int aexrt_b200_conv_f16(const AexrtB200ConvPlan* plan, const void* x_slab8, const void* residual, uint32_t res_ldc,
+                        uint32_t res_coff, void* out, uint32_t out_ldc, uint32_t out_coff, uint32_t* amax_out,
+                        uint32_t amax_stride, uint32_t amax_goff, void* stream);
+
+/* Reads and clears the plan's device status word (synchronises the device).
+ * Non-zero bits mean a pipeline wait gave up (see the kernel sources). */
+int aexrt_b200_conv_status(const AexrtB200ConvPlan* plan, uint32_t* status);
+
+/* fp16 slab8 repack of an NHWC fp16 or NCHW fp16/fp32 tensor for fp16 convs. */
+uint64_t aexrt_b200_packed_f16_bytes(uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t stride);
+int aexrt_b200_pack_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t layout, uint32_t ldc,
+                        uint32_t coff, uint32_t consumer_stride, void* out, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AEXRT_B200_H */

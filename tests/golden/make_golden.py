@@ -1,0 +1,166 @@
+"""Generate the golden fixtures under tests/golden/ (run in the build container).
+
+Two kinds of fixture are written:
+
+1. ``weights_layout8.npz`` — layout-8 payloads produced by the REFERENCE'S OWN
+   weight quantizer ``_add_packed_conv_int8`` (src/aexrt/engine.py:2418-2465),
+   imported from the reference source tree, for seeded weights including edge
+   cases (an all-zero output channel, exact half-way products, fp16 engines).
+   These pin ``oracle.w8a8.quantize_conv_weight_int8`` and the product's
+   weight packer bit-for-bit.
+2. ``tiny_w8a8.aexrt`` + ``tiny_w8a8.npz`` — a small engine compiled by the
+   reference's ``build_aexrt_engine`` with algo overrides 51/52/53 and one
+   pg16 command, plus the graph's constants.  They pin the kernel-plan record
+   semantics (kernel id, flags) and the packed-weight section format the
+   product's engine reader consumes.
+3. ``act_cases.npz`` — seeded activation / conv cases run through the CPU
+   oracle (amax, int8 codes, int32 accumulators, fp32/fp16 outputs).  The
+   reference has no W8A8 golden vectors of its own, so these are regression
+   pins of the restatement, not of the reference.
+
+Usage (needs the reference source tree, which only the build container has)::
+
+    python tests/golden/make_golden.py --reference-src <reference>/src
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+
+
+def _silu(z):
+    return z / (1.0 + np.exp(-z))
+
+
+def weight_cases():
+    rng = np.random.default_rng(1234)
+    cases = []
+    for i, (shape, prec) in enumerate([
+        ((32, 16, 3, 3), 1), ((32, 16, 3, 3), 2), ((16, 32, 1, 1), 1), ((24, 16, 3, 3), 2),
+        ((16, 48, 1, 1), 2), ((32, 32, 3, 3), 1),
+    ]):
+        w = rng.normal(0.0, 0.05, shape).astype(np.float32)
+        if i == 0:
+            w[3] = 0.0  # all-zero channel -> scale 1.0
+            # exact half-way products: amax 1.27 -> scale 0.01, inv 100 -> 0.005*100 = 0.5
+            w[5] = 0.0
+            w[5, 0, 0, 0] = 1.27
+            w[5, 1, 0, 0] = 0.005
+            w[5, 2, 0, 0] = -0.015
+        cases.append((w, prec))
+    return cases
+
+
+def make_weights(ref_engine):
+    out = {}
+    for i, (w, prec) in enumerate(weight_cases()):
+        oc, ic, kh, kw = w.shape
+        packed = {}
+        values = [{"raw": w.astype("<f4").tobytes()}]
+        ref_engine._add_packed_conv_int8(
+            packed, values, weight_id=0, in_channels=ic, out_channels=oc,
+            kernel_elems=kh * kw, precision=prec,
+        )
+        out[f"w{i}"] = w
+        out[f"prec{i}"] = np.int32(prec)
+        out[f"payload{i}"] = np.frombuffer(packed[0]["data"], dtype=np.uint8)
+    out["count"] = np.int32(len(weight_cases()))
+    np.savez_compressed(os.path.join(HERE, "weights_layout8.npz"), **out)
+
+
+def make_tiny_engine(aexrt):
+    """conv3x3 s1 16->32 (pg16) -> conv3x3 s2 32->32 -> conv1x1 32->16 -> rank-3 output."""
+    rng = np.random.default_rng(7)
+    g = aexrt.Graph("tiny_w8a8")
+    g.input("images", aexrt.TensorSpec((1, 16, 16, 16), "float32"))
+    consts = {}
+
+    def conv(name, x, ic, oc, k, s):
+        w = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
+        b = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+        g.const(name + ".w", w)
+        g.const(name + ".b", b)
+        consts[name + ".w"] = w
+        consts[name + ".b"] = b
+        p = k // 2
+        g.conv2d(name + ".c", x, name + ".w", name + ".b", strides=(s, s), pads=(p, p, p, p))
+        g.sigmoid(name + ".s", name + ".c")
+        g.mul(name + ".y", name + ".c", name + ".s")
+        return name + ".y"
+
+    y = conv("l0", "images", 16, 32, 3, 1)
+    y = conv("l1", y, 32, 32, 3, 2)
+    y = conv("l2", y, 32, 8, 1, 1)
+    g.reshape("out", y, [1, 8, 64])
+    g.output("out")
+    eng = aexrt.build_aexrt_engine(
+        g, algo_overrides={0: 52, 1: 53, 2: 51}, int8_pergroup=[0], precision="fp16",
+    )
+    with open(os.path.join(HERE, "tiny_w8a8.aexrt"), "wb") as f:
+        f.write(eng)
+    info = aexrt.inspect_aexrt_engine(eng)
+    plan = np.array(info["kernel_plan"], dtype=np.uint32)
+    np.savez_compressed(os.path.join(HERE, "tiny_w8a8.npz"), kernel_plan=plan, **consts)
+
+
+def make_act_cases():
+    sys.path.insert(0, ROOT)
+    from oracle import w8a8 as ow
+
+    rng = np.random.default_rng(2024)
+    out = {}
+    specs = [
+        # name, N, IC, H, W, OC, K, S, mode, silu, residual
+        ("c3s1_pt", 2, 32, 10, 12, 32, 3, 1, 0, True, False),
+        ("c3s1_pg", 2, 32, 10, 12, 32, 3, 1, 1, True, False),
+        ("c3s2_pt", 2, 16, 12, 14, 32, 3, 2, 0, True, False),
+        ("c3s2_pg", 1, 48, 9, 11, 16, 3, 2, 1, True, False),
+        ("c1_pt", 2, 48, 7, 9, 32, 1, 1, 0, True, False),
+        ("c1_pg", 2, 32, 7, 9, 48, 1, 1, 1, False, False),
+        ("c3s1_res", 2, 16, 8, 8, 16, 3, 1, 0, True, True),
+    ]
+    for name, n, ic, h, w, oc, k, s, mode, silu, res in specs:
+        x = _silu(rng.standard_normal((n, ic, h, w)).astype(np.float32)).astype(np.float16)
+        if name == "c3s1_pt":
+            x[1] = 0  # an all-zero image: amax 0 -> zero codes
+        wt = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
+        b = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+        p = k // 2
+        oh, ow_ = ow.conv_out_hw(h, w, k, s, p)
+        r = rng.standard_normal((n, oc, oh, ow_)).astype(np.float16) if res else None
+        o = ow.conv_w8a8(x, wt, b, k, s, p, mode=mode, silu=silu, residual=r)
+        meta = np.array([n, ic, h, w, oc, k, s, p, mode, int(silu), int(res)], dtype=np.int32)
+        out[name + ".meta"] = meta
+        out[name + ".x"] = x
+        out[name + ".w"] = wt
+        out[name + ".b"] = b
+        if r is not None:
+            out[name + ".res"] = r
+        for key in ("amax_t", "amax_g", "xq", "wq", "w_scale", "acc", "y"):
+            out[name + "." + key] = o[key]
+    out["names"] = np.array([s[0] for s in specs])
+    np.savez_compressed(os.path.join(HERE, "act_cases.npz"), **out)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference-src", default=None, help="path to the reference's src/ directory")
+    args = ap.parse_args()
+    if args.reference_src:
+        sys.path.insert(0, args.reference_src)
+        import aexrt
+        from aexrt import engine as ref_engine
+
+        make_weights(ref_engine)
+        make_tiny_engine(aexrt)
+    make_act_cases()
+
+
+if __name__ == "__main__":
+    main()

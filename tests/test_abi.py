@@ -1,0 +1,75 @@
+"""CPU tests of the C ABI boundary: the library loads, exports every declared
+symbol, and its host-side logic (weight quantizer, validation) behaves like the
+reference.  No kernel is launched here."""
+import ctypes
+import subprocess
+
+import numpy as np
+import pytest
+
+from aexrt_b200 import _native, ops
+from oracle import w8a8 as ow
+
+
+def test_library_exports_every_header_symbol():
+    lib = _native.load()
+    names = _native.header_functions()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", _native.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.split()[-1].startswith("aexrt_b200_")}
+    assert exported == set(names)
+    assert lib.aexrt_b200_abi_version() == 1
+
+
+def test_conv_desc_layout_matches_reference():
+    # native/aexrt.h:98-115: sixteen uint32 fields in this order
+    assert ctypes.sizeof(_native.AexrtConv2DDesc) == 64
+    assert [f[0] for f in _native.AexrtConv2DDesc._fields_][:4] == ["batch", "in_channels", "in_h", "in_w"]
+
+
+def test_c_weight_quantizer_matches_reference_payloads(golden_dir):
+    d = np.load(f"{golden_dir}/weights_layout8.npz")
+    for i in range(int(d["count"])):
+        q, s = ops.quantize_conv_weight_int8(d[f"w{i}"], int(d[f"prec{i}"]) == 2)
+        assert ow.layout8_payload(q, s) == d[f"payload{i}"].tobytes(), f"case {i}"
+
+
+def test_c_weight_quantizer_random_matches_oracle():
+    rng = np.random.default_rng(5)
+    for shape in [(64, 32, 3, 3), (17, 8, 1, 1), (8, 4, 3, 3)]:
+        w = (rng.standard_normal(shape) * rng.uniform(1e-3, 10)).astype(np.float32)
+        for fp16 in (False, True):
+            q, s = ops.quantize_conv_weight_int8(w, fp16)
+            q2, s2 = ow.quantize_conv_weight_int8(w, fp16)
+            assert np.array_equal(q, q2) and np.array_equal(s, s2)
+
+
+@pytest.mark.parametrize("args,msg", [
+    (dict(ic=64, k=3, s=1, pg16=False, kid=54), "unknown int8 kernel"),
+    (dict(ic=20, k=3, s=1, pg16=True, kid=52), "pg16"),
+    (dict(ic=6, k=3, s=1, pg16=False, kid=52), "in_channels % 4"),
+    (dict(ic=64, k=1, s=1, pg16=False, kid=52), "kernels 52/53"),
+    (dict(ic=64, k=3, s=1, pg16=False, kid=53), "kernel 53"),
+])
+def test_plan_create_rejects_like_the_reference_guard(args, msg):
+    """can_use_conv_int8 (runtime.cpp:9398-9422): invalid plans fail closed, with a message, before any launch."""
+    lib = _native.load()
+    k, s = args["k"], args["s"]
+    desc = ops.conv_desc(1, args["ic"], 16, 16, 32, k, s, k // 2)
+    codes = np.zeros((32, args["ic"] * k * k), np.int8)
+    scale = np.ones(32, np.float32)
+    bias = np.zeros(32, np.float32)
+    h = lib.aexrt_b200_conv_plan_create(ctypes.byref(desc), 2, args["kid"], 16 if args["pg16"] else 0,
+                                        codes.ctypes.data, scale.ctypes.data, bias.ctypes.data, 0)
+    assert not h
+    assert msg in _native.last_error()
+
+
+def test_entry_points_fail_closed_on_null():
+    lib = _native.load()
+    assert lib.aexrt_b200_act_amax_f16(None, 1, 16, 4, 4, 1, 16, 0, None, 1, 0, 1, None) == 0
+    assert "null" in _native.last_error()
+    assert lib.aexrt_b200_conv_w8a8(None, None, None, None, 0, 0, None, 0, 0, None, 0, 0, None, None) == 0
+    assert lib.aexrt_b200_packed_act_bytes(2, 20, 7, 9, 2) == 2 * 2 * 8 * 10 * 16

@@ -1,0 +1,205 @@
+"""GPU parity of the tcgen05 W8A8 conv against the oracle.
+
+Bars (BASELINE parity gates): int8 codes and int32 accumulators bit-exact;
+fp16 layer outputs within max-abs 1e-2 of the oracle's fp32 epilogue rounded to
+fp16; the next-layer amax equals the amax of the stored fp16 output exactly.
+"""
+import numpy as np
+import pytest
+
+from oracle import w8a8 as ow
+from tests._util import bits_to_f32, nchw_to_nhwc, nhwc_to_nchw, seeded_act, slab16_to_nchw
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2  # max-abs on fp16 layer outputs (BASELINE / README.md:62-63 gate family)
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def run_gpu_layer(x, weight, bias, k, s, mode, silu=True, residual=None, block_n=0, wq=None, w_scale=None,
+                  out_ldc=None, out_coff=0):
+    """quantize (NCHW fp16 input) + conv through the C ABI; returns numpy results."""
+    torch = _torch()
+    from aexrt_b200 import ops
+
+    n, ic, h, w = x.shape
+    oc = weight.shape[0]
+    if wq is None:
+        wq, w_scale = ops.quantize_conv_weight_int8(weight)
+    plan = ops.ConvPlan.int8(n, ic, h, w, oc, k, s, wq, w_scale, bias, silu=silu, pg16=(mode == 1), block_n=block_n)
+    xt = torch.from_numpy(x).cuda()
+    amax = ops.act_amax(xt, ops.LAYOUT_NCHW_F16)
+    q, rec = ops.act_quantize(xt, amax, mode, ops.LAYOUT_NCHW_F16, consumer_stride=s)
+    oh, ow_ = plan.desc.out_h, plan.desc.out_w
+    ldc = out_ldc or oc
+    out = torch.zeros((n, oh, ow_, ldc), dtype=torch.float16, device="cuda")
+    groups = (ic + 15) // 16
+    dump_shape = (groups, n * oh * ow_, oc) if mode == 1 else (n * oh * ow_, oc)
+    dump = torch.zeros(dump_shape, dtype=torch.int32, device="cuda")
+    amax_out = torch.zeros((n, ldc // 16), dtype=torch.int32, device="cuda")
+    res_t = torch.from_numpy(nchw_to_nhwc(residual)).cuda() if residual is not None else None
+    plan.run(q, rec, out=out, out_coff=out_coff, residual=res_t, amax_out=amax_out, amax_goff=out_coff // 16,
+             acc_dump=dump)
+    torch.cuda.synchronize()
+    assert plan.status() == 0
+    y = nhwc_to_nchw(out.cpu().numpy()[..., out_coff:out_coff + oc])
+    d = dump.cpu().numpy()
+    if mode == 1:
+        acc_g = d.reshape(groups, n, oh, ow_, oc).transpose(1, 0, 4, 2, 3)
+        acc = acc_g.sum(axis=1).astype(np.int32)
+    else:
+        acc_g = None
+        acc = d.reshape(n, oh, ow_, oc).transpose(0, 3, 1, 2)
+    return dict(y=y, acc=acc, acc_g=acc_g, xq=slab16_to_nchw(q.cpu().numpy(), ic, h, w), plan=plan,
+                amax_out=bits_to_f32(amax_out.cpu().numpy()), out_full=out.cpu().numpy())
+
+
+def check_against_oracle(x, weight, bias, k, s, mode, silu=True, residual=None, block_n=0):
+    g = run_gpu_layer(x, weight, bias, k, s, mode, silu=silu, residual=residual, block_n=block_n)
+    o = ow.conv_w8a8(x, weight, bias, k, s, k // 2, mode=mode, silu=silu, residual=residual)
+    assert np.array_equal(g["xq"], o["xq"]), "int8 codes differ"
+    assert np.array_equal(g["acc"], o["acc"]), "int32 accumulators differ"
+    if mode == 1:
+        assert np.array_equal(g["acc_g"], o["acc_g"]), "pg16 group sub-sums differ"
+    err = np.abs(g["y"].astype(np.float32) - o["y32"]).max()
+    assert err <= TOL, f"fp16 output max-abs error {err}"
+    # epilogue amax of the stored fp16 output (the next layer's quantizer input)
+    _, ag = ow.act_amax(g["y"])
+    assert np.array_equal(g["amax_out"][:, :ag.shape[1]], ag)
+    return g, o, err
+
+
+def test_golden_act_cases(golden_dir):
+    d = np.load(f"{golden_dir}/act_cases.npz")
+    for name in d["names"]:
+        name = str(name)
+        n, ic, h, w, oc, k, s, p, mode, silu, res = (int(v) for v in d[name + ".meta"])
+        g = run_gpu_layer(d[name + ".x"], d[name + ".w"], d[name + ".b"], k, s, mode, silu=bool(silu),
+                          residual=d[name + ".res"] if res else None)
+        assert np.array_equal(g["xq"], d[name + ".xq"]), name
+        assert np.array_equal(g["acc"], d[name + ".acc"]), name
+        err = np.abs(g["y"].astype(np.float32) - d[name + ".y"].astype(np.float32)).max()
+        assert err <= TOL, (name, err)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("n,ic,h,w,oc,k,s", [
+    (1, 64, 80, 80, 128, 3, 1),    # BASELINE config 1 (C1 block)
+    (1, 128, 40, 40, 128, 1, 1),   # config 2 sweep, batch 1
+    (1, 64, 80, 80, 64, 3, 1),
+    (1, 32, 160, 160, 64, 3, 2),
+    (1, 128, 20, 20, 256, 3, 2),
+    (2, 16, 13, 11, 32, 3, 1),     # ragged: H*W not a multiple of the tile, 16 input channels
+    (2, 48, 9, 7, 16, 1, 1),
+    (3, 32, 11, 9, 48, 3, 2),      # odd input dims for stride 2
+])
+def test_conv_parity(n, ic, h, w, oc, k, s, mode):
+    rng = np.random.default_rng(n * 1000 + ic + oc + k + s + mode)
+    x = seeded_act(rng, (n, ic, h, w))
+    weight = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    check_against_oracle(x, weight, bias, k, s, mode)
+
+
+@pytest.mark.parametrize("block_n", [16, 32, 64, 128, 256])
+def test_block_n_variants_bitexact(block_n):
+    """Every output-channel tile gives the same accumulators (the autotuner's candidates)."""
+    rng = np.random.default_rng(3)
+    x = seeded_act(rng, (2, 32, 12, 10))
+    weight = rng.normal(0, 0.05, (256, 32, 3, 3)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (256,)).astype(np.float32)
+    check_against_oracle(x, weight, bias, 3, 1, 0, block_n=block_n)
+    if block_n <= 128:
+        check_against_oracle(x, weight, bias, 3, 1, 1, block_n=block_n)
+
+
+def test_residual_and_no_silu():
+    rng = np.random.default_rng(4)
+    x = seeded_act(rng, (2, 32, 10, 10))
+    weight = rng.normal(0, 0.05, (32, 32, 3, 3)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (32,)).astype(np.float32)
+    res = rng.standard_normal((2, 32, 10, 10)).astype(np.float16)
+    check_against_oracle(x, weight, bias, 3, 1, 0, residual=res)
+    check_against_oracle(x, weight, bias, 1, 1, 1, silu=False)
+
+
+def test_output_slice_of_concat_buffer():
+    """The epilogue writes into a channel slice of a wider NHWC buffer (concat by placement)."""
+    rng = np.random.default_rng(6)
+    x = seeded_act(rng, (2, 32, 8, 8))
+    weight = rng.normal(0, 0.05, (32, 32, 3, 3)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (32,)).astype(np.float32)
+    g = run_gpu_layer(x, weight, bias, 3, 1, 0, out_ldc=96, out_coff=48)
+    o = ow.conv_w8a8(x, weight, bias, 3, 1, 1)
+    assert np.abs(g["y"].astype(np.float32) - o["y32"]).max() <= TOL
+    full = g["out_full"]
+    assert (full[..., :48] == 0).all() and (full[..., 80:] == 0).all()
+    assert (g["amax_out"][:, :3] == 0).all() and (g["amax_out"][:, 5:] == 0).all()
+
+
+def test_baseline_pg16_output_channel_variant():
+    """BASELINE.json's wording: weights quantized per 16-output-channel group; the
+    epilogue takes any per-oc scale vector, so this is the group scale broadcast."""
+    rng = np.random.default_rng(8)
+    x = seeded_act(rng, (1, 64, 20, 20))
+    weight = rng.normal(0, 0.05, (128, 64, 3, 3)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (128,)).astype(np.float32)
+    grp = np.abs(weight).reshape(8, -1).max(axis=1)
+    scale = np.repeat((grp / np.float32(127)).astype(np.float32), 16)
+    inv = (np.float32(1) / scale).astype(np.float32)
+    prod = (weight.reshape(128, -1) * inv[:, None]).astype(np.float32)
+    wq = np.clip(np.sign(prod) * np.floor(np.abs(prod) + np.float32(0.5)), -127, 127).astype(np.int8)
+    g = run_gpu_layer(x, weight, bias, 3, 1, 0, wq=wq, w_scale=scale)
+    o = ow.conv_w8a8(x, weight, bias, 3, 1, 1, wq=wq, w_scale=scale)
+    assert np.array_equal(g["acc"], o["acc"])
+    assert np.abs(g["y"].astype(np.float32) - o["y32"]).max() <= TOL
+
+
+@pytest.mark.parametrize("n,ic,h,w,oc,k,s", [
+    (64, 128, 40, 40, 128, 1, 1),
+    (64, 64, 80, 80, 64, 3, 1),
+    (64, 32, 160, 160, 64, 3, 2),
+    (64, 128, 20, 20, 256, 3, 2),
+])
+def test_conv_parity_batch64(n, ic, h, w, oc, k, s):
+    """BASELINE config 2 at batch 64: per-image scales, exact accumulators."""
+    rng = np.random.default_rng(64 + ic + oc)
+    x = seeded_act(rng, (n, ic, h, w))
+    weight = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    check_against_oracle(x, weight, bias, k, s, 0)
+
+
+@pytest.mark.parametrize("n,ic,h,w,oc,k,s,silu", [
+    (2, 3, 32, 32, 16, 3, 2, True),   # the model's stem (3 input channels padded to 8)
+    (2, 64, 10, 10, 64, 3, 1, True),
+    (2, 64, 10, 10, 64, 1, 1, False),
+    (1, 64, 20, 20, 4, 1, 1, False),  # class logits: 4 outputs
+])
+def test_fp16_conv_vs_torch(n, ic, h, w, oc, k, s, silu):
+    """fp16 conv (stem / detect head) against a plain PyTorch fp32 conv of the fp16-rounded operands."""
+    torch = _torch()
+    from aexrt_b200 import ops
+
+    rng = np.random.default_rng(ic + oc)
+    x = rng.uniform(0, 1, (n, ic, h, w)).astype(np.float32)
+    weight = rng.normal(0, 1 / np.sqrt(ic * k * k), (oc, ic, k, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    plan = ops.ConvPlan.fp16(n, ic, h, w, oc, k, s, weight, bias, silu=silu)
+    xt = torch.from_numpy(x).cuda()
+    packed = ops.pack_f16(xt, ops.LAYOUT_NCHW_F32, consumer_stride=s)
+    out = plan.run(packed)
+    torch.cuda.synchronize()
+    assert plan.status() == 0
+    xr = torch.from_numpy(x.astype(np.float16).astype(np.float32))
+    wr = torch.from_numpy(weight.astype(np.float16).astype(np.float32))
+    ref = torch.nn.functional.conv2d(xr, wr, torch.from_numpy(bias), stride=s, padding=k // 2)
+    if silu:
+        ref = ref * torch.sigmoid(ref)
+    got = torch.from_numpy(nhwc_to_nchw(out.cpu().numpy()).astype(np.float32))
+    err = (got - ref).abs().max().item()
+    assert err <= 1e-2 * max(1.0, ref.abs().max().item() / 8), err
