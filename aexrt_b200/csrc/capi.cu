@@ -84,11 +84,12 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* 
 }
 
 // Output tile (tw x th <= 128 pixels) maximising the useful fraction of the
-// 128-row MMA tile; ties prefer fewer, wider tiles.
-void pick_tile(int oh, int ow, int& tw, int& th) {
+// 128-row MMA tile; ties prefer fewer, wider tiles.  max_tw keeps one TMA box
+// row (tw pixels of 16 bytes) within the 256-element box limit.
+void pick_tile(int oh, int ow, int max_tw, int& tw, int& th) {
   double best = -1.0;
   tw = th = 1;
-  for (int w = 1; w <= std::min(ow, 128); ++w) {
+  for (int w = 1; w <= std::min(ow, max_tw); ++w) {
     const int h = std::min(oh, 128 / w);
     const long tiles = static_cast<long>((oh + h - 1) / h) * ((ow + w - 1) / w);
     const double util = static_cast<double>(oh) * ow / (static_cast<double>(tiles) * 128.0);
@@ -112,17 +113,18 @@ struct AexrtB200ConvPlan {
   int tw = 0, th = 0, tiles_w = 0, tiles_h = 0;
   int bn = 0, n_tiles = 0, oc_alloc = 0;
   int q_total = 0, kk_p = 0, sps = 0, stages = 0, smem = 0;
-  void* d_w = nullptr;
+  int grid = 0;          // persistent CTAs (one per SM, at most one per tile)
+  int total_tiles = 0;
+  void* d_w = nullptr;   // [n_tile][q_total][bn][16 bytes]
   float* d_scale = nullptr;
   float* d_bias = nullptr;
   uint32_t* d_status = nullptr;
-  CUtensorMap w_map;
   int device = 0;
 };
 
 namespace {
 
-using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const ConvTcParams);
+using KernelFn = void (*)(const CUtensorMap, const ConvTcParams);
 constexpr int kMaxConvSmem = 200 * 1024;
 
 template <bool F16, bool PG>
@@ -217,7 +219,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   p->slabs = (ic + cps - 1) / cps;
   p->in_hp = static_cast<int>(d.in_h) + (p->stride == 2 ? (d.in_h & 1) : 0);
   p->in_wp = static_cast<int>(d.in_w) + (p->stride == 2 ? (d.in_w & 1) : 0);
-  pick_tile(static_cast<int>(d.out_h), static_cast<int>(d.out_w), p->tw, p->th);
+  pick_tile(static_cast<int>(d.out_h), static_cast<int>(d.out_w), f16 ? 32 : 16, p->tw, p->th);
   p->tiles_w = (static_cast<int>(d.out_w) + p->tw - 1) / p->tw;
   p->tiles_h = (static_cast<int>(d.out_h) + p->th - 1) / p->th;
   p->bn = choose_bn(oc, p->pg, block_n);
@@ -237,16 +239,16 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   }
   p->sps = std::min(8, p->q_total);
   {
+    // one persistent CTA per SM: spend up to ~200 KB of shared memory on pipeline stages
     const ConvSmemPlan one = conv_smem_plan(p->tw, p->th, p->sps, 1, p->bn);
-    const int budget = 110 * 1024;
-    int st = (budget - 2048 - 128) / one.stage_bytes;
-    const int stage_iters = (p->q_total + p->sps - 1) / p->sps;
-    st = std::max(2, std::min({st, 6, std::max(2, stage_iters)}));
+    const int budget = 200 * 1024;
+    const int st = std::max(2, std::min((budget - 2048 - 256) / one.stage_bytes, 8));
     p->stages = st;
     p->smem = conv_smem_plan(p->tw, p->th, p->sps, st, p->bn).total_bytes;
   }
+  p->total_tiles = static_cast<int>(d.batch) * p->tiles_h * p->tiles_w * p->n_tiles;
 
-  // ---- weight repack into [slot][oc_alloc][16 bytes]
+  // ---- weight repack into [n_tile][slot][bn][16 bytes]: one stage of B is one contiguous run
   const size_t slot_row = 16;
   std::vector<uint8_t> packed(static_cast<size_t>(p->q_total) * p->oc_alloc * slot_row, 0);
   for (int q = 0; q < p->q_total; ++q) {
@@ -262,7 +264,8 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
     }
     if (tap < 0) continue;
     for (int o = 0; o < oc; ++o) {
-      uint8_t* dst = packed.data() + (static_cast<size_t>(q) * p->oc_alloc + o) * slot_row;
+      const int nt = o / p->bn, on = o - nt * p->bn;
+      uint8_t* dst = packed.data() + ((static_cast<size_t>(nt) * p->q_total + q) * p->bn + on) * slot_row;
       for (int c = 0; c < cps; ++c) {
         const int ci = slab * cps + c;
         if (ci >= ic) continue;
@@ -288,13 +291,9 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
          cuda_ok(cudaMemcpy(p->d_scale, scale, sizeof(float) * oc, cudaMemcpyHostToDevice), "copy scale");
   }
   if (ok) {
-    const uint64_t dims[3] = {static_cast<uint64_t>(f16 ? 8 : 16), static_cast<uint64_t>(p->oc_alloc),
-                              static_cast<uint64_t>(p->q_total)};
-    const uint64_t strides[2] = {16, 16ull * p->oc_alloc};
-    const uint32_t box[3] = {static_cast<uint32_t>(f16 ? 8 : 16), static_cast<uint32_t>(p->bn),
-                             static_cast<uint32_t>(p->sps)};
-    ok = encode_map(&p->w_map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, p->d_w, dims,
-                    strides, box);
+    int sms = 0;
+    ok = cuda_ok(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->device), "SM count");
+    p->grid = std::max(1, std::min(p->total_tiles, sms));
   }
   if (ok) {
     // the attribute is a per-kernel cap shared by every plan of this instance: set it to the
@@ -315,17 +314,20 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
 bool encode_act_map(const AexrtB200ConvPlan* p, const void* x, CUtensorMap* map) {
   const uint64_t hp = p->in_hp, wp = p->in_wp;
   const uint64_t sn = static_cast<uint64_t>(p->slabs) * p->desc.batch;
-  const uint32_t ce = p->f16 ? 8 : 16;  // elements per 16-byte slot
+  const uint32_t ce = p->f16 ? 8 : 16;  // elements per 16-byte slot (one pixel of one slab)
   const CUtensorMapDataType dt = p->f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const uint32_t box_x = ce * static_cast<uint32_t>(p->tw);  // one box row = tw pixels
   if (p->stride == 1) {
-    const uint64_t dims[4] = {ce, wp, hp, sn};
-    const uint64_t strides[3] = {16, 16 * wp, 16 * wp * hp};
-    const uint32_t box[4] = {ce, static_cast<uint32_t>(p->tw), static_cast<uint32_t>(p->th), 1};
-    return encode_map(map, dt, 4, x, dims, strides, box);
+    // [image*slab][H][W*16 bytes]
+    const uint64_t dims[3] = {ce * wp, hp, sn};
+    const uint64_t strides[2] = {16 * wp, 16 * wp * hp};
+    const uint32_t box[3] = {box_x, static_cast<uint32_t>(p->th), 1};
+    return encode_map(map, dt, 3, x, dims, strides, box);
   }
-  const uint64_t dims[5] = {2ull * ce, wp / 2, 2, hp / 2, sn};
-  const uint64_t strides[4] = {32, 16 * wp, 32 * wp, 16 * wp * hp};
-  const uint32_t box[5] = {ce, static_cast<uint32_t>(p->tw), 1, static_cast<uint32_t>(p->th), 1};
+  // [image*slab][H/2][2 (row parity)][2 (column parity)][W/2 * 16 bytes]
+  const uint64_t dims[5] = {ce * wp / 2, 2, 2, hp / 2, sn};
+  const uint64_t strides[4] = {8 * wp, 16 * wp, 32 * wp, 16 * wp * hp};
+  const uint32_t box[5] = {box_x, 1, 1, static_cast<uint32_t>(p->th), 1};
   return encode_map(map, dt, 5, x, dims, strides, box);
 }
 
@@ -348,8 +350,6 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
   ConvTcParams prm{};
   prm.n_img = static_cast<int>(p->desc.batch);
   prm.slabs = p->slabs;
-  prm.in_h = p->in_hp;
-  prm.in_w = p->in_wp;
   prm.oc = static_cast<int>(oc);
   prm.oh = static_cast<int>(p->desc.out_h);
   prm.ow = static_cast<int>(p->desc.out_w);
@@ -360,6 +360,9 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
   prm.th = p->th;
   prm.tiles_w = p->tiles_w;
   prm.tiles_h = p->tiles_h;
+  prm.n_tiles = p->n_tiles;
+  prm.total_tiles = p->total_tiles;
+  prm.w_packed = static_cast<const uint8_t*>(p->d_w);
   prm.q_total = p->q_total;
   prm.sps = p->sps;
   prm.stages = p->stages;
@@ -381,9 +384,8 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
   prm.amax_goff = static_cast<int>(amax_goff);
   prm.acc_dump = acc_dump;
   prm.status = p->d_status;
-  const dim3 grid(static_cast<unsigned>(p->desc.batch * p->tiles_h * p->tiles_w), static_cast<unsigned>(p->n_tiles));
   KernelFn fn = kernel_for(p->f16, p->pg, p->bn);
-  fn<<<grid, kConvThreads, p->smem, static_cast<cudaStream_t>(stream)>>>(act_map, p->w_map, prm);
+  fn<<<p->grid, kConvThreads, p->smem, static_cast<cudaStream_t>(stream)>>>(act_map, prm);
   return cuda_ok(cudaGetLastError(), "conv launch") ? 1 : 0;
 }
 
@@ -522,6 +524,7 @@ int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t 
   q.hp = static_cast<int>(h + (consumer_stride == 2 ? (h & 1) : 0));
   q.wp = static_cast<int>(w + (consumer_stride == 2 ? (w & 1) : 0));
   q.mode = static_cast<int>(mode);
+  q.split = consumer_stride == 2 ? 1 : 0;
   q.out = q_out;
   q.rec = scale_rec;
   const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, n);
@@ -540,6 +543,7 @@ int aexrt_b200_pack_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint3
   QuantParams q;
   quant_params_common(q, x, n, c, h, w, layout, ldc, coff, nullptr, 0, 0);
   q.slabs = static_cast<int>((c + 7) / 8);
+  q.split = consumer_stride == 2 ? 1 : 0;
   q.hp = static_cast<int>(h + (consumer_stride == 2 ? (h & 1) : 0));
   q.wp = static_cast<int>(w + (consumer_stride == 2 ? (w & 1) : 0));
   q.out = out;
@@ -599,6 +603,7 @@ int aexrt_b200_conv_plan_info(const AexrtB200ConvPlan* p, AexrtB200ConvPlanInfo*
   i.smem_bytes = p->smem;
   i.grid_m = p->desc.batch * p->tiles_h * p->tiles_w;
   i.grid_n = p->n_tiles;
+  i.reserved[0] = p->grid;
   i.in_hp = p->in_hp;
   i.in_wp = p->in_wp;
   *info = i;

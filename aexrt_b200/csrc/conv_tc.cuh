@@ -3,25 +3,28 @@
 // variants :3371-3812) and, with kF16, the fp16 convs around it.
 //
 // GEMM view: M = output pixels of one spatial tile of one image (TH x TW <= 128),
-// N = output channels (BN per CTA), K = "slots" of 16 bytes: one slot is one
+// N = output channels (BN per tile), K = "slots" of 16 bytes: one slot is one
 // kernel tap of one 16-channel slab (int8) or 8-channel slab (fp16).
 //
 // Activation operand: the int8 (or fp16) activation lives in HBM as
-//   [image][slab][H][W][16 bytes]
-// so a TMA tiled box (16 B, TW, TH, 1 slab) lands in shared memory as TH*TW
-// contiguous 16-byte rows: exactly one K chunk of the canonical K-major
-// no-swizzle UMMA layout.  Halo / padding rows come from the TMA's out-of-range
-// zero fill.  Stride 2 reads the same bytes through a 5-D view that splits W and
-// H into (pair, phase), so every tap of a 3x3/s2 conv is again a plain box.
+//   stride-1 consumers: [image][slab][H][W][16 bytes]
+//   stride-2 consumers: [image][slab][H][2 (column parity)][W/2][16 bytes]
+// so one TMA tiled box of (16*TW bytes, TH rows) -- TW output columns of one
+// tap -- lands in shared memory as TH*TW contiguous 16-byte rows: exactly one K
+// chunk of the canonical K-major no-swizzle UMMA layout.  A stride-2 tap reads
+// one column parity, which the parity-split layout makes contiguous.  Halo and
+// padding come from the TMA's out-of-range zero fill.
 //
-// Weight operand: pre-packed on the host as [slot][OC][16 bytes]; one TMA box
-// (16 B, BN, SPS) fills a whole pipeline stage.
+// Weight operand: pre-packed on the host as [n_tile][slot][BN][16 bytes], so a
+// stage's worth of B is one contiguous cp.async.bulk copy.
 //
-// Accumulators live in TMEM.  Per-tensor scaling accumulates all of K into one
-// buffer; pg16 scaling (INT8_PERGROUP) orders K by (slab, tap) and drains each
-// slab's int32 sub-sum from one of two ping-pong TMEM buffers into fp32
-// registers, multiplying by that slab's activation scale in ascending group
-// order as the reference's LTS kernels do (runtime.cpp:3450-3468, 3594-3618).
+// The kernel is persistent (one CTA per SM walks a static list of tiles) and
+// keeps two TMEM accumulators, so the epilogue of one accumulation unit overlaps
+// the MMAs of the next.  An accumulation unit is a whole tile for per-tensor
+// scaling, or one 16-channel input slab for pg16 scaling (INT8_PERGROUP): K is
+// then ordered (slab, tap) and each slab's int32 sub-sum is drained into fp32
+// registers scaled by that slab's activation scale, in ascending group order as
+// the reference's LTS kernels do (runtime.cpp:3450-3468, 3594-3618).
 //
 // Warp roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM allocator +
 // MMA issuer, warps 2..9 = epilogue (each owns one TMEM lane quadrant and one
@@ -38,15 +41,18 @@ constexpr int kSlotBytes = 16;
 
 struct ConvTcParams {
   // geometry
-  int n_img, slabs, in_h, in_w;  // activation view (in_h/in_w: dims of the packed buffer)
+  int n_img, slabs;
   int oc, oh, ow;
   int ksize, stride, pad;
   int tw, th, tiles_w, tiles_h;
-  int q_total;  // K slots including pads (even)
-  int sps;      // slots per pipeline stage (even)
-  int stages;   // pipeline depth
-  int kk_p;     // pg16: slots per group (taps rounded up to even)
+  int n_tiles;      // output-channel tiles
+  int total_tiles;  // n_img * tiles_h * tiles_w * n_tiles
+  int q_total;      // K slots including pads (even)
+  int sps;          // slots per pipeline stage (even)
+  int stages;       // pipeline depth
+  int kk_p;         // pg16: slots per group (taps rounded up to even)
   int silu;
+  const uint8_t* w_packed;  // [n_tile][q_total][BN][16]
   // scales (int8 only): per image record [1 + slabs] of fp32 amax values
   const float* scale_rec;
   const float* w_scale;
@@ -91,6 +97,22 @@ __host__ __device__ inline ConvSmemPlan conv_smem_plan(int tw, int th, int sps, 
   return s;
 }
 
+struct TileCoord {
+  int img, oh0, ow0, n_tile;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(const ConvTcParams& p, int t) {
+  TileCoord c;
+  const int m_tile = t / p.n_tiles;
+  c.n_tile = t - m_tile * p.n_tiles;
+  const int per_img = p.tiles_w * p.tiles_h;
+  c.img = m_tile / per_img;
+  const int r = m_tile - c.img * per_img;
+  c.oh0 = (r / p.tiles_w) * p.th;
+  c.ow0 = (r % p.tiles_w) * p.tw;
+  return c;
+}
+
 template <bool kPG>
 __device__ __forceinline__ int decode_slot(const ConvTcParams& p, int q, int& slab) {
   const int kk = p.ksize * p.ksize;
@@ -113,67 +135,103 @@ __device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&v)[8]) {
                : "r"(taddr));
 }
 
-// Epilogue of 8 consecutive output channels of one pixel: scale, bias, SiLU,
-// residual, fp16 store; returns the max |fp16 output| bits for the amax.
+__device__ __forceinline__ float tanh_approx(float x) {
+  float r;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// SiLU through the identity sigmoid(y) = (1 + tanh(y/2)) / 2: one MUFU op per element.
+__device__ __forceinline__ float silu_fast(float y) {
+  const float h = 0.5f * y;
+  return fmaf(h, tanh_approx(h), h);
+}
+
+// Epilogue of 8 consecutive output channels of one pixel: `acc` already holds
+// the dequantized sum (int8) or the fp32 accumulator (fp16); applies the
+// per-channel scale, bias, SiLU, residual, stores fp16 and returns the max
+// |fp16 output| bits for the next layer's amax.
 template <bool kF16>
 __device__ __forceinline__ uint32_t epilogue8(const ConvTcParams& p, const float (&acc)[8], int oc_base, bool valid,
                                               size_t pix) {
+  const bool full8 = oc_base + 8 <= p.oc;  // all 8 channels exist (else only oc < p.oc is touched)
+  float wsc[8], bia[8];
+  if (full8) {
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + oc_base);
+    const float4 b0 = __ldg(b4), b1 = __ldg(b4 + 1);
+    bia[0] = b0.x; bia[1] = b0.y; bia[2] = b0.z; bia[3] = b0.w;
+    bia[4] = b1.x; bia[5] = b1.y; bia[6] = b1.z; bia[7] = b1.w;
+    if (!kF16) {
+      const float4* s4 = reinterpret_cast<const float4*>(p.w_scale + oc_base);
+      const float4 s0 = __ldg(s4), s1 = __ldg(s4 + 1);
+      wsc[0] = s0.x; wsc[1] = s0.y; wsc[2] = s0.z; wsc[3] = s0.w;
+      wsc[4] = s1.x; wsc[5] = s1.y; wsc[6] = s1.z; wsc[7] = s1.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      bia[i] = oc_base + i < p.oc ? __ldg(p.bias + oc_base + i) : 0.0f;
+      wsc[i] = (!kF16 && oc_base + i < p.oc) ? __ldg(p.w_scale + oc_base + i) : 0.0f;
+    }
+  }
   float res[8];
   const bool has_res = p.res != nullptr && valid && oc_base < p.oc;
-  const bool full8 = oc_base + 8 <= p.oc;  // all 8 channels exist (else only oc < p.oc is touched)
   if (has_res) {
     const __half* rp = p.res + pix * p.res_ldc + p.res_coff + oc_base;
     if (full8 && p.res_vec) {
       const uint4 r = *reinterpret_cast<const uint4*>(rp);
-      const __half* rh = reinterpret_cast<const __half*>(&r);
+      const __half2* rh = reinterpret_cast<const __half2*>(&r);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) res[i] = __half2float(rh[i]);
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(rh[i]);
+        res[2 * i] = f.x;
+        res[2 * i + 1] = f.y;
+      }
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) res[i] = oc_base + i < p.oc ? __half2float(rp[i]) : 0.0f;
     }
   }
-  __align__(16) __half hv[8];
-  uint32_t amax_bits = 0;
+  __align__(16) __half2 hv[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int oc = oc_base + i;
-    float y = 0.0f;
-    if (oc < p.oc) {
-      y = kF16 ? __fadd_rn(acc[i], p.bias[oc]) : __fadd_rn(__fmul_rn(acc[i], p.w_scale[oc]), p.bias[oc]);
-      if (p.silu) {
-        const float e = __expf(fminf(-y, 80.0f));
-        y = __fdividef(y, 1.0f + e);
-      }
-      if (has_res) y = __fadd_rn(y, res[i]);
+  for (int i = 0; i < 4; ++i) {
+    float y[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int k = 2 * i + j;
+      float v = kF16 ? acc[k] + bia[k] : fmaf(acc[k], wsc[k], bia[k]);
+      if (p.silu) v = silu_fast(v);
+      if (has_res) v += res[k];
+      y[j] = oc_base + k < p.oc ? v : 0.0f;
     }
-    hv[i] = __float2half_rn(y);
-    amax_bits = max(amax_bits, __float_as_uint(fabsf(__half2float(hv[i]))));
+    hv[i] = __floats2half2_rn(y[0], y[1]);
   }
+  const __half2 m01 = __hmax2(__habs2(hv[0]), __habs2(hv[1]));
+  const __half2 m23 = __hmax2(__habs2(hv[2]), __habs2(hv[3]));
+  const __half2 m = __hmax2(m01, m23);
+  const float amax = fmaxf(__low2float(m), __high2float(m));
   if (valid && oc_base < p.oc) {
     __half* op = p.out + pix * p.out_ldc + p.out_coff + oc_base;
     if (full8 && p.out_vec) {
       *reinterpret_cast<uint4*>(op) = *reinterpret_cast<const uint4*>(hv);
     } else {
+      const __half* h = reinterpret_cast<const __half*>(hv);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        if (oc_base + i < p.oc) op[i] = hv[i];
+        if (oc_base + i < p.oc) op[i] = h[i];
     }
   }
-  return valid ? amax_bits : 0u;
+  return valid ? __float_as_uint(amax) : 0u;
 }
 
 template <bool kF16, bool kPG, int BN>
 __global__ void __launch_bounds__(kConvThreads, 1)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap act_map, const __grid_constant__ CUtensorMap w_map,
-                   const ConvTcParams p) {
-  constexpr int kChanPerSlot = kF16 ? 8 : 16;
+    conv_tc_kernel(const __grid_constant__ CUtensorMap act_map, const ConvTcParams p) {
   constexpr int kHalf = BN / 2;       // columns per epilogue warp
   constexpr int kChunks = kHalf / 8;  // 8-column chunks per epilogue warp
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "BN must be a multiple of 16 in [16, 256]");
   static_assert(!kPG || (!kF16 && BN <= 128), "pg16 is int8-only and keeps BN/2 fp32 partials per thread");
-  constexpr int kBufs = kPG ? 2 : 1;
-  constexpr uint32_t kTmemCols = (kBufs * BN <= 32) ? 32 : (kBufs * BN <= 64) ? 64 : (kBufs * BN <= 128) ? 128 : 256;
+  constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
 
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5;
@@ -187,19 +245,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int rows = p.th * p.tw;
-  const int m_tile = blockIdx.x;
-  const int tiles_per_img = p.tiles_w * p.tiles_h;
-  const int img = m_tile / tiles_per_img;
-  const int t_in = m_tile - img * tiles_per_img;
-  const int oh0 = (t_in / p.tiles_w) * p.th;
-  const int ow0 = (t_in % p.tiles_w) * p.tw;
-  const int n0 = blockIdx.y * BN;
-
-  const int groups = kPG ? p.slabs : 1;
-  const int ksteps = p.q_total / 2;
-  const int ksteps_per_group = kPG ? p.kk_p / 2 : ksteps;
-  const int ksteps_per_stage = p.sps / 2;
-  const int stage_iters = (p.q_total + p.sps - 1) / p.sps;
+  const int ksteps_per_unit = kPG ? p.kk_p / 2 : p.q_total / 2;
+  const size_t w_tile_bytes = static_cast<size_t>(p.q_total) * BN * kSlotBytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -212,10 +259,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     }
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&act_map);
-    tma_prefetch_desc(&w_map);
-  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&act_map);
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -228,65 +272,86 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint32_t tx = static_cast<uint32_t>(p.sps * sp.a_box_bytes + sp.b_stage_bytes);
-      for (int it = 0; it < stage_iters; ++it) {
-        const int s = it % p.stages;
-        if (it >= p.stages) {
-          if (!mbar_wait_bounded(&empty[s], ((it / p.stages) - 1) & 1, p.status, kStatusTimeoutEmpty)) break;
-        }
-        uint8_t* a_dst = smem + s * sp.stage_bytes;
-        uint8_t* b_dst = a_dst + sp.a_stage_bytes;
-        mbar_arrive_expect_tx(&full[s], tx);
-        for (int j = 0; j < p.sps; ++j) {
-          int slab;
-          const int tap = decode_slot<kPG>(p, it * p.sps + j, slab);
-          int sn = img * p.slabs + slab;
-          int kh = 0, kw = 0;
-          if (tap < 0) {
-            sn = p.n_img * p.slabs;  // fully out of range: the TMA zero-fills the slot
-          } else {
-            kh = tap / p.ksize;
-            kw = tap - kh * p.ksize;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+        const TileCoord tc = tile_coord(p, t);
+        const uint8_t* w_tile = p.w_packed + static_cast<size_t>(tc.n_tile) * w_tile_bytes;
+        for (int q0 = 0; q0 < p.q_total; q0 += p.sps, ++it) {
+          const int s = it % p.stages;
+          if (it >= p.stages && !mbar_wait_bounded(&empty[s], ((it / p.stages) - 1) & 1, p.status, kStatusTimeoutEmpty)) {
+            ok = false;
+            break;
           }
-          void* dst = a_dst + j * sp.a_slot_stride;
-          if (p.stride == 1) {
-            tma_load_4d(dst, &act_map, &full[s], 0, ow0 + kw - p.pad, oh0 + kh - p.pad, sn);
-          } else {
-            // input column 2*ow + kw - 1 == 2*(ow + dw) + pw  (same for rows)
-            const int pw = (kw + 1) & 1, dw = (kw - 1 - pw) / 2;
-            const int ph = (kh + 1) & 1, dh = (kh - 1 - ph) / 2;
-            tma_load_5d(dst, &act_map, &full[s], pw * kChanPerSlot, ow0 + dw, ph, oh0 + dh, sn);
+          const int rem = min(p.sps, p.q_total - q0);
+          uint8_t* a_dst = smem + s * sp.stage_bytes;
+          uint8_t* b_dst = a_dst + sp.a_stage_bytes;
+          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rem * (sp.a_box_bytes + BN * kSlotBytes)));
+          for (int j = 0; j < rem; ++j) {
+            int slab;
+            const int tap = decode_slot<kPG>(p, q0 + j, slab);
+            int sn = tc.img * p.slabs + slab;
+            int kh = 0, kw = 0;
+            if (tap < 0) {
+              sn = p.n_img * p.slabs;  // fully out of range: the TMA zero-fills the slot
+            } else {
+              kh = tap / p.ksize;
+              kw = tap - kh * p.ksize;
+            }
+            void* dst = a_dst + j * sp.a_slot_stride;
+            if (p.stride == 1) {
+              tma_load_3d(dst, &act_map, &full[s], kSlotBytes / (kF16 ? 2 : 1) * (tc.ow0 + kw - p.pad),
+                          tc.oh0 + kh - p.pad, sn);
+            } else {
+              // input column 2*ow + kw - 1 == 2*(ow + dw) + pw  (same for rows)
+              const int pw = (kw + 1) & 1, dw = (kw - 1 - pw) / 2;
+              const int ph = (kh + 1) & 1, dh = (kh - 1 - ph) / 2;
+              tma_load_5d(dst, &act_map, &full[s], kSlotBytes / (kF16 ? 2 : 1) * (tc.ow0 + dw), pw, ph, tc.oh0 + dh, sn);
+            }
           }
+          bulk_load(b_dst, w_tile + static_cast<size_t>(q0) * BN * kSlotBytes, static_cast<uint32_t>(rem * BN * kSlotBytes),
+                    &full[s]);
         }
-        tma_load_3d(b_dst, &w_map, &full[s], 0, n0, it * p.sps);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc<kF16>(BN);
-      for (int ks = 0; ks < ksteps; ++ks) {
-        const int it = ks / ksteps_per_stage;
-        const int j = ks - it * ksteps_per_stage;
-        const int s = it % p.stages;
-        if (j == 0) {
-          if (!mbar_wait_bounded(&full[s], (it / p.stages) & 1, p.status, kStatusTimeoutFull)) break;
+      int it = 0, u = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+        for (int q0 = 0; q0 < p.q_total && ok; q0 += p.sps, ++it) {
+          const int s = it % p.stages;
+          if (!mbar_wait_bounded(&full[s], (it / p.stages) & 1, p.status, kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
+          const int rem = min(p.sps, p.q_total - q0);
+          const uint32_t a_base = smem_u32(smem + s * sp.stage_bytes);
+          const uint32_t b_base = a_base + sp.a_stage_bytes;
+          for (int j = 0; j < rem / 2; ++j) {
+            const int ks = q0 / 2 + j;
+            const int kin = ks % ksteps_per_unit;
+            const int buf = u & 1;
+            if (kin == 0 && u >= 2) {
+              if (!mbar_wait_bounded(&acc_empty[buf], ((u - 2) >> 1) & 1, p.status, kStatusTimeoutAccEmpty)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            const uint64_t a_desc = smem_desc_kmajor_noswizzle(a_base + 2 * j * sp.a_slot_stride, sp.a_slot_stride, 128);
+            const uint64_t b_desc = smem_desc_kmajor_noswizzle(b_base + 2 * j * BN * kSlotBytes, BN * kSlotBytes, 128);
+            tc_mma<kF16>(tmem_base + buf * BN, a_desc, b_desc, idesc, kin == 0 ? 0u : 1u);
+            if (kin == ksteps_per_unit - 1) {
+              tc_commit(&acc_full[buf]);
+              ++u;
+            }
+          }
+          tc_commit(&empty[s]);
         }
-        const int g = ks / ksteps_per_group;
-        const int kin = ks - g * ksteps_per_group;
-        const int buf = kPG ? (g & 1) : 0;
-        if (kPG && kin == 0 && g >= 2) {
-          if (!mbar_wait_bounded(&acc_empty[buf], ((g - 2) >> 1) & 1, p.status, kStatusTimeoutAccEmpty)) break;
-          tc_fence_after();
-        }
-        const uint32_t a_addr = smem_u32(smem + s * sp.stage_bytes + (2 * j) * sp.a_slot_stride);
-        const uint32_t b_addr = smem_u32(smem + s * sp.stage_bytes + sp.a_stage_bytes + (2 * j) * BN * kSlotBytes);
-        const uint64_t a_desc = smem_desc_kmajor_noswizzle(a_addr, sp.a_slot_stride, 128);
-        const uint64_t b_desc = smem_desc_kmajor_noswizzle(b_addr, BN * kSlotBytes, 128);
-        tc_mma<kF16>(tmem_base + buf * BN, a_desc, b_desc, idesc, kin == 0 ? 0u : 1u);
-        if (j == ksteps_per_stage - 1 || ks == ksteps - 1) tc_commit(&empty[s]);
-        if (kin == ksteps_per_group - 1) tc_commit(&acc_full[buf]);
       }
     }
   } else {
@@ -296,72 +361,88 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     const int row = quad * 32 + lane;  // tile row == TMEM lane
     const int r_h = row / p.tw;
     const int r_w = row - r_h * p.tw;
-    const int oy = oh0 + r_h, ox = ow0 + r_w;
-    const bool valid = row < rows && oy < p.oh && ox < p.ow;
-    const size_t npix = static_cast<size_t>(p.n_img) * p.oh * p.ow;
-    const size_t pix = (static_cast<size_t>(img) * p.oh + (valid ? oy : 0)) * p.ow + (valid ? ox : 0);
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     const int col0 = colh * kHalf;
-    const float* rec = kF16 ? nullptr : p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs);
+    const size_t npix = static_cast<size_t>(p.n_img) * p.oh * p.ow;
+    int u = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      const TileCoord tc = tile_coord(p, t);
+      const int oy = tc.oh0 + r_h, ox = tc.ow0 + r_w;
+      const bool valid = row < rows && oy < p.oh && ox < p.ow;
+      const size_t pix = (static_cast<size_t>(tc.img) * p.oh + (valid ? oy : 0)) * p.ow + (valid ? ox : 0);
+      const int n0 = tc.n_tile * BN;
+      const float* rec = kF16 ? nullptr : p.scale_rec + static_cast<size_t>(tc.img) * (1 + p.slabs);
 
-    if constexpr (!kPG) {
-      if (mbar_wait_bounded(&acc_full[0], 0, p.status, kStatusTimeoutAccFull)) {
+      if constexpr (!kPG) {
+        const int buf = u & 1;
+        if (!mbar_wait_bounded(&acc_full[buf], (u >> 1) & 1, p.status, kStatusTimeoutAccFull)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const float in_scale = kF16 ? 1.0f : __fdiv_rn(rec[0], 127.0f);
 #pragma unroll 1
         for (int c = 0; c < kChunks; ++c) {
           uint32_t v[8];
-          tmem_ld_x8(lane_addr + col0 + c * 8, v);
+          tmem_ld_x8(lane_addr + buf * BN + col0 + c * 8, v);
           tmem_ld_wait();
-          float acc[8];
-          const int oc_base = n0 + col0 + c * 8;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            acc[i] = kF16 ? __uint_as_float(v[i]) : __fmul_rn(static_cast<float>(static_cast<int32_t>(v[i])), in_scale);
+          if (c == kChunks - 1) {
+            // every column of this accumulator has been read: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
           }
+          const int oc_base = n0 + col0 + c * 8;
+          float acc[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            acc[i] = kF16 ? __uint_as_float(v[i]) : __fmul_rn(static_cast<float>(static_cast<int32_t>(v[i])), in_scale);
           if (!kF16 && p.acc_dump != nullptr && valid) {
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               if (oc_base + i < p.oc) p.acc_dump[pix * p.oc + oc_base + i] = static_cast<int32_t>(v[i]);
           }
           const uint32_t m = __reduce_max_sync(0xffffffffu, epilogue8<kF16>(p, acc, oc_base, valid, pix));
-          if (p.amax_out != nullptr && lane == 0 && oc_base < p.oc) {
-            atomicMax(&p.amax_out[static_cast<size_t>(img) * p.amax_stride + p.amax_goff + oc_base / 16], m);
+          if (p.amax_out != nullptr && lane == 0 && oc_base < p.oc && m != 0u) {
+            atomicMax(&p.amax_out[static_cast<size_t>(tc.img) * p.amax_stride + p.amax_goff + oc_base / 16], m);
           }
         }
-      }
-    } else {
-      float fp[kHalf];
-      bool ok = true;
-      for (int g = 0; g < groups; ++g) {
-        const int buf = g & 1;
-        ok = mbar_wait_bounded(&acc_full[buf], (g >> 1) & 1, p.status, kStatusTimeoutAccFull);
+        ++u;
+      } else {
+        float fp[kHalf];
+        for (int g = 0; g < p.slabs; ++g) {
+          const int buf = u & 1;
+          if (!mbar_wait_bounded(&acc_full[buf], (u >> 1) & 1, p.status, kStatusTimeoutAccFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float gs = __fdiv_rn(rec[1 + g], 127.0f);
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) {
+            uint32_t v[8];
+            tmem_ld_x8(lane_addr + buf * BN + col0 + c * 8, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float term = __fmul_rn(static_cast<float>(static_cast<int32_t>(v[i])), gs);
+              fp[c * 8 + i] = g == 0 ? term : __fadd_rn(fp[c * 8 + i], term);
+            }
+            if (p.acc_dump != nullptr && valid) {
+              const int oc_base = n0 + col0 + c * 8;
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                if (oc_base + i < p.oc)
+                  p.acc_dump[(static_cast<size_t>(g) * npix + pix) * p.oc + oc_base + i] = static_cast<int32_t>(v[i]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          ++u;
+        }
         if (!ok) break;
-        tc_fence_after();
-        const float gs = __fdiv_rn(rec[1 + g], 127.0f);
-#pragma unroll
-        for (int c = 0; c < kChunks; ++c) {
-          uint32_t v[8];
-          tmem_ld_x8(lane_addr + buf * BN + col0 + c * 8, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float term = __fmul_rn(static_cast<float>(static_cast<int32_t>(v[i])), gs);
-            fp[c * 8 + i] = g == 0 ? term : __fadd_rn(fp[c * 8 + i], term);
-          }
-          if (p.acc_dump != nullptr && valid) {
-            const int oc_base = n0 + col0 + c * 8;
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              if (oc_base + i < p.oc)
-                p.acc_dump[(static_cast<size_t>(g) * npix + pix) * p.oc + oc_base + i] = static_cast<int32_t>(v[i]);
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[buf]);
-      }
-      if (ok) {
 #pragma unroll
         for (int c = 0; c < kChunks; ++c) {
           const int oc_base = n0 + col0 + c * 8;
@@ -369,8 +450,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 #pragma unroll
           for (int i = 0; i < 8; ++i) acc[i] = fp[c * 8 + i];
           const uint32_t m = __reduce_max_sync(0xffffffffu, epilogue8<false>(p, acc, oc_base, valid, pix));
-          if (p.amax_out != nullptr && lane == 0 && oc_base < p.oc) {
-            atomicMax(&p.amax_out[static_cast<size_t>(img) * p.amax_stride + p.amax_goff + oc_base / 16], m);
+          if (p.amax_out != nullptr && lane == 0 && oc_base < p.oc && m != 0u) {
+            atomicMax(&p.amax_out[static_cast<size_t>(tc.img) * p.amax_stride + p.amax_goff + oc_base / 16], m);
           }
         }
       }

@@ -125,6 +125,7 @@ struct QuantParams {
   int slabs;          // ceil(c_total / channels per slab)
   int hp, wp;         // dims of the packed output buffer (>= h, w; the extra rows/cols are zero)
   int mode;           // int8: 0 = per-tensor scale, 1 = pg16 scale
+  int split;          // 1: stride-2 consumer layout, each row stored as [even columns][odd columns]
   void* out;          // int8 [n][slabs][hp][wp][16] or fp16 [n][slabs][hp][wp][8]
   float* rec;         // int8: per image record [1 + slabs] of fp32 amax (slot 0 = tensor)
 };
@@ -204,7 +205,8 @@ __global__ void quantize_i8_kernel(const QuantParams p) {
       packed[i >> 2] |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * (i & 3));
     }
   }
-  int8_t* out = static_cast<int8_t*>(p.out) + ((static_cast<size_t>(n) * p.slabs + slab) * p.hp * p.wp + pix) * 16;
+  const int dpix = p.split ? h * p.wp + (w & 1) * (p.wp >> 1) + (w >> 1) : pix;
+  int8_t* out = static_cast<int8_t*>(p.out) + ((static_cast<size_t>(n) * p.slabs + slab) * p.hp * p.wp + dpix) * 16;
   *reinterpret_cast<uint4*>(out) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
 }
 
@@ -236,7 +238,8 @@ __global__ void pack_f16_kernel(const QuantParams p) {
       for (int i = 0; i < nch; ++i) hv[i] = __float2half_rn(load_src(s, n, h, w, cin + i));
     }
   }
-  __half* out = static_cast<__half*>(p.out) + ((static_cast<size_t>(n) * p.slabs + slab) * p.hp * p.wp + pix) * 8;
+  const int dpix = p.split ? h * p.wp + (w & 1) * (p.wp >> 1) + (w >> 1) : pix;
+  __half* out = static_cast<__half*>(p.out) + ((static_cast<size_t>(n) * p.slabs + slab) * p.hp * p.wp + dpix) * 8;
   *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(hv);
 }
 

@@ -14,6 +14,8 @@
  *   fp16 activations: NHWC slices (channel stride `ldc`, channel offset `coff`);
  *   int8 codes:       [image][ceil(C/16)][Hp][Wp][16]   ("slab16");
  *   fp16 conv input:  [image][ceil(C/8)][Hp][Wp][8]     ("slab8");
+ *                     for a stride-2 consumer Hp, Wp are rounded up to even and
+ *                     each row is stored as [even columns][odd columns];
  *   amax groups:      uint32 float bits, [image][groups_total] (one per 16 channels);
  *   scale record:     float [image][1 + ceil(C/16)]: slot 0 = per-tensor amax,
  *                     slot 1+g = amax of 16-channel group g (the reference's

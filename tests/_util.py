@@ -3,10 +3,21 @@ arrays and the device layouts of the C ABI (slab16 int8, slab8 fp16, NHWC fp16).
 import numpy as np
 
 
-def slab16_to_nchw(q: np.ndarray, c: int, h: int, w: int) -> np.ndarray:
+def unsplit_columns(q: np.ndarray) -> np.ndarray:
+    """Undo the stride-2 consumer layout: each row [even columns][odd columns] -> natural order."""
+    wp = q.shape[3]
+    out = np.empty_like(q)
+    out[:, :, :, 0::2] = q[:, :, :, : wp // 2]
+    out[:, :, :, 1::2] = q[:, :, :, wp // 2:]
+    return out
+
+
+def slab16_to_nchw(q: np.ndarray, c: int, h: int, w: int, stride: int = 1) -> np.ndarray:
     """[N][S][Hp][Wp][16] int8 -> [N][C][H][W] int8 (drops padding)."""
-    n, s, hp, wp, _ = q.shape
-    x = q.transpose(0, 1, 4, 2, 3).reshape(n, s * 16, hp, wp)
+    if stride == 2:
+        q = unsplit_columns(q)
+    n, s, hp, wp, e = q.shape
+    x = q.transpose(0, 1, 4, 2, 3).reshape(n, s * e, hp, wp)
     return np.ascontiguousarray(x[:, :c, :h, :w])
 
 

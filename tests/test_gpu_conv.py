@@ -54,7 +54,7 @@ def run_gpu_layer(x, weight, bias, k, s, mode, silu=True, residual=None, block_n
     else:
         acc_g = None
         acc = d.reshape(n, oh, ow_, oc).transpose(0, 3, 1, 2)
-    return dict(y=y, acc=acc, acc_g=acc_g, xq=slab16_to_nchw(q.cpu().numpy(), ic, h, w), plan=plan,
+    return dict(y=y, acc=acc, acc_g=acc_g, xq=slab16_to_nchw(q.cpu().numpy(), ic, h, w, s), plan=plan,
                 amax_out=bits_to_f32(amax_out.cpu().numpy()), out_full=out.cpu().numpy())
 
 
@@ -124,7 +124,8 @@ def test_residual_and_no_silu():
     bias = rng.normal(0, 0.1, (32,)).astype(np.float32)
     res = rng.standard_normal((2, 32, 10, 10)).astype(np.float16)
     check_against_oracle(x, weight, bias, 3, 1, 0, residual=res)
-    check_against_oracle(x, weight, bias, 1, 1, 1, silu=False)
+    w1 = rng.normal(0, 0.05, (32, 32, 1, 1)).astype(np.float32)
+    check_against_oracle(x, w1, bias, 1, 1, 1, silu=False)
 
 
 def test_output_slice_of_concat_buffer():

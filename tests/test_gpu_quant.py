@@ -58,7 +58,7 @@ def test_quantize_nchw_bitexact(shape, stride, mode):
     qn = q.cpu().numpy()
     at, ag = ow.act_amax(x)
     expect = ow.quantize_act(x, at, ag, mode)
-    assert np.array_equal(slab16_to_nchw(qn, c, h, w), expect)
+    assert np.array_equal(slab16_to_nchw(qn, c, h, w, stride), expect)
     # padding rows / columns of a stride-2 consumer's buffer are zero
     assert (qn[:, :, h:, :] == 0).all() and (qn[:, :, :, w:] == 0).all()
     r = rec.cpu().numpy()
