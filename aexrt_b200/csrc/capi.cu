@@ -237,7 +237,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
     p->kk_p = 0;
     p->q_total = (kk * p->slabs + 1) & ~1;
   }
-  p->sps = std::min(8, p->q_total);
+  p->sps = std::min(16, p->q_total);
   {
     // one persistent CTA per SM: spend up to ~200 KB of shared memory on pipeline stages
     const ConvSmemPlan one = conv_smem_plan(p->tw, p->th, p->sps, 1, p->bn);

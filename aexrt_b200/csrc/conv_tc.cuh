@@ -129,10 +129,21 @@ __device__ __forceinline__ int decode_slot(const ConvTcParams& p, int q, int& sl
   return tap;
 }
 
-__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&v)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-               : "r"(taddr));
+template <int CW>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[CW]) {
+  static_assert(CW == 8 || CW == 16, "8 or 16 columns");
+  if constexpr (CW == 8) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr));
+  } else {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+        "[%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+  }
 }
 
 __device__ __forceinline__ float tanh_approx(float x) {
@@ -147,35 +158,33 @@ __device__ __forceinline__ float silu_fast(float y) {
   return fmaf(h, tanh_approx(h), h);
 }
 
-// Epilogue of 8 consecutive output channels of one pixel: `acc` already holds
-// the dequantized sum (int8) or the fp32 accumulator (fp16); applies the
-// per-channel scale, bias, SiLU, residual, stores fp16 and returns the max
-// |fp16 output| bits for the next layer's amax.
-template <bool kF16>
-__device__ __forceinline__ uint32_t epilogue8(const ConvTcParams& p, const float (&acc)[8], int oc_base, bool valid,
-                                              size_t pix) {
-  const bool full8 = oc_base + 8 <= p.oc;  // all 8 channels exist (else only oc < p.oc is touched)
-  float wsc[8], bia[8];
-  if (full8) {
-    const float4* b4 = reinterpret_cast<const float4*>(p.bias + oc_base);
-    const float4 b0 = __ldg(b4), b1 = __ldg(b4 + 1);
-    bia[0] = b0.x; bia[1] = b0.y; bia[2] = b0.z; bia[3] = b0.w;
-    bia[4] = b1.x; bia[5] = b1.y; bia[6] = b1.z; bia[7] = b1.w;
-    if (!kF16) {
-      const float4* s4 = reinterpret_cast<const float4*>(p.w_scale + oc_base);
-      const float4 s0 = __ldg(s4), s1 = __ldg(s4 + 1);
-      wsc[0] = s0.x; wsc[1] = s0.y; wsc[2] = s0.z; wsc[3] = s0.w;
-      wsc[4] = s1.x; wsc[5] = s1.y; wsc[6] = s1.z; wsc[7] = s1.w;
-    }
+__device__ __forceinline__ void load8f(const float* src, bool full, int n_valid, float (&dst)[8]) {
+  if (full) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+    dst[0] = a.x; dst[1] = a.y; dst[2] = a.z; dst[3] = a.w;
+    dst[4] = b.x; dst[5] = b.y; dst[6] = b.z; dst[7] = b.w;
   } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      bia[i] = oc_base + i < p.oc ? __ldg(p.bias + oc_base + i) : 0.0f;
-      wsc[i] = (!kF16 && oc_base + i < p.oc) ? __ldg(p.w_scale + oc_base + i) : 0.0f;
-    }
+    for (int i = 0; i < 8; ++i) dst[i] = i < n_valid ? __ldg(src + i) : 0.0f;
   }
+}
+
+// Epilogue of 8 consecutive output channels of one pixel: `acc` holds the
+// dequantized sum (int8: already multiplied by the activation scale) or the
+// fp32 accumulator (fp16); applies the per-channel weight scale, bias, SiLU,
+// residual, stores fp16 and returns the max |fp16 output| for the next
+// layer's amax.
+template <bool kF16>
+__device__ __forceinline__ float epilogue8(const ConvTcParams& p, const float (&acc)[8], int oc_base, bool valid,
+                                           size_t pix) {
+  const int n_valid = p.oc - oc_base;
+  const bool full8 = n_valid >= 8;
+  float wsc[8], bia[8];
+  load8f(p.bias + oc_base, full8, n_valid, bia);
+  if (!kF16) load8f(p.w_scale + oc_base, full8, n_valid, wsc);
   float res[8];
-  const bool has_res = p.res != nullptr && valid && oc_base < p.oc;
+  const bool has_res = p.res != nullptr && valid && n_valid > 0;
   if (has_res) {
     const __half* rp = p.res + pix * p.res_ldc + p.res_coff + oc_base;
     if (full8 && p.res_vec) {
@@ -189,7 +198,7 @@ __device__ __forceinline__ uint32_t epilogue8(const ConvTcParams& p, const float
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) res[i] = oc_base + i < p.oc ? __half2float(rp[i]) : 0.0f;
+      for (int i = 0; i < 8; ++i) res[i] = i < n_valid ? __half2float(rp[i]) : 0.0f;
     }
   }
   __align__(16) __half2 hv[4];
@@ -202,15 +211,12 @@ __device__ __forceinline__ uint32_t epilogue8(const ConvTcParams& p, const float
       float v = kF16 ? acc[k] + bia[k] : fmaf(acc[k], wsc[k], bia[k]);
       if (p.silu) v = silu_fast(v);
       if (has_res) v += res[k];
-      y[j] = oc_base + k < p.oc ? v : 0.0f;
+      y[j] = k < n_valid ? v : 0.0f;
     }
     hv[i] = __floats2half2_rn(y[0], y[1]);
   }
-  const __half2 m01 = __hmax2(__habs2(hv[0]), __habs2(hv[1]));
-  const __half2 m23 = __hmax2(__habs2(hv[2]), __habs2(hv[3]));
-  const __half2 m = __hmax2(m01, m23);
-  const float amax = fmaxf(__low2float(m), __high2float(m));
-  if (valid && oc_base < p.oc) {
+  const __half2 m = __hmax2(__hmax2(__habs2(hv[0]), __habs2(hv[1])), __hmax2(__habs2(hv[2]), __habs2(hv[3])));
+  if (valid && n_valid > 0) {
     __half* op = p.out + pix * p.out_ldc + p.out_coff + oc_base;
     if (full8 && p.out_vec) {
       *reinterpret_cast<uint4*>(op) = *reinterpret_cast<const uint4*>(hv);
@@ -218,17 +224,26 @@ __device__ __forceinline__ uint32_t epilogue8(const ConvTcParams& p, const float
       const __half* h = reinterpret_cast<const __half*>(hv);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        if (oc_base + i < p.oc) op[i] = h[i];
+        if (i < n_valid) op[i] = h[i];
     }
   }
-  return valid ? __float_as_uint(amax) : 0u;
+  return valid ? fmaxf(__low2float(m), __high2float(m)) : 0.0f;
+}
+
+// Warp-wide max of the per-lane amax of one 16-channel group (or 8-channel
+// half of one) and a single atomic per warp.
+__device__ __forceinline__ void amax_commit(const ConvTcParams& p, float m, int img, int oc_base, int lane) {
+  const uint32_t r = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+  if (p.amax_out != nullptr && lane == 0 && oc_base < p.oc && r != 0u)
+    atomicMax(&p.amax_out[static_cast<size_t>(img) * p.amax_stride + p.amax_goff + oc_base / 16], r);
 }
 
 template <bool kF16, bool kPG, int BN>
 __global__ void __launch_bounds__(kConvThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap act_map, const ConvTcParams p) {
-  constexpr int kHalf = BN / 2;       // columns per epilogue warp
-  constexpr int kChunks = kHalf / 8;  // 8-column chunks per epilogue warp
+  constexpr int kHalf = BN / 2;                  // columns per epilogue warp
+  constexpr int CW = kHalf >= 16 ? 16 : 8;       // columns per TMEM load
+  constexpr int kChunks = kHalf / CW;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "BN must be a multiple of 16 in [16, 256]");
   static_assert(!kPG || (!kF16 && BN <= 128), "pg16 is int8-only and keeps BN/2 fp32 partials per thread");
   constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
@@ -245,8 +260,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
   const int rows = p.th * p.tw;
-  const int ksteps_per_unit = kPG ? p.kk_p / 2 : p.q_total / 2;
-  const size_t w_tile_bytes = static_cast<size_t>(p.q_total) * BN * kSlotBytes;
+  const int stages_per_tile = (p.q_total + p.sps - 1) / p.sps;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -271,46 +285,54 @@ __global__ void __launch_bounds__(kConvThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int it = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-        const TileCoord tc = tile_coord(p, t);
-        const uint8_t* w_tile = p.w_packed + static_cast<size_t>(tc.n_tile) * w_tile_bytes;
-        for (int q0 = 0; q0 < p.q_total; q0 += p.sps, ++it) {
-          const int s = it % p.stages;
-          if (it >= p.stages && !mbar_wait_bounded(&empty[s], ((it / p.stages) - 1) & 1, p.status, kStatusTimeoutEmpty)) {
-            ok = false;
-            break;
-          }
-          const int rem = min(p.sps, p.q_total - q0);
-          uint8_t* a_dst = smem + s * sp.stage_bytes;
-          uint8_t* b_dst = a_dst + sp.a_stage_bytes;
+    // Lane j issues the TMA box of slot j of the stage (slots decode in
+    // parallel); lane 0 also arms the barrier and issues the weight copy.
+    const size_t w_tile_bytes = static_cast<size_t>(p.q_total) * BN * kSlotBytes;
+    const int x_per_px = kSlotBytes / (kF16 ? 2 : 1);  // tensor-map elements per pixel of one slab
+    int s = 0, it = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      const TileCoord tc = tile_coord(p, t);
+      const uint8_t* w_tile = p.w_packed + static_cast<size_t>(tc.n_tile) * w_tile_bytes;
+      for (int st = 0, q0 = 0; st < stages_per_tile; ++st, q0 += p.sps) {
+        if (it >= p.stages && !mbar_wait_bounded(&empty[s], ph ^ 1u, p.status, kStatusTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        const int rem = min(p.sps, p.q_total - q0);
+        uint8_t* a_dst = smem + s * sp.stage_bytes;
+        if (lane == 0)
           mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rem * (sp.a_box_bytes + BN * kSlotBytes)));
-          for (int j = 0; j < rem; ++j) {
-            int slab;
-            const int tap = decode_slot<kPG>(p, q0 + j, slab);
-            int sn = tc.img * p.slabs + slab;
-            int kh = 0, kw = 0;
-            if (tap < 0) {
-              sn = p.n_img * p.slabs;  // fully out of range: the TMA zero-fills the slot
-            } else {
-              kh = tap / p.ksize;
-              kw = tap - kh * p.ksize;
-            }
-            void* dst = a_dst + j * sp.a_slot_stride;
-            if (p.stride == 1) {
-              tma_load_3d(dst, &act_map, &full[s], kSlotBytes / (kF16 ? 2 : 1) * (tc.ow0 + kw - p.pad),
-                          tc.oh0 + kh - p.pad, sn);
-            } else {
-              // input column 2*ow + kw - 1 == 2*(ow + dw) + pw  (same for rows)
-              const int pw = (kw + 1) & 1, dw = (kw - 1 - pw) / 2;
-              const int ph = (kh + 1) & 1, dh = (kh - 1 - ph) / 2;
-              tma_load_5d(dst, &act_map, &full[s], kSlotBytes / (kF16 ? 2 : 1) * (tc.ow0 + dw), pw, ph, tc.oh0 + dh, sn);
-            }
+        __syncwarp();
+        if (lane < rem) {
+          int slab;
+          const int tap = decode_slot<kPG>(p, q0 + lane, slab);
+          int sn = tc.img * p.slabs + slab;
+          int kh = 0, kw = 0;
+          if (tap < 0) {
+            sn = p.n_img * p.slabs;  // fully out of range: the TMA zero-fills the slot
+          } else {
+            kh = tap / p.ksize;
+            kw = tap - kh * p.ksize;
           }
-          bulk_load(b_dst, w_tile + static_cast<size_t>(q0) * BN * kSlotBytes, static_cast<uint32_t>(rem * BN * kSlotBytes),
-                    &full[s]);
+          void* dst = a_dst + lane * sp.a_slot_stride;
+          if (p.stride == 1) {
+            tma_load_3d(dst, &act_map, &full[s], x_per_px * (tc.ow0 + kw - p.pad), tc.oh0 + kh - p.pad, sn);
+          } else {
+            // input column 2*ow + kw - 1 == 2*(ow + dw) + pw  (same for rows)
+            const int pw = (kw + 1) & 1, dw = (kw - 1 - pw) / 2;
+            const int ph2 = (kh + 1) & 1, dh = (kh - 1 - ph2) / 2;
+            tma_load_5d(dst, &act_map, &full[s], x_per_px * (tc.ow0 + dw), pw, ph2, tc.oh0 + dh, sn);
+          }
+        }
+        if (lane == 0)
+          bulk_load(a_dst + sp.a_stage_bytes, w_tile + static_cast<size_t>(q0) * BN * kSlotBytes,
+                    static_cast<uint32_t>(rem * BN * kSlotBytes), &full[s]);
+        ++it;
+        if (++s == p.stages) {
+          s = 0;
+          ph ^= 1u;
         }
       }
     }
@@ -318,39 +340,51 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc<kF16>(BN);
-      int it = 0, u = 0;
+      const int ksteps_per_unit = kPG ? p.kk_p / 2 : p.q_total / 2;
+      const uint32_t smem_base = smem_u32(smem);
+      const uint64_t a_desc0 = smem_desc_kmajor_noswizzle(smem_base, sp.a_slot_stride, 128);
+      const uint64_t b_desc0 = smem_desc_kmajor_noswizzle(smem_base + sp.a_stage_bytes, BN * kSlotBytes, 128);
+      const uint64_t a_inc = static_cast<uint64_t>((2 * sp.a_slot_stride) >> 4);
+      const uint64_t b_inc = static_cast<uint64_t>((2 * BN * kSlotBytes) >> 4);
+      const uint64_t stage_inc = static_cast<uint64_t>(sp.stage_bytes >> 4);
+      int s = 0, u = 0, kin = 0, buf = 0;
+      uint32_t ph = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-        for (int q0 = 0; q0 < p.q_total && ok; q0 += p.sps, ++it) {
-          const int s = it % p.stages;
-          if (!mbar_wait_bounded(&full[s], (it / p.stages) & 1, p.status, kStatusTimeoutFull)) {
+        for (int st = 0, q0 = 0; st < stages_per_tile; ++st, q0 += p.sps) {
+          if (!mbar_wait_bounded(&full[s], ph, p.status, kStatusTimeoutFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const int rem = min(p.sps, p.q_total - q0);
-          const uint32_t a_base = smem_u32(smem + s * sp.stage_bytes);
-          const uint32_t b_base = a_base + sp.a_stage_bytes;
-          for (int j = 0; j < rem / 2; ++j) {
-            const int ks = q0 / 2 + j;
-            const int kin = ks % ksteps_per_unit;
-            const int buf = u & 1;
-            if (kin == 0 && u >= 2) {
-              if (!mbar_wait_bounded(&acc_empty[buf], ((u - 2) >> 1) & 1, p.status, kStatusTimeoutAccEmpty)) {
-                ok = false;
-                break;
+          const int ksteps = min(p.sps, p.q_total - q0) >> 1;
+          uint64_t ad = a_desc0 + s * stage_inc;
+          uint64_t bd = b_desc0 + s * stage_inc;
+          for (int j = 0; j < ksteps; ++j) {
+            if (kin == 0) {
+              buf = u & 1;
+              if (u >= 2) {
+                if (!mbar_wait_bounded(&acc_empty[buf], ((u - 2) >> 1) & 1, p.status, kStatusTimeoutAccEmpty)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
               }
-              tc_fence_after();
             }
-            const uint64_t a_desc = smem_desc_kmajor_noswizzle(a_base + 2 * j * sp.a_slot_stride, sp.a_slot_stride, 128);
-            const uint64_t b_desc = smem_desc_kmajor_noswizzle(b_base + 2 * j * BN * kSlotBytes, BN * kSlotBytes, 128);
-            tc_mma<kF16>(tmem_base + buf * BN, a_desc, b_desc, idesc, kin == 0 ? 0u : 1u);
-            if (kin == ksteps_per_unit - 1) {
+            tc_mma<kF16>(tmem_base + buf * BN, ad, bd, idesc, kin == 0 ? 0u : 1u);
+            ad += a_inc;
+            bd += b_inc;
+            if (++kin == ksteps_per_unit) {
               tc_commit(&acc_full[buf]);
               ++u;
+              kin = 0;
             }
           }
           tc_commit(&empty[s]);
+          if (++s == p.stages) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
       }
     }
@@ -384,8 +418,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         const float in_scale = kF16 ? 1.0f : __fdiv_rn(rec[0], 127.0f);
 #pragma unroll 1
         for (int c = 0; c < kChunks; ++c) {
-          uint32_t v[8];
-          tmem_ld_x8(lane_addr + buf * BN + col0 + c * 8, v);
+          uint32_t v[CW];
+          tmem_ld<CW>(lane_addr + buf * BN + col0 + c * CW, v);
           tmem_ld_wait();
           if (c == kChunks - 1) {
             // every column of this accumulator has been read: hand it back to the MMA warp
@@ -393,20 +427,24 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
           }
-          const int oc_base = n0 + col0 + c * 8;
-          float acc[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            acc[i] = kF16 ? __uint_as_float(v[i]) : __fmul_rn(static_cast<float>(static_cast<int32_t>(v[i])), in_scale);
+          const int oc_c = n0 + col0 + c * CW;
           if (!kF16 && p.acc_dump != nullptr && valid) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              if (oc_base + i < p.oc) p.acc_dump[pix * p.oc + oc_base + i] = static_cast<int32_t>(v[i]);
+            for (int i = 0; i < CW; ++i)
+              if (oc_c + i < p.oc) p.acc_dump[pix * p.oc + oc_c + i] = static_cast<int32_t>(v[i]);
           }
-          const uint32_t m = __reduce_max_sync(0xffffffffu, epilogue8<kF16>(p, acc, oc_base, valid, pix));
-          if (p.amax_out != nullptr && lane == 0 && oc_base < p.oc && m != 0u) {
-            atomicMax(&p.amax_out[static_cast<size_t>(tc.img) * p.amax_stride + p.amax_goff + oc_base / 16], m);
+          float m = 0.0f;
+#pragma unroll
+          for (int h8 = 0; h8 < CW / 8; ++h8) {
+            float acc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const uint32_t bits = v[h8 * 8 + i];
+              acc[i] = kF16 ? __uint_as_float(bits) : static_cast<float>(static_cast<int32_t>(bits)) * in_scale;
+            }
+            m = fmaxf(m, epilogue8<kF16>(p, acc, oc_c + h8 * 8, valid, pix));
           }
+          amax_commit(p, m, tc.img, oc_c, lane);
         }
         ++u;
       } else {
@@ -421,20 +459,20 @@ __global__ void __launch_bounds__(kConvThreads, 1)
           const float gs = __fdiv_rn(rec[1 + g], 127.0f);
 #pragma unroll
           for (int c = 0; c < kChunks; ++c) {
-            uint32_t v[8];
-            tmem_ld_x8(lane_addr + buf * BN + col0 + c * 8, v);
+            uint32_t v[CW];
+            tmem_ld<CW>(lane_addr + buf * BN + col0 + c * CW, v);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float term = __fmul_rn(static_cast<float>(static_cast<int32_t>(v[i])), gs);
-              fp[c * 8 + i] = g == 0 ? term : __fadd_rn(fp[c * 8 + i], term);
+            for (int i = 0; i < CW; ++i) {
+              const float term = static_cast<float>(static_cast<int32_t>(v[i])) * gs;
+              fp[c * CW + i] = g == 0 ? term : fp[c * CW + i] + term;
             }
             if (p.acc_dump != nullptr && valid) {
-              const int oc_base = n0 + col0 + c * 8;
+              const int oc_c = n0 + col0 + c * CW;
 #pragma unroll
-              for (int i = 0; i < 8; ++i)
-                if (oc_base + i < p.oc)
-                  p.acc_dump[(static_cast<size_t>(g) * npix + pix) * p.oc + oc_base + i] = static_cast<int32_t>(v[i]);
+              for (int i = 0; i < CW; ++i)
+                if (oc_c + i < p.oc)
+                  p.acc_dump[(static_cast<size_t>(g) * npix + pix) * p.oc + oc_c + i] = static_cast<int32_t>(v[i]);
             }
           }
           tc_fence_before();
@@ -445,14 +483,16 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         if (!ok) break;
 #pragma unroll
         for (int c = 0; c < kChunks; ++c) {
-          const int oc_base = n0 + col0 + c * 8;
-          float acc[8];
+          const int oc_c = n0 + col0 + c * CW;
+          float m = 0.0f;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[i] = fp[c * 8 + i];
-          const uint32_t m = __reduce_max_sync(0xffffffffu, epilogue8<false>(p, acc, oc_base, valid, pix));
-          if (p.amax_out != nullptr && lane == 0 && oc_base < p.oc && m != 0u) {
-            atomicMax(&p.amax_out[static_cast<size_t>(tc.img) * p.amax_stride + p.amax_goff + oc_base / 16], m);
+          for (int h8 = 0; h8 < CW / 8; ++h8) {
+            float acc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = fp[c * CW + h8 * 8 + i];
+            m = fmaxf(m, epilogue8<false>(p, acc, oc_c + h8 * 8, valid, pix));
           }
+          amax_commit(p, m, tc.img, oc_c, lane);
         }
       }
     }

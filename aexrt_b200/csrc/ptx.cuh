@@ -19,15 +19,11 @@ enum : uint32_t {
   kStatusBadTmem = 1u << 4,          // TMEM allocation returned an unusable base
 };
 
-// A wait gives up after this many nanoseconds of %globaltimer (200 ms): far
-// above any legitimate stall of these kernels, far below a GPU watchdog.
-constexpr uint64_t kWaitLimitNs = 200ull * 1000ull * 1000ull;
-
-__device__ __forceinline__ uint64_t global_timer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
+// A wait gives up after this many SM clock cycles (2^30, about half a second at
+// the B200's clocks): far above any legitimate stall of these kernels, far
+// below a GPU watchdog.  The SM-local cycle counter is used because reading
+// %globaltimer costs on the order of a microsecond.
+constexpr long long kWaitLimitCycles = 1ll << 30;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -64,16 +60,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Returns false (and
-// sets `flag` in *status) when the wall-clock limit passes first.  The timer is
-// read once every 64 polls so that waiting warps cost few issue slots.
+// sets `flag` in *status) when the cycle limit passes first.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t flag) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
+  const long long t0 = clock64();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 64; ++i)
+    for (int i = 0; i < 16; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (clock64() - t0 > kWaitLimitCycles) {
       atomicOr(status, flag);
       return false;
     }
