@@ -33,6 +33,17 @@ class AexrtB200ConvPlanInfo(ctypes.Structure):
     )] + [("reserved", c_uint32 * 4)]
 
 
+class AexrtB200ActSource(ctypes.Structure):
+    _fields_ = [("ptr", c_void_p), ("layout", c_uint32), ("ldc", c_uint32), ("coff", c_uint32), ("channels", c_uint32),
+                ("upsample", c_uint32), ("src_h", c_uint32), ("src_w", c_uint32), ("amax_groups", c_void_p),
+                ("amax_stride", c_uint32), ("amax_goff", c_uint32)]
+
+
+class AexrtB200DecodeLevel(ctypes.Structure):
+    _fields_ = [("box", c_void_p), ("box_ldc", c_uint32), ("box_coff", c_uint32), ("cls", c_void_p),
+                ("cls_ldc", c_uint32), ("cls_coff", c_uint32), ("h", c_uint32), ("w", c_uint32), ("stride", c_float)]
+
+
 class AexrtError(RuntimeError):
     """A C-ABI call returned failure; the message is the library's last error."""
 
@@ -58,6 +69,15 @@ _SIGNATURES = {
     "aexrt_b200_conv_status": (c_int, [c_void_p, POINTER(c_uint32)]),
     "aexrt_b200_packed_f16_bytes": (c_uint64, [c_uint32] * 5),
     "aexrt_b200_pack_f16": (c_int, [c_void_p] + [c_uint32] * 8 + [c_void_p, c_void_p]),
+    "aexrt_b200_act_quantize_concat": (c_int, [POINTER(AexrtB200ActSource), c_uint32, c_uint32, c_uint32, c_uint32,
+                                               c_uint32, c_uint32, c_void_p, c_void_p, c_void_p]),
+    "aexrt_b200_pack_f16_concat": (c_int, [POINTER(AexrtB200ActSource), c_uint32, c_uint32, c_uint32, c_uint32,
+                                           c_uint32, c_void_p, c_void_p]),
+    "aexrt_b200_sppf_pool": (c_int, [c_void_p] + [c_uint32] * 6 + [c_void_p, c_uint32, c_uint32, c_void_p, c_uint32,
+                                                                   c_uint32, c_void_p]),
+    "aexrt_b200_yolo_decode": (c_int, [POINTER(AexrtB200DecodeLevel), c_uint32, c_uint32, c_uint32, c_uint32, c_void_p,
+                                       c_void_p]),
+    "aexrt_b200_zero": (c_int, [c_void_p, c_uint64, c_void_p]),
 }
 
 _LIB = None

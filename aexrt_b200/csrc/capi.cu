@@ -21,6 +21,7 @@
 #include "../../include/aexrt_b200.h"
 #include "conv_tc.cuh"
 #include "quant.cuh"
+#include "yolo_ops.cuh"
 
 using namespace aexrt;
 
@@ -640,6 +641,138 @@ int aexrt_b200_conv_status(const AexrtB200ConvPlan* plan, uint32_t* status) {
   if (!plan || !status) return fail("null pointer");
   if (!cuda_ok(cudaMemcpy(status, plan->d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost), "read status")) return 0;
   return cuda_ok(cudaMemset(plan->d_status, 0, sizeof(uint32_t)), "clear status") ? 1 : 0;
+}
+
+static bool fill_sources(QuantParams& q, const AexrtB200ActSource* srcs, uint32_t nsrc, uint32_t n, uint32_t h,
+                         uint32_t w, int cps, bool need_amax) {
+  if (!srcs || nsrc == 0 || nsrc > static_cast<uint32_t>(kMaxQuantSrc))
+    return fail("between 1 and %d sources", kMaxQuantSrc) != 0;
+  std::memset(&q, 0, sizeof(q));
+  q.nsrc = static_cast<int>(nsrc);
+  q.n = static_cast<int>(n);
+  q.h = static_cast<int>(h);
+  q.w = static_cast<int>(w);
+  int total = 0;
+  for (uint32_t i = 0; i < nsrc; ++i) {
+    const AexrtB200ActSource& a = srcs[i];
+    QuantSrc& d = q.src[i];
+    if (!a.ptr || (need_amax && !a.amax_groups)) return fail("source %u: null pointer", i) != 0;
+    if (a.layout > AEXRT_B200_LAYOUT_NCHW_F32 || (need_amax && a.layout == AEXRT_B200_LAYOUT_NCHW_F32))
+      return fail("source %u: unsupported layout", i) != 0;
+    if (a.upsample != 1 && a.upsample != 2) return fail("source %u: upsample must be 1 or 2", i) != 0;
+    if (a.src_h * a.upsample != h || a.src_w * a.upsample != w) return fail("source %u: spatial size mismatch", i) != 0;
+    if (i + 1 < nsrc && a.channels % cps) return fail("source %u: channels must be a multiple of %d", i, cps) != 0;
+    if (a.layout == AEXRT_B200_LAYOUT_NHWC_F16 &&
+        (a.ldc < a.coff + a.channels || a.ldc % 8 || a.coff % 8 || reinterpret_cast<uintptr_t>(a.ptr) % 16))
+      return fail("source %u: NHWC slice must be 16-byte aligned (ldc, coff multiples of 8)", i) != 0;
+    if (need_amax && (a.coff % 16 || a.amax_goff * 16 + a.channels > a.amax_stride * 16))
+      return fail("source %u: amax slots out of range", i) != 0;
+    d.ptr = a.ptr;
+    d.layout = static_cast<int>(a.layout);
+    d.ldc = static_cast<int>(a.layout == AEXRT_B200_LAYOUT_NHWC_F16 ? a.ldc : a.channels);
+    d.coff = static_cast<int>(a.layout == AEXRT_B200_LAYOUT_NHWC_F16 ? a.coff : 0);
+    d.ch = static_cast<int>(a.channels);
+    d.up = static_cast<int>(a.upsample);
+    d.src_h = static_cast<int>(a.src_h);
+    d.src_w = static_cast<int>(a.src_w);
+    d.amax_g = a.amax_groups;
+    d.amax_stride = static_cast<int>(a.amax_stride);
+    d.amax_goff = static_cast<int>(a.amax_goff);
+    total += static_cast<int>(a.channels);
+  }
+  q.c_total = total;
+  return true;
+}
+
+int aexrt_b200_act_quantize_concat(const AexrtB200ActSource* srcs, uint32_t nsrc, uint32_t n, uint32_t h, uint32_t w,
+                                   uint32_t mode, uint32_t consumer_stride, void* q_out, float* scale_rec,
+                                   void* stream) {
+  QuantParams q;
+  if (!fill_sources(q, srcs, nsrc, n, h, w, 16, true)) return 0;
+  if (!q_out || reinterpret_cast<uintptr_t>(q_out) % 16) return fail("q_out must be a 16-byte aligned pointer");
+  if (mode > 1 || (mode == 1 && q.c_total % 16)) return fail("bad mode (pg16 needs channels %% 16 == 0)");
+  if (n == 0 || h == 0 || w == 0) return 1;
+  q.slabs = (q.c_total + 15) / 16;
+  q.hp = static_cast<int>(h + (consumer_stride == 2 ? (h & 1) : 0));
+  q.wp = static_cast<int>(w + (consumer_stride == 2 ? (w & 1) : 0));
+  q.mode = static_cast<int>(mode);
+  q.split = consumer_stride == 2 ? 1 : 0;
+  q.out = q_out;
+  q.rec = scale_rec;
+  const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, n);
+  quantize_i8_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(q);
+  return cuda_ok(cudaGetLastError(), "quantize launch") ? 1 : 0;
+}
+
+int aexrt_b200_pack_f16_concat(const AexrtB200ActSource* srcs, uint32_t nsrc, uint32_t n, uint32_t h, uint32_t w,
+                               uint32_t consumer_stride, void* out, void* stream) {
+  QuantParams q;
+  if (!fill_sources(q, srcs, nsrc, n, h, w, 8, false)) return 0;
+  if (!out || reinterpret_cast<uintptr_t>(out) % 16) return fail("out must be a 16-byte aligned pointer");
+  if (n == 0 || h == 0 || w == 0) return 1;
+  q.slabs = (q.c_total + 7) / 8;
+  q.hp = static_cast<int>(h + (consumer_stride == 2 ? (h & 1) : 0));
+  q.wp = static_cast<int>(w + (consumer_stride == 2 ? (w & 1) : 0));
+  q.split = consumer_stride == 2 ? 1 : 0;
+  q.out = out;
+  const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, n);
+  pack_f16_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(q);
+  return cuda_ok(cudaGetLastError(), "pack launch") ? 1 : 0;
+}
+
+int aexrt_b200_sppf_pool(const void* x, uint32_t n, uint32_t h, uint32_t w, uint32_t c, uint32_t ldc, uint32_t coff,
+                         void* out, uint32_t out_ldc, uint32_t out_coff, uint32_t* amax, uint32_t amax_stride,
+                         uint32_t amax_goff, void* stream) {
+  if (!x || !out) return fail("null pointer");
+  if (c % 16 || ldc % 8 || coff % 8 || out_ldc % 8 || out_coff % 16 || ldc < coff + c || out_ldc < out_coff + 3 * c ||
+      reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return fail("sppf: c %% 16 == 0 and 16-byte aligned slices required");
+  if (amax && amax_goff * 16 + 3 * c > amax_stride * 16) return fail("sppf: amax slots out of range");
+  const long total = static_cast<long>(n) * h * w * (c / 8);
+  if (total == 0) return 1;
+  sppf_pool_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(x), n, h, w, c, ldc, coff, static_cast<__half*>(out), out_ldc, out_coff, amax,
+      amax_stride, amax_goff);
+  return cuda_ok(cudaGetLastError(), "sppf launch") ? 1 : 0;
+}
+
+int aexrt_b200_yolo_decode(const AexrtB200DecodeLevel* levels, uint32_t nlevels, uint32_t n, uint32_t nc,
+                           uint32_t reg_max, float* out, void* stream) {
+  if (!levels || !out || nlevels == 0 || nlevels > static_cast<uint32_t>(kMaxLevels)) return fail("bad decode levels");
+  if (reg_max == 0 || reg_max > 64 || nc == 0) return fail("bad nc / reg_max");
+  DecodeParams d;
+  std::memset(&d, 0, sizeof(d));
+  int anchors = 0;
+  for (uint32_t i = 0; i < nlevels; ++i) {
+    const AexrtB200DecodeLevel& l = levels[i];
+    if (!l.box || !l.cls || l.box_ldc < l.box_coff + 4 * reg_max || l.cls_ldc < l.cls_coff + nc)
+      return fail("decode level %u: bad slices", i);
+    d.box[i] = static_cast<const __half*>(l.box);
+    d.cls[i] = static_cast<const __half*>(l.cls);
+    d.box_ldc[i] = l.box_ldc;
+    d.box_coff[i] = l.box_coff;
+    d.cls_ldc[i] = l.cls_ldc;
+    d.cls_coff[i] = l.cls_coff;
+    d.h[i] = l.h;
+    d.w[i] = l.w;
+    d.stride[i] = l.stride;
+    anchors += static_cast<int>(l.h * l.w);
+  }
+  d.levels = static_cast<int>(nlevels);
+  d.n = static_cast<int>(n);
+  d.nc = static_cast<int>(nc);
+  d.reg_max = static_cast<int>(reg_max);
+  d.anchors = anchors;
+  d.out = out;
+  const long total = static_cast<long>(n) * anchors;
+  if (total == 0) return 1;
+  yolo_decode_kernel<<<static_cast<unsigned>((total + 127) / 128), 128, 0, static_cast<cudaStream_t>(stream)>>>(d);
+  return cuda_ok(cudaGetLastError(), "decode launch") ? 1 : 0;
+}
+
+int aexrt_b200_zero(void* ptr, uint64_t bytes, void* stream) {
+  if (!ptr) return fail("null pointer");
+  return cuda_ok(cudaMemsetAsync(ptr, 0, bytes, static_cast<cudaStream_t>(stream)), "memset") ? 1 : 0;
 }
 
 }  // extern "C"

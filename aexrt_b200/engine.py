@@ -1,0 +1,223 @@
+"""Compile a YOLO command stream into device plans and replay it as a CUDA graph.
+
+This is the B200 counterpart of the reference runtime's prepared physical
+replay (``ensure_prepared_yolo_replay`` / ``record_prepared_physical_stream``,
+native/aexrt_d3d12_runtime.cpp:28758-29010, replayed per frame at :29732-29940):
+the command list is lowered once into C-ABI launches on one stream, recorded
+into one CUDA graph per batch size, and replayed per batch.
+
+Memory plan: every value of the program is one fp16 NHWC buffer (the reference
+keeps fp16 "activation islands" in arena pages, memory_v2.py:202); producers
+write their channel slice of the consumer-facing buffer, so CONCAT and C2f
+split/chunk cost nothing.  Every value also owns one amax slot per (image,
+16-channel group) that its producers max into (epilogue amax), and that the
+consumers' quantizers read.  All amax slots live in one arena cleared at the
+start of each replay.
+
+Kernel plan: int8 convs become W8A8 plans with the reference's kernel ids
+(51 1x1, 52 3x3 s1, 53 3x3 s2) and INT8_PERGROUP flag; the rest (stem with 3
+input channels, detect head) become fp16 plans.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List, Optional
+
+import numpy as np
+
+from . import _native, ops
+from ._native import AexrtB200ActSource, AexrtB200DecodeLevel, check
+from .yolo import ConvCmd, DecodeCmd, Part, SppfCmd, YoloProgram
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+class CompiledYolo:
+    """One program compiled for one batch size on the current CUDA device."""
+
+    def __init__(self, program: YoloProgram, batch: int, device=None, block_n: Optional[Dict[str, int]] = None):
+        torch = _torch()
+        self.program = program
+        self.batch = batch
+        self.device = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        self.lib = _native.load()
+        n = batch
+        p = program
+        int8_inputs = set()
+        for c in p.commands:
+            if isinstance(c, ConvCmd) and c.precision == "int8":
+                int8_inputs.update(pt.value for pt in c.inputs)
+        self.needs_amax = int8_inputs
+        # ---- values: fp16 NHWC buffers + amax slots
+        self.values: Dict[str, "torch.Tensor"] = {}
+        self.amax_off: Dict[str, int] = {}
+        self.amax_groups: Dict[str, int] = {}
+        off = 0
+        for name, v in p.values.items():
+            if name == "images":
+                continue
+            self.values[name] = torch.empty((n, v.h, v.w, v.channels), dtype=torch.float16, device=self.device)
+            g = (v.channels + 15) // 16
+            self.amax_off[name] = off
+            self.amax_groups[name] = g
+            off += n * g
+        self.amax_arena = torch.zeros(max(off, 1), dtype=torch.int32, device=self.device)
+        self.images = torch.zeros((n, p.in_channels, p.imgsz, p.imgsz), dtype=torch.float32, device=self.device)
+        self.output = torch.zeros((n, 4 + p.nc, p.anchors), dtype=torch.float32, device=self.device)
+        # ---- plans and per-command scratch
+        self.steps: List[tuple] = []
+        self.plans: Dict[str, ops.ConvPlan] = {}
+        for c in p.commands:
+            if isinstance(c, ConvCmd):
+                self._compile_conv(c, (block_n or {}).get(c.name, 0))
+            elif isinstance(c, SppfCmd):
+                self.steps.append(("sppf", c))
+            elif isinstance(c, DecodeCmd):
+                self.steps.append(("decode", c))
+        self.graph = None
+        self.launches_per_run = self._count_launches()
+
+    # ------------------------------------------------------------------ compile
+    def _amax_view(self, value: str):
+        g = self.amax_groups[value]
+        o = self.amax_off[value]
+        return self.amax_arena[o:o + self.batch * g].view(self.batch, g)
+
+    def _spatial(self, part: Part):
+        if part.value == "images":
+            return self.program.imgsz, self.program.imgsz
+        v = self.program.values[part.value]
+        return v.h, v.w
+
+    def _compile_conv(self, c: ConvCmd, block_n: int):
+        torch = _torch()
+        n = self.batch
+        sh, sw = self._spatial(c.inputs[0])
+        h, w = sh * c.inputs[0].upsample, sw * c.inputs[0].upsample
+        if c.precision == "int8":
+            codes, scale = ops.quantize_conv_weight_int8(c.weight)
+            plan = ops.ConvPlan.int8(n, c.ic, h, w, c.oc, c.k, c.s, codes, scale, c.bias, silu=c.silu, pg16=c.pg16,
+                                     block_n=block_n)
+            shape = ops.packed_act_shape(n, c.ic, h, w, c.s)
+            q = torch.empty(shape, dtype=torch.int8, device=self.device)
+            rec = torch.empty((n, 1 + shape[1]), dtype=torch.float32, device=self.device)
+            scratch = (q, rec)
+        else:
+            plan = ops.ConvPlan.fp16(n, c.ic, h, w, c.oc, c.k, c.s, c.weight, c.bias, silu=c.silu, block_n=block_n)
+            hp = h + (h & 1 if c.s == 2 else 0)
+            wp = w + (w & 1 if c.s == 2 else 0)
+            x8 = torch.empty((n, (c.ic + 7) // 8, hp, wp, 8), dtype=torch.float16, device=self.device)
+            scratch = (x8,)
+        self.plans[c.name] = plan
+        srcs = (AexrtB200ActSource * len(c.inputs))()
+        for i, pt in enumerate(c.inputs):
+            ph, pw = self._spatial(pt)
+            s = srcs[i]
+            if pt.value == "images":
+                s.ptr = self.images.data_ptr()
+                s.layout = ops.LAYOUT_NCHW_F32
+                s.ldc = self.program.in_channels
+                s.coff = 0
+            else:
+                buf = self.values[pt.value]
+                s.ptr = buf.data_ptr()
+                s.layout = ops.LAYOUT_NHWC_F16
+                s.ldc = buf.shape[-1]
+                s.coff = pt.coff
+                if c.precision == "int8":
+                    s.amax_groups = self._amax_view(pt.value).data_ptr()
+                    s.amax_stride = self.amax_groups[pt.value]
+                    s.amax_goff = pt.coff // 16
+            s.channels = pt.channels
+            s.upsample = pt.upsample
+            s.src_h, s.src_w = ph, pw
+        self.steps.append(("conv", c, plan, srcs, scratch, (h, w)))
+
+    def _count_launches(self) -> int:
+        k = 1  # amax arena clear
+        for st in self.steps:
+            k += 2 if st[0] == "conv" else 1
+        return k
+
+    # ------------------------------------------------------------------ run
+    def launch(self, stream: int) -> None:
+        """Issues every launch of one forward on `stream` (capturable)."""
+        lib = self.lib
+        n = self.batch
+        check(lib.aexrt_b200_zero(self.amax_arena.data_ptr(), self.amax_arena.numel() * 4, stream), "zero amax")
+        for st in self.steps:
+            kind = st[0]
+            if kind == "conv":
+                _, c, plan, srcs, scratch, (h, w) = st
+                out = self.values[c.out[0]]
+                amax_out = self._amax_view(c.out[0]) if c.out[0] in self.needs_amax else None
+                res = self.values[c.residual[0]] if c.residual is not None else None
+                res_coff = c.residual[1] if c.residual is not None else 0
+                if c.precision == "int8":
+                    q, rec = scratch
+                    check(lib.aexrt_b200_act_quantize_concat(srcs, len(srcs), n, h, w, int(c.pg16), c.s, q.data_ptr(),
+                                                             rec.data_ptr(), stream), f"quantize {c.name}")
+                    plan.run(q, rec, out=out, out_coff=c.out[1], residual=res, res_coff=res_coff, amax_out=amax_out,
+                             amax_goff=c.out[1] // 16, stream=stream)
+                else:
+                    (x8,) = scratch
+                    check(lib.aexrt_b200_pack_f16_concat(srcs, len(srcs), n, h, w, c.s, x8.data_ptr(), stream),
+                          f"pack {c.name}")
+                    plan.run(x8, out=out, out_coff=c.out[1], residual=res, res_coff=res_coff, amax_out=amax_out,
+                             amax_goff=c.out[1] // 16, stream=stream)
+            elif kind == "sppf":
+                c = st[1]
+                x = self.values[c.x.value]
+                out = self.values[c.out[0]]
+                v = self.program.values[c.x.value]
+                am = self._amax_view(c.out[0])
+                check(lib.aexrt_b200_sppf_pool(x.data_ptr(), n, v.h, v.w, c.x.channels, x.shape[-1], c.x.coff,
+                                               out.data_ptr(), out.shape[-1], c.out[1], am.data_ptr(), am.shape[1],
+                                               c.out[1] // 16, stream), "sppf")
+            elif kind == "decode":
+                c = st[1]
+                lv = (AexrtB200DecodeLevel * len(c.levels))()
+                for i, (bp, cp, stride) in enumerate(c.levels):
+                    bb, cb = self.values[bp.value], self.values[cp.value]
+                    v = self.program.values[bp.value]
+                    lv[i].box, lv[i].box_ldc, lv[i].box_coff = bb.data_ptr(), bb.shape[-1], bp.coff
+                    lv[i].cls, lv[i].cls_ldc, lv[i].cls_coff = cb.data_ptr(), cb.shape[-1], cp.coff
+                    lv[i].h, lv[i].w, lv[i].stride = v.h, v.w, stride
+                check(lib.aexrt_b200_yolo_decode(lv, len(c.levels), n, c.nc, c.reg_max, self.output.data_ptr(), stream),
+                      "decode")
+
+    def capture(self) -> None:
+        """Records one forward into a CUDA graph (warm-up run first, as graph capture requires)."""
+        torch = _torch()
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.launch(s.cuda_stream)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):
+            self.launch(s.cuda_stream)
+        torch.cuda.synchronize(self.device)
+
+    def forward(self, images=None):
+        """One forward on device-resident `images` (copied into the input buffer if given)."""
+        if images is not None:
+            self.images.copy_(images, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            torch = _torch()
+            self.launch(torch.cuda.current_stream(self.device).cuda_stream)
+        return self.output
+
+    def status(self) -> int:
+        """OR of every plan's device status word (non-zero: a pipeline wait gave up)."""
+        st = 0
+        for p in self.plans.values():
+            st |= p.status()
+        return st

@@ -1,0 +1,253 @@
+"""YOLOv8-architecture command streams for the W8A8 backend.
+
+The reference lowers an ONNX YOLO graph into a prepared command stream of
+CONV / CONV_SILU / CONCAT / RESIZE / MAXPOOL / BINARY ... commands
+(src/aexrt/yolo.py:464-537, kinds in src/aexrt/engine.py:103-118) and then
+chooses a kernel per command (kernel plan, engine.py:1046-1222; W8A8 ids
+51/52/53 via algo overrides, engine.py:1112-1215).  This module builds the same
+kind of command stream directly from the architecture (no ONNX is available on
+this machine), with random seeded weights, already in the fused form this
+backend executes:
+
+* CONCAT + conv            -> one conv whose input lists the concatenated parts
+* RESIZE (nearest 2x)      -> an upsample flag on the consumer's input part
+* C2f split / chunk        -> channel slices of one NHWC buffer
+* C2f bottleneck Add       -> the residual operand of the second conv's epilogue
+* SPPF MaxPool x3 + CONCAT -> one SPPF pool command writing three slices
+
+Architecture and scaling follow the public YOLOv8 definition (width / depth
+multipliers, C2f, SPPF k=5, anchor-free decoupled Detect head with DFL
+reg_max=16).  Weights are random: N(0, 1/sqrt(fan_in)) and biases N(0, 0.1),
+seeded, so activations stay O(1) through the network.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+
+
+@dataclass
+class Part:
+    """One channel range of a command input: value[..., coff:coff+channels], read through an upsample."""
+
+    value: str
+    coff: int
+    channels: int
+    upsample: int = 1
+
+
+@dataclass
+class ConvCmd:
+    name: str
+    inputs: List[Part]
+    out: Tuple[str, int]          # (value, channel offset)
+    ic: int
+    oc: int
+    k: int
+    s: int
+    silu: bool
+    weight: np.ndarray            # [oc, ic, k, k] fp32
+    bias: np.ndarray              # [oc] fp32
+    precision: str = "int8"       # "int8" (W8A8 kernel 51/52/53) or "fp16"
+    residual: Optional[Tuple[str, int]] = None  # (value, channel offset), added after SiLU
+    pg16: bool = False            # INT8_PERGROUP plan flag
+
+    @property
+    def kind(self) -> str:
+        return "CONV_SILU" if self.silu else "CONV"
+
+
+@dataclass
+class SppfCmd:
+    name: str
+    x: Part
+    out: Tuple[str, int]  # three consecutive slices of x.channels each
+
+
+@dataclass
+class DecodeCmd:
+    name: str
+    levels: List[Tuple[Part, Part, float]]  # (box logits, class logits, stride)
+    nc: int
+    reg_max: int
+
+
+@dataclass
+class ValueSpec:
+    channels: int
+    h: int
+    w: int
+
+
+@dataclass
+class YoloProgram:
+    """Command stream + value table of one model at one input size."""
+
+    name: str
+    in_channels: int
+    imgsz: int
+    nc: int
+    reg_max: int
+    values: Dict[str, ValueSpec] = field(default_factory=dict)
+    commands: list = field(default_factory=list)
+    output: str = "output0"
+
+    @property
+    def anchors(self) -> int:
+        return sum((self.imgsz // s) ** 2 for s in (8, 16, 32))
+
+    def conv_macs_per_image(self, precision: Optional[str] = None) -> int:
+        total = 0
+        for c in self.commands:
+            if isinstance(c, ConvCmd) and (precision is None or c.precision == precision):
+                v = self.values[c.out[0]]
+                total += v.h * v.w * c.oc * c.ic * c.k * c.k
+        return total
+
+
+def _make_divisible(x: float, d: int = 8) -> int:
+    return int(math.ceil(x / d) * d)
+
+
+class _Builder:
+    def __init__(self, name: str, imgsz: int, nc: int, seed: int, reg_max: int = 16):
+        self.p = YoloProgram(name=name, in_channels=3, imgsz=imgsz, nc=nc, reg_max=reg_max)
+        self.rng = np.random.default_rng(seed)
+        self.p.values["images"] = ValueSpec(3, imgsz, imgsz)
+
+    def value(self, name: str, channels: int, h: int, w: int) -> str:
+        self.p.values[name] = ValueSpec(channels, h, w)
+        return name
+
+    def _weights(self, oc: int, ic: int, k: int) -> Tuple[np.ndarray, np.ndarray]:
+        w = self.rng.normal(0.0, 1.0 / math.sqrt(ic * k * k), (oc, ic, k, k)).astype(np.float32)
+        b = self.rng.normal(0.0, 0.1, (oc,)).astype(np.float32)
+        return w, b
+
+    def conv(self, name: str, inputs: List[Part], out: Tuple[str, int], oc: int, k: int, s: int, silu: bool = True,
+             precision: str = "int8", residual=None) -> ConvCmd:
+        ic = sum(pt.channels for pt in inputs)
+        w, b = self._weights(oc, ic, k)
+        cmd = ConvCmd(name, inputs, out, ic, oc, k, s, silu, w, b, precision, residual)
+        self.p.commands.append(cmd)
+        return cmd
+
+    def spatial(self, value: str) -> Tuple[int, int]:
+        v = self.p.values[value]
+        return v.h, v.w
+
+    # ---------------------------------------------------------------- blocks
+    def conv_block(self, name: str, src: List[Part], oc: int, k: int, s: int, precision: str = "int8") -> str:
+        h, w = self.spatial(src[0].value)
+        h *= src[0].upsample
+        w *= src[0].upsample
+        oh, ow = (h + 2 * (k // 2) - k) // s + 1, (w + 2 * (k // 2) - k) // s + 1
+        out = self.value(name, oc, oh, ow)
+        self.conv(name, src, (out, 0), oc, k, s, precision=precision)
+        return out
+
+    def c2f(self, name: str, src: List[Part], c2: int, n: int, shortcut: bool) -> str:
+        """C2f: cv1 -> split(c, c) -> n bottlenecks on the last chunk -> concat -> cv2."""
+        h, w = self.spatial(src[0].value)
+        h *= src[0].upsample
+        w *= src[0].upsample
+        c = c2 // 2
+        y = self.value(name + ".y", (2 + n) * c, h, w)
+        self.conv(name + ".cv1", src, (y, 0), 2 * c, 1, 1)
+        for i in range(n):
+            t = self.value(f"{name}.m{i}.t", c, h, w)
+            self.conv(f"{name}.m{i}.cv1", [Part(y, (1 + i) * c, c)], (t, 0), c, 3, 1)
+            self.conv(f"{name}.m{i}.cv2", [Part(t, 0, c)], (y, (2 + i) * c), c, 3, 1,
+                      residual=(y, (1 + i) * c) if shortcut else None)
+        out = self.value(name, c2, h, w)
+        self.conv(name + ".cv2", [Part(y, 0, (2 + n) * c)], (out, 0), c2, 1, 1)
+        return out
+
+    def sppf(self, name: str, src: str, c2: int) -> str:
+        v = self.p.values[src]
+        c_ = v.channels // 2
+        cat = self.value(name + ".cat", 4 * c_, v.h, v.w)
+        self.conv(name + ".cv1", [Part(src, 0, v.channels)], (cat, 0), c_, 1, 1)
+        self.p.commands.append(SppfCmd(name + ".m", Part(cat, 0, c_), (cat, c_)))
+        out = self.value(name, c2, v.h, v.w)
+        self.conv(name + ".cv2", [Part(cat, 0, 4 * c_)], (out, 0), c2, 1, 1)
+        return out
+
+    def detect(self, name: str, feats: List[str], strides: List[float]):
+        nc, reg_max = self.p.nc, self.p.reg_max
+        chs = [self.p.values[f].channels for f in feats]
+        c2 = max(16, chs[0] // 4, reg_max * 4)
+        c3 = max(chs[0], min(nc, 100))
+        levels = []
+        for i, (f, st) in enumerate(zip(feats, strides)):
+            v = self.p.values[f]
+            h0 = self.value(f"{name}.{i}.h0", c2 + c3, v.h, v.w)
+            h1 = self.value(f"{name}.{i}.h1", c2 + c3, v.h, v.w)
+            o = self.value(f"{name}.{i}.out", 4 * reg_max + nc, v.h, v.w)
+            # cv2[i][0] and cv3[i][0] read the same input: one conv with c2 + c3 outputs
+            self.conv(f"{name}.{i}.cv23_0", [Part(f, 0, chs[i])], (h0, 0), c2 + c3, 3, 1, precision="fp16")
+            self.conv(f"{name}.{i}.cv2_1", [Part(h0, 0, c2)], (h1, 0), c2, 3, 1, precision="fp16")
+            self.conv(f"{name}.{i}.cv3_1", [Part(h0, c2, c3)], (h1, c2), c3, 3, 1, precision="fp16")
+            self.conv(f"{name}.{i}.cv2_2", [Part(h1, 0, c2)], (o, 0), 4 * reg_max, 1, 1, silu=False, precision="fp16")
+            self.conv(f"{name}.{i}.cv3_2", [Part(h1, c2, c3)], (o, 4 * reg_max), nc, 1, 1, silu=False,
+                      precision="fp16")
+            levels.append((Part(o, 0, 4 * reg_max), Part(o, 4 * reg_max, nc), float(st)))
+        self.p.commands.append(DecodeCmd(name + ".decode", levels, nc, reg_max))
+
+
+def build_yolov8(width: float = 0.25, depth: float = 0.33, nc: int = 4, imgsz: int = 320, seed: int = 0,
+                 max_channels: int = 1024, name: Optional[str] = None) -> YoloProgram:
+    """YOLOv8 command stream (n: width 0.25 depth 0.33; s: width 0.5 depth 0.33)."""
+    def ch(c):
+        return _make_divisible(min(c, max_channels) * width, 8)
+
+    def dep(n):
+        return max(round(n * depth), 1) if n > 1 else n
+
+    b = _Builder(name or f"yolov8_w{width}_d{depth}_{imgsz}", imgsz, nc, seed)
+    img = [Part("images", 0, 3)]
+    x = b.conv_block("l0", img, ch(64), 3, 2, precision="fp16")  # stem: 3 input channels fail IC % 4
+    x = b.conv_block("l1", [Part(x, 0, ch(64))], ch(128), 3, 2)
+    x = b.c2f("l2", [Part(x, 0, ch(128))], ch(128), dep(3), True)
+    x = b.conv_block("l3", [Part(x, 0, ch(128))], ch(256), 3, 2)
+    p3 = b.c2f("l4", [Part(x, 0, ch(256))], ch(256), dep(6), True)
+    x = b.conv_block("l5", [Part(p3, 0, ch(256))], ch(512), 3, 2)
+    p4 = b.c2f("l6", [Part(x, 0, ch(512))], ch(512), dep(6), True)
+    x = b.conv_block("l7", [Part(p4, 0, ch(512))], ch(1024), 3, 2)
+    x = b.c2f("l8", [Part(x, 0, ch(1024))], ch(1024), dep(3), True)
+    p5 = b.sppf("l9", x, ch(1024))
+    # neck (PAN): upsample + concat feed the next C2f's cv1 directly
+    h12 = b.c2f("l12", [Part(p5, 0, ch(1024), 2), Part(p4, 0, ch(512))], ch(512), dep(3), False)
+    h15 = b.c2f("l15", [Part(h12, 0, ch(512), 2), Part(p3, 0, ch(256))], ch(256), dep(3), False)
+    x = b.conv_block("l16", [Part(h15, 0, ch(256))], ch(256), 3, 2)
+    h18 = b.c2f("l18", [Part(x, 0, ch(256)), Part(h12, 0, ch(512))], ch(512), dep(3), False)
+    x = b.conv_block("l19", [Part(h18, 0, ch(512))], ch(512), 3, 2)
+    h21 = b.c2f("l21", [Part(x, 0, ch(512)), Part(p5, 0, ch(1024))], ch(1024), dep(3), False)
+    b.detect("l22", [h15, h18, h21], [8.0, 16.0, 32.0])
+    return b.p
+
+
+def build_yolov8n(nc: int = 4, imgsz: int = 320, seed: int = 0) -> YoloProgram:
+    """YOLOv8n (width 0.25, depth 0.33), nc=4, 320x320."""
+    return build_yolov8(0.25, 0.33, nc, imgsz, seed, name=f"yolov8n_{imgsz}")
+
+
+def build_yolov8s(nc: int = 80, imgsz: int = 640, seed: int = 0) -> YoloProgram:
+    """YOLOv8s (width 0.5, depth 0.33), nc=80, 640x640."""
+    return build_yolov8(0.5, 0.33, nc, imgsz, seed, name=f"yolov8s_{imgsz}")
+
+
+def apply_algo_map(program: YoloProgram, int8: Optional[set] = None, pergroup: Optional[set] = None) -> None:
+    """The analogue of ``aexrtc --algo-map`` / ``int8_pergroup`` (engine.py:192-210):
+    ``int8`` limits the W8A8 kernels to the named convs (others run fp16),
+    ``pergroup`` sets the INT8_PERGROUP flag (pg16 activation scales)."""
+    for c in program.commands:
+        if not isinstance(c, ConvCmd) or c.precision != "int8":
+            continue
+        if int8 is not None and c.name not in int8:
+            c.precision = "fp16"
+        if pergroup is not None and c.name in pergroup:
+            c.pg16 = True

@@ -1,0 +1,336 @@
+"""Benchmark: W8A8 YOLOv8n-320 images/s on 1..8 B200s (data-parallel replicas).
+
+    python bench.py [--gpus N --steps K --warmup W --batch B] [--impl reference]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N ...
+
+One step = one forward of the YOLOv8n-320 W8A8 command stream (backbone and
+neck on the tcgen05 int8 convs, fp16 detect head, DFL decode) over a batch of
+B synthetic images per GPU, replayed as one CUDA graph.  Images never exchange
+data, so each rank runs its own replica on its own batch ("weak" scaling, no
+collective on the data path; torch.distributed only brackets the timed region
+and takes the max over ranks).  Rank 0 prints one JSON line.
+
+--impl reference times the reference's W8A8 arithmetic on the host cores (the
+reference path is D3D12/HLSL and cannot run here; its CPU restatement in
+oracle/ is the reference implementation) on a bounded sample of the same
+workload, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "W8A8 YOLOv8n-320 images/s"
+WORKLOAD = "yolov8n-320 W8A8 forward (int8 backbone+neck, fp16 head, DFL decode)"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=256, help="images per GPU per step")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-sample", type=int, default=24, help="images in the CPU baseline sample")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_reference(program, n_images: int, seed: int = 1):
+    """Times the oracle (the reference's W8A8 arithmetic on the CPU) on n_images."""
+    from oracle import yolo_model as om
+
+    rng = np.random.default_rng(seed)
+    imgs = rng.uniform(0, 1, (n_images, 3, program.imgsz, program.imgsz)).astype(np.float32)
+    om.run_program(program, imgs[:1])  # warm-up (builds/loads the C helper)
+    chunk = 4
+    t0 = time.perf_counter()
+    for i in range(0, n_images, chunk):
+        om.run_program(program, imgs[i:i + chunk])
+    dt = time.perf_counter() - t0
+    return n_images / dt, dt
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        import tempfile
+
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(parts)
+            except Exception:
+                pass
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def conv_roofline(eng, torch, stream):
+    """Per-launch CUDA-event timing of the W8A8 conv kernels (eager pass, after the timed region).
+
+    Algorithmic ops per launch = 2*N*OH*OW*OC*IC*KH*KW (benchmarks/roofline_report.py:94 convention);
+    achieved = sum(ops) / sum(kernel time) over all W8A8 conv launches of one step."""
+    from aexrt_b200 import _native
+    from aexrt_b200._native import check
+
+    lib = eng.lib
+    n = eng.batch
+    recs = []
+    check(lib.aexrt_b200_zero(eng.amax_arena.data_ptr(), eng.amax_arena.numel() * 4, stream), "zero")
+    for st in eng.steps:
+        if st[0] != "conv":
+            continue
+        _, c, plan, srcs, scratch, (h, w) = st
+        if c.precision != "int8":
+            continue
+        q, rec = scratch
+        check(lib.aexrt_b200_act_quantize_concat(srcs, len(srcs), n, h, w, int(c.pg16), c.s, q.data_ptr(),
+                                                 rec.data_ptr(), stream), "quantize")
+        out = eng.values[c.out[0]]
+        res = eng.values[c.residual[0]] if c.residual else None
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(torch.cuda.current_stream())
+        plan.run(q, rec, out=out, out_coff=c.out[1], residual=res, res_coff=c.residual[1] if c.residual else 0,
+                 amax_out=None, stream=stream)
+        e1.record(torch.cuda.current_stream())
+        d = eng.program.values[c.out[0]]
+        ops = 2.0 * n * d.h * d.w * c.oc * c.ic * c.k * c.k
+        byts = n * (c.ic * h * w + 2 * c.oc * d.h * d.w) + c.oc * c.ic * c.k * c.k
+        recs.append((e0, e1, ops, byts))
+    torch.cuda.synchronize()
+    t = sum(e0.elapsed_time(e1) for e0, e1, _, _ in recs) / 1e3
+    ops = sum(r[2] for r in recs)
+    byts = sum(r[3] for r in recs)
+    return {"time_s": t, "ops": ops, "bytes": byts, "launches": len(recs)}
+
+
+def run_reference(args):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return 0
+    from aexrt_b200 import yolo
+
+    program = yolo.build_yolov8n(nc=4, imgsz=320, seed=0)
+    cores = host_cores()
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+    per_step = 4
+    for _ in range(args.warmup):
+        cpu_reference(program, per_step, seed=2)
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        cpu_reference(program, per_step, seed=3 + k)
+    dt = time.perf_counter() - t0
+    ips = args.steps * per_step / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": ips, "unit": "images/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": WORKLOAD + " on the host CPU", "global_batch": per_step, "imgsz": 320, "nc": 4,
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": ips, "unit": "images/s", "cores": cores, "kind": "port",
+                         "sample": f"{per_step} images per step x {args.steps} steps through the CPU restatement "
+                                   "of the reference's W8A8 arithmetic (oracle/), C/OpenMP int32 convolutions"},
+        "e2e": {"value": ips, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    from aexrt_b200 import engine, yolo
+
+    program = yolo.build_yolov8n(nc=4, imgsz=320, seed=0)
+    B = args.batch
+    eng = engine.CompiledYolo(program, B)
+    rng = np.random.default_rng(1000 + rank)
+    host_in = torch.from_numpy(rng.uniform(0, 1, (B, 3, 320, 320)).astype(np.float32)).pin_memory()
+    host_out = torch.empty(tuple(eng.output.shape), dtype=torch.float32).pin_memory()
+    eng.images.copy_(host_in)
+    eng.capture()
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def timed(fn, steps):
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t = e0.elapsed_time(e1) / 1e3
+        if dist is not None:
+            tt = torch.tensor([t], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
+    def step_device():
+        eng.graph.replay()
+
+    def step_e2e():
+        eng.images.copy_(host_in, non_blocking=True)
+        eng.graph.replay()
+        host_out.copy_(eng.output, non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        step_device()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t_dev = timed(step_device, args.steps)
+    clocks = clk.summary()
+    e2e = None
+    if not args.no_e2e:
+        for _ in range(3):
+            step_e2e()
+        t_e2e = timed(step_e2e, args.steps)
+        e2e = {"value": world * B * args.steps / t_e2e, "unit": "images/s",
+               "h2d_bytes_per_step": int(host_in.numel() * 4), "d2h_bytes_per_step": int(host_out.numel() * 4)}
+    status = eng.status()
+    # roofline of the dominant kernel (W8A8 conv), measured per launch with CUDA events
+    rf = conv_roofline(eng, torch, stream.cuda_stream)
+    hbm, bf16, src = measured_peaks()
+    int8_peak = 2.0 * bf16  # dense int8 tensor throughput is twice bf16 on B200
+    achieved = rf["ops"] / rf["time_s"] / 1e12
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1:
+            os.environ.setdefault("OMP_NUM_THREADS", str(host_cores()))
+            ips, dt = cpu_reference(program, args.cpu_sample)
+            cpu = {"value": ips, "unit": "images/s", "cores": host_cores(), "kind": "port",
+                   "sample": f"{args.cpu_sample} images through the CPU restatement of the reference's W8A8 "
+                             f"arithmetic (oracle/, C/OpenMP int32 convolutions), {dt:.1f} s"}
+        line = {
+            "metric": METRIC, "value": world * B * args.steps / t_dev, "unit": "images/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_dev / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (uniform[0,1] fp32 images, seeded random-init YOLOv8n weights)",
+            "config": {"workload": WORKLOAD, "global_batch": world * B, "per_gpu_batch": B, "imgsz": 320, "nc": 4,
+                       "parallelism": f"dp{world} (independent replicas)",
+                       "l2": f"inputs larger than L2 ({B * 3 * 320 * 320 * 4 / 1e6:.0f} MB of fp32 images per step)"},
+            "e2e": e2e,
+            "gpu_launches": eng.launches_per_run * args.steps,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
+                         "frac": achieved / int8_peak, "traffic": None,
+                         "kernel": "conv_tc_kernel (all W8A8 conv launches of one step)",
+                         "peak_source": f"2 x {src} bf16 dense ({bf16} TFLOP/s) from MEASURED_PEAKS.json",
+                         "conv_ms_per_step": rf["time_s"] * 1e3, "conv_launches": rf["launches"],
+                         "conv_hbm_gbs_equiv": rf["bytes"] / rf["time_s"] / 1e9, "hbm_peak_gbs": hbm},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        eng.graph = None
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

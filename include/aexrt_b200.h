@@ -187,6 +187,63 @@ uint64_t aexrt_b200_packed_f16_bytes(uint32_t n, uint32_t c, uint32_t h, uint32_
 int aexrt_b200_pack_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t layout, uint32_t ldc,
                         uint32_t coff, uint32_t consumer_stride, void* out, void* stream);
 
+/* ---------------------------------------------------------------- a10: fused neighbours
+ * One input part of a conv whose input is a channel concatenation (CONCAT,
+ * engine.py:103-118), optionally read through a nearest 2x upsample (RESIZE)
+ * and/or as a channel slice of a wider NHWC buffer (SLICE / C2f split).  The
+ * quantizer reads the parts in place, so the concatenated fp16 tensor is never
+ * materialised: the reference instead runs CONCAT, then quantizes the
+ * concatenated value (runtime.cpp:21466-21665). */
+typedef struct AexrtB200ActSource {
+    const void* ptr;
+    uint32_t layout;              /* AEXRT_B200_LAYOUT_* */
+    uint32_t ldc, coff;           /* NHWC slice: channel stride and offset */
+    uint32_t channels;            /* multiple of 16 except for the last part (int8) / 8 (fp16) */
+    uint32_t upsample;            /* 1, or 2 for nearest-neighbour 2x */
+    uint32_t src_h, src_w;        /* spatial dims of this part (consumer dims / upsample) */
+    const uint32_t* amax_groups;  /* per (image, group) amax bits of this part's buffer (int8 only) */
+    uint32_t amax_stride, amax_goff;
+} AexrtB200ActSource;
+
+/* Quantize a concatenation of parts into one slab16 int8 input (+ scale record). */
+int aexrt_b200_act_quantize_concat(const AexrtB200ActSource* srcs, uint32_t nsrc, uint32_t n, uint32_t h, uint32_t w,
+                                   uint32_t mode, uint32_t consumer_stride, void* q_out, float* scale_rec,
+                                   void* stream);
+
+/* fp16 slab8 repack of a concatenation of parts (fp16 convs). */
+int aexrt_b200_pack_f16_concat(const AexrtB200ActSource* srcs, uint32_t nsrc, uint32_t n, uint32_t h, uint32_t w,
+                               uint32_t consumer_stride, void* out, void* stream);
+
+/* SPPF pooling (YOLOv8 SPPF: three cascaded MaxPool2d(5, 1, 2) whose outputs
+ * are concatenated; reference kind MAXPOOL, engine.py:103-118): writes the 5x5,
+ * 9x9 and 13x13 window maxima of the NHWC slice x into three consecutive
+ * c-channel slices of out starting at out_coff, and max-es their |y| per
+ * 16-channel group into amax (optional). */
+int aexrt_b200_sppf_pool(const void* x, uint32_t n, uint32_t h, uint32_t w, uint32_t c, uint32_t ldc, uint32_t coff,
+                         void* out, uint32_t out_ldc, uint32_t out_coff, uint32_t* amax, uint32_t amax_stride,
+                         uint32_t amax_goff, void* stream);
+
+/* One detect level: box-distribution logits (4*reg_max channels) and class
+ * logits (nc channels), both fp16 NHWC slices, with the level's stride. */
+typedef struct AexrtB200DecodeLevel {
+    const void* box;
+    uint32_t box_ldc, box_coff;
+    const void* cls;
+    uint32_t cls_ldc, cls_coff;
+    uint32_t h, w;
+    float stride;
+} AexrtB200DecodeLevel;
+
+/* Anchor-free YOLOv8 decode (DFL expectation over reg_max bins, distance to
+ * box, class sigmoid) into out[n][4 + nc][anchors] fp32 (cx, cy, w, h in input
+ * pixels, then class scores): the layout of the model's output0 that the
+ * reference post-processes (src/aexrt/yolo.py:92-138). */
+int aexrt_b200_yolo_decode(const AexrtB200DecodeLevel* levels, uint32_t nlevels, uint32_t n, uint32_t nc,
+                           uint32_t reg_max, float* out, void* stream);
+
+/* cudaMemsetAsync(ptr, 0, bytes, stream): clears amax slots inside a captured graph. */
+int aexrt_b200_zero(void* ptr, uint64_t bytes, void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif
