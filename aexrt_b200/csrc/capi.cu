@@ -19,7 +19,7 @@
 #include <vector>
 
 #include "../../include/aexrt_b200.h"
-#include "conv_tc.cuh"
+#include "conv_halo.cuh"
 #include "quant.cuh"
 #include "yolo_ops.cuh"
 
@@ -116,6 +116,9 @@ struct AexrtB200ConvPlan {
   int q_total = 0, kk_p = 0, sps = 0, stages = 0, smem = 0;
   int grid = 0;          // persistent CTAs (one per SM, at most one per tile)
   int total_tiles = 0;
+  // halo variant (conv_halo.cuh): whole weight tile resident, one halo per slab and tile
+  bool halo = false;
+  int pitch = 0, halo_rows = 0, boxes_per_slab = 1, slab_pairs = 0, taps = 1, w_tile_bytes = 0, m_tiles = 0;
   void* d_w = nullptr;   // [n_tile][q_total][bn][16 bytes]
   float* d_scale = nullptr;
   float* d_bias = nullptr;
@@ -145,6 +148,53 @@ KernelFn kernel_for_bn(int bn) {
 KernelFn kernel_for(bool f16, bool pg, int bn) {
   if (f16) return kernel_for_bn<true, false>(bn);
   return pg ? kernel_for_bn<false, true>(bn) : kernel_for_bn<false, false>(bn);
+}
+
+using HaloFn = void (*)(const CUtensorMap, const ConvHaloParams);
+
+struct HaloKernel {
+  HaloFn fn;
+  int threads;
+};
+
+template <bool F16, bool SILU, bool RES>
+HaloKernel halo_kernel_for_bn(int bn) {
+  switch (bn) {
+    case 16: return {conv_halo_kernel<F16, 16, SILU, RES>, halo_threads<16>()};
+    case 32: return {conv_halo_kernel<F16, 32, SILU, RES>, halo_threads<32>()};
+    case 64: return {conv_halo_kernel<F16, 64, SILU, RES>, halo_threads<64>()};
+    case 128: return {conv_halo_kernel<F16, 128, SILU, RES>, halo_threads<128>()};
+    case 256: return {conv_halo_kernel<F16, 256, SILU, RES>, halo_threads<256>()};
+    default: return {nullptr, 0};
+  }
+}
+
+// fp16 convs (stem, detect head) never carry a residual; the int8 convs do (C2f tail).
+HaloKernel halo_kernel_for(bool f16, int bn, bool silu, bool res) {
+  if (f16) return silu ? halo_kernel_for_bn<true, true, false>(bn) : halo_kernel_for_bn<true, false, false>(bn);
+  if (silu) return res ? halo_kernel_for_bn<false, true, true>(bn) : halo_kernel_for_bn<false, true, false>(bn);
+  return res ? halo_kernel_for_bn<false, false, true>(bn) : halo_kernel_for_bn<false, false, false>(bn);
+}
+
+// Halo tile: output tw x th on an M grid of pitch = tw + (2 for 3x3 s1, 1 for 3x3 s2, 0 for 1x1)
+// <= max_pitch (one TMA box row of pitch pixels within the 256-element limit), th*pitch <= 128.
+bool pick_halo_tile(int oh, int ow, int k, int s, int max_pitch, int& tw, int& th, int& pitch) {
+  const int extra = k == 1 ? 0 : (s == 1 ? 2 : 1);
+  double best = -1.0;
+  for (int w = 1; w + extra <= max_pitch && w <= ow; ++w) {
+    const int pt = w + extra;
+    const int h = std::min(oh, 128 / pt);
+    if (h < 1) continue;
+    const long tiles = static_cast<long>((oh + h - 1) / h) * ((ow + w - 1) / w);
+    const double util = static_cast<double>(oh) * ow / (static_cast<double>(tiles) * 128.0);
+    if (util > best + 1e-9) {
+      best = util;
+      tw = w;
+      th = h;
+      pitch = pt;
+    }
+  }
+  return best > 0.0;
 }
 
 int choose_bn(int oc, bool pg, uint32_t requested) {
@@ -194,6 +244,15 @@ bool check_desc_int8(const AexrtConv2DDesc& d, uint32_t kernel_id, bool pg) {
   return true;
 }
 
+cudaError_t set_halo_smem(bool f16, int bn, bool silu) {
+  for (int res = 0; res < (f16 ? 1 : 2); ++res) {
+    const cudaError_t e = cudaFuncSetAttribute(halo_kernel_for(f16, bn, silu, res).fn,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxConvSmem);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t kernel_id, uint32_t flags, bool f16,
                               const void* host_w, const float* scale, const float* bias, uint32_t block_n) {
   if (kind != AEXRT_B200_KIND_CONV && kind != AEXRT_B200_KIND_CONV_SILU) {
@@ -223,6 +282,8 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   pick_tile(static_cast<int>(d.out_h), static_cast<int>(d.out_w), f16 ? 32 : 16, p->tw, p->th);
   p->tiles_w = (static_cast<int>(d.out_w) + p->tw - 1) / p->tw;
   p->tiles_h = (static_cast<int>(d.out_h) + p->th - 1) / p->th;
+  const uint32_t variant = (block_n >> 16) & 0xF;  // 0 auto, 1 slot streaming, 2 halo
+  block_n &= 0xFFFF;
   p->bn = choose_bn(oc, p->pg, block_n);
   if (!kernel_for(f16, p->pg, p->bn)) {
     fail("unsupported block_n %d", p->bn);
@@ -249,10 +310,77 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   }
   p->total_tiles = static_cast<int>(d.batch) * p->tiles_h * p->tiles_w * p->n_tiles;
 
-  // ---- weight repack into [n_tile][slot][bn][16 bytes]: one stage of B is one contiguous run
+  // ---- halo variant: per-tensor int8 or fp16, when the whole weight tile fits next to >= 2 stages
+  if (!p->pg && variant != 1) {
+    int tw = 0, th = 0, pitch = 0;
+    const int taps = kk;
+    const int pairs = (p->slabs + 1) / 2;
+    const int w_tile = pairs * taps * 2 * p->bn * 16;
+    if (pick_halo_tile(static_cast<int>(d.out_h), static_cast<int>(d.out_w), p->k, p->stride, f16 ? 32 : 16, tw, th,
+                       pitch)) {
+      const int halo_h = p->k == 1 ? th : (p->stride == 1 ? th + 2 : th + 1);
+      const int boxes = p->stride == 2 ? 4 : 1;
+      const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile);
+      const int budget = kMaxConvSmem - 1024;
+      const int st = std::min(16, (budget - one.total_bytes) / one.stage_bytes + 1);
+      if (st >= 2) {
+        p->halo = true;
+        p->tw = tw;
+        p->th = th;
+        p->pitch = pitch;
+        p->halo_rows = halo_h * pitch;
+        p->boxes_per_slab = boxes;
+        p->slab_pairs = pairs;
+        p->taps = taps;
+        p->w_tile_bytes = w_tile;
+        p->stages = st;
+        p->smem = halo_smem_plan(p->halo_rows, boxes, st, w_tile).total_bytes;
+        p->tiles_w = (static_cast<int>(d.out_w) + tw - 1) / tw;
+        p->tiles_h = (static_cast<int>(d.out_h) + th - 1) / th;
+        p->m_tiles = static_cast<int>(d.batch) * p->tiles_h * p->tiles_w;
+        p->total_tiles = p->m_tiles * p->n_tiles;
+      }
+    }
+    if (variant == 2 && !p->halo) {
+      fail("halo variant does not fit this conv");
+      delete p;
+      return nullptr;
+    }
+  }
+
+  // ---- weight repack.  Slot streaming: [n_tile][slot][bn][16 bytes] (one stage of B is one
+  // contiguous run).  Halo: [n_tile][slab pair][tap][2][bn][16 bytes] (the resident tile).
   const size_t slot_row = 16;
-  std::vector<uint8_t> packed(static_cast<size_t>(p->q_total) * p->oc_alloc * slot_row, 0);
-  for (int q = 0; q < p->q_total; ++q) {
+  std::vector<uint8_t> packed(static_cast<size_t>(p->halo ? p->n_tiles * p->w_tile_bytes
+                                                          : static_cast<size_t>(p->q_total) * p->oc_alloc * slot_row),
+                              0);
+  if (p->halo) {
+    for (int nt = 0; nt < p->n_tiles; ++nt)
+      for (int pr = 0; pr < p->slab_pairs; ++pr)
+        for (int tap = 0; tap < kk; ++tap)
+          for (int ch = 0; ch < 2; ++ch) {
+            const int slab = 2 * pr + ch;
+            if (slab >= p->slabs) continue;
+            for (int on = 0; on < p->bn; ++on) {
+              const int o = nt * p->bn + on;
+              if (o >= oc) continue;
+              uint8_t* dst = packed.data() + static_cast<size_t>(nt) * p->w_tile_bytes +
+                             ((((static_cast<size_t>(pr) * kk + tap) * 2 + ch) * p->bn) + on) * slot_row;
+              for (int c = 0; c < cps; ++c) {
+                const int ci = slab * cps + c;
+                if (ci >= ic) continue;
+                const size_t src = (static_cast<size_t>(o) * ic + ci) * kk + tap;
+                if (f16) {
+                  const __half h = __float2half_rn(static_cast<const float*>(host_w)[src]);
+                  std::memcpy(dst + 2 * c, &h, 2);
+                } else {
+                  dst[c] = static_cast<uint8_t>(static_cast<const int8_t*>(host_w)[src]);
+                }
+              }
+            }
+          }
+  }
+  for (int q = 0; q < (p->halo ? 0 : p->q_total); ++q) {
     int tap, slab;
     if (p->pg) {
       slab = q / p->kk_p;
@@ -300,8 +428,9 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
     // the attribute is a per-kernel cap shared by every plan of this instance: set it to the
     // largest dynamic shared memory any plan may request, never to this plan's size
     ok = p->smem <= kMaxConvSmem &&
-         cuda_ok(cudaFuncSetAttribute(kernel_for(f16, p->pg, p->bn), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      kMaxConvSmem),
+         cuda_ok(p->halo ? set_halo_smem(f16, p->bn, kind == AEXRT_B200_KIND_CONV_SILU)
+                         : cudaFuncSetAttribute(kernel_for(f16, p->pg, p->bn),
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxConvSmem),
                  "cudaFuncSetAttribute");
     if (p->smem > kMaxConvSmem) fail("conv plan needs %d bytes of shared memory", p->smem);
   }
@@ -317,6 +446,20 @@ bool encode_act_map(const AexrtB200ConvPlan* p, const void* x, CUtensorMap* map)
   const uint64_t sn = static_cast<uint64_t>(p->slabs) * p->desc.batch;
   const uint32_t ce = p->f16 ? 8 : 16;  // elements per 16-byte slot (one pixel of one slab)
   const CUtensorMapDataType dt = p->f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  if (p->halo) {
+    const uint32_t box_x = ce * static_cast<uint32_t>(p->pitch);  // one box row = pitch pixels
+    const uint32_t box_h = static_cast<uint32_t>(p->halo_rows / p->pitch);
+    if (p->stride == 1) {
+      const uint64_t dims[3] = {ce * wp, hp, sn};
+      const uint64_t strides[2] = {16 * wp, 16 * wp * hp};
+      const uint32_t box[3] = {box_x, box_h, 1};
+      return encode_map(map, dt, 3, x, dims, strides, box);
+    }
+    const uint64_t dims[5] = {ce * wp / 2, 2, 2, hp / 2, sn};
+    const uint64_t strides[4] = {8 * wp, 16 * wp, 32 * wp, 16 * wp * hp};
+    const uint32_t box[5] = {box_x, 1, 1, box_h, 1};
+    return encode_map(map, dt, 5, x, dims, strides, box);
+  }
   const uint32_t box_x = ce * static_cast<uint32_t>(p->tw);  // one box row = tw pixels
   if (p->stride == 1) {
     // [image*slab][H][W*16 bytes]
@@ -348,6 +491,54 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
   if (reinterpret_cast<uintptr_t>(x) % 16) return fail("packed input must be 16-byte aligned");
   CUtensorMap act_map;
   if (!encode_act_map(p, x, &act_map)) return 0;
+  const int out_vec = (out_ldc % 8 == 0 && out_coff % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) ? 1 : 0;
+  const int res_vec = (res && res_ldc % 8 == 0 && res_coff % 8 == 0 && reinterpret_cast<uintptr_t>(res) % 16 == 0) ? 1 : 0;
+  if (p->halo) {
+    ConvHaloParams h{};
+    h.n_img = static_cast<int>(p->desc.batch);
+    h.slabs = p->slabs;
+    h.slab_pairs = p->slab_pairs;
+    h.oc = static_cast<int>(oc);
+    h.oh = static_cast<int>(p->desc.out_h);
+    h.ow = static_cast<int>(p->desc.out_w);
+    h.ksize = p->k;
+    h.stride = p->stride;
+    h.tw = p->tw;
+    h.th = p->th;
+    h.pitch = p->pitch;
+    h.halo_rows = p->halo_rows;
+    h.boxes_per_slab = p->boxes_per_slab;
+    h.tiles_w = p->tiles_w;
+    h.tiles_h = p->tiles_h;
+    h.n_tiles = p->n_tiles;
+    h.m_tiles = p->m_tiles;
+    h.total_tiles = p->total_tiles;
+    h.taps = p->taps;
+    h.stages = p->stages;
+    h.w_packed = static_cast<const uint8_t*>(p->d_w);
+    h.w_tile_bytes = p->w_tile_bytes;
+    h.scale_rec = scale_rec;
+    h.w_scale = p->d_scale;
+    h.bias = p->d_bias;
+    h.res = static_cast<const __half*>(res);
+    h.res_ldc = static_cast<int>(res_ldc);
+    h.res_coff = static_cast<int>(res_coff);
+    h.out = static_cast<__half*>(out);
+    h.out_ldc = static_cast<int>(out_ldc);
+    h.out_coff = static_cast<int>(out_coff);
+    h.out_vec = out_vec;
+    h.res_vec = res_vec;
+    h.amax_out = amax_out;
+    h.amax_stride = static_cast<int>(amax_stride);
+    h.amax_goff = static_cast<int>(amax_goff);
+    h.acc_dump = acc_dump;
+    h.status = p->d_status;
+    h.silu = p->kind == AEXRT_B200_KIND_CONV_SILU;
+    if (p->f16 && res) return fail("fp16 convs take no residual");
+    const HaloKernel k = halo_kernel_for(p->f16, p->bn, h.silu != 0, res != nullptr);
+    k.fn<<<p->grid, k.threads, p->smem, static_cast<cudaStream_t>(stream)>>>(act_map, h);
+    return cuda_ok(cudaGetLastError(), "conv launch") ? 1 : 0;
+  }
   ConvTcParams prm{};
   prm.n_img = static_cast<int>(p->desc.batch);
   prm.slabs = p->slabs;
@@ -605,6 +796,8 @@ int aexrt_b200_conv_plan_info(const AexrtB200ConvPlan* p, AexrtB200ConvPlanInfo*
   i.grid_m = p->desc.batch * p->tiles_h * p->tiles_w;
   i.grid_n = p->n_tiles;
   i.reserved[0] = p->grid;
+  i.reserved[1] = p->halo ? 2u : 1u;  // variant
+  i.reserved[2] = p->pitch;
   i.in_hp = p->in_hp;
   i.in_wp = p->in_wp;
   *info = i;

@@ -1,0 +1,421 @@
+// Halo-tile tcgen05 convolution: the per-tensor W8A8 conv (kernels 51/52/53,
+// native/aexrt_d3d12_runtime.cpp:4614-4762) and the fp16 convs, with the whole
+// weight tile resident in shared memory and each activation slab loaded ONCE
+// per output tile.
+//
+// Each output tile is TH rows x TW columns of one image, computed on an M grid
+// of TH rows with a row pitch P >= TW (the extra columns are junk rows of the
+// MMA that the epilogue drops).  For a stride-1 3x3 conv the tile's input halo
+// ((TH+2) x P pixels of one 16-byte slab chunk) is one TMA box; the MMA of tap
+// (kh, kw) reads that halo through a descriptor whose start address is shifted
+// by kh*P + kw rows -- the canonical K-major no-swizzle UMMA layout only needs
+// 16-byte aligned starts, so a shifted window is itself a valid operand.  A
+// stride-2 conv loads the halo of each of the four (row, column) parities of
+// the parity-split input layout ((TH+1) x P pixels each, P = TW+1) and a tap
+// reads its parity's halo with a shift of 0 or 1 row/column.  A 1x1 conv loads
+// the TH x TW tile itself.
+//
+// One MMA K step covers two 16-byte chunks: the same pixel window of two
+// consecutive slabs (LBO = bytes of one slab's halo).  Pipeline stages carry
+// the halo of one slab pair; all K of the CTA's output-channel tile
+// ([slab pair][tap][2][BN][16 B]) stays resident.  Activation traffic from L2
+// drops from 9x the input (one box per tap) to ~1.3x (one halo per tile), and
+// weight traffic to one copy per CTA.
+#pragma once
+#include "conv_tc.cuh"
+
+namespace aexrt {
+
+struct ConvHaloParams {
+  int n_img, slabs, slab_pairs;
+  int oc, oh, ow;
+  int ksize, stride;
+  int tw, th, pitch;        // output tile and M-grid row pitch
+  int halo_rows;            // rows (pixels) of one halo box
+  int boxes_per_slab;       // 1 (s1, 1x1) or 4 (s2 parities)
+  int tiles_w, tiles_h, n_tiles, m_tiles, total_tiles;
+  int taps;                 // 9 or 1
+  int stages;
+  const uint8_t* w_packed;  // [n_tile][slab_pair][tap][2][BN][16]
+  int w_tile_bytes;
+  const float* scale_rec;
+  const float* w_scale;
+  const float* bias;
+  const __half* res;
+  int res_ldc, res_coff;
+  __half* out;
+  int out_ldc, out_coff;
+  int out_vec, res_vec;
+  uint32_t* amax_out;
+  int amax_stride, amax_goff;
+  int32_t* acc_dump;
+  uint32_t* status;
+  int silu;
+};
+
+struct HaloSmemPlan {
+  int slab_bytes;   // one slab's halo (all parity boxes), multiple of 128
+  int stage_bytes;  // two slabs
+  int a_bytes;      // all stages
+  int b_offset;
+  int bar_offset;
+  int total_bytes;
+};
+
+__host__ __device__ inline HaloSmemPlan halo_smem_plan(int halo_rows, int boxes_per_slab, int stages,
+                                                       int w_tile_bytes) {
+  HaloSmemPlan s;
+  const int box_bytes = ((halo_rows * kSlotBytes + 127) / 128) * 128;
+  s.slab_bytes = box_bytes * boxes_per_slab;
+  s.stage_bytes = 2 * s.slab_bytes;
+  // 4 KB of slack: a shifted 128-row window may run past the last halo row
+  s.a_bytes = stages * s.stage_bytes + 4096;
+  s.b_offset = ((s.a_bytes + 1023) / 1024) * 1024;
+  s.bar_offset = s.b_offset + ((w_tile_bytes + 127) / 128) * 128;
+  // barriers: full[stages], empty[stages], acc_full[4], acc_empty[4], w_full[2]; then the TMEM address
+  s.total_bytes = s.bar_offset + (2 * stages + 10) * 8 + 16;
+  return s;
+}
+
+// Epilogue warps: 4 per TMEM lane quadrant (each owning BN/4 columns) when BN >= 64.
+template <int BN>
+constexpr int halo_epi_warps() {
+  return BN >= 64 ? 16 : (BN >= 32 ? 8 : 4);
+}
+template <int BN>
+constexpr int halo_threads() {
+  return 64 + 32 * halo_epi_warps<BN>();
+}
+
+// Epilogue of 8 consecutive output channels of one pixel (full-width fast path
+// when all 8 channels exist and the row is 16-byte aligned): scale, bias,
+// SiLU, residual, fp16 store.  Returns the max |fp16 output| of the 8 values.
+template <bool kF16, bool kSilu, bool kRes>
+__device__ __forceinline__ float halo_epilogue8(const ConvHaloParams& p, const uint32_t* v, float in_scale, int oc,
+                                                bool valid, __half* out_row, const __half* res_row) {
+  const int n_valid = p.oc - oc;
+  float y[8];
+  if (n_valid >= 8) {
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.bias + oc));
+    const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.bias + oc) + 1);
+    const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    if constexpr (kF16) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[i]) + bb[i];
+    } else {
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.w_scale + oc));
+      const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.w_scale + oc) + 1);
+      const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = fmaf(static_cast<float>(static_cast<int32_t>(v[i])) * in_scale, ss[i], bb[i]);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i < n_valid) {
+        const float a = kF16 ? __uint_as_float(v[i]) : static_cast<float>(static_cast<int32_t>(v[i])) * in_scale;
+        y[i] = kF16 ? a + __ldg(p.bias + oc + i) : fmaf(a, __ldg(p.w_scale + oc + i), __ldg(p.bias + oc + i));
+      } else {
+        y[i] = 0.0f;
+      }
+    }
+  }
+  if constexpr (kSilu) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = silu_fast(y[i]);
+  }
+  const bool vec = n_valid >= 8 && p.out_vec;
+  if constexpr (kRes) {
+    if (valid) {
+      if (n_valid >= 8 && p.res_vec) {
+        const uint4 r = *reinterpret_cast<const uint4*>(res_row + oc);
+        const __half2* rh = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(rh[i]);
+          y[2 * i] += f.x;
+          y[2 * i + 1] += f.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (i < n_valid) y[i] += __half2float(res_row[oc + i]);
+      }
+    }
+  }
+  if (n_valid < 8) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i >= n_valid) y[i] = 0.0f;
+  }
+  __align__(16) __half2 hv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) hv[i] = __floats2half2_rn(y[2 * i], y[2 * i + 1]);
+  if (valid) {
+    if (vec) {
+      *reinterpret_cast<uint4*>(out_row + oc) = *reinterpret_cast<const uint4*>(hv);
+    } else if (n_valid > 0) {
+      const __half* h = reinterpret_cast<const __half*>(hv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < n_valid) out_row[oc + i] = h[i];
+    }
+  }
+  const __half2 m = __hmax2(__hmax2(__habs2(hv[0]), __habs2(hv[1])), __hmax2(__habs2(hv[2]), __habs2(hv[3])));
+  return valid ? fmaxf(__low2float(m), __high2float(m)) : 0.0f;
+}
+
+template <bool kF16, int BN, bool kSilu, bool kRes>
+__global__ void __launch_bounds__(halo_threads<BN>(), 1)
+    conv_halo_kernel(const __grid_constant__ CUtensorMap act_map, const ConvHaloParams p) {
+  constexpr int kEpiWarps = halo_epi_warps<BN>();
+  constexpr int kCols = BN / (kEpiWarps / 4);  // columns per epilogue warp
+  constexpr int CW = kCols >= 32 ? 32 : 16;     // columns per TMEM load
+  constexpr int kChunks = kCols / CW;
+  // accumulator buffers in TMEM: up to 4, so the MMA can run several tiles ahead of the epilogue
+  constexpr int kAcc = BN <= 128 ? 4 : 2;
+  constexpr uint32_t kTmemCols = (kAcc * BN <= 32) ? 32 : (kAcc * BN <= 64) ? 64 : (kAcc * BN <= 128) ? 128 : (kAcc * BN <= 256) ? 256 : 512;
+  constexpr int kCS = kF16 ? 8 : 16;  // tensor-map elements per 16-byte chunk
+
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const HaloSmemPlan sp = halo_smem_plan(p.halo_rows, p.boxes_per_slab, p.stages, p.w_tile_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.bar_offset);
+  uint64_t* empty = full + p.stages;
+  uint64_t* acc_full = full + 2 * p.stages;  // [kAcc]
+  uint64_t* acc_empty = acc_full + 4;        // [kAcc]
+  uint64_t* w_full = acc_empty + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(w_full + 2);
+  const int box_bytes = sp.slab_bytes / p.boxes_per_slab;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < kAcc; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiWarps);
+    }
+    mbar_init(&w_full[0], 1);
+    mbar_init(&w_full[1], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&act_map);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // tiles are ordered n-tile major, so a persistent CTA keeps one weight tile for long runs
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    int s = 0, it = 0, cur_n = -1, wloads = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      const int n_tile = t / p.m_tiles;
+      const int m_tile = t - n_tile * p.m_tiles;
+      const int per_img = p.tiles_w * p.tiles_h;
+      const int img = m_tile / per_img;
+      const int r = m_tile - img * per_img;
+      const int oh0 = (r / p.tiles_w) * p.th, ow0 = (r % p.tiles_w) * p.tw;
+      if (n_tile != cur_n) {
+        // a new weight tile: wait until every MMA reading the old one has completed
+        if (wloads > 0 && !mbar_wait_bounded(&w_full[1], (wloads - 1) & 1, p.status, kStatusTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&w_full[0], static_cast<uint32_t>(p.w_tile_bytes));
+          const uint8_t* src = p.w_packed + static_cast<size_t>(n_tile) * p.w_tile_bytes;
+          for (int off = 0; off < p.w_tile_bytes; off += 32768)
+            bulk_load(smem + sp.b_offset + off, src + off, static_cast<uint32_t>(min(32768, p.w_tile_bytes - off)),
+                      &w_full[0]);
+        }
+        cur_n = n_tile;
+        ++wloads;
+      }
+      for (int pr = 0; pr < p.slab_pairs; ++pr) {
+        if (it >= p.stages && !mbar_wait_bounded(&empty[s], ph ^ 1u, p.status, kStatusTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0)
+          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(2 * p.boxes_per_slab * p.halo_rows * kSlotBytes));
+        __syncwarp();
+        const int nbox = 2 * p.boxes_per_slab;
+        if (lane < nbox) {
+          const int which = lane / p.boxes_per_slab;  // slab of the pair
+          const int box = lane - which * p.boxes_per_slab;
+          const int slab = 2 * pr + which;
+          const int sn = slab < p.slabs ? img * p.slabs + slab : p.n_img * p.slabs;  // odd count: zero slab
+          uint8_t* dst = smem + s * sp.stage_bytes + which * sp.slab_bytes + box * box_bytes;
+          if (p.stride == 2) {
+            const int phr = box >> 1, phc = box & 1;
+            tma_load_5d(dst, &act_map, &full[s], kCS * (ow0 - 1), phc, phr, oh0 - 1, sn);
+          } else if (p.ksize == 3) {
+            tma_load_3d(dst, &act_map, &full[s], kCS * (ow0 - 1), oh0 - 1, sn);
+          } else {
+            tma_load_3d(dst, &act_map, &full[s], kCS * ow0, oh0, sn);
+          }
+        }
+        ++it;
+        if (++s == p.stages) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc<kF16>(BN);
+      // descriptor of (stage 0, tap 0) and per-tap start offsets, in 16-byte descriptor units
+      const uint64_t a_desc0 = smem_desc_kmajor_noswizzle(smem_u32(smem), sp.slab_bytes, 128);
+      const uint64_t b_desc0 = smem_desc_kmajor_noswizzle(smem_u32(smem + sp.b_offset), BN * kSlotBytes, 128);
+      const uint32_t b_step = (2 * BN * kSlotBytes) >> 4;  // one (pair, tap) of resident B
+      const uint32_t stage_step = sp.stage_bytes >> 4;
+      uint32_t tap_off[9];
+#pragma unroll
+      for (int tap = 0; tap < 9; ++tap) {
+        const int kh = tap / 3, kw = tap % 3;
+        uint32_t off = 0;
+        if (p.stride == 2) {
+          // parity box of the tap, shifted by 0 (kh/kw == 0) or 1 pixel
+          off = ((((kh + 1) & 1) * 2 + ((kw + 1) & 1)) * box_bytes + ((kh ? 1 : 0) * p.pitch + (kw ? 1 : 0)) * kSlotBytes);
+        } else if (p.ksize == 3) {
+          off = (kh * p.pitch + kw) * kSlotBytes;
+        }
+        tap_off[tap] = off >> 4;
+      }
+      int s = 0, u = 0, cur_n = -1, wloads = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+        const int n_tile = t / p.m_tiles;
+        if (n_tile != cur_n) {
+          if (wloads > 0) tc_commit(&w_full[1]);  // releases the old weights once prior MMAs finish
+          if (!mbar_wait_bounded(&w_full[0], wloads & 1, p.status, kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          cur_n = n_tile;
+          ++wloads;
+        }
+        const int buf = u % kAcc;
+        if (u >= kAcc) {
+          if (!mbar_wait_bounded(&acc_empty[buf], ((u / kAcc) - 1) & 1, p.status, kStatusTimeoutAccEmpty)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        const uint32_t d = tmem_base + buf * BN;
+        uint64_t bd = b_desc0;
+        for (int pr = 0; pr < p.slab_pairs; ++pr) {
+          if (!mbar_wait_bounded(&full[s], ph, p.status, kStatusTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = a_desc0 + s * stage_step;
+          if (p.taps == 9) {
+#pragma unroll
+            for (int tap = 0; tap < 9; ++tap) {
+              tc_mma<kF16>(d, ad + tap_off[tap], bd, idesc, (pr | tap) ? 1u : 0u);
+              bd += b_step;
+            }
+          } else {
+            tc_mma<kF16>(d, ad, bd, idesc, pr ? 1u : 0u);
+            bd += b_step;
+          }
+          tc_commit(&empty[s]);
+          if (++s == p.stages) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[buf]);
+        ++u;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;              // TMEM lane quadrant this warp may access
+    const int colq = (warp - 2) >> 2;       // which kCols-wide column block
+    const int row = quad * 32 + lane;
+    const int r_h = row / p.pitch;
+    const int r_w = row - r_h * p.pitch;
+    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    const int col0 = colq * kCols;
+    const int per_img = p.tiles_w * p.tiles_h;
+    int u = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      const int n_tile = t / p.m_tiles;
+      const int m_tile = t - n_tile * p.m_tiles;
+      const int img = m_tile / per_img;
+      const int r = m_tile - img * per_img;
+      const int oy = (r / p.tiles_w) * p.th + r_h, ox = (r % p.tiles_w) * p.tw + r_w;
+      const bool valid = r_h < p.th && r_w < p.tw && oy < p.oh && ox < p.ow;
+      const size_t pix = (static_cast<size_t>(img) * p.oh + (valid ? oy : 0)) * p.ow + (valid ? ox : 0);
+      __half* out_row = p.out + pix * p.out_ldc + p.out_coff;
+      const __half* res_row = kRes ? p.res + pix * p.res_ldc + p.res_coff : nullptr;
+      const int n0 = n_tile * BN;
+      const int buf = u % kAcc;
+      // the scale record is ready before the launch: read it while the accumulator fills
+      const float amax_in = kF16 ? 0.0f : __ldg(p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs));
+      if (!mbar_wait_bounded(&acc_full[buf], (u / kAcc) & 1, p.status, kStatusTimeoutAccFull)) break;
+      tc_fence_after();
+      const float in_scale = kF16 ? 1.0f : __fdiv_rn(amax_in, 127.0f);
+#pragma unroll 1
+      for (int c = 0; c < kChunks; ++c) {
+        uint32_t v[CW];
+        const uint32_t taddr = lane_addr + buf * BN + col0 + c * CW;
+        if constexpr (CW == 32) {
+          tmem_ld_32x32(taddr, v);
+        } else {
+          tmem_ld<16>(taddr, v);
+        }
+        tmem_ld_wait();
+        if (c == kChunks - 1) {
+          // every column of this accumulator has been read: hand it back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
+        const int oc_c = n0 + col0 + c * CW;
+        if (!kF16 && p.acc_dump != nullptr && valid) {
+#pragma unroll
+          for (int i = 0; i < CW; ++i)
+            if (oc_c + i < p.oc) p.acc_dump[pix * p.oc + oc_c + i] = static_cast<int32_t>(v[i]);
+        }
+#pragma unroll
+        for (int g = 0; g < CW / 16; ++g) {
+          const float m0 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g, in_scale, oc_c + 16 * g, valid, out_row, res_row);
+          const float m1 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g + 8, in_scale, oc_c + 16 * g + 8, valid, out_row, res_row);
+          const uint32_t mr = __reduce_max_sync(0xffffffffu, __float_as_uint(fmaxf(m0, m1)));
+          if (p.amax_out != nullptr && lane == 0 && oc_c + 16 * g < p.oc && mr != 0u)
+            atomicMax(&p.amax_out[static_cast<size_t>(img) * p.amax_stride + p.amax_goff + (oc_c + 16 * g) / 16], mr);
+        }
+      }
+      ++u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace aexrt

@@ -21,7 +21,7 @@ def _torch():
 
 
 def run_gpu_layer(x, weight, bias, k, s, mode, silu=True, residual=None, block_n=0, wq=None, w_scale=None,
-                  out_ldc=None, out_coff=0):
+                  out_ldc=None, out_coff=0, variant=0):
     """quantize (NCHW fp16 input) + conv through the C ABI; returns numpy results."""
     torch = _torch()
     from aexrt_b200 import ops
@@ -30,7 +30,8 @@ def run_gpu_layer(x, weight, bias, k, s, mode, silu=True, residual=None, block_n
     oc = weight.shape[0]
     if wq is None:
         wq, w_scale = ops.quantize_conv_weight_int8(weight)
-    plan = ops.ConvPlan.int8(n, ic, h, w, oc, k, s, wq, w_scale, bias, silu=silu, pg16=(mode == 1), block_n=block_n)
+    plan = ops.ConvPlan.int8(n, ic, h, w, oc, k, s, wq, w_scale, bias, silu=silu, pg16=(mode == 1),
+                             block_n=block_n | (variant << 16))
     xt = torch.from_numpy(x).cuda()
     amax = ops.act_amax(xt, ops.LAYOUT_NCHW_F16)
     q, rec = ops.act_quantize(xt, amax, mode, ops.LAYOUT_NCHW_F16, consumer_stride=s)
@@ -58,8 +59,8 @@ def run_gpu_layer(x, weight, bias, k, s, mode, silu=True, residual=None, block_n
                 amax_out=bits_to_f32(amax_out.cpu().numpy()), out_full=out.cpu().numpy())
 
 
-def check_against_oracle(x, weight, bias, k, s, mode, silu=True, residual=None, block_n=0):
-    g = run_gpu_layer(x, weight, bias, k, s, mode, silu=silu, residual=residual, block_n=block_n)
+def check_against_oracle(x, weight, bias, k, s, mode, silu=True, residual=None, block_n=0, variant=0):
+    g = run_gpu_layer(x, weight, bias, k, s, mode, silu=silu, residual=residual, block_n=block_n, variant=variant)
     o = ow.conv_w8a8(x, weight, bias, k, s, k // 2, mode=mode, silu=silu, residual=residual)
     assert np.array_equal(g["xq"], o["xq"]), "int8 codes differ"
     assert np.array_equal(g["acc"], o["acc"]), "int32 accumulators differ"
@@ -204,3 +205,54 @@ def test_fp16_conv_vs_torch(n, ic, h, w, oc, k, s, silu):
     got = torch.from_numpy(nhwc_to_nchw(out.cpu().numpy()).astype(np.float32))
     err = (got - ref).abs().max().item()
     assert err <= 1e-2 * max(1.0, ref.abs().max().item() / 8), err
+
+
+@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("n,ic,h,w,oc,k,s", [
+    (2, 64, 20, 20, 64, 3, 1),
+    (2, 48, 17, 13, 32, 3, 1),   # odd slab count (3 slabs): zero-padded slab pair
+    (2, 16, 10, 10, 16, 3, 1),   # one slab
+    (2, 32, 20, 18, 64, 3, 2),
+    (1, 32, 9, 11, 48, 3, 2),
+    (2, 96, 10, 10, 32, 1, 1),
+    (1, 64, 80, 80, 128, 3, 1),
+])
+def test_kernel_variants_bitexact(n, ic, h, w, oc, k, s, variant):
+    """Slot-streaming (1) and halo (2) kernels: identical int32 accumulators, both equal to the oracle."""
+    rng = np.random.default_rng(ic * 7 + oc + s)
+    x = seeded_act(rng, (n, ic, h, w))
+    weight = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    g, _, _ = check_against_oracle(x, weight, bias, k, s, 0, variant=variant)
+    assert g["plan"].info  # plan built with the requested variant
+
+
+@pytest.mark.parametrize("n,ic,h,w,oc,k,s,silu", [
+    (2, 64, 20, 20, 128, 3, 1, True),
+    (2, 16, 32, 32, 16, 3, 2, True),
+    (2, 64, 10, 10, 64, 1, 1, False),
+])
+def test_fp16_halo_vs_slot_streaming(n, ic, h, w, oc, k, s, silu):
+    """The fp16 conv variants agree with each other and with a torch fp32 reference."""
+    torch = _torch()
+    from aexrt_b200 import ops
+
+    rng = np.random.default_rng(ic + 3 * oc)
+    x = rng.uniform(0, 1, (n, ic, h, w)).astype(np.float32)
+    weight = rng.normal(0, 1 / np.sqrt(ic * k * k), (oc, ic, k, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    outs = []
+    for variant in (1, 2):
+        plan = ops.ConvPlan.fp16(n, ic, h, w, oc, k, s, weight, bias, silu=silu, block_n=variant << 16)
+        packed = ops.pack_f16(torch.from_numpy(x).cuda(), ops.LAYOUT_NCHW_F32, consumer_stride=s)
+        outs.append(plan.run(packed).float().cpu())
+        torch.cuda.synchronize()
+        assert plan.status() == 0
+    xr = torch.from_numpy(x.astype(np.float16).astype(np.float32))
+    wr = torch.from_numpy(weight.astype(np.float16).astype(np.float32))
+    ref = torch.nn.functional.conv2d(xr, wr, torch.from_numpy(bias), stride=s, padding=k // 2)
+    if silu:
+        ref = ref * torch.sigmoid(ref)
+    ref = ref.permute(0, 2, 3, 1)
+    for o in outs:
+        assert (o - ref).abs().max().item() <= 1e-2 * max(1.0, ref.abs().max().item() / 8)
