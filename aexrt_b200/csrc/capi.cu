@@ -320,7 +320,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
                        pitch)) {
       const int halo_h = p->k == 1 ? th : (p->stride == 1 ? th + 2 : th + 1);
       const int boxes = p->stride == 2 ? 4 : 1;
-      const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile);
+      const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, p->oc_alloc);
       const int budget = kMaxConvSmem - 1024;
       const int st = std::min(16, (budget - one.total_bytes) / one.stage_bytes + 1);
       if (st >= 2) {
@@ -334,7 +334,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
         p->taps = taps;
         p->w_tile_bytes = w_tile;
         p->stages = st;
-        p->smem = halo_smem_plan(p->halo_rows, boxes, st, w_tile).total_bytes;
+        p->smem = halo_smem_plan(p->halo_rows, boxes, st, w_tile, p->oc_alloc).total_bytes;
         p->tiles_w = (static_cast<int>(d.out_w) + tw - 1) / tw;
         p->tiles_h = (static_cast<int>(d.out_h) + th - 1) / th;
         p->m_tiles = static_cast<int>(d.batch) * p->tiles_h * p->tiles_w;
@@ -411,13 +411,17 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   bool ok = cuda_ok(cudaGetDevice(&p->device), "cudaGetDevice") &&
             cuda_ok(cudaMalloc(&p->d_w, packed.size()), "cudaMalloc(weights)") &&
             cuda_ok(cudaMemcpy(p->d_w, packed.data(), packed.size(), cudaMemcpyHostToDevice), "copy weights") &&
-            cuda_ok(cudaMalloc(reinterpret_cast<void**>(&p->d_bias), sizeof(float) * oc), "cudaMalloc(bias)") &&
+            cuda_ok(cudaMalloc(reinterpret_cast<void**>(&p->d_bias), sizeof(float) * p->oc_alloc), "cudaMalloc(bias)") &&
+            cuda_ok(cudaMemset(p->d_bias, 0, sizeof(float) * p->oc_alloc), "memset(bias)") &&
             cuda_ok(cudaMemcpy(p->d_bias, bias, sizeof(float) * oc, cudaMemcpyHostToDevice), "copy bias") &&
             cuda_ok(cudaMalloc(reinterpret_cast<void**>(&p->d_status), sizeof(uint32_t)), "cudaMalloc(status)") &&
             cuda_ok(cudaMemset(p->d_status, 0, sizeof(uint32_t)), "memset(status)");
-  if (ok && !f16) {
-    ok = cuda_ok(cudaMalloc(reinterpret_cast<void**>(&p->d_scale), sizeof(float) * oc), "cudaMalloc(scale)") &&
-         cuda_ok(cudaMemcpy(p->d_scale, scale, sizeof(float) * oc, cudaMemcpyHostToDevice), "copy scale");
+  if (ok) {
+    // per-output-channel weight scale, zero-padded to the n-tile multiple (1.0 for fp16 plans)
+    std::vector<float> sc(p->oc_alloc, 0.0f);
+    for (int o = 0; o < oc; ++o) sc[o] = f16 ? 1.0f : scale[o];
+    ok = cuda_ok(cudaMalloc(reinterpret_cast<void**>(&p->d_scale), sizeof(float) * p->oc_alloc), "cudaMalloc(scale)") &&
+         cuda_ok(cudaMemcpy(p->d_scale, sc.data(), sizeof(float) * p->oc_alloc, cudaMemcpyHostToDevice), "copy scale");
   }
   if (ok) {
     int sms = 0;
@@ -517,6 +521,7 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     h.stages = p->stages;
     h.w_packed = static_cast<const uint8_t*>(p->d_w);
     h.w_tile_bytes = p->w_tile_bytes;
+    h.oc_alloc = p->oc_alloc;
     h.scale_rec = scale_rec;
     h.w_scale = p->d_scale;
     h.bias = p->d_bias;

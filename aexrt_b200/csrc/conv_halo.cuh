@@ -38,6 +38,7 @@ struct ConvHaloParams {
   int stages;
   const uint8_t* w_packed;  // [n_tile][slab_pair][tap][2][BN][16]
   int w_tile_bytes;
+  int oc_alloc;             // n_tiles * BN: length of the (zero-padded) w_scale and bias vectors
   const float* scale_rec;
   const float* w_scale;
   const float* bias;
@@ -58,12 +59,13 @@ struct HaloSmemPlan {
   int stage_bytes;  // two slabs
   int a_bytes;      // all stages
   int b_offset;
+  int sb_offset;
   int bar_offset;
   int total_bytes;
 };
 
 __host__ __device__ inline HaloSmemPlan halo_smem_plan(int halo_rows, int boxes_per_slab, int stages,
-                                                       int w_tile_bytes) {
+                                                       int w_tile_bytes, int oc_alloc) {
   HaloSmemPlan s;
   const int box_bytes = ((halo_rows * kSlotBytes + 127) / 128) * 128;
   s.slab_bytes = box_bytes * boxes_per_slab;
@@ -71,9 +73,10 @@ __host__ __device__ inline HaloSmemPlan halo_smem_plan(int halo_rows, int boxes_
   // 4 KB of slack: a shifted 128-row window may run past the last halo row
   s.a_bytes = stages * s.stage_bytes + 4096;
   s.b_offset = ((s.a_bytes + 1023) / 1024) * 1024;
-  s.bar_offset = s.b_offset + ((w_tile_bytes + 127) / 128) * 128;
-  // barriers: full[stages], empty[stages], acc_full[4], acc_empty[4], w_full[2]; then the TMEM address
-  s.total_bytes = s.bar_offset + (2 * stages + 10) * 8 + 16;
+  s.sb_offset = s.b_offset + ((w_tile_bytes + 127) / 128) * 128;  // w_scale[oc_alloc], bias[oc_alloc]
+  s.bar_offset = s.sb_offset + ((8 * oc_alloc + 127) / 128) * 128;
+  // barriers: full[stages], empty[stages], acc_full[4], acc_empty[4], w_full[2], sb_full; then the TMEM address
+  s.total_bytes = s.bar_offset + (2 * stages + 11) * 8 + 16;
   return s;
 }
 
@@ -90,34 +93,27 @@ constexpr int halo_threads() {
 // Epilogue of 8 consecutive output channels of one pixel (full-width fast path
 // when all 8 channels exist and the row is 16-byte aligned): scale, bias,
 // SiLU, residual, fp16 store.  Returns the max |fp16 output| of the 8 values.
+// `sscale` / `sbias` point at this 8-column group's weight scale and bias in the
+// CTA's resident weight tile (shared memory; zero past the last channel).
 template <bool kF16, bool kSilu, bool kRes>
 __device__ __forceinline__ float halo_epilogue8(const ConvHaloParams& p, const uint32_t* v, float in_scale, int oc,
-                                                bool valid, __half* out_row, const __half* res_row) {
+                                                const float* sscale, const float* sbias, bool valid, __half* out_row,
+                                                const __half* res_row) {
   const int n_valid = p.oc - oc;
   float y[8];
-  if (n_valid >= 8) {
-    const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.bias + oc));
-    const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.bias + oc) + 1);
+  {
+    const float4 b0 = *reinterpret_cast<const float4*>(sbias);
+    const float4 b1 = *reinterpret_cast<const float4*>(sbias + 4);
     const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
     if constexpr (kF16) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[i]) + bb[i];
     } else {
-      const float4 s0 = __ldg(reinterpret_cast<const float4*>(p.w_scale + oc));
-      const float4 s1 = __ldg(reinterpret_cast<const float4*>(p.w_scale + oc) + 1);
+      const float4 s0 = *reinterpret_cast<const float4*>(sscale);
+      const float4 s1 = *reinterpret_cast<const float4*>(sscale + 4);
       const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
       for (int i = 0; i < 8; ++i) y[i] = fmaf(static_cast<float>(static_cast<int32_t>(v[i])) * in_scale, ss[i], bb[i]);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (i < n_valid) {
-        const float a = kF16 ? __uint_as_float(v[i]) : static_cast<float>(static_cast<int32_t>(v[i])) * in_scale;
-        y[i] = kF16 ? a + __ldg(p.bias + oc + i) : fmaf(a, __ldg(p.w_scale + oc + i), __ldg(p.bias + oc + i));
-      } else {
-        y[i] = 0.0f;
-      }
     }
   }
   if constexpr (kSilu) {
@@ -180,13 +176,14 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const HaloSmemPlan sp = halo_smem_plan(p.halo_rows, p.boxes_per_slab, p.stages, p.w_tile_bytes);
+  const HaloSmemPlan sp = halo_smem_plan(p.halo_rows, p.boxes_per_slab, p.stages, p.w_tile_bytes, p.oc_alloc);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.bar_offset);
   uint64_t* empty = full + p.stages;
   uint64_t* acc_full = full + 2 * p.stages;  // [kAcc]
   uint64_t* acc_empty = acc_full + 4;        // [kAcc]
   uint64_t* w_full = acc_empty + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(w_full + 2);
+  uint64_t* sb_full = w_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sb_full + 1);
   const int box_bytes = sp.slab_bytes / p.boxes_per_slab;
 
   if (threadIdx.x == 0) {
@@ -200,6 +197,7 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
     }
     mbar_init(&w_full[0], 1);
     mbar_init(&w_full[1], 1);
+    mbar_init(sb_full, 1);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) tma_prefetch_desc(&act_map);
@@ -215,6 +213,11 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
   // tiles are ordered n-tile major, so a persistent CTA keeps one weight tile for long runs
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(sb_full, static_cast<uint32_t>(8 * p.oc_alloc));
+      bulk_load(smem + sp.sb_offset, p.w_scale, static_cast<uint32_t>(4 * p.oc_alloc), sb_full);
+      bulk_load(smem + sp.sb_offset + 4 * p.oc_alloc, p.bias, static_cast<uint32_t>(4 * p.oc_alloc), sb_full);
+    }
     int s = 0, it = 0, cur_n = -1, wloads = 0;
     uint32_t ph = 0;
     bool ok = true;
@@ -357,6 +360,9 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     const int col0 = colq * kCols;
     const int per_img = p.tiles_w * p.tiles_h;
+    const float* s_scale = reinterpret_cast<const float*>(smem + sp.sb_offset);  // [oc_alloc]
+    const float* s_bias = s_scale + p.oc_alloc;
+    mbar_wait_bounded(sb_full, 0, p.status, kStatusTimeoutFull);
     int u = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
       const int n_tile = t / p.m_tiles;
@@ -399,8 +405,11 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
         }
 #pragma unroll
         for (int g = 0; g < CW / 16; ++g) {
-          const float m0 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g, in_scale, oc_c + 16 * g, valid, out_row, res_row);
-          const float m1 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g + 8, in_scale, oc_c + 16 * g + 8, valid, out_row, res_row);
+          const int lc = oc_c + 16 * g;  // output channel (the vectors are zero-padded to oc_alloc)
+          const float m0 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g, in_scale, oc_c + 16 * g, s_scale + lc,
+                                                             s_bias + lc, valid, out_row, res_row);
+          const float m1 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g + 8, in_scale, oc_c + 16 * g + 8,
+                                                             s_scale + lc + 8, s_bias + lc + 8, valid, out_row, res_row);
           const uint32_t mr = __reduce_max_sync(0xffffffffu, __float_as_uint(fmaxf(m0, m1)));
           if (p.amax_out != nullptr && lane == 0 && oc_c + 16 * g < p.oc && mr != 0u)
             atomicMax(&p.amax_out[static_cast<size_t>(img) * p.amax_stride + p.amax_goff + (oc_c + 16 * g) / 16], mr);

@@ -47,14 +47,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps
+// (up to the hint, in ns) until the phase completes instead of re-polling, so
+// waiting warps leave the issue slots to the working ones.
+constexpr uint32_t kSuspendHintNs = 100000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -66,7 +71,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   const long long t0 = clock64();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 16; ++i)
+    for (int i = 0; i < 4; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (clock64() - t0 > kWaitLimitCycles) {
       atomicOr(status, flag);
