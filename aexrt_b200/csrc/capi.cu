@@ -586,6 +586,36 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
   return cuda_ok(cudaGetLastError(), "conv launch") ? 1 : 0;
 }
 
+// Picks the quantize kernel: NHWC sources go through the transposing kernel,
+// stride-1 NCHW fp16 with H*W % 8 == 0 through the register-transpose kernel,
+// anything else through the per-slab generic kernel.
+void launch_quantize(const QuantParams& q, cudaStream_t st) {
+  bool nhwc = true;
+  for (int i = 0; i < q.nsrc; ++i) nhwc = nhwc && q.src[i].layout == 0;
+  if (nhwc && q.slabs <= kMaxSlabs) {
+    const dim3 grid((q.hp * q.wp + kTransThreads - 1) / kTransThreads, q.n);
+    transpose_quant_kernel<true><<<grid, kTransThreads, 0, st>>>(q);
+  } else if (q.nsrc == 1 && q.src[0].layout == 1 && !q.split && (q.h * q.w) % 8 == 0 && q.slabs <= kMaxSlabs) {
+    const dim3 grid((q.h * q.w / 8 + 255) / 256, q.slabs, q.n);
+    quantize_nchw_kernel<<<grid, 256, 0, st>>>(q);
+  } else {
+    const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, q.n);
+    quantize_i8_kernel<<<grid, 256, 0, st>>>(q);
+  }
+}
+
+void launch_pack(const QuantParams& q, cudaStream_t st) {
+  bool nhwc = true;
+  for (int i = 0; i < q.nsrc; ++i) nhwc = nhwc && q.src[i].layout == 0;
+  if (nhwc && q.slabs <= kMaxSlabs) {
+    const dim3 grid((q.hp * q.wp + kTransThreads - 1) / kTransThreads, q.n);
+    transpose_quant_kernel<false><<<grid, kTransThreads, 0, st>>>(q);
+  } else {
+    const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, q.n);
+    pack_f16_kernel<<<grid, 256, 0, st>>>(q);
+  }
+}
+
 void quant_params_common(QuantParams& q, const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w,
                          uint32_t layout, uint32_t ldc, uint32_t coff, const uint32_t* amax_groups,
                          uint32_t groups_total, uint32_t group_offset) {
@@ -672,7 +702,7 @@ int aexrt_b200_act_amax_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, u
   const int hw = static_cast<int>(h * w);
   if (reinterpret_cast<uintptr_t>(x) % 16) return fail("x must be 16-byte aligned");
   if (layout == AEXRT_B200_LAYOUT_NCHW_F16) {
-    const int chunk = 8192;
+    const int chunk = 32768;  // halves per block: 64 KB, 16 loads of 16 bytes per thread
     const int blocks = static_cast<int>((16ull * hw + chunk - 1) / chunk);
     amax_nchw_f16_kernel<<<dim3(blocks, groups, n), 256, 0, st>>>(static_cast<const __half*>(x), static_cast<int>(c),
                                                                    hw, static_cast<int>(groups_total), chunk,
@@ -724,8 +754,7 @@ int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t 
   q.split = consumer_stride == 2 ? 1 : 0;
   q.out = q_out;
   q.rec = scale_rec;
-  const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, n);
-  quantize_i8_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(q);
+  launch_quantize(q, static_cast<cudaStream_t>(stream));
   return cuda_ok(cudaGetLastError(), "quantize launch") ? 1 : 0;
 }
 
@@ -744,8 +773,7 @@ int aexrt_b200_pack_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint3
   q.hp = static_cast<int>(h + (consumer_stride == 2 ? (h & 1) : 0));
   q.wp = static_cast<int>(w + (consumer_stride == 2 ? (w & 1) : 0));
   q.out = out;
-  const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, n);
-  pack_f16_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(q);
+  launch_pack(q, static_cast<cudaStream_t>(stream));
   return cuda_ok(cudaGetLastError(), "pack launch") ? 1 : 0;
 }
 
@@ -897,8 +925,7 @@ int aexrt_b200_act_quantize_concat(const AexrtB200ActSource* srcs, uint32_t nsrc
   q.split = consumer_stride == 2 ? 1 : 0;
   q.out = q_out;
   q.rec = scale_rec;
-  const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, n);
-  quantize_i8_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(q);
+  launch_quantize(q, static_cast<cudaStream_t>(stream));
   return cuda_ok(cudaGetLastError(), "quantize launch") ? 1 : 0;
 }
 
@@ -913,8 +940,7 @@ int aexrt_b200_pack_f16_concat(const AexrtB200ActSource* srcs, uint32_t nsrc, ui
   q.wp = static_cast<int>(w + (consumer_stride == 2 ? (w & 1) : 0));
   q.split = consumer_stride == 2 ? 1 : 0;
   q.out = out;
-  const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, n);
-  pack_f16_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(q);
+  launch_pack(q, static_cast<cudaStream_t>(stream));
   return cuda_ok(cudaGetLastError(), "pack launch") ? 1 : 0;
 }
 

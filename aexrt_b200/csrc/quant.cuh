@@ -36,15 +36,28 @@ __global__ void amax_nchw_f16_kernel(const __half* __restrict__ x, int c, int hw
     const bool vec = ((base & 7) == 0) && ((begin & 7) == 0);
     if (vec) {
       const size_t vend = begin + ((end - begin) / 8) * 8;
-      for (size_t i = begin + static_cast<size_t>(threadIdx.x) * 8; i < vend; i += static_cast<size_t>(blockDim.x) * 8) {
+      const size_t step = static_cast<size_t>(blockDim.x) * 8;
+      size_t i = begin + static_cast<size_t>(threadIdx.x) * 8;
+      // four independent 16-byte loads in flight per thread, then the max
+      __half2 hm = __float2half2_rn(0.0f);
+      for (; i + 3 * step < vend; i += 4 * step) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const uint4*>(s + i + u * step);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const __half2* h2 = reinterpret_cast<const __half2*>(&v[u]);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) hm = __hmax2(hm, __habs2(h2[k]));
+        }
+      }
+      for (; i < vend; i += step) {
         const uint4 v = *reinterpret_cast<const uint4*>(s + i);
         const __half2* h2 = reinterpret_cast<const __half2*>(&v);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 f = __half22float2(h2[k]);
-          m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
-        }
+        for (int k = 0; k < 4; ++k) hm = __hmax2(hm, __habs2(h2[k]));
       }
+      m = fmaxf(__low2float(hm), __high2float(hm));
       for (size_t t = vend + threadIdx.x; t < end; t += blockDim.x) m = fmaxf(m, fabsf(__half2float(s[t])));
     } else {
       for (size_t t = begin + threadIdx.x; t < end; t += blockDim.x) m = fmaxf(m, fabsf(__half2float(s[t])));
@@ -241,6 +254,152 @@ __global__ void pack_f16_kernel(const QuantParams p) {
   const int dpix = p.split ? h * p.wp + (w & 1) * (p.wp >> 1) + (w >> 1) : pix;
   __half* out = static_cast<__half*>(p.out) + ((static_cast<size_t>(n) * p.slabs + slab) * p.hp * p.wp + dpix) * 8;
   *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(hv);
+}
+
+// ----------------------------------------------------------------------------
+// transposing quantize / repack for NHWC sources (the model path)
+// ----------------------------------------------------------------------------
+
+constexpr int kTransThreads = 256;  // output pixels per block of the transposing kernel
+constexpr int kMaxSlabs = 64;       // up to 1024 int8 / 512 fp16 channels
+
+// Activation scale of every output slab of image n (pg16: the slab's own group
+// amax; per tensor: max over all groups of all sources), as the quantizer
+// multiplier fl32(127/amax) (0 when amax <= 0).  Computed by the whole block in
+// parallel; block 0 of each image also writes the scale record.
+__device__ __forceinline__ void slab_multipliers(const QuantParams& p, int n, float* s_mult, float* s_red) {
+  const int t = threadIdx.x;
+  float ag = 0.0f;
+  if (t < p.slabs) {
+    int base = 0, k = 0;
+    while (k < p.nsrc - 1 && t * 16 >= base + p.src[k].ch) {
+      base += p.src[k].ch;
+      ++k;
+    }
+    const QuantSrc& s = p.src[k];
+    ag = __uint_as_float(s.amax_g[static_cast<size_t>(n) * s.amax_stride + s.amax_goff + (t * 16 - base) / 16]);
+  }
+  // per-tensor amax: block max over the slab amaxes (every group of every source is one slab)
+  float m = ag;
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((t & 31) == 0 && t < kMaxSlabs) s_red[t >> 5] = m;
+  __syncthreads();
+  const float at = fmaxf(s_red[0], s_red[1]);
+  if (t < p.slabs) {
+    const float a = p.mode == 1 ? ag : at;
+    s_mult[t] = a > 0.0f ? __fdiv_rn(127.0f, a) : 0.0f;
+    if (blockIdx.x == 0 && p.rec != nullptr) {
+      float* r = p.rec + static_cast<size_t>(n) * (1 + p.slabs);
+      r[1 + t] = ag;
+      if (t == 0) r[0] = at;
+    }
+  }
+  __syncthreads();
+}
+
+// NHWC fp16 sources (optionally concatenated / upsampled) -> slab layout, one
+// thread per output pixel: the thread walks the pixel's channels with 16-byte
+// loads (8 channels each; the L1 keeps each pixel's lines for its later loads)
+// and writes one 16-byte chunk per slab, so for every slab the 32 lanes of a
+// warp store 512 contiguous bytes.  kI8: int8 codes q = round_half_even(x *
+// 127/amax) with no clamp, 16 channels per slab; else fp16 copied, 8 per slab.
+template <bool kI8>
+__global__ void __launch_bounds__(kTransThreads)
+    transpose_quant_kernel(const QuantParams p) {
+  __shared__ float s_mult[kMaxSlabs];
+  __shared__ float s_red[2];
+  const int n = blockIdx.y;
+  if (kI8) slab_multipliers(p, n, s_mult, s_red);
+  const int pix = blockIdx.x * kTransThreads + threadIdx.x;
+  if (pix >= p.hp * p.wp) return;
+  const int h = pix / p.wp, w = pix - (pix / p.wp) * p.wp;
+  const bool inside = h < p.h && w < p.w;
+  const size_t plane = static_cast<size_t>(p.hp) * p.wp;
+  const int dpix = p.split ? h * p.wp + (w & 1) * (p.wp >> 1) + (w >> 1) : pix;
+  uint8_t* out = static_cast<uint8_t*>(p.out) + (static_cast<size_t>(n) * p.slabs * plane + dpix) * 16;
+  int slab = 0;
+  for (int k = 0; k < p.nsrc; ++k) {
+    const QuantSrc& s = p.src[k];
+    const __half* src = inside ? static_cast<const __half*>(s.ptr) +
+                                     (static_cast<size_t>(n) * s.src_h * s.src_w + static_cast<size_t>(h / s.up) * s.src_w +
+                                      w / s.up) * s.ldc + s.coff
+                               : nullptr;
+    for (int c0 = 0; c0 < s.ch; c0 += (kI8 ? 16 : 8), ++slab) {
+      uint4 o = make_uint4(0, 0, 0, 0);
+      if (inside) {
+        if (kI8) {
+          const float mult = s_mult[slab];
+          uint32_t q[4] = {0u, 0u, 0u, 0u};
+          if (mult != 0.0f) {
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              const int cc = c0 + 8 * half;
+              __align__(16) __half hv[8];
+              if (cc + 8 <= s.ch) {
+                *reinterpret_cast<uint4*>(hv) = *reinterpret_cast<const uint4*>(src + cc);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) hv[i] = cc + i < s.ch ? src[cc + i] : __float2half_rn(0.0f);
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const uint32_t b = static_cast<uint32_t>(__float2int_rn(__fmul_rn(__half2float(hv[i]), mult))) & 0xFFu;
+                q[2 * half + (i >> 2)] |= b << (8 * (i & 3));
+              }
+            }
+          }
+          o = make_uint4(q[0], q[1], q[2], q[3]);
+        } else {
+          if (c0 + 8 <= s.ch) {
+            o = *reinterpret_cast<const uint4*>(src + c0);
+          } else {
+            __align__(16) __half hv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) hv[i] = c0 + i < s.ch ? src[c0 + i] : __float2half_rn(0.0f);
+            o = *reinterpret_cast<const uint4*>(hv);
+          }
+        }
+      }
+      *reinterpret_cast<uint4*>(out + slab * plane * 16) = o;
+    }
+  }
+}
+
+// NCHW fp16 single source -> int8 slab16, stride-1 layout, H*W % 8 == 0: each
+// thread quantizes 8 consecutive pixels of the 16 channels of one slab (16
+// coalesced 16-byte loads) and transposes in registers into eight 16-byte
+// pixel rows (128 contiguous bytes per thread).
+__global__ void __launch_bounds__(256) quantize_nchw_kernel(const QuantParams p) {
+  __shared__ float s_mult[kMaxSlabs];
+  __shared__ float s_red[2];
+  const int slab = blockIdx.y;
+  const int n = blockIdx.z;
+  slab_multipliers(p, n, s_mult, s_red);
+  const int hw = p.h * p.w;
+  const int px0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (px0 >= hw) return;
+  const QuantSrc& s = p.src[0];
+  const float mult = s_mult[slab];
+  uint32_t q[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) q[j][k] = 0u;
+  const __half* base = static_cast<const __half*>(s.ptr) + (static_cast<size_t>(n) * s.ch + slab * 16) * hw + px0;
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    if (slab * 16 + c >= s.ch) break;
+    const uint4 v = *reinterpret_cast<const uint4*>(base + static_cast<size_t>(c) * hw);
+    const __half* hv = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t b = mult != 0.0f ? static_cast<uint32_t>(__float2int_rn(__fmul_rn(__half2float(hv[j]), mult))) & 0xFFu : 0u;
+      q[j][c >> 2] |= b << (8 * (c & 3));
+    }
+  }
+  uint4* out = reinterpret_cast<uint4*>(static_cast<int8_t*>(p.out) + ((static_cast<size_t>(n) * p.slabs + slab) * hw + px0) * 16);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) out[j] = make_uint4(q[j][0], q[j][1], q[j][2], q[j][3]);
 }
 
 }  // namespace aexrt
