@@ -40,13 +40,93 @@ L2_BYTES = 126 * 1024 * 1024
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=256, help="images per GPU per step")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=24, help="images in the CPU baseline sample")
+    ap.add_argument("--workload", default="yolov8n-320",
+                    help="yolov8n-320 (the metric), or a BASELINE layer: " + ", ".join(LAYERS) + ", or amax-quant")
+    ap.add_argument("--mode", type=int, default=0, help="layer workloads: 0 per-tensor, 1 pg16 scales")
     return ap.parse_args()
+
+
+# the C1 block and the layer sweep (name: ic, h, w, oc, k, s)
+LAYERS = {
+    "c1": (64, 80, 80, 128, 3, 1),
+    "sweep-1x1": (128, 40, 40, 128, 1, 1),
+    "sweep-3x3s1": (64, 80, 80, 64, 3, 1),
+    "sweep-3x3s2": (32, 160, 160, 64, 3, 2),
+    "sweep-3x3s2-small": (128, 20, 20, 256, 3, 2),
+}
+
+
+def run_layer(args):
+    """One BASELINE layer (or the standalone amax + quantize tensor) on one GPU: quantize + conv per step."""
+    import torch
+
+    from aexrt_b200 import ops
+
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(0)
+    n = args.batch
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    hbm, bf16, src = measured_peaks()
+    if args.workload == "amax-quant":
+        x = torch.from_numpy((lambda z: z / (1 + np.exp(-z)))(rng.standard_normal((n, 64, 80, 80)).astype(np.float32))
+                             .astype(np.float16)).cuda()
+        amax = ops.act_amax(x, ops.LAYOUT_NCHW_F16)
+        q, rec = ops.act_quantize(x, amax, args.mode, ops.LAYOUT_NCHW_F16)
+
+        def step():
+            ops.act_amax(x, ops.LAYOUT_NCHW_F16, out=amax)
+            ops.act_quantize(x, amax, args.mode, ops.LAYOUT_NCHW_F16, q_out=q, rec_out=rec)
+
+        byts, ops_ = 5.0 * x.numel(), 0.0
+        desc = f"standalone amax + quantize of {n}x64x80x80 fp16 NCHW (BASELINE config 2)"
+    else:
+        ic, h, w, oc, k, s = LAYERS[args.workload]
+        wt = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
+        b = rng.normal(0, 0.1, oc).astype(np.float32)
+        codes, scale = ops.quantize_conv_weight_int8(wt)
+        plan = ops.ConvPlan.int8(n, ic, h, w, oc, k, s, codes, scale, b, pg16=bool(args.mode))
+        x = torch.from_numpy((lambda z: z / (1 + np.exp(-z)))(rng.standard_normal((n, ic, h, w)).astype(np.float32))
+                             .astype(np.float16)).cuda()
+        amax = ops.act_amax(x, ops.LAYOUT_NCHW_F16)
+        q, rec = ops.act_quantize(x, amax, args.mode, ops.LAYOUT_NCHW_F16, consumer_stride=s)
+        out = torch.empty(plan.out_shape, dtype=torch.float16, device="cuda")
+
+        def step():
+            plan.run(q, rec, out=out)
+
+        d = plan.desc
+        ops_ = 2.0 * n * d.out_h * d.out_w * oc * ic * k * k
+        byts = n * ic * h * w + 2.0 * n * oc * d.out_h * d.out_w + oc * ic * k * k
+        desc = f"conv {ic}->{oc} k{k} s{s} @{h}x{w}, batch {n}, {'pg16' if args.mode else 'per-tensor'} (BASELINE configs 1-2)"
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(args.steps):
+        flush.zero_()  # inputs of some layers fit in L2: flush it between timed iterations
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) / 1e3)
+    t = statistics.median(ts)
+    int8_peak = 2.0 * bf16
+    line = {"metric": f"{args.workload} kernel time", "value": t * 1e3, "unit": "ms", "higher_is_better": False,
+            "steps": args.steps, "warmup": args.warmup, "config": {"workload": desc, "l2": "flushed between steps"},
+            "achieved_gbs": byts / t / 1e9, "hbm_frac": byts / t / 1e9 / hbm}
+    if ops_:
+        line.update({"achieved_tops": ops_ / t / 1e12, "tensor_frac": ops_ / t / 1e12 / int8_peak,
+                     "plan": vars(plan.info)})
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 def dist_env():
@@ -79,7 +159,7 @@ def cpu_reference(program, n_images: int, seed: int = 1):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while running."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -98,7 +178,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
         return self
@@ -269,10 +349,10 @@ def run_ours(args):
         eng.graph.replay()
         host_out.copy_(eng.output, non_blocking=True)
 
-    for _ in range(max(3, args.warmup)):
-        step_device()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        for _ in range(max(3, args.warmup) + 50):  # warm-up (also lets the clock sampler start)
+            step_device()
+        torch.cuda.synchronize()
         t_dev = timed(step_device, args.steps)
     clocks = clk.summary()
     e2e = None
@@ -307,12 +387,15 @@ def run_ours(args):
                        "l2": f"inputs larger than L2 ({B * 3 * 320 * 320 * 4 / 1e6:.0f} MB of fp32 images per step)"},
             "e2e": e2e,
             "gpu_launches": eng.launches_per_run * args.steps,
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
-                         "frac": achieved / int8_peak, "traffic": None,
-                         "kernel": "conv_tc_kernel (all W8A8 conv launches of one step)",
-                         "peak_source": f"2 x {src} bf16 dense ({bf16} TFLOP/s) from MEASURED_PEAKS.json",
-                         "conv_ms_per_step": rf["time_s"] * 1e3, "conv_launches": rf["launches"],
-                         "conv_hbm_gbs_equiv": rf["bytes"] / rf["time_s"] / 1e9, "hbm_peak_gbs": hbm},
+            "roofline": {"bound": "hbm", "achieved": rf["bytes"] / rf["time_s"] / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": rf["bytes"] / rf["time_s"] / 1e9 / hbm, "traffic": None,
+                         "kernel": "conv_halo_kernel / conv_tc_kernel: all W8A8 conv launches of one step "
+                                   "(algorithmic bytes: int8 input + fp16 output + weights per launch)",
+                         "peak_source": f"{src} hbm_gbs from MEASURED_PEAKS.json",
+                         "tensor_achieved_tops": achieved, "tensor_peak_tops": int8_peak,
+                         "tensor_frac": achieved / int8_peak,
+                         "tensor_peak_source": f"2 x {src} bf16 dense ({bf16} TFLOP/s), MEASURED_PEAKS.json",
+                         "conv_ms_per_step": rf["time_s"] * 1e3, "conv_launches": rf["launches"]},
             "cpu_baseline": cpu,
             "clocks": clocks,
             "status": status,
@@ -327,6 +410,8 @@ def run_ours(args):
 
 def main():
     args = parse_args()
+    if args.workload != "yolov8n-320":
+        return run_layer(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
