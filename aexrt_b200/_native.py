@@ -78,6 +78,7 @@ _SIGNATURES = {
     "aexrt_b200_yolo_decode": (c_int, [POINTER(AexrtB200DecodeLevel), c_uint32, c_uint32, c_uint32, c_uint32, c_void_p,
                                        c_void_p]),
     "aexrt_b200_zero": (c_int, [c_void_p, c_uint64, c_void_p]),
+    "aexrt_b200_act_quantize_f16_noalloc": (c_int, [c_void_p] + [c_uint32] * 9 + [c_void_p, c_void_p, c_void_p]),
 }
 
 _LIB = None

@@ -1000,3 +1000,59 @@ int aexrt_b200_zero(void* ptr, uint64_t bytes, void* stream) {
 }
 
 }  // extern "C"
+
+// ----------------------------------------------------------------------------
+// Allocation-free amax + quantize
+//
+// Some callers cannot call cudaMalloc: a host that runs this step while it is
+// capturing a CUDA graph (allocation is not capturable), a real-time loop that
+// forbids allocation after start-up, or a plugin host whose memory is owned by
+// its own allocator.  For them the per-(image, group) amax slots, which are
+// scratch between the amax and the quantize kernels, live in a fixed device
+// array owned by the library instead of in caller memory.
+// ----------------------------------------------------------------------------
+
+namespace {
+
+constexpr uint32_t kNoAllocAmaxSlots = 65536;  // 256 KB: images x ceil(channels / 16) slots
+static __device__ __align__(256) uint32_t g_noalloc_amax[kNoAllocAmaxSlots];
+
+std::mutex g_noalloc_mutex;
+uint32_t* g_noalloc_ptr[128] = {};  // device address of g_noalloc_amax, per device
+
+// The host-side name g_noalloc_amax is not a device address: resolve it once per
+// device, with that device current.
+uint32_t* noalloc_slots() {
+  int dev = 0;
+  if (!cuda_ok(cudaGetDevice(&dev), "cudaGetDevice")) return nullptr;
+  if (dev < 0 || dev >= 128) {
+    fail("device index %d out of range", dev);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    if (!cuda_ok(cudaGetSymbolAddress(&ptr, g_noalloc_amax), "cudaGetSymbolAddress")) return nullptr;
+    g_noalloc_ptr[dev] = static_cast<uint32_t*>(ptr);
+  }
+  return g_noalloc_ptr[dev];
+}
+
+}  // namespace
+
+extern "C" int aexrt_b200_act_quantize_f16_noalloc(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w,
+                                                   uint32_t layout, uint32_t ldc, uint32_t coff, uint32_t mode,
+                                                   uint32_t consumer_stride, void* q_out, float* scale_rec,
+                                                   void* stream) {
+  const uint64_t slots = static_cast<uint64_t>(n) * ((c + 15) / 16);
+  if (slots > kNoAllocAmaxSlots)
+    return fail("act_quantize_noalloc: %llu amax slots (images x ceil(channels/16)) exceed the fixed %u",
+                static_cast<unsigned long long>(slots), kNoAllocAmaxSlots);
+  uint32_t* amax = noalloc_slots();
+  if (!amax) return 0;
+  const uint32_t groups = (c + 15) / 16;
+  // zero_first clears this call's slots: the array keeps the previous call's maxima
+  if (!aexrt_b200_act_amax_f16(x, n, c, h, w, layout, ldc, coff, amax, groups, 0, 1, stream)) return 0;
+  return aexrt_b200_act_quantize_f16(x, n, c, h, w, layout, ldc, coff, amax, groups, 0, mode, consumer_stride, q_out,
+                                     scale_rec, stream);
+}

@@ -244,6 +244,27 @@ int aexrt_b200_yolo_decode(const AexrtB200DecodeLevel* levels, uint32_t nlevels,
 /* cudaMemsetAsync(ptr, 0, bytes, stream): clears amax slots inside a captured graph. */
 int aexrt_b200_zero(void* ptr, uint64_t bytes, void* stream);
 
+/* ---------------------------------------------------------------- allocation-free variant
+ * amax + quantize in one call for callers that cannot call cudaMalloc (a host
+ * capturing a CUDA graph, a real-time loop that allocates nothing after
+ * start-up, a plugin whose memory belongs to its host's allocator): the
+ * per-(image, 16-channel group) amax scratch lives in a fixed device array
+ * inside the library instead of caller memory.  No counterpart in the
+ * reference (there the amax buffer is allocated by the recorder).
+ *   - The caller still passes the input, q_out and scale_rec, as for
+ *     aexrt_b200_act_amax_f16 + aexrt_b200_act_quantize_f16, whose results it equals.
+ *   - Limit: n * ceil(c / 16) <= 65536 slots (256 KB, held on every GPU that
+ *     loads the library until exit); larger calls fail with a message.
+ *   - The first call on a device resolves the array's device address
+ *     (cudaGetSymbolAddress) with that device current: make it before any
+ *     stream capture.  Each call clears its slots first.
+ *   - Every call shares the one array, so calls that overlap on the GPU (other
+ *     streams, other host threads) race; serialize them.
+ *   - Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
+int aexrt_b200_act_quantize_f16_noalloc(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t layout,
+                                        uint32_t ldc, uint32_t coff, uint32_t mode, uint32_t consumer_stride,
+                                        void* q_out, float* scale_rec, void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif
