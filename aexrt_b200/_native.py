@@ -29,8 +29,8 @@ class AexrtConv2DDesc(ctypes.Structure):
 class AexrtB200ConvPlanInfo(ctypes.Structure):
     _fields_ = [(name, c_uint32) for name in (
         "struct_size", "kernel_id", "flags", "kind", "is_f16", "tile_w", "tile_h", "block_n", "k_slots", "stages",
-        "smem_bytes", "grid_m", "grid_n", "in_hp", "in_wp",
-    )] + [("reserved", c_uint32 * 4)]
+        "smem_bytes", "grid_m", "grid_n", "in_hp", "in_wp", "grid", "variant", "pitch", "image_input",
+    )]
 
 
 class AexrtB200ActSource(ctypes.Structure):
@@ -66,6 +66,8 @@ _SIGNATURES = {
                                      c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
     "aexrt_b200_conv_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_uint32, c_uint32, c_void_p,
                                     c_uint32, c_uint32, c_void_p]),
+    "aexrt_b200_conv_f16_image": (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_uint32, c_uint32,
+                                          c_void_p]),
     "aexrt_b200_conv_status": (c_int, [c_void_p, POINTER(c_uint32)]),
     "aexrt_b200_packed_f16_bytes": (c_uint64, [c_uint32] * 5),
     "aexrt_b200_pack_f16": (c_int, [c_void_p] + [c_uint32] * 8 + [c_void_p, c_void_p]),

@@ -19,7 +19,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libaexrt_b200.so")
 SOURCES = ["capi.cu"]
-HEADERS = ["conv_halo.cuh", "conv_tc.cuh", "ptx.cuh", "quant.cuh", "yolo_ops.cuh"]
+HEADERS = ["conv_halo.cuh", "conv_tc.cuh", "ptx.cuh", "quant.cuh", "stem.cuh", "yolo_ops.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

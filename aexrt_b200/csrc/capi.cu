@@ -21,6 +21,7 @@
 #include "../../include/aexrt_b200.h"
 #include "conv_halo.cuh"
 #include "quant.cuh"
+#include "stem.cuh"
 #include "yolo_ops.cuh"
 
 using namespace aexrt;
@@ -118,12 +119,16 @@ struct AexrtB200ConvPlan {
   int total_tiles = 0;
   // halo variant (conv_halo.cuh): whole weight tile resident, one halo per slab and tile
   bool halo = false;
+  int order = 0;  // halo tile order (see conv_halo.cuh): 0 auto, 1 strided, 2 contiguous runs
   int pitch = 0, halo_rows = 0, boxes_per_slab = 1, slab_pairs = 0, taps = 1, w_tile_bytes = 0, m_tiles = 0;
   void* d_w = nullptr;   // [n_tile][q_total][bn][16 bytes]
   float* d_scale = nullptr;
   float* d_bias = nullptr;
   uint32_t* d_status = nullptr;
   int device = 0;
+  // image stem (fp16, 3 input channels, 3x3): direct kernel reading fp32 NCHW images
+  bool image_input = false;
+  StemWeights stem{};
 };
 
 namespace {
@@ -283,6 +288,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   p->tiles_w = (static_cast<int>(d.out_w) + p->tw - 1) / p->tw;
   p->tiles_h = (static_cast<int>(d.out_h) + p->th - 1) / p->th;
   const uint32_t variant = (block_n >> 16) & 0xF;  // 0 auto, 1 slot streaming, 2 halo
+  const uint32_t order = (block_n >> 20) & 0xF;    // halo tile order: 0 auto, 1 strided, 2 contiguous
   block_n &= 0xFFFF;
   p->bn = choose_bn(oc, p->pg, block_n);
   if (!kernel_for(f16, p->pg, p->bn)) {
@@ -325,6 +331,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
       const int st = std::min(16, (budget - one.total_bytes) / one.stage_bytes + 1);
       if (st >= 2) {
         p->halo = true;
+        p->order = static_cast<int>(order);
         p->tw = tw;
         p->th = th;
         p->pitch = pitch;
@@ -520,6 +527,9 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     h.taps = p->taps;
     h.stages = p->stages;
     h.w_packed = static_cast<const uint8_t*>(p->d_w);
+    // auto: contiguous runs when the epilogue maxes |y| for the next layer (their register
+    // folding saves the amax atomics), strided otherwise (neighbouring tiles run together)
+    h.contiguous = (p->order == 2 || (p->order == 0 && amax_out != nullptr)) ? 1 : 0;
     h.w_tile_bytes = p->w_tile_bytes;
     h.oc_alloc = p->oc_alloc;
     h.scale_rec = scale_rec;
@@ -586,15 +596,27 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
   return cuda_ok(cudaGetLastError(), "conv launch") ? 1 : 0;
 }
 
-// Picks the quantize kernel: NHWC sources go through the transposing kernel,
-// stride-1 NCHW fp16 with H*W % 8 == 0 through the register-transpose kernel,
-// anything else through the per-slab generic kernel.
+// NHWC sources whose slices all allow 16-byte loads (and, for int8, whose
+// slabs do not straddle two sources): the coalesced row kernel applies.
+bool rows_ok(const QuantParams& q, bool i8) {
+  for (int i = 0; i < q.nsrc; ++i) {
+    const QuantSrc& s = q.src[i];
+    if (s.layout != 0 || s.ch % 8 || s.ldc % 8 || s.coff % 8 || reinterpret_cast<uintptr_t>(s.ptr) % 16) return false;
+    if (i8 && i + 1 < q.nsrc && s.ch % 16) return false;
+  }
+  return q.slabs <= kMaxSlabs;
+}
+
+// Picks the quantize kernel: NHWC sources (16-byte aligned slices, enforced by
+// the entry points) go through the coalesced row kernel, stride-1 NCHW fp16
+// with H*W % 8 == 0 through the register-transpose kernel, anything else
+// (more than 1024 channels, NCHW with ragged planes) through the per-slab
+// generic kernel.
 void launch_quantize(const QuantParams& q, cudaStream_t st) {
-  bool nhwc = true;
-  for (int i = 0; i < q.nsrc; ++i) nhwc = nhwc && q.src[i].layout == 0;
-  if (nhwc && q.slabs <= kMaxSlabs) {
-    const dim3 grid((q.hp * q.wp + kTransThreads - 1) / kTransThreads, q.n);
-    transpose_quant_kernel<true><<<grid, kTransThreads, 0, st>>>(q);
+  if (rows_ok(q, true)) {
+    const int pw = rows_pixels_per_warp(q, true);
+    const dim3 grid((q.hp * q.wp + 8 * pw - 1) / (8 * pw), q.n);
+    quant_rows_kernel<true><<<grid, 256, 0, st>>>(q, pw);
   } else if (q.nsrc == 1 && q.src[0].layout == 1 && !q.split && (q.h * q.w) % 8 == 0 && q.slabs <= kMaxSlabs) {
     const dim3 grid((q.h * q.w / 8 + 255) / 256, q.slabs, q.n);
     quantize_nchw_kernel<<<grid, 256, 0, st>>>(q);
@@ -605,11 +627,18 @@ void launch_quantize(const QuantParams& q, cudaStream_t st) {
 }
 
 void launch_pack(const QuantParams& q, cudaStream_t st) {
-  bool nhwc = true;
-  for (int i = 0; i < q.nsrc; ++i) nhwc = nhwc && q.src[i].layout == 0;
-  if (nhwc && q.slabs <= kMaxSlabs) {
-    const dim3 grid((q.hp * q.wp + kTransThreads - 1) / kTransThreads, q.n);
-    transpose_quant_kernel<false><<<grid, kTransThreads, 0, st>>>(q);
+  if (q.nsrc == 1 && q.src[0].layout == 2 && q.src[0].ch <= 8 && q.src[0].up == 1) {
+    // images (fp32 NCHW, <= 8 channels): one slab, four pixels per thread
+    const int quads = q.hp * ((q.wp + 3) / 4);
+    const dim3 grid((quads + 255) / 256, q.n);
+    pack_nchw_f32_kernel<<<grid, 256, 0, st>>>(static_cast<const float*>(q.src[0].ptr), q.src[0].ch, q.h, q.w, q.hp,
+                                               q.wp, q.split, static_cast<__half*>(q.out));
+    return;
+  }
+  if (rows_ok(q, false)) {
+    const int pw = rows_pixels_per_warp(q, false);
+    const dim3 grid((q.hp * q.wp + 8 * pw - 1) / (8 * pw), q.n);
+    quant_rows_kernel<false><<<grid, 256, 0, st>>>(q, pw);
   } else {
     const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, q.n);
     pack_f16_kernel<<<grid, 256, 0, st>>>(q);
@@ -740,6 +769,7 @@ int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t 
   if (layout > AEXRT_B200_LAYOUT_NCHW_F16) return fail("quantize supports fp16 NHWC or NCHW input");
   if (mode > 1) return fail("mode must be 0 (per tensor) or 1 (pg16)");
   if (mode == 1 && c % 16) return fail("pg16 needs c %% 16 == 0");
+  if (reinterpret_cast<uintptr_t>(x) % 16) return fail("x must be 16-byte aligned");
   if (layout == AEXRT_B200_LAYOUT_NHWC_F16 && (ldc < coff + c || ldc % 8 || coff % 8))
     return fail("NHWC slice must be 16-byte aligned (ldc, coff multiples of 8)");
   if (group_offset + (c + 15) / 16 > groups_total) return fail("amax group range exceeds groups_total");
@@ -762,6 +792,7 @@ int aexrt_b200_pack_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint3
                         uint32_t coff, uint32_t consumer_stride, void* out, void* stream) {
   if (!x || !out) return fail("null pointer");
   if (layout > AEXRT_B200_LAYOUT_NCHW_F32) return fail("unknown layout");
+  if (reinterpret_cast<uintptr_t>(x) % 16) return fail("x must be 16-byte aligned");
   if (layout == AEXRT_B200_LAYOUT_NHWC_F16 && (ldc < coff + c || ldc % 8 || coff % 8))
     return fail("NHWC slice must be 16-byte aligned (ldc, coff multiples of 8)");
   if (reinterpret_cast<uintptr_t>(out) % 16) return fail("out must be 16-byte aligned");
@@ -809,7 +840,49 @@ AexrtB200ConvPlan* aexrt_b200_conv_plan_create_f16(const AexrtConv2DDesc* desc, 
     fail("fp16 conv output size mismatch");
     return nullptr;
   }
-  return build_plan(d, kind, 0, 0, true, weight, nullptr, bias, block_n);
+  AexrtB200ConvPlan* p = build_plan(d, kind, 0, 0, true, weight, nullptr, bias, block_n);
+  const uint32_t oc = d.out_channels;
+  if (p && d.in_channels == static_cast<uint32_t>(kStemIC) && d.kernel_h == 3 && oc % 16 == 0 &&
+      oc <= static_cast<uint32_t>(kStemMaxOC)) {
+    p->image_input = true;
+    for (uint32_t i = 0; i < oc * kStemIC * 9; ++i) p->stem.w[i] = __half2float(__float2half_rn(weight[i]));
+    for (uint32_t i = 0; i < oc; ++i) p->stem.b[i] = bias[i];
+  }
+  return p;
+}
+
+int aexrt_b200_conv_f16_image(const AexrtB200ConvPlan* p, const float* images, void* out, uint32_t out_ldc,
+                              uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride, uint32_t amax_goff,
+                              void* stream) {
+  if (!p) return fail("null plan");
+  if (!p->image_input) return fail("plan does not take images directly (need fp16, 3 input channels, 3x3, oc %% 16 == 0 <= 64)");
+  if (!images || !out) return fail("null input/output pointer");
+  const uint32_t oc = p->desc.out_channels;
+  if (out_ldc < out_coff + oc || out_ldc % 8 || out_coff % 8 || reinterpret_cast<uintptr_t>(out) % 16)
+    return fail("output slice must fit (coff + oc <= ldc) with ldc, coff multiples of 8 and a 16-byte aligned base");
+  if (amax_out && (amax_goff * 16 + oc > amax_stride * 16 || out_coff % 16))
+    return fail("amax_out slots out of range (need amax_goff + ceil(oc/16) <= amax_stride, coff %% 16 == 0)");
+  const int oh = static_cast<int>(p->desc.out_h), ow = static_cast<int>(p->desc.out_w);
+  const int per_img = oh * ow;
+  const dim3 grid((per_img + 255) / 256, p->desc.batch);
+  auto* st = static_cast<cudaStream_t>(stream);
+  const bool silu = p->kind == AEXRT_B200_KIND_CONV_SILU;
+  const auto* x = images;
+  auto* o = static_cast<__half*>(out);
+  const int h = static_cast<int>(p->desc.in_h), w = static_cast<int>(p->desc.in_w), s = p->stride;
+#define AEXRT_STEM_LAUNCH(OC)                                                                                    \
+  (silu ? stem_conv_kernel<OC, true><<<grid, 256, 0, st>>>(x, h, w, oh, ow, s, o, out_ldc, out_coff, amax_out,   \
+                                                           amax_stride, amax_goff, p->stem)                      \
+        : stem_conv_kernel<OC, false><<<grid, 256, 0, st>>>(x, h, w, oh, ow, s, o, out_ldc, out_coff, amax_out,  \
+                                                            amax_stride, amax_goff, p->stem))
+  switch (oc) {
+    case 16: AEXRT_STEM_LAUNCH(16); break;
+    case 32: AEXRT_STEM_LAUNCH(32); break;
+    case 48: AEXRT_STEM_LAUNCH(48); break;
+    default: AEXRT_STEM_LAUNCH(64); break;
+  }
+#undef AEXRT_STEM_LAUNCH
+  return cuda_ok(cudaGetLastError(), "stem conv launch") ? 1 : 0;
 }
 
 int aexrt_b200_conv_plan_info(const AexrtB200ConvPlan* p, AexrtB200ConvPlanInfo* info) {
@@ -828,9 +901,10 @@ int aexrt_b200_conv_plan_info(const AexrtB200ConvPlan* p, AexrtB200ConvPlanInfo*
   i.smem_bytes = p->smem;
   i.grid_m = p->desc.batch * p->tiles_h * p->tiles_w;
   i.grid_n = p->n_tiles;
-  i.reserved[0] = p->grid;
-  i.reserved[1] = p->halo ? 2u : 1u;  // variant
-  i.reserved[2] = p->pitch;
+  i.grid = p->grid;
+  i.variant = p->halo ? 2u : 1u;
+  i.pitch = p->pitch;
+  i.image_input = p->image_input ? 1u : 0u;
   i.in_hp = p->in_hp;
   i.in_wp = p->in_wp;
   *info = i;
@@ -954,6 +1028,22 @@ int aexrt_b200_sppf_pool(const void* x, uint32_t n, uint32_t h, uint32_t w, uint
   if (amax && amax_goff * 16 + 3 * c > amax_stride * 16) return fail("sppf: amax slots out of range");
   const long total = static_cast<long>(n) * h * w * (c / 8);
   if (total == 0) return 1;
+  {
+    // whole map per (image, channel block) in shared memory when it fits
+    int cb = 64;
+    while (cb > 16 && (c % cb || 4L * h * w * cb * 2 > 160 * 1024)) cb /= 2;
+    const long smem = 4L * h * w * cb * 2;
+    if (c % cb == 0 && smem <= 160 * 1024) {
+      // per call: the attribute belongs to the current device's context
+      if (!cuda_ok(cudaFuncSetAttribute(sppf_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024),
+                   "cudaFuncSetAttribute"))
+        return 0;
+      sppf_smem_kernel<<<dim3(c / cb, n), 256, smem, static_cast<cudaStream_t>(stream)>>>(
+          static_cast<const __half*>(x), h, w, c, ldc, coff, cb, static_cast<__half*>(out), out_ldc, out_coff, amax,
+          amax_stride, amax_goff);
+      return cuda_ok(cudaGetLastError(), "sppf launch") ? 1 : 0;
+    }
+  }
   sppf_pool_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(x), n, h, w, c, ldc, coff, static_cast<__half*>(out), out_ldc, out_coff, amax,
       amax_stride, amax_goff);

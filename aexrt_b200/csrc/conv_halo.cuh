@@ -52,6 +52,7 @@ struct ConvHaloParams {
   int32_t* acc_dump;
   uint32_t* status;
   int silu;
+  int contiguous;           // tile order: 0 strided over CTAs, 1 one contiguous run per CTA
 };
 
 struct HaloSmemPlan {
@@ -60,9 +61,12 @@ struct HaloSmemPlan {
   int a_bytes;      // all stages
   int b_offset;
   int sb_offset;
+  int am_offset;    // per-tile amax reduction ring (strided order): [8][16] maxima + [8][4] counters
   int bar_offset;
   int total_bytes;
 };
+
+constexpr int kAmaxRing = 8;  // >= 2 x accumulator buffers: a slot is reset before any warp can reuse it
 
 __host__ __device__ inline HaloSmemPlan halo_smem_plan(int halo_rows, int boxes_per_slab, int stages,
                                                        int w_tile_bytes, int oc_alloc) {
@@ -74,16 +78,24 @@ __host__ __device__ inline HaloSmemPlan halo_smem_plan(int halo_rows, int boxes_
   s.a_bytes = stages * s.stage_bytes + 4096;
   s.b_offset = ((s.a_bytes + 1023) / 1024) * 1024;
   s.sb_offset = s.b_offset + ((w_tile_bytes + 127) / 128) * 128;  // w_scale[oc_alloc], bias[oc_alloc]
-  s.bar_offset = s.sb_offset + ((8 * oc_alloc + 127) / 128) * 128;
+  s.am_offset = s.sb_offset + ((8 * oc_alloc + 127) / 128) * 128;
+  s.bar_offset = s.am_offset + kAmaxRing * (16 + 4) * 4;
   // barriers: full[stages], empty[stages], acc_full[4], acc_empty[4], w_full[2], sb_full; then the TMEM address
   s.total_bytes = s.bar_offset + (2 * stages + 11) * 8 + 16;
   return s;
 }
 
-// Epilogue warps: 4 per TMEM lane quadrant (each owning BN/4 columns) when BN >= 64.
+// Epilogue: 16 warps, 4 per TMEM lane quadrant.  The four warps of a quadrant
+// split the tile's columns into min(4, BN/16) blocks; when BN < 64 the spare
+// warps form tile groups that take alternate tiles (accumulator buffers), so
+// narrow layers get the same epilogue throughput per SM as wide ones.
 template <int BN>
 constexpr int halo_epi_warps() {
-  return BN >= 64 ? 16 : (BN >= 32 ? 8 : 4);
+  return 16;
+}
+template <int BN>
+constexpr int halo_col_blocks() {
+  return BN >= 64 ? 4 : BN / 16;
 }
 template <int BN>
 constexpr int halo_threads() {
@@ -165,7 +177,9 @@ template <bool kF16, int BN, bool kSilu, bool kRes>
 __global__ void __launch_bounds__(halo_threads<BN>(), 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap act_map, const ConvHaloParams p) {
   constexpr int kEpiWarps = halo_epi_warps<BN>();
-  constexpr int kCols = BN / (kEpiWarps / 4);  // columns per epilogue warp
+  constexpr int kColBlocks = halo_col_blocks<BN>();
+  constexpr int kTileGroups = 4 / kColBlocks;   // epilogue tile groups (tiles i with i % groups == g)
+  constexpr int kCols = BN / kColBlocks;        // columns per epilogue warp
   constexpr int CW = kCols >= 32 ? 32 : 16;     // columns per TMEM load
   constexpr int kChunks = kCols / CW;
   // accumulator buffers in TMEM: up to 4, so the MMA can run several tiles ahead of the epilogue
@@ -193,13 +207,14 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
     }
     for (int b = 0; b < kAcc; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kEpiWarps);
+      mbar_init(&acc_empty[b], 4 * kColBlocks);  // the warps of the tile group that drains buffer b
     }
     mbar_init(&w_full[0], 1);
     mbar_init(&w_full[1], 1);
     mbar_init(sb_full, 1);
     fence_mbar_init();
   }
+  if (threadIdx.x < kAmaxRing * (16 + 4)) reinterpret_cast<uint32_t*>(smem + sp.am_offset)[threadIdx.x] = 0u;
   if (warp == 0 && lane == 0) tma_prefetch_desc(&act_map);
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -210,7 +225,15 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  // tiles are ordered n-tile major, so a persistent CTA keeps one weight tile for long runs
+  // Tiles are ordered n-tile major, so a persistent CTA keeps one weight tile for long runs.
+  // Strided order (CTA b takes b, b+G, ...): concurrent CTAs work on neighbouring tiles; the
+  // |y| maxima of a tile are reduced across its four lane quadrants in shared memory (one
+  // atomic per tile and 16-channel group).  Contiguous order (one run per CTA): consecutive
+  // tiles of one image fold their maxima in registers (one atomic per run, image and group).
+  // Every role walks k = b, b+G, ... (G CTAs); the i-th tile of CTA b is t = k (strided) or
+  // t = run_start + i (contiguous: CTA b owns as many tiles as the strided walk gives it).
+  const int run_start = static_cast<int>(blockIdx.x) * (p.total_tiles / static_cast<int>(gridDim.x)) +
+                        min(static_cast<int>(blockIdx.x), p.total_tiles % static_cast<int>(gridDim.x));
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -221,7 +244,8 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
     int s = 0, it = 0, cur_n = -1, wloads = 0;
     uint32_t ph = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+    for (int k = blockIdx.x, i = 0; k < p.total_tiles && ok; k += gridDim.x, ++i) {
+      const int t = p.contiguous ? run_start + i : k;
       const int n_tile = t / p.m_tiles;
       const int m_tile = t - n_tile * p.m_tiles;
       const int per_img = p.tiles_w * p.tiles_h;
@@ -300,7 +324,8 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
       int s = 0, u = 0, cur_n = -1, wloads = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      for (int k = blockIdx.x, i = 0; k < p.total_tiles && ok; k += gridDim.x, ++i) {
+      const int t = p.contiguous ? run_start + i : k;
         const int n_tile = t / p.m_tiles;
         if (n_tile != cur_n) {
           if (wloads > 0) tc_commit(&w_full[1]);  // releases the old weights once prior MMAs finish
@@ -352,8 +377,9 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3;              // TMEM lane quadrant this warp may access
-    const int colq = (warp - 2) >> 2;       // which kCols-wide column block
+    const int quad = warp & 3;                   // TMEM lane quadrant this warp may access
+    const int colq = ((warp - 2) >> 2) % kColBlocks;  // which kCols-wide column block
+    const int tgroup = ((warp - 2) >> 2) / kColBlocks;  // which tiles: i % kTileGroups == tgroup
     const int row = quad * 32 + lane;
     const int r_h = row / p.pitch;
     const int r_w = row - r_h * p.pitch;
@@ -363,8 +389,27 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
     const float* s_scale = reinterpret_cast<const float*>(smem + sp.sb_offset);  // [oc_alloc]
     const float* s_bias = s_scale + p.oc_alloc;
     mbar_wait_bounded(sb_full, 0, p.status, kStatusTimeoutFull);
-    int u = 0;
-    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+    constexpr int kGroups = kChunks * (CW / 16);  // 16-channel amax groups of this warp
+    float run_max[kGroups];
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g) run_max[g] = 0.0f;
+    int run_key = -1, run_img = 0, run_oc = 0;  // (n-tile, image) the maxima belong to
+    auto flush_amax = [&]() {
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g) {
+        const uint32_t mr = __reduce_max_sync(0xffffffffu, __float_as_uint(run_max[g]));
+        const int oc_g = run_oc + 16 * g;
+        if (lane == 0 && oc_g < p.oc && mr != 0u)
+          atomicMax(&p.amax_out[static_cast<size_t>(run_img) * p.amax_stride + p.amax_goff + oc_g / 16], mr);
+        run_max[g] = 0.0f;
+      }
+    };
+    uint32_t* am_ring = reinterpret_cast<uint32_t*>(smem + sp.am_offset);  // [kAmaxRing][16] maxima
+    uint32_t* am_count = am_ring + kAmaxRing * 16;                          // [kAmaxRing][4] arrivals
+    for (int k = blockIdx.x, i = 0; k < p.total_tiles; k += gridDim.x, ++i) {
+      if (kTileGroups > 1 && i % kTileGroups != tgroup) continue;
+      const int u = i;  // the tile's place in this CTA's sequence: accumulator buffer and phase
+      const int t = p.contiguous ? run_start + i : k;
       const int n_tile = t / p.m_tiles;
       const int m_tile = t - n_tile * p.m_tiles;
       const int img = m_tile / per_img;
@@ -375,13 +420,19 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
       __half* out_row = p.out + pix * p.out_ldc + p.out_coff;
       const __half* res_row = kRes ? p.res + pix * p.res_ldc + p.res_coff : nullptr;
       const int n0 = n_tile * BN;
+      if (p.amax_out != nullptr && p.contiguous && t / per_img != run_key) {
+        if (run_key >= 0) flush_amax();
+        run_key = t / per_img;
+        run_img = img;
+        run_oc = n0 + col0;
+      }
       const int buf = u % kAcc;
       // the scale record is ready before the launch: read it while the accumulator fills
       const float amax_in = kF16 ? 0.0f : __ldg(p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs));
       if (!mbar_wait_bounded(&acc_full[buf], (u / kAcc) & 1, p.status, kStatusTimeoutAccFull)) break;
       tc_fence_after();
       const float in_scale = kF16 ? 1.0f : __fdiv_rn(amax_in, 127.0f);
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < kChunks; ++c) {
         uint32_t v[CW];
         const uint32_t taddr = lane_addr + buf * BN + col0 + c * CW;
@@ -410,13 +461,39 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
                                                              s_bias + lc, valid, out_row, res_row);
           const float m1 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g + 8, in_scale, oc_c + 16 * g + 8,
                                                              s_scale + lc + 8, s_bias + lc + 8, valid, out_row, res_row);
-          const uint32_t mr = __reduce_max_sync(0xffffffffu, __float_as_uint(fmaxf(m0, m1)));
-          if (p.amax_out != nullptr && lane == 0 && oc_c + 16 * g < p.oc && mr != 0u)
-            atomicMax(&p.amax_out[static_cast<size_t>(img) * p.amax_stride + p.amax_goff + (oc_c + 16 * g) / 16], mr);
+          run_max[c * (CW / 16) + g] = fmaxf(run_max[c * (CW / 16) + g], fmaxf(m0, m1));
         }
       }
-      ++u;
+      if (p.amax_out != nullptr && !p.contiguous) {
+        // this tile's maxima: warp max, then shared max over the four lane quadrants; the last
+        // quadrant to arrive at this (ring slot, column block) issues the global atomics
+        const int slot = u % kAmaxRing;
+        uint32_t wmax[kGroups];
+#pragma unroll
+        for (int g = 0; g < kGroups; ++g) {
+          wmax[g] = __reduce_max_sync(0xffffffffu, __float_as_uint(run_max[g]));
+          run_max[g] = 0.0f;
+        }
+        if (lane == 0) {
+#pragma unroll
+          for (int g = 0; g < kGroups; ++g)
+            if (wmax[g] != 0u) atomicMax(&am_ring[slot * 16 + col0 / 16 + g], wmax[g]);
+          __threadfence_block();
+          if (atomicAdd(&am_count[slot * 4 + colq], 1u) == 3u) {
+            __threadfence_block();
+            am_count[slot * 4 + colq] = 0u;
+#pragma unroll
+            for (int g = 0; g < kGroups; ++g) {
+              const uint32_t v = atomicExch(&am_ring[slot * 16 + col0 / 16 + g], 0u);
+              const int oc_g = n0 + col0 + 16 * g;
+              if (v != 0u && oc_g < p.oc)
+                atomicMax(&p.amax_out[static_cast<size_t>(img) * p.amax_stride + p.amax_goff + oc_g / 16], v);
+            }
+          }
+        }
+      }
     }
+    if (p.amax_out != nullptr && p.contiguous && run_key >= 0) flush_amax();
   }
 
   tc_fence_before();

@@ -282,6 +282,10 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // each persistent CTA takes one contiguous run of tiles, so consecutive tiles of one image
+  // fold their |y| maxima in registers before one atomic per image and group
+  const int t_begin = static_cast<int>(static_cast<long long>(blockIdx.x) * p.total_tiles / gridDim.x);
+  const int t_end = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * p.total_tiles / gridDim.x);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -292,7 +296,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     int s = 0, it = 0;
     uint32_t ph = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+    for (int t = t_begin; t < t_end && ok; ++t) {
       const TileCoord tc = tile_coord(p, t);
       const uint8_t* w_tile = p.w_packed + static_cast<size_t>(tc.n_tile) * w_tile_bytes;
       for (int st = 0, q0 = 0; st < stages_per_tile; ++st, q0 += p.sps) {
@@ -350,7 +354,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
       int s = 0, u = 0, kin = 0, buf = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      for (int t = t_begin; t < t_end && ok; ++t) {
         for (int st = 0, q0 = 0; st < stages_per_tile; ++st, q0 += p.sps) {
           if (!mbar_wait_bounded(&full[s], ph, p.status, kStatusTimeoutFull)) {
             ok = false;
@@ -400,8 +404,25 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     const size_t npix = static_cast<size_t>(p.n_img) * p.oh * p.ow;
     int u = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+    float run_max[kChunks];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) run_max[c] = 0.0f;
+    int run_key = -1, run_img = 0, run_oc = 0;  // (image, n-tile) the maxima belong to
+    auto flush_amax = [&]() {
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        amax_commit(p, run_max[c], run_img, run_oc + c * CW, lane);
+        run_max[c] = 0.0f;
+      }
+    };
+    for (int t = t_begin; t < t_end && ok; ++t) {
       const TileCoord tc = tile_coord(p, t);
+      if (!kPG && p.amax_out != nullptr && tc.img * p.n_tiles + tc.n_tile != run_key) {
+        if (run_key >= 0) flush_amax();
+        run_key = tc.img * p.n_tiles + tc.n_tile;
+        run_img = tc.img;
+        run_oc = tc.n_tile * BN + col0;
+      }
       const int oy = tc.oh0 + r_h, ox = tc.ow0 + r_w;
       const bool valid = row < rows && oy < p.oh && ox < p.ow;
       const size_t pix = (static_cast<size_t>(tc.img) * p.oh + (valid ? oy : 0)) * p.ow + (valid ? ox : 0);
@@ -416,7 +437,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         }
         tc_fence_after();
         const float in_scale = kF16 ? 1.0f : __fdiv_rn(rec[0], 127.0f);
-#pragma unroll 1
+#pragma unroll
         for (int c = 0; c < kChunks; ++c) {
           uint32_t v[CW];
           tmem_ld<CW>(lane_addr + buf * BN + col0 + c * CW, v);
@@ -444,7 +465,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             }
             m = fmaxf(m, epilogue8<kF16>(p, acc, oc_c + h8 * 8, valid, pix));
           }
-          amax_commit(p, m, tc.img, oc_c, lane);
+          run_max[c] = fmaxf(run_max[c], m);
         }
         ++u;
       } else {
@@ -492,10 +513,11 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             for (int i = 0; i < 8; ++i) acc[i] = fp[c * CW + h8 * 8 + i];
             m = fmaxf(m, epilogue8<false>(p, acc, oc_c + h8 * 8, valid, pix));
           }
-          amax_commit(p, m, tc.img, oc_c, lane);
+          amax_commit(p, m, tc.img, oc_c, lane);  // pg16 keeps its registers for the partial sums
         }
       }
     }
+    if (!kPG && p.amax_out != nullptr && run_key >= 0) flush_amax();
   }
 
   tc_fence_before();

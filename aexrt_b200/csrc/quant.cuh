@@ -257,10 +257,9 @@ __global__ void pack_f16_kernel(const QuantParams p) {
 }
 
 // ----------------------------------------------------------------------------
-// transposing quantize / repack for NHWC sources (the model path)
+// quantize / repack of NHWC sources (the model path)
 // ----------------------------------------------------------------------------
 
-constexpr int kTransThreads = 256;  // output pixels per block of the transposing kernel
 constexpr int kMaxSlabs = 64;       // up to 1024 int8 / 512 fp16 channels
 
 // Activation scale of every output slab of image n (pg16: the slab's own group
@@ -297,71 +296,151 @@ __device__ __forceinline__ void slab_multipliers(const QuantParams& p, int n, fl
   __syncthreads();
 }
 
-// NHWC fp16 sources (optionally concatenated / upsampled) -> slab layout, one
-// thread per output pixel: the thread walks the pixel's channels with 16-byte
-// loads (8 channels each; the L1 keeps each pixel's lines for its later loads)
-// and writes one 16-byte chunk per slab, so for every slab the 32 lanes of a
-// warp store 512 contiguous bytes.  kI8: int8 codes q = round_half_even(x *
-// 127/amax) with no clamp, 16 channels per slab; else fp16 copied, 8 per slab.
+// NHWC fp16 sources with 16-byte aligned slices (ldc, coff, ch multiples of 8;
+// 16-byte aligned base) -> slab layout, coalesced.  A warp covers
+// kRowsPixPerWarp output pixels.  Within one load instruction L lanes share a
+// pixel (L = the source's 16-byte chunks per pixel rounded up to a power of
+// two, at most 8), so P = 32/L pixels x L*16 contiguous bytes are read
+// together; every lane keeps 8 loads in flight whatever the source width.
+// kI8: each chunk is quantized to 8 codes and the two chunks of a 16-channel
+// slab (neighbouring lanes) are joined with a shuffle into one 16-byte slab
+// row; fp16: each chunk is one slab row.  Pixel coordinates come from a
+// per-warp table computed once (no divisions in the copy loops).  A warp's
+// pixel count pw = 32 * 8 / (widest source's L), so the widest source keeps
+// 8 loads per lane in flight in one batch and narrower ones as many or more.
+constexpr int kRowsMaxPixPerWarp = 256;
+
+inline int rows_pixels_per_warp(const QuantParams& q, bool i8) {
+  int lmax = 1;
+  for (int i = 0; i < q.nsrc; ++i) {
+    const int nchunks = q.src[i].ch / 8;
+    int l = nchunks >= 8 ? 8 : (nchunks >= 4 ? 4 : (nchunks >= 2 ? 2 : 1));
+    if (i8 && l < 2) l = 2;
+    lmax = l > lmax ? l : lmax;
+  }
+  return 32 * 8 / lmax;
+}
+
 template <bool kI8>
-__global__ void __launch_bounds__(kTransThreads)
-    transpose_quant_kernel(const QuantParams p) {
+__global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p, int pw) {
   __shared__ float s_mult[kMaxSlabs];
   __shared__ float s_red[2];
+  __shared__ int2 s_pix[8][kRowsMaxPixPerWarp];  // per pixel: (row << 16 | column), destination pixel (-1: none)
   const int n = blockIdx.y;
   if (kI8) slab_multipliers(p, n, s_mult, s_red);
-  const int pix = blockIdx.x * kTransThreads + threadIdx.x;
-  if (pix >= p.hp * p.wp) return;
-  const int h = pix / p.wp, w = pix - (pix / p.wp) * p.wp;
-  const bool inside = h < p.h && w < p.w;
-  const size_t plane = static_cast<size_t>(p.hp) * p.wp;
-  const int dpix = p.split ? h * p.wp + (w & 1) * (p.wp >> 1) + (w >> 1) : pix;
-  uint8_t* out = static_cast<uint8_t*>(p.out) + (static_cast<size_t>(n) * p.slabs * plane + dpix) * 16;
-  int slab = 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int npix = p.hp * p.wp;
+  const int pix0 = (blockIdx.x * 8 + warp) * pw;
+  if (pix0 >= npix) return;  // no barrier follows
+  for (int j = 0; j < pw / 32; ++j) {
+    const int pix = pix0 + j * 32 + lane;
+    const int h = pix / p.wp, w = pix - (pix / p.wp) * p.wp;
+    const int dpix = p.split ? h * p.wp + (w & 1) * (p.wp >> 1) + (w >> 1) : pix;
+    s_pix[warp][j * 32 + lane] = make_int2((h << 16) | w, pix < npix ? dpix : -1);
+  }
+  __syncwarp();
+  const size_t plane = static_cast<size_t>(npix);
+  uint8_t* out = static_cast<uint8_t*>(p.out) + static_cast<size_t>(n) * p.slabs * plane * 16;
+  int chunk_base = 0;  // 8-channel chunks of the sources before this one
   for (int k = 0; k < p.nsrc; ++k) {
     const QuantSrc& s = p.src[k];
-    const __half* src = inside ? static_cast<const __half*>(s.ptr) +
-                                     (static_cast<size_t>(n) * s.src_h * s.src_w + static_cast<size_t>(h / s.up) * s.src_w +
-                                      w / s.up) * s.ldc + s.coff
-                               : nullptr;
-    for (int c0 = 0; c0 < s.ch; c0 += (kI8 ? 16 : 8), ++slab) {
-      uint4 o = make_uint4(0, 0, 0, 0);
-      if (inside) {
-        if (kI8) {
-          const float mult = s_mult[slab];
-          uint32_t q[4] = {0u, 0u, 0u, 0u};
-          if (mult != 0.0f) {
+    const int nchunks = s.ch / 8;
+    int L = nchunks >= 8 ? 8 : (nchunks >= 4 ? 4 : (nchunks >= 2 ? 2 : 1));
+    if (kI8 && L < 2) L = 2;  // a slab is two chunks: keep the pair in neighbouring lanes
+    const int P = 32 / L;
+    const int cl = lane & (L - 1), pl = lane / L;
+    const int ush = s.up == 2 ? 1 : 0;
+    const __half* base = static_cast<const __half*>(s.ptr) + static_cast<size_t>(n) * s.src_h * s.src_w * s.ldc + s.coff;
+    const int per_lane = pw / P;                   // loads per lane covering the warp's pixels
+    const int batches = (per_lane + 7) / 8;        // in groups of up to 8
+    for (int j0 = 0; j0 < nchunks; j0 += L) {
+      const int cidx = j0 + cl;  // chunk of this lane within the source
+      const bool cact = cidx < nchunks;
+      const int slab = kI8 ? (chunk_base + cidx) >> 1 : chunk_base + cidx;
+      const float mult = kI8 && cact ? s_mult[slab] : 0.0f;
+      uint8_t* dst = out + static_cast<size_t>(slab) * plane * 16;
+      for (int b = 0; b < batches; ++b) {
+        uint4 v[8];
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              const int cc = c0 + 8 * half;
-              __align__(16) __half hv[8];
-              if (cc + 8 <= s.ch) {
-                *reinterpret_cast<uint4*>(hv) = *reinterpret_cast<const uint4*>(src + cc);
-              } else {
+        for (int it = 0; it < 8; ++it) {
+          v[it] = make_uint4(0u, 0u, 0u, 0u);
+          if (b * 8 + it >= per_lane) continue;
+          const int2 px = s_pix[warp][(b * 8 + it) * P + pl];
+          const int h = px.x >> 16, w = px.x & 0xFFFF;
+          if (cact && px.y >= 0 && h < p.h && w < p.w)
+            v[it] = *reinterpret_cast<const uint4*>(
+                base + (static_cast<size_t>(h >> ush) * s.src_w + (w >> ush)) * s.ldc + cidx * 8);
+        }
 #pragma unroll
-                for (int i = 0; i < 8; ++i) hv[i] = cc + i < s.ch ? src[cc + i] : __float2half_rn(0.0f);
-              }
+        for (int it = 0; it < 8; ++it) {
+          if (b * 8 + it >= per_lane) break;  // warp-uniform
+          const int dpix = s_pix[warp][(b * 8 + it) * P + pl].y;
+          if (kI8) {
+            const __half2* h2 = reinterpret_cast<const __half2*>(&v[it]);
+            int q[8];
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const uint32_t b = static_cast<uint32_t>(__float2int_rn(__fmul_rn(__half2float(hv[i]), mult))) & 0xFFu;
-                q[2 * half + (i >> 2)] |= b << (8 * (i & 3));
-              }
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(h2[e]);
+              q[2 * e] = __float2int_rn(__fmul_rn(f.x, mult));
+              q[2 * e + 1] = __float2int_rn(__fmul_rn(f.y, mult));
             }
-          }
-          o = make_uint4(q[0], q[1], q[2], q[3]);
-        } else {
-          if (c0 + 8 <= s.ch) {
-            o = *reinterpret_cast<const uint4*>(src + c0);
+            // low byte of each code (two's complement wrap, no clamp), four per word
+            const uint32_t q0 = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
+            const uint32_t q1 = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
+            const uint32_t r0 = __shfl_down_sync(0xffffffffu, q0, 1);
+            const uint32_t r1 = __shfl_down_sync(0xffffffffu, q1, 1);
+            if ((cl & 1) == 0 && cact && dpix >= 0)
+              *reinterpret_cast<uint4*>(dst + static_cast<size_t>(dpix) * 16) = make_uint4(q0, q1, r0, r1);
           } else {
-            __align__(16) __half hv[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) hv[i] = c0 + i < s.ch ? src[c0 + i] : __float2half_rn(0.0f);
-            o = *reinterpret_cast<const uint4*>(hv);
+            if (cact && dpix >= 0) *reinterpret_cast<uint4*>(dst + static_cast<size_t>(dpix) * 16) = v[it];
           }
         }
       }
-      *reinterpret_cast<uint4*>(out + slab * plane * 16) = o;
     }
+    chunk_base += nchunks;
+  }
+}
+
+// fp32 NCHW images with <= 8 channels -> fp16 slab8 (the stem input): each
+// thread converts 4 consecutive pixels (one float4 per channel) and writes four
+// 16-byte pixel rows (stride-2 consumers: into the column-parity-split layout).
+__global__ void __launch_bounds__(256) pack_nchw_f32_kernel(const float* __restrict__ x, int c, int h, int w, int hp,
+                                                          int wp, int split, __half* __restrict__ out) {
+  const int n = blockIdx.y;
+  const int quads_per_row = (wp + 3) / 4;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= hp * quads_per_row) return;
+  const int row = idx / quads_per_row;
+  const int w0 = (idx - row * quads_per_row) * 4;
+  __align__(16) __half px[4][8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) px[j][ch] = __float2half_rn(0.0f);
+  if (row < h) {
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      if (ch >= c) break;
+      const float* src = x + ((static_cast<size_t>(n) * c + ch) * h + row) * w;
+      float f[4];
+      if (w0 + 4 <= w && (w % 4) == 0) {
+        const float4 v = *reinterpret_cast<const float4*>(src + w0);
+        f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f[j] = w0 + j < w ? src[w0 + j] : 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) px[j][ch] = __float2half_rn(f[j]);
+    }
+  }
+  __half* plane = out + static_cast<size_t>(n) * hp * wp * 8;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int ww = w0 + j;
+    if (ww >= wp) break;
+    const int dpix = split ? row * wp + (ww & 1) * (wp >> 1) + (ww >> 1) : row * wp + ww;
+    *reinterpret_cast<uint4*>(plane + static_cast<size_t>(dpix) * 8) = *reinterpret_cast<const uint4*>(px[j]);
   }
 }
 
@@ -386,11 +465,14 @@ __global__ void __launch_bounds__(256) quantize_nchw_kernel(const QuantParams p)
 #pragma unroll
     for (int k = 0; k < 4; ++k) q[j][k] = 0u;
   const __half* base = static_cast<const __half*>(s.ptr) + (static_cast<size_t>(n) * s.ch + slab * 16) * hw + px0;
+  uint4 v[16];
+  const int nch = min(16, s.ch - slab * 16);
+#pragma unroll
+  for (int c = 0; c < 16; ++c)  // all 16 loads issued before any is used
+    v[c] = c < nch ? *reinterpret_cast<const uint4*>(base + static_cast<size_t>(c) * hw) : make_uint4(0, 0, 0, 0);
 #pragma unroll
   for (int c = 0; c < 16; ++c) {
-    if (slab * 16 + c >= s.ch) break;
-    const uint4 v = *reinterpret_cast<const uint4*>(base + static_cast<size_t>(c) * hw);
-    const __half* hv = reinterpret_cast<const __half*>(&v);
+    const __half* hv = reinterpret_cast<const __half*>(&v[c]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const uint32_t b = mult != 0.0f ? static_cast<uint32_t>(__float2int_rn(__fmul_rn(__half2float(hv[j]), mult))) & 0xFFu : 0u;

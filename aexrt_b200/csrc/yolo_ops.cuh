@@ -64,6 +64,89 @@ __global__ void sppf_pool_kernel(const __half* __restrict__ x, int n, int h, int
   }
 }
 
+// SPPF from shared memory: one block holds an image's whole map for a block of
+// `cb` channels, computes the row maxima of the 5/9/13 windows (separable), then
+// the column maxima, and writes the three pooled slices.  amax per 16-channel
+// group is reduced in shared memory (one global atomic per group and block).
+__global__ void __launch_bounds__(256) sppf_smem_kernel(const __half* __restrict__ x, int h, int w, int c, int ldc,
+                                                       int coff, int cb, __half* __restrict__ out, int out_ldc,
+                                                       int out_coff, uint32_t* __restrict__ amax, int amax_stride,
+                                                       int amax_goff) {
+  extern __shared__ __align__(16) __half sm[];  // [4][h*w][cb]: input, then row maxima for 5, 9, 13
+  __shared__ uint32_t s_amax[3 * 16];           // cb <= 256 -> <= 16 groups per slice
+  const int n = blockIdx.y;
+  const int c0 = blockIdx.x * cb;
+  const int hw = h * w;
+  const int vec = cb / 8;
+  const int plane = hw * cb;
+  for (int i = threadIdx.x; i < 3 * 16; i += blockDim.x) s_amax[i] = 0u;
+  for (int idx = threadIdx.x; idx < hw * vec; idx += blockDim.x) {
+    const int pix = idx / vec, v = idx - (idx / vec) * vec;
+    *reinterpret_cast<uint4*>(sm + pix * cb + 8 * v) =
+        *reinterpret_cast<const uint4*>(x + (static_cast<size_t>(n) * hw + pix) * ldc + coff + c0 + 8 * v);
+  }
+  __syncthreads();
+  const __half2 ninf = __halves2half2(__ushort_as_half(0xFC00), __ushort_as_half(0xFC00));
+  for (int idx = threadIdx.x; idx < hw * vec; idx += blockDim.x) {
+    const int pix = idx / vec, v = idx - (idx / vec) * vec;
+    const int yy = pix / w, xx = pix - (pix / w) * w;
+    __half2 m5[4], m9[4], m13[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m5[i] = m9[i] = m13[i] = ninf;
+    for (int dx = -6; dx <= 6; ++dx) {
+      const int xs = xx + dx;
+      if (xs < 0 || xs >= w) continue;
+      const uint4 t = *reinterpret_cast<const uint4*>(sm + (yy * w + xs) * cb + 8 * v);
+      const __half2* t2 = reinterpret_cast<const __half2*>(&t);
+      const int ad = abs(dx);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        m13[i] = __hmax2(m13[i], t2[i]);
+        if (ad <= 4) m9[i] = __hmax2(m9[i], t2[i]);
+        if (ad <= 2) m5[i] = __hmax2(m5[i], t2[i]);
+      }
+    }
+    *reinterpret_cast<uint4*>(sm + plane + pix * cb + 8 * v) = *reinterpret_cast<const uint4*>(m5);
+    *reinterpret_cast<uint4*>(sm + 2 * plane + pix * cb + 8 * v) = *reinterpret_cast<const uint4*>(m9);
+    *reinterpret_cast<uint4*>(sm + 3 * plane + pix * cb + 8 * v) = *reinterpret_cast<const uint4*>(m13);
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < hw * vec; idx += blockDim.x) {
+    const int pix = idx / vec, v = idx - (idx / vec) * vec;
+    const int yy = pix / w, xx = pix - (pix / w) * w;
+    __half* o = out + (static_cast<size_t>(n) * hw + pix) * out_ldc + out_coff + c0 + 8 * v;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int r = k == 0 ? 2 : (k == 1 ? 4 : 6);
+      __half2 m[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) m[i] = ninf;
+      for (int dy = -r; dy <= r; ++dy) {
+        const int ys = yy + dy;
+        if (ys < 0 || ys >= h) continue;
+        const uint4 t = *reinterpret_cast<const uint4*>(sm + (k + 1) * plane + (ys * w + xx) * cb + 8 * v);
+        const __half2* t2 = reinterpret_cast<const __half2*>(&t);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) m[i] = __hmax2(m[i], t2[i]);
+      }
+      *reinterpret_cast<uint4*>(o + k * c) = *reinterpret_cast<const uint4*>(m);
+      if (amax != nullptr) {
+        const __half2 a = __hmax2(__hmax2(__habs2(m[0]), __habs2(m[1])), __hmax2(__habs2(m[2]), __habs2(m[3])));
+        atomicMax(&s_amax[k * 16 + (8 * v) / 16], __float_as_uint(fmaxf(__low2float(a), __high2float(a))));
+      }
+    }
+  }
+  __syncthreads();
+  if (amax != nullptr) {
+    const int g = cb / 16;
+    for (int i = threadIdx.x; i < 3 * g; i += blockDim.x) {
+      const int k = i / g, gi = i - (i / g) * g;
+      const uint32_t val = s_amax[k * 16 + gi];
+      if (val) atomicMax(&amax[static_cast<size_t>(n) * amax_stride + amax_goff + (k * c + c0) / 16 + gi], val);
+    }
+  }
+}
+
 constexpr int kMaxLevels = 3;
 
 struct DecodeParams {
@@ -93,16 +176,38 @@ __global__ void yolo_decode_kernel(const DecodeParams p) {
   const long pix = (static_cast<long>(img) * p.h[lv] + gy) * p.w[lv] + gx;
   const __half* bl = p.box[lv] + pix * p.box_ldc[lv] + p.box_coff[lv];
   float dist[4];
-  for (int side = 0; side < 4; ++side) {
-    float mx = -INFINITY;
-    for (int i = 0; i < p.reg_max; ++i) mx = fmaxf(mx, __half2float(bl[side * p.reg_max + i]));
-    float den = 0.f, num = 0.f;
-    for (int i = 0; i < p.reg_max; ++i) {
-      const float e = __expf(__half2float(bl[side * p.reg_max + i]) - mx);
-      den += e;
-      num += e * static_cast<float>(i);
+  if (p.reg_max == 16 && (reinterpret_cast<uintptr_t>(bl) & 15) == 0) {
+    // 64 logits as eight 16-byte loads, all issued before use
+    uint4 raw[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) raw[i] = reinterpret_cast<const uint4*>(bl)[i];
+#pragma unroll
+    for (int side = 0; side < 4; ++side) {
+      const __half* hv = reinterpret_cast<const __half*>(&raw[2 * side]);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) mx = fmaxf(mx, __half2float(hv[i]));
+      float den = 0.f, num = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float e = __expf(__half2float(hv[i]) - mx);
+        den += e;
+        num += e * static_cast<float>(i);
+      }
+      dist[side] = num / den;
     }
-    dist[side] = num / den;
+  } else {
+    for (int side = 0; side < 4; ++side) {
+      float mx = -INFINITY;
+      for (int i = 0; i < p.reg_max; ++i) mx = fmaxf(mx, __half2float(bl[side * p.reg_max + i]));
+      float den = 0.f, num = 0.f;
+      for (int i = 0; i < p.reg_max; ++i) {
+        const float e = __expf(__half2float(bl[side * p.reg_max + i]) - mx);
+        den += e;
+        num += e * static_cast<float>(i);
+      }
+      dist[side] = num / den;
+    }
   }
   const float cx = gx + 0.5f, cy = gy + 0.5f, st = p.stride[lv];
   const float x1 = cx - dist[0], y1 = cy - dist[1], x2 = cx + dist[2], y2 = cy + dist[3];

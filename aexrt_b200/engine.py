@@ -108,6 +108,12 @@ class CompiledYolo:
             scratch = (q, rec)
         else:
             plan = ops.ConvPlan.fp16(n, c.ic, h, w, c.oc, c.k, c.s, c.weight, c.bias, silu=c.silu, block_n=block_n)
+            if (len(c.inputs) == 1 and c.inputs[0].value == "images" and plan.info.image_input
+                    and c.residual is None):
+                # the stem reads the fp32 images directly: no packed copy
+                self.plans[c.name] = plan
+                self.steps.append(("stem", c, plan))
+                return
             hp = h + (h & 1 if c.s == 2 else 0)
             wp = w + (w & 1 if c.s == 2 else 0)
             x8 = torch.empty((n, (c.ic + 7) // 8, hp, wp, 8), dtype=torch.float16, device=self.device)
@@ -169,6 +175,12 @@ class CompiledYolo:
                           f"pack {c.name}")
                     plan.run(x8, out=out, out_coff=c.out[1], residual=res, res_coff=res_coff, amax_out=amax_out,
                              amax_goff=c.out[1] // 16, stream=stream)
+            elif kind == "stem":
+                _, c, plan = st
+                out = self.values[c.out[0]]
+                amax_out = self._amax_view(c.out[0]) if c.out[0] in self.needs_amax else None
+                plan.run_image(self.images, out=out, out_coff=c.out[1], amax_out=amax_out, amax_goff=c.out[1] // 16,
+                               stream=stream)
             elif kind == "sppf":
                 c = st[1]
                 x = self.values[c.x.value]

@@ -170,6 +170,16 @@ class PlanInfo:
     grid_n: int
     in_hp: int
     in_wp: int
+    grid: int = 0
+    variant: int = 0
+    pitch: int = 0
+    image_input: int = 0
+
+    @staticmethod
+    def from_c(i: AexrtB200ConvPlanInfo) -> "PlanInfo":
+        return PlanInfo(i.kernel_id, i.flags, i.kind, bool(i.is_f16), i.tile_w, i.tile_h, i.block_n, i.k_slots,
+                        i.stages, i.smem_bytes, i.grid_m, i.grid_n, i.in_hp, i.in_wp, i.grid, i.variant, i.pitch,
+                        i.image_input)
 
 
 class ConvPlan:
@@ -216,8 +226,7 @@ class ConvPlan:
     def _info(self) -> PlanInfo:
         i = AexrtB200ConvPlanInfo()
         check(_native.load().aexrt_b200_conv_plan_info(self._h, ctypes.byref(i)), "conv_plan_info")
-        return PlanInfo(i.kernel_id, i.flags, i.kind, bool(i.is_f16), i.tile_w, i.tile_h, i.block_n, i.k_slots,
-                        i.stages, i.smem_bytes, i.grid_m, i.grid_n, i.in_hp, i.in_wp)
+        return PlanInfo.from_c(i)
 
     @property
     def out_shape(self):
@@ -242,6 +251,17 @@ class ConvPlan:
             check(lib.aexrt_b200_conv_w8a8(self._h, x.data_ptr(), rec.data_ptr(), _ptr(residual), res_ldc, res_coff,
                                            out.data_ptr(), out_ldc, out_coff, _ptr(amax_out), amax_stride, amax_goff,
                                            _ptr(acc_dump), _stream(stream)), "conv_w8a8")
+        return out
+
+    def run_image(self, images, out=None, out_coff: int = 0, amax_out=None, amax_goff: int = 0, stream=None):
+        """The image stem: fp32 NCHW ``images`` straight into the fp16 NHWC ``out`` (plans with info.image_input)."""
+        torch = _torch()
+        if out is None:
+            out = torch.empty(self.out_shape, dtype=torch.float16, device=images.device)
+        amax_stride = amax_out.shape[-1] if amax_out is not None else 0
+        check(_native.load().aexrt_b200_conv_f16_image(self._h, images.data_ptr(), out.data_ptr(), out.shape[-1],
+                                                       out_coff, _ptr(amax_out), amax_stride, amax_goff,
+                                                       _stream(stream)), "conv_f16_image")
         return out
 
     def status(self) -> int:

@@ -186,7 +186,8 @@ class _Builder:
             v = self.p.values[f]
             h0 = self.value(f"{name}.{i}.h0", c2 + c3, v.h, v.w)
             h1 = self.value(f"{name}.{i}.h1", c2 + c3, v.h, v.w)
-            o = self.value(f"{name}.{i}.out", 4 * reg_max + nc, v.h, v.w)
+            # box logits then class logits; rows padded to a multiple of 8 channels (16-byte stores)
+            o = self.value(f"{name}.{i}.out", _make_divisible(4 * reg_max + nc, 8), v.h, v.w)
             # cv2[i][0] and cv3[i][0] read the same input: one conv with c2 + c3 outputs
             self.conv(f"{name}.{i}.cv23_0", [Part(f, 0, chs[i])], (h0, 0), c2 + c3, 3, 1, precision="fp16")
             self.conv(f"{name}.{i}.cv2_1", [Part(h0, 0, c2)], (h1, 0), c2, 3, 1, precision="fp16")

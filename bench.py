@@ -47,8 +47,13 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=24, help="images in the CPU baseline sample")
     ap.add_argument("--workload", default="yolov8n-320",
-                    help="yolov8n-320 (the metric), or a BASELINE layer: " + ", ".join(LAYERS) + ", or amax-quant")
+                    help="yolov8n-320 (the metric), or a BASELINE layer: " + ", ".join(LAYERS)
+                    + ", or amax-quant, " + ", ".join(QUANTS))
     ap.add_argument("--mode", type=int, default=0, help="layer workloads: 0 per-tensor, 1 pg16 scales")
+    ap.add_argument("--order", type=int, default=0,
+                    help="layer workloads: halo tile order (0 auto, 1 strided, 2 contiguous)")
+    ap.add_argument("--amax-out", action="store_true",
+                    help="layer workloads: the conv also maxes |y| per 16-channel group for the next layer")
     return ap.parse_args()
 
 
@@ -59,7 +64,13 @@ LAYERS = {
     "sweep-3x3s1": (64, 80, 80, 64, 3, 1),
     "sweep-3x3s2": (32, 160, 160, 64, 3, 2),
     "sweep-3x3s2-small": (128, 20, 20, 256, 3, 2),
+    # narrow high-resolution layers of YOLOv8n-320 (l1, l2.m0.cv1, l2.cv1)
+    "n-l1": (16, 160, 160, 32, 3, 2),
+    "n-l2m": (16, 80, 80, 16, 3, 1),
+    "n-l2cv1": (32, 80, 80, 32, 1, 1),
 }
+# between-layer quantize passes of YOLOv8n-320: (h, w, channels)
+QUANTS = {"quant-nhwc": (40, 40, 192), "quant-nhwc-16": (160, 160, 16), "quant-nhwc-32": (80, 80, 32)}
 
 
 def run_layer(args):
@@ -85,25 +96,42 @@ def run_layer(args):
 
         byts, ops_ = 5.0 * x.numel(), 0.0
         desc = f"standalone amax + quantize of {n}x64x80x80 fp16 NCHW (BASELINE config 2)"
+    elif args.workload in QUANTS:
+        # the model's between-layer quantize: fp16 NHWC activations (amax already in the slots)
+        qh, qw, qc = QUANTS[args.workload]
+        x = torch.from_numpy((lambda z: z / (1 + np.exp(-z)))(rng.standard_normal((n, qh, qw, qc)).astype(np.float32))
+                             .astype(np.float16)).cuda()
+        amax = ops.act_amax(x, ops.LAYOUT_NHWC_F16)
+        q, rec = ops.act_quantize(x, amax, args.mode, ops.LAYOUT_NHWC_F16)
+
+        def step():
+            ops.act_quantize(x, amax, args.mode, ops.LAYOUT_NHWC_F16, q_out=q, rec_out=rec)
+
+        byts, ops_ = 3.0 * x.numel(), 0.0
+        desc = f"quantize of {n}x{qh}x{qw}x{qc} fp16 NHWC into int8 slabs (the model's between-layer pass)"
     else:
         ic, h, w, oc, k, s = LAYERS[args.workload]
         wt = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
         b = rng.normal(0, 0.1, oc).astype(np.float32)
         codes, scale = ops.quantize_conv_weight_int8(wt)
-        plan = ops.ConvPlan.int8(n, ic, h, w, oc, k, s, codes, scale, b, pg16=bool(args.mode))
+        plan = ops.ConvPlan.int8(n, ic, h, w, oc, k, s, codes, scale, b, pg16=bool(args.mode),
+                                 block_n=args.order << 20)
         x = torch.from_numpy((lambda z: z / (1 + np.exp(-z)))(rng.standard_normal((n, ic, h, w)).astype(np.float32))
                              .astype(np.float16)).cuda()
         amax = ops.act_amax(x, ops.LAYOUT_NCHW_F16)
         q, rec = ops.act_quantize(x, amax, args.mode, ops.LAYOUT_NCHW_F16, consumer_stride=s)
         out = torch.empty(plan.out_shape, dtype=torch.float16, device="cuda")
+        amax_next = torch.zeros((n, (oc + 15) // 16), dtype=torch.int32, device="cuda") if args.amax_out else None
 
         def step():
-            plan.run(q, rec, out=out)
+            plan.run(q, rec, out=out, amax_out=amax_next)
 
         d = plan.desc
         ops_ = 2.0 * n * d.out_h * d.out_w * oc * ic * k * k
         byts = n * ic * h * w + 2.0 * n * oc * d.out_h * d.out_w + oc * ic * k * k
-        desc = f"conv {ic}->{oc} k{k} s{s} @{h}x{w}, batch {n}, {'pg16' if args.mode else 'per-tensor'} (BASELINE configs 1-2)"
+        desc = (f"conv {ic}->{oc} k{k} s{s} @{h}x{w}, batch {n}, {'pg16' if args.mode else 'per-tensor'}"
+                f"{', amax out' if args.amax_out else ''}{f', order {args.order}' if args.order else ''}"
+                " (BASELINE configs 1-2)")
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
@@ -248,8 +276,9 @@ def conv_roofline(eng, torch, stream):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(torch.cuda.current_stream())
+        amax_out = eng._amax_view(c.out[0]) if c.out[0] in eng.needs_amax else None
         plan.run(q, rec, out=out, out_coff=c.out[1], residual=res, res_coff=c.residual[1] if c.residual else 0,
-                 amax_out=None, stream=stream)
+                 amax_out=amax_out, amax_goff=c.out[1] // 16, stream=stream)
         e1.record(torch.cuda.current_stream())
         d = eng.program.values[c.out[0]]
         ops = 2.0 * n * d.h * d.w * c.oc * c.ic * c.k * c.k

@@ -89,7 +89,10 @@ typedef struct AexrtB200ConvPlanInfo {
     uint32_t smem_bytes;
     uint32_t grid_m, grid_n;
     uint32_t in_hp, in_wp;     /* packed input buffer dims expected by the launch */
-    uint32_t reserved[4];
+    uint32_t grid;             /* persistent CTAs per launch */
+    uint32_t variant;          /* 1 slot streaming, 2 halo tile */
+    uint32_t pitch;            /* halo variant: M rows per tile row */
+    uint32_t image_input;      /* 1: aexrt_b200_conv_f16_image accepts this plan */
 } AexrtB200ConvPlanInfo;
 
 /* ---------------------------------------------------------------- library */
@@ -142,8 +145,11 @@ int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t 
  * reference's guard can_use_conv_int8 (native/aexrt_d3d12_runtime.cpp:9398-9422)
  * plus IC % 16 == 0 when flags has INT8_PERGROUP; the weight repack replaces
  * ensure_conv_int8_weight's uint32 repack (runtime.cpp:21744-21775).
- * block_n = 0 picks the output-channel tile automatically.  Allocates device
- * memory (set-up time only).  Returns NULL on error. */
+ * block_n = 0 picks the output-channel tile automatically.  Tuning bits above
+ * the tile (bits 0-15): bits 16-19 kernel variant (0 auto, 1 slot streaming,
+ * 2 halo tile), bits 20-23 halo tile order (0 auto, 1 strided over CTAs,
+ * 2 one contiguous run per CTA); results are identical for every choice.
+ * Allocates device memory (set-up time only).  Returns NULL on error. */
 AexrtB200ConvPlan* aexrt_b200_conv_plan_create(const AexrtConv2DDesc* desc, uint32_t kind, uint32_t kernel_id,
                                                uint32_t flags, const int8_t* codes, const float* w_scale,
                                                const float* bias, uint32_t block_n);
@@ -180,6 +186,19 @@ int aexrt_b200_conv_f16(const AexrtB200ConvPlan* plan, const void* x_slab8, cons
 
 /* Reads and clears the plan's device status word (synchronises the device).
  * Non-zero bits mean a pipeline wait gave up (see the kernel sources). */
+/* The image stem: an fp16 plan with 3 input channels, a 3x3 window (pad 1)
+ * and 16/32/48/64 output channels (info.image_input == 1) read straight from
+ * the fp32 NCHW image batch [batch][3][in_h][in_w], with no packed copy.
+ * Same arithmetic as aexrt_b200_conv_f16 (fp16-rounded inputs and weights,
+ * fp32 accumulation, fp32 bias + SiLU, fp16 output); out_ldc and out_coff
+ * multiples of 8 (16 with amax_out), out 16-byte aligned.  Replaces the
+ * reference's first fp16 conv command with its input conversion
+ * (the image upload + NCHW fp16 conv of the stem in prepared replay,
+ * native/aexrt_d3d12_runtime.cpp:28758-29010). */
+int aexrt_b200_conv_f16_image(const AexrtB200ConvPlan* plan, const float* images, void* out, uint32_t out_ldc,
+                              uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride, uint32_t amax_goff,
+                              void* stream);
+
 int aexrt_b200_conv_status(const AexrtB200ConvPlan* plan, uint32_t* status);
 
 /* fp16 slab8 repack of an NHWC fp16 or NCHW fp16/fp32 tensor for fp16 convs. */

@@ -29,6 +29,16 @@ def test_conv_desc_layout_matches_reference():
     assert [f[0] for f in _native.AexrtConv2DDesc._fields_][:4] == ["batch", "in_channels", "in_h", "in_w"]
 
 
+def test_plan_info_struct_matches_header():
+    # 19 uint32 fields (struct_size .. image_input); the Python view carries every one but struct_size
+    assert ctypes.sizeof(_native.AexrtB200ConvPlanInfo) == 19 * 4
+    i = _native.AexrtB200ConvPlanInfo()
+    for k, (name, _) in enumerate(_native.AexrtB200ConvPlanInfo._fields_):
+        setattr(i, name, k + 1)
+    info = ops.PlanInfo.from_c(i)
+    assert info.kernel_id == 2 and info.in_wp == 15 and info.grid == 16 and info.image_input == 19
+
+
 def test_c_weight_quantizer_matches_reference_payloads(golden_dir):
     d = np.load(f"{golden_dir}/weights_layout8.npz")
     for i in range(int(d["count"])):
@@ -73,3 +83,25 @@ def test_entry_points_fail_closed_on_null():
     assert "null" in _native.last_error()
     assert lib.aexrt_b200_conv_w8a8(None, None, None, None, 0, 0, None, 0, 0, None, 0, 0, None, None) == 0
     assert lib.aexrt_b200_packed_act_bytes(2, 20, 7, 9, 2) == 2 * 2 * 8 * 10 * 16
+
+
+def test_unaligned_nhwc_slices_are_refused_before_any_launch():
+    """16-byte loads need 16-byte aligned slices: the entry points refuse others up front (no kernel runs)."""
+    from aexrt_b200._native import AexrtB200ActSource
+
+    lib = _native.load()
+    dummy = ctypes.c_void_p(4096)
+    srcs = (AexrtB200ActSource * 1)()
+    s = srcs[0]
+    s.ptr, s.layout, s.ldc, s.coff, s.channels, s.upsample, s.src_h, s.src_w = 4096, 0, 40, 4, 32, 1, 4, 4
+    s.amax_groups, s.amax_stride, s.amax_goff = 4096, 4, 0
+    assert lib.aexrt_b200_act_quantize_concat(srcs, 1, 1, 4, 4, 0, 1, dummy, dummy, None) == 0
+    assert "aligned" in _native.last_error()
+    assert lib.aexrt_b200_pack_f16_concat(srcs, 1, 1, 4, 4, 1, dummy, None) == 0
+    assert "aligned" in _native.last_error()
+    # a misaligned base pointer
+    assert lib.aexrt_b200_act_quantize_f16(ctypes.c_void_p(4104), 1, 32, 4, 4, 0, 32, 0, dummy, 2, 0, 0, 1, dummy,
+                                           dummy, None) == 0
+    assert "aligned" in _native.last_error()
+    assert lib.aexrt_b200_pack_f16(ctypes.c_void_p(4104), 1, 32, 4, 4, 0, 32, 0, 1, dummy, None) == 0
+    assert "aligned" in _native.last_error()

@@ -207,7 +207,8 @@ def test_fp16_conv_vs_torch(n, ic, h, w, oc, k, s, silu):
     assert err <= 1e-2 * max(1.0, ref.abs().max().item() / 8), err
 
 
-@pytest.mark.parametrize("variant", [1, 2])
+# variant bits: 1 slot streaming, 2 halo (auto order), 0x12 halo strided, 0x22 halo contiguous runs
+@pytest.mark.parametrize("variant", [1, 2, 0x12, 0x22])
 @pytest.mark.parametrize("n,ic,h,w,oc,k,s", [
     (2, 64, 20, 20, 64, 3, 1),
     (2, 48, 17, 13, 32, 3, 1),   # odd slab count (3 slabs): zero-padded slab pair
@@ -218,7 +219,8 @@ def test_fp16_conv_vs_torch(n, ic, h, w, oc, k, s, silu):
     (1, 64, 80, 80, 128, 3, 1),
 ])
 def test_kernel_variants_bitexact(n, ic, h, w, oc, k, s, variant):
-    """Slot-streaming (1) and halo (2) kernels: identical int32 accumulators, both equal to the oracle."""
+    """Slot-streaming and halo kernels (both halo tile orders): identical int32 accumulators and
+    epilogue amax, all equal to the oracle."""
     rng = np.random.default_rng(ic * 7 + oc + s)
     x = seeded_act(rng, (n, ic, h, w))
     weight = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
@@ -256,3 +258,47 @@ def test_fp16_halo_vs_slot_streaming(n, ic, h, w, oc, k, s, silu):
     ref = ref.permute(0, 2, 3, 1)
     for o in outs:
         assert (o - ref).abs().max().item() <= 1e-2 * max(1.0, ref.abs().max().item() / 8)
+
+
+@pytest.mark.parametrize("n,h,w,oc,s,silu", [
+    (2, 64, 64, 16, 2, True),    # the YOLOv8n stem shape, small
+    (3, 33, 47, 32, 2, True),    # odd sizes: clipped windows on the right/bottom
+    (2, 20, 20, 64, 1, False),
+    (1, 17, 16, 48, 2, True),
+])
+def test_stem_image_input(n, h, w, oc, s, silu):
+    """The direct stem (fp32 NCHW images in) against torch fp32 and the packed fp16 path; amax_out exact."""
+    torch = _torch()
+    from aexrt_b200 import ops
+
+    rng = np.random.default_rng(oc + h)
+    x = rng.uniform(0, 1, (n, 3, h, w)).astype(np.float32)
+    weight = rng.normal(0, 1 / np.sqrt(27), (oc, 3, 3, 3)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    plan = ops.ConvPlan.fp16(n, 3, h, w, oc, 3, s, weight, bias, silu=silu)
+    assert plan.info.image_input == 1
+    xt = torch.from_numpy(x).cuda()
+    # write into a channel slice of a wider buffer, with amax slots behind the slice
+    oh, ow = plan.out_shape[1], plan.out_shape[2]
+    buf = torch.full((n, oh, ow, oc + 32), 7.0, dtype=torch.float16, device="cuda")
+    amax = torch.zeros((n, (oc + 32) // 16), dtype=torch.int32, device="cuda")
+    plan.run_image(xt, out=buf, out_coff=16, amax_out=amax, amax_goff=1)
+    packed_out = plan.run(ops.pack_f16(xt, ops.LAYOUT_NCHW_F32, consumer_stride=s))
+    torch.cuda.synchronize()
+    got = buf[..., 16:16 + oc].float().cpu()
+    assert torch.all(buf[..., :16] == 7.0) and torch.all(buf[..., 16 + oc:] == 7.0)
+    xr = torch.from_numpy(x.astype(np.float16).astype(np.float32))
+    wr = torch.from_numpy(weight.astype(np.float16).astype(np.float32))
+    ref = torch.nn.functional.conv2d(xr, wr, torch.from_numpy(bias), stride=s, padding=1)
+    if silu:
+        ref = ref * torch.sigmoid(ref)
+    ref = ref.permute(0, 2, 3, 1)
+    tol = 1e-2 * max(1.0, ref.abs().max().item() / 8)
+    assert (got - ref).abs().max().item() <= tol
+    assert (got - packed_out.float().cpu()).abs().max().item() <= tol
+    # amax slots: exact max |y| of the fp16 outputs per (image, 16-channel group)
+    g = got.abs().reshape(n, -1, oc // 16, 16).amax(dim=(1, 3))
+    want = g.numpy().astype(np.float32).view(np.int32)
+    am = amax.cpu().numpy()
+    assert np.array_equal(am[:, 1:1 + oc // 16], want)
+    assert not am[:, 0].any() and not am[:, 1 + oc // 16:].any()

@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 
 from oracle import w8a8 as ow
-from tests._util import bits_to_f32, nchw_to_nhwc, seeded_act, slab16_to_nchw
+from tests._util import bits_to_f32, nchw_to_nhwc, seeded_act, slab16_to_nchw, unsplit_columns
 
 pytestmark = pytest.mark.gpu
 
@@ -94,3 +94,103 @@ def test_quantize_baseline_standalone_64x64x80x80():
         q, _ = ops.act_quantize(xt, amax, mode, ops.LAYOUT_NCHW_F16)
         expect = ow.quantize_act(x, at, ag, mode)
         assert np.array_equal(slab16_to_nchw(q.cpu().numpy(), 64, 80, 80), expect)
+
+
+def _concat_case(rng, n, h, w, specs):
+    """NHWC fp16 source buffers for one concatenated consumer input.
+
+    specs: (buffer channels, slice offset, slice channels, upsample) per source.  Returns the
+    device buffers, the C source descriptors (amax slots filled by act_amax) and the logical
+    NCHW concatenation the quantizer must see."""
+    torch = _torch()
+    from aexrt_b200 import ops
+    from aexrt_b200._native import AexrtB200ActSource
+
+    srcs = (AexrtB200ActSource * len(specs))()
+    keep, parts = [], []
+    for i, (ldc, coff, ch, up) in enumerate(specs):
+        sh, sw = (h + up - 1) // up, (w + up - 1) // up
+        full = seeded_act(rng, (n, ldc, sh, sw))
+        buf = torch.from_numpy(nchw_to_nhwc(full)).cuda()
+        amax = ops.act_amax(buf, ops.LAYOUT_NHWC_F16, c=ch, coff=coff)
+        keep += [buf, amax]
+        part = full[:, coff:coff + ch]
+        if up == 2:
+            part = part.repeat(2, axis=2).repeat(2, axis=3)
+        parts.append(part[:, :, :h, :w])
+        s = srcs[i]
+        s.ptr, s.layout, s.ldc, s.coff, s.channels, s.upsample = buf.data_ptr(), ops.LAYOUT_NHWC_F16, ldc, coff, ch, up
+        s.src_h, s.src_w = sh, sw
+        s.amax_groups, s.amax_stride, s.amax_goff = amax.data_ptr(), amax.shape[1], 0
+    return srcs, keep, np.concatenate(parts, axis=1)
+
+
+@pytest.mark.parametrize("stride", [1, 2])
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("specs,h,w", [
+    # aligned slices: the coalesced row kernel (upsampled source, odd chunk count in the last one)
+    ([(64, 16, 32, 2), (48, 0, 48, 1), (24, 0, 24, 1)], 10, 14),
+    ([(128, 0, 128, 1), (64, 0, 64, 1)], 9, 11),
+    ([(16, 0, 16, 1)], 7, 5),
+    ([(256, 0, 192, 1)], 6, 6),
+    ([(1152, 0, 1040, 1)], 3, 4),  # more than 1024 channels: the per-slab generic kernel
+])
+def test_quantize_concat_sources_bitexact(specs, h, w, mode, stride):
+    """Concatenated / upsampled NHWC sources quantized in one pass equal the oracle on the concatenation."""
+    torch = _torch()
+    from aexrt_b200 import _native, ops
+    from aexrt_b200._native import check
+
+    rng = np.random.default_rng(h * 100 + w + len(specs))
+    n = 3
+    srcs, keep, cat = _concat_case(rng, n, h, w, specs)
+    c = cat.shape[1]
+    shape = ops.packed_act_shape(n, c, h, w, stride)
+    q = torch.full(shape, 99, dtype=torch.int8, device="cuda")
+    rec = torch.empty((n, 1 + shape[1]), dtype=torch.float32, device="cuda")
+    lib = _native.load()
+    if mode == 1 and c % 16:
+        # pg16 scales are per 16-channel group: a ragged last group is refused, as in the reference
+        assert lib.aexrt_b200_act_quantize_concat(srcs, len(specs), n, h, w, mode, stride, q.data_ptr(),
+                                                  rec.data_ptr(), None) == 0
+        return
+    check(lib.aexrt_b200_act_quantize_concat(srcs, len(specs), n, h, w, mode, stride, q.data_ptr(), rec.data_ptr(),
+                                             None), "quantize concat")
+    torch.cuda.synchronize()
+    at, ag = ow.act_amax(cat)
+    qn = q.cpu().numpy()
+    assert np.array_equal(slab16_to_nchw(qn, c, h, w, stride), ow.quantize_act(cat, at, ag, mode))
+    # channel padding of the last slab and the stride-2 padding rows / columns are zero
+    full = slab16_to_nchw(qn, shape[1] * 16, shape[2], shape[3], stride)
+    assert (full[:, c:] == 0).all() and (full[:, :, h:] == 0).all() and (full[:, :, :, w:] == 0).all()
+    r = rec.cpu().numpy()
+    assert np.array_equal(r[:, 0], at) and np.array_equal(r[:, 1:], ag)
+
+
+@pytest.mark.parametrize("stride", [1, 2])
+@pytest.mark.parametrize("specs,h,w", [
+    ([(64, 16, 32, 2), (48, 0, 48, 1), (24, 0, 24, 1)], 10, 14),
+    ([(64, 0, 64, 1)], 9, 11),
+    ([(24, 8, 16, 1), (16, 0, 8, 1)], 9, 7),
+])
+def test_pack_f16_concat_sources_exact(specs, h, w, stride):
+    """The fp16 repack of concatenated sources is a pure copy into the slab8 layout."""
+    torch = _torch()
+    from aexrt_b200 import _native
+    from aexrt_b200._native import check
+
+    rng = np.random.default_rng(h * 10 + w)
+    n = 2
+    srcs, keep, cat = _concat_case(rng, n, h, w, specs)
+    c = cat.shape[1]
+    hp, wp = (h + (h & 1), w + (w & 1)) if stride == 2 else (h, w)
+    out = torch.full((n, (c + 7) // 8, hp, wp, 8), 5.0, dtype=torch.float16, device="cuda")
+    check(_native.load().aexrt_b200_pack_f16_concat(srcs, len(specs), n, h, w, stride, out.data_ptr(), None),
+          "pack concat")
+    torch.cuda.synchronize()
+    o = out.cpu().numpy()
+    if stride == 2:
+        o = unsplit_columns(o)
+    got = o.transpose(0, 1, 4, 2, 3).reshape(n, -1, hp, wp)
+    assert np.array_equal(got[:, :c, :h, :w], cat)
+    assert (got[:, c:] == 0).all() and (got[:, :, h:] == 0).all() and (got[:, :, :, w:] == 0).all()
