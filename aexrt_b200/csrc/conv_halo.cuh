@@ -53,6 +53,7 @@ struct ConvHaloParams {
   uint32_t* status;
   int silu;
   int contiguous;           // tile order: 0 strided over CTAs, 1 one contiguous run per CTA
+  int issuers;              // MMA issuing threads (1 or 2; 2 needs a half ring to hold a whole tile)
 };
 
 struct HaloSmemPlan {
@@ -66,7 +67,8 @@ struct HaloSmemPlan {
   int total_bytes;
 };
 
-constexpr int kAmaxRing = 8;  // >= 2 x accumulator buffers: a slot is reset before any warp can reuse it
+constexpr int kMaxAcc = 16;                 // TMEM accumulator buffers (narrow tiles keep more in flight)
+constexpr int kAmaxRing = 2 * kMaxAcc;      // >= 2 x accumulator buffers: a slot is reset before any warp reuses it
 
 __host__ __device__ inline HaloSmemPlan halo_smem_plan(int halo_rows, int boxes_per_slab, int stages,
                                                        int w_tile_bytes, int oc_alloc) {
@@ -80,8 +82,8 @@ __host__ __device__ inline HaloSmemPlan halo_smem_plan(int halo_rows, int boxes_
   s.sb_offset = s.b_offset + ((w_tile_bytes + 127) / 128) * 128;  // w_scale[oc_alloc], bias[oc_alloc]
   s.am_offset = s.sb_offset + ((8 * oc_alloc + 127) / 128) * 128;
   s.bar_offset = s.am_offset + kAmaxRing * (16 + 4) * 4;
-  // barriers: full[stages], empty[stages], acc_full[4], acc_empty[4], w_full[2], sb_full; then the TMEM address
-  s.total_bytes = s.bar_offset + (2 * stages + 11) * 8 + 16;
+  // barriers: full[stages], empty[stages], acc_full[16], acc_empty[16], w_full[2], sb_full; then the TMEM address
+  s.total_bytes = s.bar_offset + (2 * stages + 2 * kMaxAcc + 3) * 8 + 16;
   return s;
 }
 
@@ -97,9 +99,16 @@ template <int BN>
 constexpr int halo_col_blocks() {
   return BN >= 64 ? 4 : BN / 16;
 }
+// MMA issuers: tcgen05.mma issue blocks while the tensor core is busy, so one
+// issuing thread leaves the tensor core idle during its per-tile barrier waits
+// and commits; two issuers (tiles alternate between them) hide each other's.
+// With two, the stage ring is split in halves, one per issuer, so that every
+// ring slot still has a single consumer taking its phases in order (mbarrier
+// parity waits are only unambiguous one phase ahead).
+constexpr int kMmaIssuers = 2;
 template <int BN>
 constexpr int halo_threads() {
-  return 64 + 32 * halo_epi_warps<BN>();
+  return 32 * (1 + halo_epi_warps<BN>() + kMmaIssuers);  // producer, epilogue, issuers (warp 1 and the last)
 }
 
 // Epilogue of 8 consecutive output channels of one pixel (full-width fast path
@@ -182,8 +191,9 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
   constexpr int kCols = BN / kColBlocks;        // columns per epilogue warp
   constexpr int CW = kCols >= 32 ? 32 : 16;     // columns per TMEM load
   constexpr int kChunks = kCols / CW;
-  // accumulator buffers in TMEM: up to 4, so the MMA can run several tiles ahead of the epilogue
-  constexpr int kAcc = BN <= 128 ? 4 : 2;
+  // accumulator buffers in TMEM (256-512 columns): the MMA runs up to kAcc tiles ahead of the epilogue
+  constexpr int kAcc = BN <= 16 ? 16 : (BN <= 32 ? 8 : (BN <= 128 ? 4 : 2));
+  static_assert(kAcc <= kMaxAcc && kAcc % (4 / halo_col_blocks<BN>()) == 0, "accumulator buffers per tile group");
   constexpr uint32_t kTmemCols = (kAcc * BN <= 32) ? 32 : (kAcc * BN <= 64) ? 64 : (kAcc * BN <= 128) ? 128 : (kAcc * BN <= 256) ? 256 : 512;
   constexpr int kCS = kF16 ? 8 : 16;  // tensor-map elements per 16-byte chunk
 
@@ -194,8 +204,8 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.bar_offset);
   uint64_t* empty = full + p.stages;
   uint64_t* acc_full = full + 2 * p.stages;  // [kAcc]
-  uint64_t* acc_empty = acc_full + 4;        // [kAcc]
-  uint64_t* w_full = acc_empty + 4;
+  uint64_t* acc_empty = acc_full + kMaxAcc;  // [kAcc]
+  uint64_t* w_full = acc_empty + kMaxAcc;
   uint64_t* sb_full = w_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sb_full + 1);
   const int box_bytes = sp.slab_bytes / p.boxes_per_slab;
@@ -210,11 +220,11 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
       mbar_init(&acc_empty[b], 4 * kColBlocks);  // the warps of the tile group that drains buffer b
     }
     mbar_init(&w_full[0], 1);
-    mbar_init(&w_full[1], 1);
+    mbar_init(&w_full[1], p.issuers);  // every active issuer releases the old weights
     mbar_init(sb_full, 1);
     fence_mbar_init();
   }
-  if (threadIdx.x < kAmaxRing * (16 + 4)) reinterpret_cast<uint32_t*>(smem + sp.am_offset)[threadIdx.x] = 0u;
+  for (int i = threadIdx.x; i < kAmaxRing * (16 + 4); i += blockDim.x) reinterpret_cast<uint32_t*>(smem + sp.am_offset)[i] = 0u;
   if (warp == 0 && lane == 0) tma_prefetch_desc(&act_map);
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -241,18 +251,36 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
       bulk_load(smem + sp.sb_offset, p.w_scale, static_cast<uint32_t>(4 * p.oc_alloc), sb_full);
       bulk_load(smem + sp.sb_offset + 4 * p.oc_alloc, p.bias, static_cast<uint32_t>(4 * p.oc_alloc), sb_full);
     }
-    int s = 0, it = 0, cur_n = -1, wloads = 0;
-    uint32_t ph = 0;
+    // Lane-parallel issue: the CTA's stages (tile i, slab pair pr) are numbered q = i * pairs + pr
+    // and handed out in groups of up to min(32, stages) consecutive stages with one weight tile;
+    // lane j of the warp computes stage q0 + j's coordinates, waits for its ring slot and issues
+    // its boxes, so the per-stage integer arithmetic and barrier latencies overlap across lanes.
+    const int my_tiles = static_cast<int>(blockIdx.x) < p.total_tiles
+                             ? (p.total_tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                             : 0;
+    const int total_q = my_tiles * p.slab_pairs;
+    const int R = p.issuers, H = p.stages / p.issuers;  // rings and slots per ring
+    const int group = min(32, H);
+    const int per_img = p.tiles_w * p.tiles_h;
+    const int nbox = 2 * p.boxes_per_slab;
+    const uint32_t stage_tx = static_cast<uint32_t>(nbox * p.halo_rows * kSlotBytes);
+    int cur_n = -1, wloads = 0;
     bool ok = true;
-    for (int k = blockIdx.x, i = 0; k < p.total_tiles && ok; k += gridDim.x, ++i) {
-      const int t = p.contiguous ? run_start + i : k;
+    for (int q0 = 0; q0 < total_q && ok;) {
+      const int q = q0 + lane;
+      const int i = q / p.slab_pairs;
+      const int pr = q - i * p.slab_pairs;
+      const int t = p.contiguous ? run_start + i : static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
       const int n_tile = t / p.m_tiles;
       const int m_tile = t - n_tile * p.m_tiles;
-      const int per_img = p.tiles_w * p.tiles_h;
       const int img = m_tile / per_img;
       const int r = m_tile - img * per_img;
       const int oh0 = (r / p.tiles_w) * p.th, ow0 = (r % p.tiles_w) * p.tw;
-      if (n_tile != cur_n) {
+      const int n_first = __shfl_sync(0xffffffffu, n_tile, 0);
+      // n-tiles never decrease along q: the stages of this group form a prefix of the lanes
+      const bool mine = lane < group && q < total_q && n_tile == n_first;
+      const int count = __popc(__ballot_sync(0xffffffffu, mine));
+      if (n_first != cur_n) {
         // a new weight tile: wait until every MMA reading the old one has completed
         if (wloads > 0 && !mbar_wait_bounded(&w_full[1], (wloads - 1) & 1, p.status, kStatusTimeoutEmpty)) {
           ok = false;
@@ -260,48 +288,47 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
         }
         if (lane == 0) {
           mbar_arrive_expect_tx(&w_full[0], static_cast<uint32_t>(p.w_tile_bytes));
-          const uint8_t* src = p.w_packed + static_cast<size_t>(n_tile) * p.w_tile_bytes;
+          const uint8_t* src = p.w_packed + static_cast<size_t>(n_first) * p.w_tile_bytes;
           for (int off = 0; off < p.w_tile_bytes; off += 32768)
             bulk_load(smem + sp.b_offset + off, src + off, static_cast<uint32_t>(min(32768, p.w_tile_bytes - off)),
                       &w_full[0]);
         }
-        cur_n = n_tile;
+        __syncwarp();
+        cur_n = n_first;
         ++wloads;
       }
-      for (int pr = 0; pr < p.slab_pairs; ++pr) {
-        if (it >= p.stages && !mbar_wait_bounded(&empty[s], ph ^ 1u, p.status, kStatusTimeoutEmpty)) {
-          ok = false;
-          break;
-        }
-        if (lane == 0)
-          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(2 * p.boxes_per_slab * p.halo_rows * kSlotBytes));
-        __syncwarp();
-        const int nbox = 2 * p.boxes_per_slab;
-        if (lane < nbox) {
-          const int which = lane / p.boxes_per_slab;  // slab of the pair
-          const int box = lane - which * p.boxes_per_slab;
-          const int slab = 2 * pr + which;
-          const int sn = slab < p.slabs ? img * p.slabs + slab : p.n_img * p.slabs;  // odd count: zero slab
-          uint8_t* dst = smem + s * sp.stage_bytes + which * sp.slab_bytes + box * box_bytes;
-          if (p.stride == 2) {
-            const int phr = box >> 1, phc = box & 1;
-            tma_load_5d(dst, &act_map, &full[s], kCS * (ow0 - 1), phc, phr, oh0 - 1, sn);
-          } else if (p.ksize == 3) {
-            tma_load_3d(dst, &act_map, &full[s], kCS * (ow0 - 1), oh0 - 1, sn);
-          } else {
-            tma_load_3d(dst, &act_map, &full[s], kCS * ow0, oh0, sn);
+      bool lane_ok = true;
+      if (mine) {
+        // tile i's stages go to ring i % R, in that ring's own order
+        const int qr = (i / R) * p.slab_pairs + pr;
+        const int s = (i % R) * H + qr % H;
+        const uint32_t ph = static_cast<uint32_t>(qr / H) & 1u;
+        lane_ok = qr < H || mbar_wait_bounded(&empty[s], ph ^ 1u, p.status, kStatusTimeoutEmpty);
+        if (lane_ok) {
+          mbar_arrive_expect_tx(&full[s], stage_tx);
+          for (int b = 0; b < nbox; ++b) {
+            const int which = b >= p.boxes_per_slab ? 1 : 0;  // slab of the pair
+            const int box = b - which * p.boxes_per_slab;
+            const int slab = 2 * pr + which;
+            const int sn = slab < p.slabs ? img * p.slabs + slab : p.n_img * p.slabs;  // odd count: zero slab
+            uint8_t* dst = smem + s * sp.stage_bytes + which * sp.slab_bytes + box * box_bytes;
+            if (p.stride == 2) {
+              tma_load_5d(dst, &act_map, &full[s], kCS * (ow0 - 1), box & 1, box >> 1, oh0 - 1, sn);
+            } else if (p.ksize == 3) {
+              tma_load_3d(dst, &act_map, &full[s], kCS * (ow0 - 1), oh0 - 1, sn);
+            } else {
+              tma_load_3d(dst, &act_map, &full[s], kCS * ow0, oh0, sn);
+            }
           }
         }
-        ++it;
-        if (++s == p.stages) {
-          s = 0;
-          ph ^= 1u;
-        }
       }
+      ok = __all_sync(0xffffffffu, lane_ok);
+      q0 += count;
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+  } else if (warp == 1 || warp == 2 + kEpiWarps) {
+    // ------------------------------------------------------------ MMA issuers
+    const int me = warp == 1 ? 0 : 1;  // issues the tiles i with i % p.issuers == me, from ring me
+    if (lane == 0 && me < p.issuers) {
       const uint32_t idesc = make_idesc<kF16>(BN);
       // descriptor of (stage 0, tap 0) and per-tap start offsets, in 16-byte descriptor units
       const uint64_t a_desc0 = smem_desc_kmajor_noswizzle(smem_u32(smem), sp.slab_bytes, 128);
@@ -321,58 +348,78 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
         }
         tap_off[tap] = off >> 4;
       }
-      int s = 0, u = 0, cur_n = -1, wloads = 0;
+      const int H = p.stages / p.issuers;
+      int s = me * H, cur_n = -1, wloads = 0;  // s, ph: position in this issuer's ring
       uint32_t ph = 0;
-      bool ok = true;
+      bool ok = true, need_w = false;
+      int n_tile = -1, n_end = 0;  // current n-tile and the first tile index past it (no division per tile)
       for (int k = blockIdx.x, i = 0; k < p.total_tiles && ok; k += gridDim.x, ++i) {
-      const int t = p.contiguous ? run_start + i : k;
-        const int n_tile = t / p.m_tiles;
+        const int t = p.contiguous ? run_start + i : k;
+        if (t >= n_end) {
+          n_tile = t / p.m_tiles;
+          n_end = (n_tile + 1) * p.m_tiles;
+        }
         if (n_tile != cur_n) {
-          if (wloads > 0) tc_commit(&w_full[1]);  // releases the old weights once prior MMAs finish
-          if (!mbar_wait_bounded(&w_full[0], wloads & 1, p.status, kStatusTimeoutFull)) {
-            ok = false;
-            break;
+          // every issuer releases the old weights at the change (after its own MMAs that read
+          // them), once it has seen them arrive: its releases then stay one per weight load
+          if (wloads > 0) {
+            if (need_w && !mbar_wait_bounded(&w_full[0], (wloads - 1) & 1, p.status, kStatusTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            need_w = false;
+            tc_commit(&w_full[1]);
           }
-          tc_fence_after();
           cur_n = n_tile;
           ++wloads;
+          need_w = true;
         }
-        const int buf = u % kAcc;
-        if (u >= kAcc) {
-          if (!mbar_wait_bounded(&acc_empty[buf], ((u / kAcc) - 1) & 1, p.status, kStatusTimeoutAccEmpty)) {
-            ok = false;
-            break;
+        if (i % p.issuers == me) {
+          if (need_w) {
+            if (!mbar_wait_bounded(&w_full[0], (wloads - 1) & 1, p.status, kStatusTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            need_w = false;
           }
-          tc_fence_after();
-        }
-        const uint32_t d = tmem_base + buf * BN;
-        uint64_t bd = b_desc0;
-        for (int pr = 0; pr < p.slab_pairs; ++pr) {
-          if (!mbar_wait_bounded(&full[s], ph, p.status, kStatusTimeoutFull)) {
-            ok = false;
-            break;
+          const int u = i;
+          const int buf = u % kAcc;
+          if (u >= kAcc) {
+            if (!mbar_wait_bounded(&acc_empty[buf], ((u / kAcc) - 1) & 1, p.status, kStatusTimeoutAccEmpty)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
           }
-          tc_fence_after();
-          const uint64_t ad = a_desc0 + s * stage_step;
-          if (p.taps == 9) {
+          const uint32_t d = tmem_base + buf * BN;
+          uint64_t bd = b_desc0;
+          for (int pr = 0; pr < p.slab_pairs; ++pr) {
+            if (!mbar_wait_bounded(&full[s], ph, p.status, kStatusTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t ad = a_desc0 + s * stage_step;
+            if (p.taps == 9) {
 #pragma unroll
-            for (int tap = 0; tap < 9; ++tap) {
-              tc_mma<kF16>(d, ad + tap_off[tap], bd, idesc, (pr | tap) ? 1u : 0u);
+              for (int tap = 0; tap < 9; ++tap) {
+                tc_mma<kF16>(d, ad + tap_off[tap], bd, idesc, (pr | tap) ? 1u : 0u);
+                bd += b_step;
+              }
+            } else {
+              tc_mma<kF16>(d, ad, bd, idesc, pr ? 1u : 0u);
               bd += b_step;
             }
-          } else {
-            tc_mma<kF16>(d, ad, bd, idesc, pr ? 1u : 0u);
-            bd += b_step;
+            tc_commit(&empty[s]);
+            if (++s == (me + 1) * H) {
+              s = me * H;
+              ph ^= 1u;
+            }
           }
-          tc_commit(&empty[s]);
-          if (++s == p.stages) {
-            s = 0;
-            ph ^= 1u;
-          }
+          if (!ok) break;
+          tc_commit(&acc_full[buf]);
         }
-        if (!ok) break;
-        tc_commit(&acc_full[buf]);
-        ++u;
       }
     }
   } else {

@@ -302,3 +302,39 @@ def test_stem_image_input(n, h, w, oc, s, silu):
     am = amax.cpu().numpy()
     assert np.array_equal(am[:, 1:1 + oc // 16], want)
     assert not am[:, 0].any() and not am[:, 1 + oc // 16:].any()
+
+
+@pytest.mark.parametrize("n,ic,h,w,oc,k,s,block_n", [
+    (256, 128, 20, 20, 128, 3, 2, 0),   # few ring stages (large resident weights), 1-2 tiles per CTA
+    (256, 512, 10, 10, 256, 1, 1, 0),   # a whole tile's slab pairs fill the ring
+    (64, 64, 10, 10, 256, 3, 1, 64),    # 4 weight tiles, fewer M tiles than CTAs: weight reloads mid-run
+    (64, 16, 40, 40, 16, 3, 1, 0),      # narrow: deep ring, two MMA issuers
+])
+def test_halo_pipeline_corner_cases_match_slot_kernel(n, ic, h, w, oc, k, s, block_n):
+    """Halo-tile pipeline corner cases (ring depth vs tile stages, weight reloads, issuer split):
+    int32 accumulators equal the slot-streaming kernel's, and no pipeline wait gives up."""
+    torch = _torch()
+    from aexrt_b200 import ops
+
+    rng = np.random.default_rng(n + ic + oc)
+    x = seeded_act(rng, (n, ic, h, w))
+    weight = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    wq, w_scale = ops.quantize_conv_weight_int8(weight)
+    xt = torch.from_numpy(x).cuda()
+    amax = ops.act_amax(xt, ops.LAYOUT_NCHW_F16)
+    q, rec = ops.act_quantize(xt, amax, 0, ops.LAYOUT_NCHW_F16, consumer_stride=s)
+    accs = []
+    for variant in (1, 2):
+        plan = ops.ConvPlan.int8(n, ic, h, w, oc, k, s, wq, w_scale, bias, block_n=block_n | (variant << 16))
+        assert plan.info.variant == variant
+        d = plan.desc
+        dump = torch.zeros((n * d.out_h * d.out_w, oc), dtype=torch.int32, device="cuda")
+        am = torch.zeros((n, (oc + 15) // 16), dtype=torch.int32, device="cuda")
+        out = plan.run(q, rec, amax_out=am, acc_dump=dump)
+        torch.cuda.synchronize()
+        assert plan.status() == 0
+        accs.append((dump.cpu(), out.cpu(), am.cpu()))
+    assert torch.equal(accs[0][0], accs[1][0])
+    assert torch.equal(accs[0][1], accs[1][1])
+    assert torch.equal(accs[0][2], accs[1][2])
