@@ -317,19 +317,26 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   p->total_tiles = static_cast<int>(d.batch) * p->tiles_h * p->tiles_w * p->n_tiles;
 
   // ---- halo variant: per-tensor int8 or fp16, when the whole weight tile fits next to >= 2 stages
+  // (with an automatic tile width, narrower output-channel tiles are tried before giving up)
   if (!p->pg && variant != 1) {
     int tw = 0, th = 0, pitch = 0;
     const int taps = kk;
     const int pairs = (p->slabs + 1) / 2;
-    const int w_tile = pairs * taps * 2 * p->bn * 16;
-    if (pick_halo_tile(static_cast<int>(d.out_h), static_cast<int>(d.out_w), p->k, p->stride, f16 ? 32 : 16, tw, th,
-                       pitch)) {
+    const bool tile_ok = pick_halo_tile(static_cast<int>(d.out_h), static_cast<int>(d.out_w), p->k, p->stride,
+                                        f16 ? 32 : 16, tw, th, pitch);
+    for (int bn = p->bn; tile_ok && !p->halo && bn >= 16; bn = block_n ? 0 : bn / 2) {
+      const int n_tiles = (oc + bn - 1) / bn;
+      const int oc_alloc = n_tiles * bn;
+      const int w_tile = pairs * taps * 2 * bn * 16;
       const int halo_h = p->k == 1 ? th : (p->stride == 1 ? th + 2 : th + 1);
       const int boxes = p->stride == 2 ? 4 : 1;
-      const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, p->oc_alloc);
+      const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, oc_alloc);
       const int budget = kMaxConvSmem - 1024;
       const int st = std::min(16, (budget - one.total_bytes) / one.stage_bytes + 1);
       if (st >= 2) {
+        p->bn = bn;
+        p->n_tiles = n_tiles;
+        p->oc_alloc = oc_alloc;
         p->halo = true;
         p->order = static_cast<int>(order);
         p->tw = tw;

@@ -227,9 +227,98 @@ class CompiledYolo:
             self.launch(torch.cuda.current_stream(self.device).cuda_stream)
         return self.output
 
+    # ------------------------------------------------------------------ streaming
+    def capture_slots(self, slots: int = 2) -> None:
+        """Records one graph per input/output slot for :meth:`stream` (double-buffered I/O).
+
+        The slots own their image and output buffers; the activations between the layers are
+        shared, since the graphs replay one after another on the compute stream."""
+        torch = _torch()
+        n, p = self.batch, self.program
+        self.slot_images, self.slot_outputs, self.slot_graphs = [], [], []
+        images, output, graph = self.images, self.output, self.graph
+        for _ in range(slots):
+            self.images = torch.zeros((n, p.in_channels, p.imgsz, p.imgsz), dtype=torch.float32, device=self.device)
+            self.output = torch.zeros((n, 4 + p.nc, p.anchors), dtype=torch.float32, device=self.device)
+            self.graph = None
+            self.capture()
+            self.slot_images.append(self.images)
+            self.slot_outputs.append(self.output)
+            self.slot_graphs.append(self.graph)
+        self.images, self.output, self.graph = images, output, graph
+        self.compute_stream = torch.cuda.Stream(device=self.device)
+        self.upload_stream = torch.cuda.Stream(device=self.device)
+        self.download_stream = torch.cuda.Stream(device=self.device)
+
+    def stream(self, host_inputs, host_outputs) -> None:
+        """Runs len(host_inputs) batches host -> device -> host with the copies of one batch
+        overlapping the forward of the previous one (uploads, forwards and read-backs run on three
+        streams; the caller's current stream waits for all of them, so synchronize it before
+        reading host_outputs).
+
+        host_inputs[k] (pinned fp32 [batch, 3, imgsz, imgsz]) is uploaded into slot k % slots,
+        its forward replays that slot's graph, and the detections are read back into
+        host_outputs[k % len(host_outputs)] (pinned fp32 [batch, 4 + nc, anchors])."""
+        torch = _torch()
+        slots = len(self.slot_graphs)
+        cs, us, ds = self.compute_stream, self.upload_stream, self.download_stream
+        if not hasattr(self, "_slot_events"):
+            ev = lambda: [torch.cuda.Event() for _ in range(slots)]  # noqa: E731
+            self._slot_events = (ev(), ev(), ev())  # uploaded, computed, downloaded
+        uploaded, computed, downloaded = self._slot_events
+        cur = torch.cuda.current_stream(self.device)
+        for st in (us, cs, ds):
+            st.wait_stream(cur)
+        for k, host in enumerate(host_inputs):
+            j = k % slots
+            with torch.cuda.stream(us):
+                if k >= slots:
+                    us.wait_event(computed[j])  # the slot's previous forward has read its images
+                self.slot_images[j].copy_(host, non_blocking=True)
+                uploaded[j].record(us)
+            with torch.cuda.stream(cs):
+                cs.wait_event(uploaded[j])
+                if k >= slots:
+                    cs.wait_event(downloaded[j])  # the slot's previous detections have been read back
+                self.slot_graphs[j].replay()
+                computed[j].record(cs)
+            with torch.cuda.stream(ds):
+                ds.wait_event(computed[j])
+                host_outputs[k % len(host_outputs)].copy_(self.slot_outputs[j], non_blocking=True)
+                downloaded[j].record(ds)
+        for st in (us, cs, ds):
+            cur.wait_stream(st)
+
     def status(self) -> int:
         """OR of every plan's device status word (non-zero: a pipeline wait gave up)."""
         st = 0
         for p in self.plans.values():
             st |= p.status()
         return st
+
+
+def main(argv=None) -> int:
+    """Runs eager forwards of the synthetic YOLOv8n model (profiling entry: one forward = one launch list)."""
+    import argparse
+
+    from . import yolo
+
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--imgsz", type=int, default=320)
+    ap.add_argument("--forwards", type=int, default=2)
+    a = ap.parse_args(argv)
+    torch = _torch()
+    program = yolo.build_yolov8n(nc=4, imgsz=a.imgsz, seed=0)
+    eng = CompiledYolo(program, a.batch)
+    x = torch.from_numpy(np.random.default_rng(0).uniform(0, 1, (a.batch, 3, a.imgsz, a.imgsz)).astype(np.float32))
+    x = x.to(eng.device)
+    for _ in range(a.forwards):
+        eng.forward(x)
+    torch.cuda.synchronize(eng.device)
+    print(f"{a.forwards} forwards of batch {a.batch}: {eng.launches_per_run - 1} kernels each, status {eng.status()}")
+    return 0 if eng.status() == 0 else 1
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

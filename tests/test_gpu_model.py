@@ -106,3 +106,19 @@ def test_graph_replay_matches_eager_and_batch_independence(v8n):
     torch.cuda.synchronize()
     assert torch.equal(single[0], eager[2])
     assert eng4.status() == 0 and eng1.status() == 0
+
+
+def test_streaming_slots_match_single_forwards(v8n):
+    """The double-buffered streaming API returns, per batch, what a plain forward returns."""
+    torch = _torch()
+    eng = _engine(v8n, 2)
+    batches = [_images(2, seed=10 + k) for k in range(5)]
+    want = [eng.forward(torch.from_numpy(b).cuda()).clone().cpu() for b in batches]
+    eng.capture_slots(2)
+    host_in = [torch.from_numpy(b).pin_memory() for b in batches]
+    host_out = [torch.empty_like(want[0]).pin_memory() for _ in batches]
+    eng.stream(host_in, host_out)
+    torch.cuda.synchronize()
+    for k in range(len(batches)):
+        assert torch.equal(host_out[k], want[k]), k
+    assert eng.status() == 0
