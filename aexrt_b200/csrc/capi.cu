@@ -124,6 +124,8 @@ struct AexrtB200ConvPlan {
   void* d_w = nullptr;   // [n_tile][q_total][bn][16 bytes]
   float* d_scale = nullptr;
   float* d_bias = nullptr;
+  // SiLU plans: [scale/2 | bias/2] for the halo epilogue, which forms h = y/2 directly
+  float* d_half_sb = nullptr;
   uint32_t* d_status = nullptr;
   int device = 0;
   // image stem (fp16, 3 input channels, 3x3): direct kernel reading fp32 NCHW images
@@ -436,6 +438,15 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
     for (int o = 0; o < oc; ++o) sc[o] = f16 ? 1.0f : scale[o];
     ok = cuda_ok(cudaMalloc(reinterpret_cast<void**>(&p->d_scale), sizeof(float) * p->oc_alloc), "cudaMalloc(scale)") &&
          cuda_ok(cudaMemcpy(p->d_scale, sc.data(), sizeof(float) * p->oc_alloc, cudaMemcpyHostToDevice), "copy scale");
+    if (ok && kind == AEXRT_B200_KIND_CONV_SILU) {
+      std::vector<float> hsb(2 * static_cast<size_t>(p->oc_alloc), 0.0f);
+      for (int o = 0; o < oc; ++o) {
+        hsb[o] = 0.5f * sc[o];
+        hsb[p->oc_alloc + o] = 0.5f * bias[o];
+      }
+      ok = cuda_ok(cudaMalloc(reinterpret_cast<void**>(&p->d_half_sb), sizeof(float) * hsb.size()), "cudaMalloc(sb)") &&
+           cuda_ok(cudaMemcpy(p->d_half_sb, hsb.data(), sizeof(float) * hsb.size(), cudaMemcpyHostToDevice), "copy sb");
+    }
   }
   if (ok) {
     int sms = 0;
@@ -542,8 +553,9 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     h.w_tile_bytes = p->w_tile_bytes;
     h.oc_alloc = p->oc_alloc;
     h.scale_rec = scale_rec;
-    h.w_scale = p->d_scale;
-    h.bias = p->d_bias;
+    // SiLU epilogues take half the scale and bias (they form h = y/2, see conv_halo.cuh)
+    h.w_scale = p->d_half_sb ? p->d_half_sb : p->d_scale;
+    h.bias = p->d_half_sb ? p->d_half_sb + p->oc_alloc : p->d_bias;
     h.res = static_cast<const __half*>(res);
     h.res_ldc = static_cast<int>(res_ldc);
     h.res_coff = static_cast<int>(res_coff);
@@ -925,6 +937,7 @@ void aexrt_b200_conv_plan_destroy(AexrtB200ConvPlan* p) {
   if (p->d_w) cudaFree(p->d_w);
   if (p->d_scale) cudaFree(p->d_scale);
   if (p->d_bias) cudaFree(p->d_bias);
+  if (p->d_half_sb) cudaFree(p->d_half_sb);
   if (p->d_status) cudaFree(p->d_status);
   delete p;
 }

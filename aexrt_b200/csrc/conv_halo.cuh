@@ -115,7 +115,11 @@ constexpr int halo_threads() {
 // when all 8 channels exist and the row is 16-byte aligned): scale, bias,
 // SiLU, residual, fp16 store.  Returns the max |fp16 output| of the 8 values.
 // `sscale` / `sbias` point at this 8-column group's weight scale and bias in the
-// CTA's resident weight tile (shared memory; zero past the last channel).
+// CTA's resident weight tile (shared memory; zero past the last channel).  For
+// SiLU layers both vectors hold half the plan's values, so the affine step
+// yields h = y/2 directly (exact: halving commutes with rounding) and
+// SiLU(y) = y * sigmoid(y) = h + h * tanh(h).  This scalar form serves
+// partial chunks; halo_epilogue16_packed below is the full-chunk path.
 template <bool kF16, bool kSilu, bool kRes>
 __device__ __forceinline__ float halo_epilogue8(const ConvHaloParams& p, const uint32_t* v, float in_scale, int oc,
                                                 const float* sscale, const float* sbias, bool valid, __half* out_row,
@@ -128,7 +132,7 @@ __device__ __forceinline__ float halo_epilogue8(const ConvHaloParams& p, const u
     const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
     if constexpr (kF16) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = __uint_as_float(v[i]) + bb[i];
+      for (int i = 0; i < 8; ++i) y[i] = kSilu ? fmaf(__uint_as_float(v[i]), 0.5f, bb[i]) : __uint_as_float(v[i]) + bb[i];
     } else {
       const float4 s0 = *reinterpret_cast<const float4*>(sscale);
       const float4 s1 = *reinterpret_cast<const float4*>(sscale + 4);
@@ -138,8 +142,9 @@ __device__ __forceinline__ float halo_epilogue8(const ConvHaloParams& p, const u
     }
   }
   if constexpr (kSilu) {
+    // y holds h = y/2 (halved scale and bias): SiLU(y) = h + h * tanh(h)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = silu_fast(y[i]);
+    for (int i = 0; i < 8; ++i) y[i] = fmaf(y[i], tanh_approx(y[i]), y[i]);
   }
   const bool vec = n_valid >= 8 && p.out_vec;
   if constexpr (kRes) {
@@ -180,6 +185,97 @@ __device__ __forceinline__ float halo_epilogue8(const ConvHaloParams& p, const u
   }
   const __half2 m = __hmax2(__hmax2(__habs2(hv[0]), __habs2(hv[1])), __hmax2(__habs2(hv[2]), __habs2(hv[3])));
   return valid ? fmaxf(__low2float(m), __high2float(m)) : 0.0f;
+}
+
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// The epilogue of 16 consecutive output channels of one pixel when all 16
+// exist and the output (and residual) rows allow 16-byte accesses: the same
+// arithmetic as halo_epilogue8, element for element, with the affine, SiLU
+// and residual steps on packed fp32 pairs (fma/mul/add .f32x2).  Returns the
+// max |fp16 output| as a half2 pair (the caller folds it).
+template <bool kF16, bool kSilu, bool kRes>
+__device__ __forceinline__ __half2 halo_epilogue16_packed(const uint32_t* v, float in_scale, const float* sscale,
+                                                          const float* sbias, bool valid, __half* out,
+                                                          const __half* res) {
+  const uint64_t s2 = f2_pack(in_scale, in_scale);
+  const uint64_t half2c = f2_pack(0.5f, 0.5f);
+  __half2 m = __float2half2_rn(0.0f);
+#pragma unroll
+  for (int h8 = 0; h8 < 2; ++h8) {
+    const float4 b0 = *reinterpret_cast<const float4*>(sbias + 8 * h8);
+    const float4 b1 = *reinterpret_cast<const float4*>(sbias + 8 * h8 + 4);
+    const uint64_t bb[4] = {f2_pack(b0.x, b0.y), f2_pack(b0.z, b0.w), f2_pack(b1.x, b1.y), f2_pack(b1.z, b1.w)};
+    uint64_t y[4];
+    if constexpr (kF16) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint64_t a = f2_pack(__uint_as_float(v[8 * h8 + 2 * i]), __uint_as_float(v[8 * h8 + 2 * i + 1]));
+        y[i] = kSilu ? f2_fma(a, half2c, bb[i]) : f2_add(a, bb[i]);
+      }
+    } else {
+      const float4 c0 = *reinterpret_cast<const float4*>(sscale + 8 * h8);
+      const float4 c1 = *reinterpret_cast<const float4*>(sscale + 8 * h8 + 4);
+      const uint64_t ss[4] = {f2_pack(c0.x, c0.y), f2_pack(c0.z, c0.w), f2_pack(c1.x, c1.y), f2_pack(c1.z, c1.w)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint64_t a = f2_pack(static_cast<float>(static_cast<int32_t>(v[8 * h8 + 2 * i])),
+                                   static_cast<float>(static_cast<int32_t>(v[8 * h8 + 2 * i + 1])));
+        y[i] = f2_fma(f2_mul(a, s2), ss[i], bb[i]);
+      }
+    }
+    if constexpr (kSilu) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float h0, h1;
+        f2_unpack(y[i], h0, h1);
+        y[i] = f2_fma(y[i], f2_pack(tanh_approx(h0), tanh_approx(h1)), y[i]);
+      }
+    }
+    if constexpr (kRes) {
+      if (valid) {
+        const uint4 r = *reinterpret_cast<const uint4*>(res + 8 * h8);
+        const __half2* rh = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(rh[i]);
+          y[i] = f2_add(y[i], f2_pack(f.x, f.y));
+        }
+      }
+    }
+    __align__(16) __half2 hv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float a, b;
+      f2_unpack(y[i], a, b);
+      hv[i] = __floats2half2_rn(a, b);
+      m = __hmax2(m, __habs2(hv[i]));
+    }
+    if (valid) *reinterpret_cast<uint4*>(out + 8 * h8) = *reinterpret_cast<const uint4*>(hv);
+  }
+  return valid ? m : __float2half2_rn(0.0f);
 }
 
 template <bool kF16, int BN, bool kSilu, bool kRes>
@@ -501,14 +597,25 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
           for (int i = 0; i < CW; ++i)
             if (oc_c + i < p.oc) p.acc_dump[pix * p.oc + oc_c + i] = static_cast<int32_t>(v[i]);
         }
+        // the whole chunk exists and its rows allow 16-byte accesses: packed path (warp-uniform)
+        const bool packed = oc_c + CW <= p.oc && p.out_vec && (!kRes || p.res_vec);
 #pragma unroll
         for (int g = 0; g < CW / 16; ++g) {
           const int lc = oc_c + 16 * g;  // output channel (the vectors are zero-padded to oc_alloc)
-          const float m0 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g, in_scale, oc_c + 16 * g, s_scale + lc,
-                                                             s_bias + lc, valid, out_row, res_row);
-          const float m1 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g + 8, in_scale, oc_c + 16 * g + 8,
-                                                             s_scale + lc + 8, s_bias + lc + 8, valid, out_row, res_row);
-          run_max[c * (CW / 16) + g] = fmaxf(run_max[c * (CW / 16) + g], fmaxf(m0, m1));
+          float mg;
+          if (packed) {
+            const __half2 m2 = halo_epilogue16_packed<kF16, kSilu, kRes>(
+                v + 16 * g, in_scale, s_scale + lc, s_bias + lc, valid, out_row + lc,
+                kRes ? res_row + lc : nullptr);
+            mg = fmaxf(__low2float(m2), __high2float(m2));
+          } else {
+            const float m0 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g, in_scale, lc, s_scale + lc, s_bias + lc,
+                                                               valid, out_row, res_row);
+            const float m1 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g + 8, in_scale, lc + 8, s_scale + lc + 8,
+                                                               s_bias + lc + 8, valid, out_row, res_row);
+            mg = fmaxf(m0, m1);
+          }
+          run_max[c * (CW / 16) + g] = fmaxf(run_max[c * (CW / 16) + g], mg);
         }
       }
       if (p.amax_out != nullptr && !p.contiguous) {
