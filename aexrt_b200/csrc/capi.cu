@@ -872,10 +872,12 @@ AexrtB200ConvPlan* aexrt_b200_conv_plan_create_f16(const AexrtConv2DDesc* desc, 
   return p;
 }
 
-int aexrt_b200_conv_f16_image(const AexrtB200ConvPlan* p, const float* images, void* out, uint32_t out_ldc,
-                              uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride, uint32_t amax_goff,
-                              void* stream) {
+int aexrt_b200_conv_f16_image(const AexrtB200ConvPlan* p, const void* images, uint32_t layout, void* out,
+                              uint32_t out_ldc, uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride,
+                              uint32_t amax_goff, void* stream) {
   if (!p) return fail("null plan");
+  if (layout != AEXRT_B200_LAYOUT_NCHW_F16 && layout != AEXRT_B200_LAYOUT_NCHW_F32)
+    return fail("images must be NCHW fp16 or fp32");
   if (!p->image_input) return fail("plan does not take images directly (need fp16, 3 input channels, 3x3, oc %% 16 == 0 <= 64)");
   if (!images || !out) return fail("null input/output pointer");
   const uint32_t oc = p->desc.out_channels;
@@ -888,20 +890,27 @@ int aexrt_b200_conv_f16_image(const AexrtB200ConvPlan* p, const float* images, v
   const dim3 grid((per_img + 255) / 256, p->desc.batch);
   auto* st = static_cast<cudaStream_t>(stream);
   const bool silu = p->kind == AEXRT_B200_KIND_CONV_SILU;
-  const auto* x = images;
   auto* o = static_cast<__half*>(out);
   const int h = static_cast<int>(p->desc.in_h), w = static_cast<int>(p->desc.in_w), s = p->stride;
-#define AEXRT_STEM_LAUNCH(OC)                                                                                    \
-  (silu ? stem_conv_kernel<OC, true><<<grid, 256, 0, st>>>(x, h, w, oh, ow, s, o, out_ldc, out_coff, amax_out,   \
-                                                           amax_stride, amax_goff, p->stem)                      \
-        : stem_conv_kernel<OC, false><<<grid, 256, 0, st>>>(x, h, w, oh, ow, s, o, out_ldc, out_coff, amax_out,  \
-                                                            amax_stride, amax_goff, p->stem))
+#define AEXRT_STEM_LAUNCH_T(OC, T)                                                                                   \
+  (silu ? stem_conv_kernel<OC, true, T><<<grid, 256, 0, st>>>(static_cast<const T*>(images), h, w, oh, ow, s, o,        \
+                                                              out_ldc, out_coff, amax_out, amax_stride, amax_goff,    \
+                                                              p->stem)                                                \
+        : stem_conv_kernel<OC, false, T><<<grid, 256, 0, st>>>(static_cast<const T*>(images), h, w, oh, ow, s, o,       \
+                                                               out_ldc, out_coff, amax_out, amax_stride, amax_goff,   \
+                                                               p->stem))
+#define AEXRT_STEM_LAUNCH(OC)                      \
+  if (layout == AEXRT_B200_LAYOUT_NCHW_F16)        \
+    AEXRT_STEM_LAUNCH_T(OC, __half);               \
+  else                                             \
+    AEXRT_STEM_LAUNCH_T(OC, float)
   switch (oc) {
     case 16: AEXRT_STEM_LAUNCH(16); break;
     case 32: AEXRT_STEM_LAUNCH(32); break;
     case 48: AEXRT_STEM_LAUNCH(48); break;
     default: AEXRT_STEM_LAUNCH(64); break;
   }
+#undef AEXRT_STEM_LAUNCH_T
 #undef AEXRT_STEM_LAUNCH
   return cuda_ok(cudaGetLastError(), "stem conv launch") ? 1 : 0;
 }

@@ -1,5 +1,5 @@
 // Direct fp16 conv for the image stem: 3 input channels, 3x3 window, read
-// straight from the fp32 NCHW image batch.
+// straight from the NCHW image batch (fp16 or fp32).
 //
 // The stem of the YOLO graphs (Conv(3, c, 3, 2) + SiLU, the reference's first
 // fp16 command) has K = 27: a tensor-core tile would need the image repacked
@@ -27,9 +27,13 @@ struct StemWeights {
   float b[kStemMaxOC];
 };
 
-// grid (ceil(oh*ow / 256), n); block 256, one output pixel per thread.
-template <int OC, bool kSilu>
-__global__ void __launch_bounds__(256) stem_conv_kernel(const float* __restrict__ x, int h, int w, int oh, int ow,
+__device__ __forceinline__ float stem_load(const float* p) { return __ldg(p); }
+__device__ __forceinline__ float stem_load(const __half* p) { return __half2float(__ldg(p)); }
+
+// grid (ceil(oh*ow / 256), n); block 256, one output pixel per thread.  TIn: float or
+// __half images (fp16 images are already what the conv rounds its inputs to).
+template <int OC, bool kSilu, typename TIn>
+__global__ void __launch_bounds__(256) stem_conv_kernel(const TIn* __restrict__ x, int h, int w, int oh, int ow,
                                                         int stride, __half* __restrict__ out, int out_ldc,
                                                         int out_coff, uint32_t* __restrict__ amax, int amax_stride,
                                                         int amax_goff, const __grid_constant__ StemWeights wt) {
@@ -44,7 +48,7 @@ __global__ void __launch_bounds__(256) stem_conv_kernel(const float* __restrict_
   for (int g = 0; g < kGroups; ++g) run[g] = 0.0f;
   const int npix = oh * ow;
   const size_t plane = static_cast<size_t>(h) * w;
-  const float* img = x + static_cast<size_t>(n) * kStemIC * plane;
+  const TIn* img = x + static_cast<size_t>(n) * kStemIC * plane;
   // one pixel per thread: no loop for the compiler to hoist the weight operands out of
   const int pix = blockIdx.x * blockDim.x + threadIdx.x;
   if (pix < npix) {
@@ -59,7 +63,7 @@ __global__ void __launch_bounds__(256) stem_conv_kernel(const float* __restrict_
         for (int kw = 0; kw < 3; ++kw) {
           const int iy = iy0 + kh, ix = ix0 + kw;
           const bool in = iy >= 0 && iy < h && ix >= 0 && ix < w;
-          const float v = in ? __ldg(img + ic * plane + static_cast<size_t>(iy) * w + ix) : 0.0f;
+          const float v = in ? stem_load(img + ic * plane + static_cast<size_t>(iy) * w + ix) : 0.0f;
           xv[(ic * 3 + kh) * 3 + kw] = __half2float(__float2half_rn(v));
         }
     __half* orow = out + (static_cast<size_t>(n) * npix + pix) * out_ldc + out_coff;

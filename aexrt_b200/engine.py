@@ -39,7 +39,8 @@ def _torch():
 class CompiledYolo:
     """One program compiled for one batch size on the current CUDA device."""
 
-    def __init__(self, program: YoloProgram, batch: int, device=None, block_n: Optional[Dict[str, int]] = None):
+    def __init__(self, program: YoloProgram, batch: int, device=None, block_n: Optional[Dict[str, int]] = None,
+                 image_dtype=None):
         torch = _torch()
         self.program = program
         self.batch = batch
@@ -66,7 +67,9 @@ class CompiledYolo:
             self.amax_groups[name] = g
             off += n * g
         self.amax_arena = torch.zeros(max(off, 1), dtype=torch.int32, device=self.device)
-        self.images = torch.zeros((n, p.in_channels, p.imgsz, p.imgsz), dtype=torch.float32, device=self.device)
+        # fp16 images by default (the reference feeds fp16; the stem rounds fp32 inputs to fp16 anyway)
+        self.image_dtype = torch.float16 if image_dtype is None else image_dtype
+        self.images = torch.zeros((n, p.in_channels, p.imgsz, p.imgsz), dtype=self.image_dtype, device=self.device)
         self.output = torch.zeros((n, 4 + p.nc, p.anchors), dtype=torch.float32, device=self.device)
         # ---- plans and per-command scratch
         self.steps: List[tuple] = []
@@ -110,7 +113,7 @@ class CompiledYolo:
             plan = ops.ConvPlan.fp16(n, c.ic, h, w, c.oc, c.k, c.s, c.weight, c.bias, silu=c.silu, block_n=block_n)
             if (len(c.inputs) == 1 and c.inputs[0].value == "images" and plan.info.image_input
                     and c.residual is None):
-                # the stem reads the fp32 images directly: no packed copy
+                # the stem reads the images directly: no packed copy
                 self.plans[c.name] = plan
                 self.steps.append(("stem", c, plan))
                 return
@@ -125,7 +128,7 @@ class CompiledYolo:
             s = srcs[i]
             if pt.value == "images":
                 s.ptr = self.images.data_ptr()
-                s.layout = ops.LAYOUT_NCHW_F32
+                s.layout = ops.LAYOUT_NCHW_F16 if self.image_dtype == torch.float16 else ops.LAYOUT_NCHW_F32
                 s.ldc = self.program.in_channels
                 s.coff = 0
             else:
@@ -238,7 +241,7 @@ class CompiledYolo:
         self.slot_images, self.slot_outputs, self.slot_graphs = [], [], []
         images, output, graph = self.images, self.output, self.graph
         for _ in range(slots):
-            self.images = torch.zeros((n, p.in_channels, p.imgsz, p.imgsz), dtype=torch.float32, device=self.device)
+            self.images = torch.zeros((n, p.in_channels, p.imgsz, p.imgsz), dtype=self.image_dtype, device=self.device)
             self.output = torch.zeros((n, 4 + p.nc, p.anchors), dtype=torch.float32, device=self.device)
             self.graph = None
             self.capture()
@@ -256,7 +259,7 @@ class CompiledYolo:
         streams; the caller's current stream waits for all of them, so synchronize it before
         reading host_outputs).
 
-        host_inputs[k] (pinned fp32 [batch, 3, imgsz, imgsz]) is uploaded into slot k % slots,
+        host_inputs[k] (pinned, the engine's image dtype, [batch, 3, imgsz, imgsz]) is uploaded into slot k % slots,
         its forward replays that slot's graph, and the detections are read back into
         host_outputs[k % len(host_outputs)] (pinned fp32 [batch, 4 + nc, anchors])."""
         torch = _torch()
@@ -311,7 +314,7 @@ def main(argv=None) -> int:
     torch = _torch()
     program = yolo.build_yolov8n(nc=4, imgsz=a.imgsz, seed=0)
     eng = CompiledYolo(program, a.batch)
-    x = torch.from_numpy(np.random.default_rng(0).uniform(0, 1, (a.batch, 3, a.imgsz, a.imgsz)).astype(np.float32))
+    x = torch.from_numpy(np.random.default_rng(0).uniform(0, 1, (a.batch, 3, a.imgsz, a.imgsz)).astype(np.float16))
     x = x.to(eng.device)
     for _ in range(a.forwards):
         eng.forward(x)

@@ -254,14 +254,16 @@ class ConvPlan:
         return out
 
     def run_image(self, images, out=None, out_coff: int = 0, amax_out=None, amax_goff: int = 0, stream=None):
-        """The image stem: fp32 NCHW ``images`` straight into the fp16 NHWC ``out`` (plans with info.image_input)."""
+        """The image stem: fp16 or fp32 NCHW ``images`` straight into the fp16 NHWC ``out``
+        (plans with info.image_input)."""
         torch = _torch()
         if out is None:
             out = torch.empty(self.out_shape, dtype=torch.float16, device=images.device)
         amax_stride = amax_out.shape[-1] if amax_out is not None else 0
-        check(_native.load().aexrt_b200_conv_f16_image(self._h, images.data_ptr(), out.data_ptr(), out.shape[-1],
-                                                       out_coff, _ptr(amax_out), amax_stride, amax_goff,
-                                                       _stream(stream)), "conv_f16_image")
+        layout = LAYOUT_NCHW_F16 if images.dtype == torch.float16 else LAYOUT_NCHW_F32
+        check(_native.load().aexrt_b200_conv_f16_image(self._h, images.data_ptr(), layout, out.data_ptr(),
+                                                       out.shape[-1], out_coff, _ptr(amax_out), amax_stride,
+                                                       amax_goff, _stream(stream)), "conv_f16_image")
         return out
 
     def status(self) -> int:

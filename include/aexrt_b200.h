@@ -188,16 +188,18 @@ int aexrt_b200_conv_f16(const AexrtB200ConvPlan* plan, const void* x_slab8, cons
  * Non-zero bits mean a pipeline wait gave up (see the kernel sources). */
 /* The image stem: an fp16 plan with 3 input channels, a 3x3 window (pad 1)
  * and 16/32/48/64 output channels (info.image_input == 1) read straight from
- * the fp32 NCHW image batch [batch][3][in_h][in_w], with no packed copy.
+ * the NCHW image batch [batch][3][in_h][in_w], fp16 (layout
+ * AEXRT_B200_LAYOUT_NCHW_F16) or fp32 (AEXRT_B200_LAYOUT_NCHW_F32), with no
+ * packed copy.
  * Same arithmetic as aexrt_b200_conv_f16 (fp16-rounded inputs and weights,
  * fp32 accumulation, fp32 bias + SiLU, fp16 output); out_ldc and out_coff
  * multiples of 8 (16 with amax_out), out 16-byte aligned.  Replaces the
  * reference's first fp16 conv command with its input conversion
  * (the image upload + NCHW fp16 conv of the stem in prepared replay,
  * native/aexrt_d3d12_runtime.cpp:28758-29010). */
-int aexrt_b200_conv_f16_image(const AexrtB200ConvPlan* plan, const float* images, void* out, uint32_t out_ldc,
-                              uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride, uint32_t amax_goff,
-                              void* stream);
+int aexrt_b200_conv_f16_image(const AexrtB200ConvPlan* plan, const void* images, uint32_t layout, void* out,
+                              uint32_t out_ldc, uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride,
+                              uint32_t amax_goff, void* stream);
 
 int aexrt_b200_conv_status(const AexrtB200ConvPlan* plan, uint32_t* status);
 

@@ -260,19 +260,20 @@ def test_fp16_halo_vs_slot_streaming(n, ic, h, w, oc, k, s, silu):
         assert (o - ref).abs().max().item() <= 1e-2 * max(1.0, ref.abs().max().item() / 8)
 
 
+@pytest.mark.parametrize("dtype", ["float32", "float16"])
 @pytest.mark.parametrize("n,h,w,oc,s,silu", [
     (2, 64, 64, 16, 2, True),    # the YOLOv8n stem shape, small
     (3, 33, 47, 32, 2, True),    # odd sizes: clipped windows on the right/bottom
     (2, 20, 20, 64, 1, False),
     (1, 17, 16, 48, 2, True),
 ])
-def test_stem_image_input(n, h, w, oc, s, silu):
-    """The direct stem (fp32 NCHW images in) against torch fp32 and the packed fp16 path; amax_out exact."""
+def test_stem_image_input(n, h, w, oc, s, silu, dtype):
+    """The direct stem (fp32 or fp16 NCHW images in) against torch fp32 and the packed fp16 path; amax_out exact."""
     torch = _torch()
     from aexrt_b200 import ops
 
     rng = np.random.default_rng(oc + h)
-    x = rng.uniform(0, 1, (n, 3, h, w)).astype(np.float32)
+    x = rng.uniform(0, 1, (n, 3, h, w)).astype(dtype)
     weight = rng.normal(0, 1 / np.sqrt(27), (oc, 3, 3, 3)).astype(np.float32)
     bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
     plan = ops.ConvPlan.fp16(n, 3, h, w, oc, 3, s, weight, bias, silu=silu)
@@ -283,7 +284,8 @@ def test_stem_image_input(n, h, w, oc, s, silu):
     buf = torch.full((n, oh, ow, oc + 32), 7.0, dtype=torch.float16, device="cuda")
     amax = torch.zeros((n, (oc + 32) // 16), dtype=torch.int32, device="cuda")
     plan.run_image(xt, out=buf, out_coff=16, amax_out=amax, amax_goff=1)
-    packed_out = plan.run(ops.pack_f16(xt, ops.LAYOUT_NCHW_F32, consumer_stride=s))
+    layout = ops.LAYOUT_NCHW_F16 if dtype == "float16" else ops.LAYOUT_NCHW_F32
+    packed_out = plan.run(ops.pack_f16(xt, layout, consumer_stride=s))
     torch.cuda.synchronize()
     got = buf[..., 16:16 + oc].float().cpu()
     assert torch.all(buf[..., :16] == 7.0) and torch.all(buf[..., 16 + oc:] == 7.0)
