@@ -546,8 +546,10 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     h.stages = p->stages;
     h.w_packed = static_cast<const uint8_t*>(p->d_w);
     // auto: contiguous runs when the epilogue maxes |y| for the next layer (their register
-    // folding saves the amax atomics), strided otherwise (neighbouring tiles run together)
-    h.contiguous = (p->order == 2 || (p->order == 0 && amax_out != nullptr)) ? 1 : 0;
+    // folding saves the amax atomics) or when there are several weight tiles (a run stays on
+    // one, where the strided walk reloads weights at every n-tile), strided otherwise
+    // (neighbouring tiles run together)
+    h.contiguous = (p->order == 2 || (p->order == 0 && (amax_out != nullptr || p->n_tiles > 1))) ? 1 : 0;
     // two MMA issuers when each half of the stage ring holds a whole tile's stages
     h.issuers = 2 * p->slab_pairs <= p->stages ? 2 : 1;
     h.w_tile_bytes = p->w_tile_bytes;
