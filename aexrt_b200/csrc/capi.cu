@@ -119,7 +119,9 @@ struct AexrtB200ConvPlan {
   int total_tiles = 0;
   // halo variant (conv_halo.cuh): whole weight tile resident, one halo per slab and tile
   bool halo = false;
-  int order = 0;  // halo tile order (see conv_halo.cuh): 0 auto, 1 strided, 2 contiguous runs
+  int order = 0;  // halo tile order (see conv_halo.cuh): 0 auto, 1 strided, 2 contiguous
+  // pg16 halo: K steps pair two taps of one slab, ordered by their shared-memory offset
+  int tap_pairs = 0, tap_a[5] = {0, 0, 0, 0, 0}, tap_b[5] = {-1, -1, -1, -1, -1};
   int pitch = 0, halo_rows = 0, boxes_per_slab = 1, slab_pairs = 0, taps = 1, w_tile_bytes = 0, m_tiles = 0;
   void* d_w = nullptr;   // [n_tile][q_total][bn][16 bytes]
   float* d_scale = nullptr;
@@ -176,8 +178,23 @@ HaloKernel halo_kernel_for_bn(int bn) {
   }
 }
 
+template <bool SILU, bool RES>
+HaloKernel halo_pg_kernel_for_bn(int bn) {
+  switch (bn) {
+    case 64: return {conv_halo_kernel<false, 64, SILU, RES, true>, halo_threads<64>()};
+    case 128: return {conv_halo_kernel<false, 128, SILU, RES, true>, halo_threads<128>()};
+    default: return {nullptr, 0};
+  }
+}
+
 // fp16 convs (stem, detect head) never carry a residual; the int8 convs do (C2f tail).
-HaloKernel halo_kernel_for(bool f16, int bn, bool silu, bool res) {
+// pg16 (INT8_PERGROUP) has a halo kernel for 64- and 128-wide output-channel tiles.
+HaloKernel halo_kernel_for(bool f16, int bn, bool silu, bool res, bool pg = false) {
+  if (pg) {
+    if (f16) return {nullptr, 0};
+    if (silu) return res ? halo_pg_kernel_for_bn<true, true>(bn) : halo_pg_kernel_for_bn<true, false>(bn);
+    return res ? halo_pg_kernel_for_bn<false, true>(bn) : halo_pg_kernel_for_bn<false, false>(bn);
+  }
   if (f16) return silu ? halo_kernel_for_bn<true, true, false>(bn) : halo_kernel_for_bn<true, false, false>(bn);
   if (silu) return res ? halo_kernel_for_bn<false, true, true>(bn) : halo_kernel_for_bn<false, true, false>(bn);
   return res ? halo_kernel_for_bn<false, false, true>(bn) : halo_kernel_for_bn<false, false, false>(bn);
@@ -251,9 +268,9 @@ bool check_desc_int8(const AexrtConv2DDesc& d, uint32_t kernel_id, bool pg) {
   return true;
 }
 
-cudaError_t set_halo_smem(bool f16, int bn, bool silu) {
+cudaError_t set_halo_smem(bool f16, int bn, bool silu, bool pg) {
   for (int res = 0; res < (f16 ? 1 : 2); ++res) {
-    const cudaError_t e = cudaFuncSetAttribute(halo_kernel_for(f16, bn, silu, res).fn,
+    const cudaError_t e = cudaFuncSetAttribute(halo_kernel_for(f16, bn, silu, res, pg).fn,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxConvSmem);
     if (e != cudaSuccess) return e;
   }
@@ -318,18 +335,23 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   }
   p->total_tiles = static_cast<int>(d.batch) * p->tiles_h * p->tiles_w * p->n_tiles;
 
-  // ---- halo variant: per-tensor int8 or fp16, when the whole weight tile fits next to >= 2 stages
-  // (with an automatic tile width, narrower output-channel tiles are tried before giving up)
-  if (!p->pg && variant != 1) {
+  // ---- halo variant: per-tensor int8, fp16, or pg16 with 64/128-wide output tiles, when the whole
+  // weight tile fits next to >= 2 stages (with an automatic tile width, narrower output-channel
+  // tiles are tried before giving up)
+  if (variant != 1) {
     int tw = 0, th = 0, pitch = 0;
     const int taps = kk;
     const int pairs = (p->slabs + 1) / 2;
+    const int tap_pairs = (kk + 1) / 2;
     const bool tile_ok = pick_halo_tile(static_cast<int>(d.out_h), static_cast<int>(d.out_w), p->k, p->stride,
                                         f16 ? 32 : 16, tw, th, pitch);
-    for (int bn = p->bn; tile_ok && !p->halo && bn >= 16; bn = block_n ? 0 : bn / 2) {
+    const int bn_min = p->pg ? 64 : 16;
+    for (int bn = p->bn; tile_ok && !p->halo && bn >= bn_min; bn = block_n ? 0 : bn / 2) {
+      if (p->pg && bn != 64 && bn != 128) continue;
       const int n_tiles = (oc + bn - 1) / bn;
       const int oc_alloc = n_tiles * bn;
-      const int w_tile = pairs * taps * 2 * bn * 16;
+      // resident weights: [pair][tap][2][bn][16] (per tensor) or [slab][tap pair][2][bn][16] (pg16)
+      const int w_tile = p->pg ? p->slabs * tap_pairs * 2 * bn * 16 : pairs * taps * 2 * bn * 16;
       const int halo_h = p->k == 1 ? th : (p->stride == 1 ? th + 2 : th + 1);
       const int boxes = p->stride == 2 ? 4 : 1;
       const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, oc_alloc);
@@ -355,6 +377,26 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
         p->tiles_h = (static_cast<int>(d.out_h) + th - 1) / th;
         p->m_tiles = static_cast<int>(d.batch) * p->tiles_h * p->tiles_w;
         p->total_tiles = p->m_tiles * p->n_tiles;
+        if (p->pg) {
+          // tap offsets inside a stage slab (the kernel's tap_off), then pairs in ascending order
+          const int box_bytes = ((p->halo_rows * 16 + 127) / 128) * 128;
+          int order_t[9], off[9];
+          for (int tap = 0; tap < kk; ++tap) {
+            const int kh = tap / 3, kw = tap % 3;
+            off[tap] = 0;
+            if (p->stride == 2)
+              off[tap] = (((kh + 1) & 1) * 2 + ((kw + 1) & 1)) * box_bytes + ((kh ? 1 : 0) * pitch + (kw ? 1 : 0)) * 16;
+            else if (p->k == 3)
+              off[tap] = (kh * pitch + kw) * 16;
+            order_t[tap] = tap;
+          }
+          std::sort(order_t, order_t + kk, [&](int a, int b) { return off[a] < off[b]; });
+          p->tap_pairs = tap_pairs;
+          for (int m = 0; m < tap_pairs; ++m) {
+            p->tap_a[m] = order_t[2 * m];
+            p->tap_b[m] = 2 * m + 1 < kk ? order_t[2 * m + 1] : -1;
+          }
+        }
       }
     }
     if (variant == 2 && !p->halo) {
@@ -370,7 +412,28 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   std::vector<uint8_t> packed(static_cast<size_t>(p->halo ? p->n_tiles * p->w_tile_bytes
                                                           : static_cast<size_t>(p->q_total) * p->oc_alloc * slot_row),
                               0);
-  if (p->halo) {
+  if (p->halo && p->pg) {
+    // pg16 halo: [n_tile][slab][tap pair][2 (tap a, tap b)][bn][16 bytes]; a missing tap b is zero
+    for (int nt = 0; nt < p->n_tiles; ++nt)
+      for (int slab = 0; slab < p->slabs; ++slab)
+        for (int m = 0; m < p->tap_pairs; ++m)
+          for (int ch = 0; ch < 2; ++ch) {
+            const int tap = ch ? p->tap_b[m] : p->tap_a[m];
+            if (tap < 0) continue;
+            for (int on = 0; on < p->bn; ++on) {
+              const int o = nt * p->bn + on;
+              if (o >= oc) continue;
+              uint8_t* dst = packed.data() + static_cast<size_t>(nt) * p->w_tile_bytes +
+                             ((((static_cast<size_t>(slab) * p->tap_pairs + m) * 2 + ch) * p->bn) + on) * slot_row;
+              for (int c = 0; c < cps; ++c) {
+                const int ci = slab * cps + c;
+                if (ci >= ic) continue;
+                dst[c] = static_cast<uint8_t>(
+                    static_cast<const int8_t*>(host_w)[(static_cast<size_t>(o) * ic + ci) * kk + tap]);
+              }
+            }
+          }
+  } else if (p->halo) {
     for (int nt = 0; nt < p->n_tiles; ++nt)
       for (int pr = 0; pr < p->slab_pairs; ++pr)
         for (int tap = 0; tap < kk; ++tap)
@@ -457,7 +520,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
     // the attribute is a per-kernel cap shared by every plan of this instance: set it to the
     // largest dynamic shared memory any plan may request, never to this plan's size
     ok = p->smem <= kMaxConvSmem &&
-         cuda_ok(p->halo ? set_halo_smem(f16, p->bn, kind == AEXRT_B200_KIND_CONV_SILU)
+         cuda_ok(p->halo ? set_halo_smem(f16, p->bn, kind == AEXRT_B200_KIND_CONV_SILU, p->pg)
                          : cudaFuncSetAttribute(kernel_for(f16, p->pg, p->bn),
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxConvSmem),
                  "cudaFuncSetAttribute");
@@ -573,7 +636,12 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     h.status = p->d_status;
     h.silu = p->kind == AEXRT_B200_KIND_CONV_SILU;
     if (p->f16 && res) return fail("fp16 convs take no residual");
-    const HaloKernel k = halo_kernel_for(p->f16, p->bn, h.silu != 0, res != nullptr);
+    h.tap_pairs = p->tap_pairs;
+    for (int m = 0; m < 5; ++m) {
+      h.tap_a[m] = p->tap_a[m];
+      h.tap_b[m] = p->tap_b[m];
+    }
+    const HaloKernel k = halo_kernel_for(p->f16, p->bn, h.silu != 0, res != nullptr, p->pg);
     k.fn<<<p->grid, k.threads, p->smem, static_cast<cudaStream_t>(stream)>>>(act_map, h);
     return cuda_ok(cudaGetLastError(), "conv launch") ? 1 : 0;
   }

@@ -54,6 +54,10 @@ struct ConvHaloParams {
   int silu;
   int contiguous;           // tile order: 0 strided over CTAs, 1 one contiguous run per CTA
   int issuers;              // MMA issuing threads (1 or 2; 2 needs a half ring to hold a whole tile)
+  // pg16 (INT8_PERGROUP): every slab is its own accumulation unit; a K step pairs two taps of
+  // one slab (tap_a[m], tap_b[m] < 0: the second half of K has zero weights)
+  int tap_pairs;
+  int tap_a[5], tap_b[5];
 };
 
 struct HaloSmemPlan {
@@ -278,17 +282,85 @@ __device__ __forceinline__ __half2 halo_epilogue16_packed(const uint32_t* v, flo
   return valid ? m : __float2half2_rn(0.0f);
 }
 
-template <bool kF16, int BN, bool kSilu, bool kRes>
+// pg16 final epilogue of 8 consecutive channels from the fp32 group sums `fp2` (packed pairs):
+// y = fp * w_scale + bias (two roundings, as the reference's LTS kernels), then
+// SiLU (halved vectors, as above), residual, fp16 store.  Packed when all 8
+// channels exist and the rows allow 16-byte accesses.  Returns max |fp16 y|.
+template <bool kSilu, bool kRes>
+__device__ __forceinline__ float halo_pg_finish8(const ConvHaloParams& p, const uint64_t* fp2, int oc,
+                                                 const float* sscale, const float* sbias, bool valid, __half* out_row,
+                                                 const __half* res_row) {
+  const int n_valid = p.oc - oc;
+  const bool full = n_valid >= 8 && p.out_vec && (!kRes || p.res_vec);
+  const float4 c0 = *reinterpret_cast<const float4*>(sscale), c1 = *reinterpret_cast<const float4*>(sscale + 4);
+  const float4 b0 = *reinterpret_cast<const float4*>(sbias), b1 = *reinterpret_cast<const float4*>(sbias + 4);
+  const uint64_t ss[4] = {f2_pack(c0.x, c0.y), f2_pack(c0.z, c0.w), f2_pack(c1.x, c1.y), f2_pack(c1.z, c1.w)};
+  const uint64_t bb[4] = {f2_pack(b0.x, b0.y), f2_pack(b0.z, b0.w), f2_pack(b1.x, b1.y), f2_pack(b1.z, b1.w)};
+  float y[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint64_t v = f2_add(f2_mul(fp2[i], ss[i]), bb[i]);
+    if constexpr (kSilu) {
+      float h0, h1;
+      f2_unpack(v, h0, h1);
+      v = f2_fma(v, f2_pack(tanh_approx(h0), tanh_approx(h1)), v);
+    }
+    f2_unpack(v, y[2 * i], y[2 * i + 1]);
+  }
+  if constexpr (kRes) {
+    if (valid) {
+      if (full) {
+        const uint4 r = *reinterpret_cast<const uint4*>(res_row + oc);
+        const __half2* rh = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(rh[i]);
+          y[2 * i] += f.x;
+          y[2 * i + 1] += f.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (i < n_valid) y[i] += __half2float(res_row[oc + i]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (i >= n_valid) y[i] = 0.0f;
+  __align__(16) __half2 hv[4];
+  __half2 m = __float2half2_rn(0.0f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    hv[i] = __floats2half2_rn(y[2 * i], y[2 * i + 1]);
+    m = __hmax2(m, __habs2(hv[i]));
+  }
+  if (valid) {
+    if (full) {
+      *reinterpret_cast<uint4*>(out_row + oc) = *reinterpret_cast<const uint4*>(hv);
+    } else {
+      const __half* h = reinterpret_cast<const __half*>(hv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < n_valid) out_row[oc + i] = h[i];
+    }
+  }
+  return valid ? fmaxf(__low2float(m), __high2float(m)) : 0.0f;
+}
+
+template <bool kF16, int BN, bool kSilu, bool kRes, bool kPG = false>
 __global__ void __launch_bounds__(halo_threads<BN>(), 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap act_map, const ConvHaloParams p) {
+  static_assert(!kPG || (!kF16 && (BN == 64 || BN == 128)), "pg16 halo: int8, BN 64 or 128 (no epilogue tile groups)");
   constexpr int kEpiWarps = halo_epi_warps<BN>();
   constexpr int kColBlocks = halo_col_blocks<BN>();
   constexpr int kTileGroups = 4 / kColBlocks;   // epilogue tile groups (tiles i with i % groups == g)
   constexpr int kCols = BN / kColBlocks;        // columns per epilogue warp
-  constexpr int CW = kCols >= 32 ? 32 : 16;     // columns per TMEM load
+  constexpr int CW = (kCols >= 32 && !kPG) ? 32 : 16;  // columns per TMEM load (pg16 keeps fp32 sums live)
   constexpr int kChunks = kCols / CW;
   // accumulator buffers in TMEM (256-512 columns): the MMA runs up to kAcc tiles ahead of the epilogue
-  constexpr int kAcc = BN <= 16 ? 16 : (BN <= 32 ? 8 : (BN <= 128 ? 4 : 2));
+  // (pg16: accumulation units are (tile, slab); 512 columns in units of BN)
+  constexpr int kAcc = kPG ? 512 / BN : (BN <= 16 ? 16 : (BN <= 32 ? 8 : (BN <= 128 ? 4 : 2)));
   static_assert(kAcc <= kMaxAcc && kAcc % (4 / halo_col_blocks<BN>()) == 0, "accumulator buffers per tile group");
   constexpr uint32_t kTmemCols = (kAcc * BN <= 32) ? 32 : (kAcc * BN <= 64) ? 64 : (kAcc * BN <= 128) ? 128 : (kAcc * BN <= 256) ? 256 : 512;
   constexpr int kCS = kF16 ? 8 : 16;  // tensor-map elements per 16-byte chunk
@@ -445,6 +517,19 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
         tap_off[tap] = off >> 4;
       }
       const int H = p.stages / p.issuers;
+      // pg16: per tap pair m, the A descriptor of (stage 0, slab 0): start at tap a, LBO = tap b - tap a
+      uint64_t pair_desc[5];
+      if constexpr (kPG) {
+#pragma unroll
+        for (int m = 0; m < 5; ++m) {
+          const int ta = m < p.tap_pairs ? p.tap_a[m] : 0, tb = m < p.tap_pairs ? p.tap_b[m] : -1;
+          const uint32_t oa = tap_off[ta] << 4;
+          const uint32_t lbo = tb >= 0 ? (tap_off[tb] << 4) - oa : 16u;
+          pair_desc[m] = smem_desc_kmajor_noswizzle(smem_u32(smem) + oa, lbo, 128);
+        }
+      }
+      const uint32_t slab_step = sp.slab_bytes >> 4;
+      int uu = 0;  // pg16: this issuer's accumulation units so far
       int s = me * H, cur_n = -1, wloads = 0;  // s, ph: position in this issuer's ring
       uint32_t ph = 0;
       bool ok = true, need_w = false;
@@ -478,6 +563,45 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
             }
             tc_fence_after();
             need_w = false;
+          }
+          if constexpr (kPG) {
+            // pg16: every slab is an accumulation unit in this issuer's half of the buffers;
+            // a K step pairs two taps of the slab (the reference's per-group sub-sums)
+            const int Hh = kAcc / p.issuers;
+            for (int pr = 0; pr < p.slab_pairs && ok; ++pr) {
+              if (!mbar_wait_bounded(&full[s], ph, p.status, kStatusTimeoutFull)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              for (int which = 0; which < 2; ++which) {
+                const int slab = 2 * pr + which;
+                if (slab >= p.slabs) break;
+                const int buf = me * Hh + uu % Hh;
+                if (uu >= Hh) {
+                  if (!mbar_wait_bounded(&acc_empty[buf], ((uu / Hh) - 1) & 1, p.status, kStatusTimeoutAccEmpty)) {
+                    ok = false;
+                    break;
+                  }
+                  tc_fence_after();
+                }
+                const uint32_t d = tmem_base + buf * BN;
+                const uint32_t a_off = s * stage_step + which * slab_step;
+                const uint64_t bslab = b_desc0 + ((static_cast<uint32_t>(slab * p.tap_pairs) * b_step));
+#pragma unroll
+                for (int m = 0; m < 5; ++m)
+                  if (m < p.tap_pairs) tc_mma<false>(d, pair_desc[m] + a_off, bslab + m * b_step, idesc, m ? 1u : 0u);
+                tc_commit(&acc_full[buf]);
+                ++uu;
+              }
+              if (!ok) break;
+              tc_commit(&empty[s]);
+              if (++s == (me + 1) * H) {
+                s = me * H;
+                ph ^= 1u;
+              }
+            }
+            continue;
           }
           const int u = i;
           const int buf = u % kAcc;
@@ -569,6 +693,71 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
         run_img = img;
         run_oc = n0 + col0;
       }
+      if constexpr (kPG) {
+        // pg16: drain the tile's slab units in ascending group order into fp32 sums,
+        // fp = sum_g fl32(fl32(S_g) * fl32(amax_g / 127)), then the final epilogue
+        const float* rec = p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs);
+        const int Hh = kAcc / p.issuers;
+        const int r_iss = i % p.issuers;
+        const int ubase = (i / p.issuers) * p.slabs;
+        uint64_t fp2[kCols / 2];  // packed fp32 pairs of the group sums
+        bool pg_ok = true;
+        for (int g = 0; g < p.slabs; ++g) {
+          const int uu = ubase + g;
+          const int gbuf = r_iss * Hh + uu % Hh;
+          const float gs = __fdiv_rn(__ldg(rec + 1 + g), 127.0f);
+          const uint64_t gs2 = f2_pack(gs, gs);
+          if (!mbar_wait_bounded(&acc_full[gbuf], (uu / Hh) & 1, p.status, kStatusTimeoutAccFull)) {
+            pg_ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) {
+            uint32_t v[CW];
+            const uint32_t taddr = lane_addr + gbuf * BN + col0 + c * CW;
+            if constexpr (CW == 32) {
+              tmem_ld_32x32(taddr, v);
+            } else {
+              tmem_ld<16>(taddr, v);
+            }
+            tmem_ld_wait();
+            if (c == kChunks - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&acc_empty[gbuf]);
+            }
+            const int oc_c = n0 + col0 + c * CW;
+            if (p.acc_dump != nullptr && valid) {
+              const size_t npix = static_cast<size_t>(p.n_img) * p.oh * p.ow;
+#pragma unroll
+              for (int j = 0; j < CW; ++j)
+                if (oc_c + j < p.oc) p.acc_dump[(static_cast<size_t>(g) * npix + pix) * p.oc + oc_c + j] = static_cast<int32_t>(v[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < CW / 2; ++j) {
+              // fl32(S) * gs, then added in ascending group order (no fused multiply-add)
+              const uint64_t term = f2_mul(f2_pack(static_cast<float>(static_cast<int32_t>(v[2 * j])),
+                                                   static_cast<float>(static_cast<int32_t>(v[2 * j + 1]))),
+                                           gs2);
+              fp2[c * (CW / 2) + j] = g == 0 ? term : f2_add(fp2[c * (CW / 2) + j], term);
+            }
+          }
+        }
+        if (!pg_ok) break;
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+#pragma unroll
+          for (int g16 = 0; g16 < CW / 16; ++g16) {
+            const int lc = n0 + col0 + c * CW + 16 * g16;
+            const float m0 = halo_pg_finish8<kSilu, kRes>(p, fp2 + (c * CW + 16 * g16) / 2, lc, s_scale + lc,
+                                                          s_bias + lc, valid, out_row, res_row);
+            const float m1 = halo_pg_finish8<kSilu, kRes>(p, fp2 + (c * CW + 16 * g16 + 8) / 2, lc + 8,
+                                                          s_scale + lc + 8, s_bias + lc + 8, valid, out_row, res_row);
+            run_max[c * (CW / 16) + g16] = fmaxf(run_max[c * (CW / 16) + g16], fmaxf(m0, m1));
+          }
+        }
+      } else {
       const int buf = u % kAcc;
       // the scale record is ready before the launch: read it while the accumulator fills
       const float amax_in = kF16 ? 0.0f : __ldg(p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs));
@@ -618,6 +807,7 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
           run_max[c * (CW / 16) + g] = fmaxf(run_max[c * (CW / 16) + g], mg);
         }
       }
+      }  // per-tensor
       if (p.amax_out != nullptr && !p.contiguous) {
         // this tile's maxima: warp max, then shared max over the four lane quadrants; the last
         // quadrant to arrive at this (ring slot, column block) issues the global atomics

@@ -340,3 +340,33 @@ def test_halo_pipeline_corner_cases_match_slot_kernel(n, ic, h, w, oc, k, s, blo
     assert torch.equal(accs[0][0], accs[1][0])
     assert torch.equal(accs[0][1], accs[1][1])
     assert torch.equal(accs[0][2], accs[1][2])
+
+
+@pytest.mark.parametrize("variant", [1, 2, 0x12, 0x22])
+@pytest.mark.parametrize("n,ic,h,w,oc,k,s", [
+    (2, 64, 20, 20, 128, 3, 1),
+    (2, 48, 17, 13, 64, 3, 1),    # 3 slabs: the odd slab of the last pair has no MMAs
+    (2, 32, 20, 18, 64, 3, 2),    # stride 2: tap pairs across parity boxes
+    (2, 96, 10, 10, 128, 1, 1),   # 1x1: one tap per slab, zero second half of K
+    (1, 64, 80, 80, 128, 3, 1),   # BASELINE config 1 (C1), batch 1
+])
+def test_pg16_kernel_variants_bitexact(n, ic, h, w, oc, k, s, variant):
+    """pg16 on the slot-streaming kernel and on the halo kernel (tap-paired K steps, one
+    accumulation unit per slab): identical per-group int32 sub-sums, all equal to the oracle."""
+    rng = np.random.default_rng(ic * 5 + oc + s + k)
+    x = seeded_act(rng, (n, ic, h, w))
+    weight = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    g, _, _ = check_against_oracle(x, weight, bias, k, s, 1, variant=variant)
+    assert g["plan"].info.variant == (1 if variant == 1 else 2)
+
+
+def test_pg16_halo_residual_and_linear():
+    """pg16 halo epilogue without SiLU and with the C2f residual."""
+    rng = np.random.default_rng(7)
+    x = seeded_act(rng, (2, 64, 12, 12))
+    weight = rng.normal(0, 0.05, (64, 64, 3, 3)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (64,)).astype(np.float32)
+    res = seeded_act(rng, (2, 64, 12, 12))
+    check_against_oracle(x, weight, bias, 3, 1, 1, silu=True, residual=res, variant=2)
+    check_against_oracle(x, weight, bias, 3, 1, 1, silu=False, variant=2)
