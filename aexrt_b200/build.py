@@ -18,15 +18,19 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libaexrt_b200.so")
-SOURCES = ["capi.cu"]
-HEADERS = ["conv_halo.cuh", "conv_tc.cuh", "ptx.cuh", "quant.cuh", "stem.cuh", "yolo_ops.cuh"]
+# capi.cu holds the C ABI and the memory-bound kernels; the conv kernel instances are split over
+# translation units that compile in parallel
+SOURCES = ["capi.cu", "kernels_slot.cu", "kernels_halo_i8_silu.cu", "kernels_halo_i8_linear.cu",
+           "kernels_halo_f16.cu", "kernels_halo_mb.cu", "kernels_halo_pg.cu",
+           "kernels_stem16.cu", "kernels_stem32.cu", "kernels_stem48.cu", "kernels_stem64.cu"]
+HEADERS = ["conv_halo.cuh", "conv_tc.cuh", "kernels.cuh", "ptx.cuh", "quant.cuh", "stem.cuh", "yolo_ops.cuh"]
+OBJ_DIR = os.path.join(HERE, "_build")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
     "-Xcompiler", "-fPIC,-ffp-contract=off,-fvisibility=hidden",
     "--expt-relaxed-constexpr",
-    "-shared",
 ]
 
 
@@ -51,19 +55,31 @@ def needs_build() -> bool:
     return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
 
 
-def build(verbose: bool = False, force: bool = False) -> str:
-    if not force and not needs_build():
-        return LIB
-    cmd = [_nvcc()] + _host_compiler_flags() + NVCC_FLAGS
-    if verbose:
-        cmd += ["-Xptxas", "-v"]
-    cmd += [os.path.join(CSRC, f) for f in SOURCES] + ["-o", LIB + ".tmp"]
+def _run(cmd: list, what: str, verbose: bool) -> None:
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)
-        raise RuntimeError("nvcc failed building libaexrt_b200.so")
+        raise RuntimeError(f"nvcc failed: {what}")
     if verbose:
         sys.stderr.write(res.stderr)
+
+
+def build(verbose: bool = False, force: bool = False) -> str:
+    if not force and not needs_build():
+        return LIB
+    from concurrent.futures import ThreadPoolExecutor
+
+    os.makedirs(OBJ_DIR, exist_ok=True)
+    base = [_nvcc()] + _host_compiler_flags() + NVCC_FLAGS
+    objs = [os.path.join(OBJ_DIR, os.path.splitext(f)[0] + ".o") for f in SOURCES]
+    jobs = []
+    for src, obj in zip(SOURCES, objs):
+        cmd = base + (["-Xptxas", "-v"] if verbose else []) + ["-c", os.path.join(CSRC, src), "-o", obj]
+        jobs.append((cmd, src))
+    with ThreadPoolExecutor(max_workers=len(jobs)) as ex:
+        for f in [ex.submit(_run, cmd, src, verbose) for cmd, src in jobs]:
+            f.result()
+    _run(base + ["-shared"] + objs + ["-o", LIB + ".tmp"], "link", verbose)
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

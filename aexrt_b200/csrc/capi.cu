@@ -20,6 +20,7 @@
 
 #include "../../include/aexrt_b200.h"
 #include "conv_halo.cuh"
+#include "kernels.cuh"
 #include "quant.cuh"
 #include "stem.cuh"
 #include "yolo_ops.cuh"
@@ -122,6 +123,7 @@ struct AexrtB200ConvPlan {
   int order = 0;  // halo tile order (see conv_halo.cuh): 0 auto, 1 strided, 2 contiguous
   // pg16 halo: K steps pair two taps of one slab, ordered by their shared-memory offset
   int tap_pairs = 0, tap_a[5] = {0, 0, 0, 0, 0}, tap_b[5] = {-1, -1, -1, -1, -1};
+  int mblocks = 1, nacc = 4, tmem_cols = 512;  // super-tile M blocks, TMEM buffers and columns
   int pitch = 0, halo_rows = 0, boxes_per_slab = 1, slab_pairs = 0, taps = 1, w_tile_bytes = 0, m_tiles = 0;
   void* d_w = nullptr;   // [n_tile][q_total][bn][16 bytes]
   float* d_scale = nullptr;
@@ -137,69 +139,8 @@ struct AexrtB200ConvPlan {
 
 namespace {
 
-using KernelFn = void (*)(const CUtensorMap, const ConvTcParams);
+// Kernel instances live in their own translation units (kernels_*.cu), compiled in parallel.
 constexpr int kMaxConvSmem = 200 * 1024;
-
-template <bool F16, bool PG>
-KernelFn kernel_for_bn(int bn) {
-  switch (bn) {
-    case 16: return conv_tc_kernel<F16, PG, 16>;
-    case 32: return conv_tc_kernel<F16, PG, 32>;
-    case 64: return conv_tc_kernel<F16, PG, 64>;
-    case 128: return conv_tc_kernel<F16, PG, 128>;
-    case 256:
-      if constexpr (!PG) return conv_tc_kernel<F16, PG, 256>;
-      return nullptr;
-    default: return nullptr;
-  }
-}
-
-KernelFn kernel_for(bool f16, bool pg, int bn) {
-  if (f16) return kernel_for_bn<true, false>(bn);
-  return pg ? kernel_for_bn<false, true>(bn) : kernel_for_bn<false, false>(bn);
-}
-
-using HaloFn = void (*)(const CUtensorMap, const ConvHaloParams);
-
-struct HaloKernel {
-  HaloFn fn;
-  int threads;
-};
-
-template <bool F16, bool SILU, bool RES>
-HaloKernel halo_kernel_for_bn(int bn) {
-  switch (bn) {
-    case 16: return {conv_halo_kernel<F16, 16, SILU, RES>, halo_threads<16>()};
-    case 32: return {conv_halo_kernel<F16, 32, SILU, RES>, halo_threads<32>()};
-    case 64: return {conv_halo_kernel<F16, 64, SILU, RES>, halo_threads<64>()};
-    case 128: return {conv_halo_kernel<F16, 128, SILU, RES>, halo_threads<128>()};
-    case 256: return {conv_halo_kernel<F16, 256, SILU, RES>, halo_threads<256>()};
-    default: return {nullptr, 0};
-  }
-}
-
-template <bool SILU, bool RES>
-HaloKernel halo_pg_kernel_for_bn(int bn) {
-  switch (bn) {
-    case 64: return {conv_halo_kernel<false, 64, SILU, RES, true>, halo_threads<64>()};
-    case 128: return {conv_halo_kernel<false, 128, SILU, RES, true>, halo_threads<128>()};
-    default: return {nullptr, 0};
-  }
-}
-
-// fp16 convs (stem, detect head) never carry a residual; the int8 convs do (C2f tail).
-// pg16 (INT8_PERGROUP) has a halo kernel for 64- and 128-wide output-channel tiles.
-HaloKernel halo_kernel_for(bool f16, int bn, bool silu, bool res, bool pg = false) {
-  if (pg) {
-    if (f16) return {nullptr, 0};
-    if (silu) return res ? halo_pg_kernel_for_bn<true, true>(bn) : halo_pg_kernel_for_bn<true, false>(bn);
-    return res ? halo_pg_kernel_for_bn<false, true>(bn) : halo_pg_kernel_for_bn<false, false>(bn);
-  }
-  if (f16) return silu ? halo_kernel_for_bn<true, true, false>(bn) : halo_kernel_for_bn<true, false, false>(bn);
-  if (silu) return res ? halo_kernel_for_bn<false, true, true>(bn) : halo_kernel_for_bn<false, true, false>(bn);
-  return res ? halo_kernel_for_bn<false, false, true>(bn) : halo_kernel_for_bn<false, false, false>(bn);
-}
-
 // Halo tile: output tw x th on an M grid of pitch = tw + (2 for 3x3 s1, 1 for 3x3 s2, 0 for 1x1)
 // <= max_pitch (one TMA box row of pitch pixels within the 256-element limit), th*pitch <= 128.
 bool pick_halo_tile(int oh, int ow, int k, int s, int max_pitch, int& tw, int& th, int& pitch) {
@@ -268,9 +209,9 @@ bool check_desc_int8(const AexrtConv2DDesc& d, uint32_t kernel_id, bool pg) {
   return true;
 }
 
-cudaError_t set_halo_smem(bool f16, int bn, bool silu, bool pg) {
+cudaError_t set_halo_smem(bool f16, int bn, bool silu, bool pg, bool mb) {
   for (int res = 0; res < (f16 ? 1 : 2); ++res) {
-    const cudaError_t e = cudaFuncSetAttribute(halo_kernel_for(f16, bn, silu, res, pg).fn,
+    const cudaError_t e = cudaFuncSetAttribute(halo_kernel_for(f16, bn, silu, res, pg, mb).fn,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxConvSmem);
     if (e != cudaSuccess) return e;
   }
@@ -308,6 +249,12 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   p->tiles_h = (static_cast<int>(d.out_h) + p->th - 1) / p->th;
   const uint32_t variant = (block_n >> 16) & 0xF;  // 0 auto, 1 slot streaming, 2 halo
   const uint32_t order = (block_n >> 20) & 0xF;    // halo tile order: 0 auto, 1 strided, 2 contiguous
+  const int mblocks_cap = static_cast<int>((block_n >> 24) & 0xF);  // super-tile M blocks: 0 auto, else at most
+  int sms = 148;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
   block_n &= 0xFFFF;
   p->bn = choose_bn(oc, p->pg, block_n);
   if (!kernel_for(f16, p->pg, p->bn)) {
@@ -352,12 +299,41 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
       const int oc_alloc = n_tiles * bn;
       // resident weights: [pair][tap][2][bn][16] (per tensor) or [slab][tap pair][2][bn][16] (pg16)
       const int w_tile = p->pg ? p->slabs * tap_pairs * 2 * bn * 16 : pairs * taps * 2 * bn * 16;
-      const int halo_h = p->k == 1 ? th : (p->stride == 1 ? th + 2 : th + 1);
+      // super-tiles for narrow per-tensor tiles: stack M blocks (halving the per-tile pipeline costs
+      // each time) while the map has the rows and the batch still gives every SM >= 2 tiles
+      // (3x3 stride 1 only: there they also share halo rows; measured no gain for 1x1 and stride 2)
+      int mblocks = 1;
+      const int kernel_mb = p->pg || bn > 64 ? 1 : (bn <= 32 ? 4 : 2);  // the kernel's kMaxMB
+      if (p->k == 3 && p->stride == 1 && mblocks_cap != 1) {
+        const int max_r = std::min(kernel_mb, mblocks_cap ? mblocks_cap : kernel_mb);
+        const long tw_tiles = (static_cast<long>(d.out_w) + tw - 1) / tw;
+        while (mblocks * 2 <= max_r && mblocks * 2 * th <= static_cast<int>(d.out_h) &&
+               static_cast<long>(d.batch) * ((d.out_h + mblocks * 2 * th - 1) / (mblocks * 2 * th)) * tw_tiles *
+                       n_tiles >= 2L * sms)
+          mblocks *= 2;
+      }
       const int boxes = p->stride == 2 ? 4 : 1;
-      const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, oc_alloc);
       const int budget = kMaxConvSmem - 1024;
-      const int st = std::min(16, (budget - one.total_bytes) / one.stage_bytes + 1);
+      int halo_h = 0, st = 0;
+      for (;; mblocks /= 2) {
+        // keep >= 4 stages (and a whole tile per issuer half ring) for a super-tile, else fewer blocks
+        halo_h = mblocks * th + (p->k == 1 ? 0 : (p->stride == 1 ? 2 : 1));
+        const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, oc_alloc);
+        st = std::min(16, (budget - one.total_bytes) / one.stage_bytes + 1);
+        if (mblocks == 1 || st >= std::max(4, 2 * pairs)) break;
+      }
       if (st >= 2) {
+        // TMEM accumulators: nacc buffers of mblocks*bn columns (a multiple of the two issuers and of
+        // the epilogue tile groups); pg16 uses 512 / bn units of bn columns
+        const int acc_cols = mblocks * bn;
+        int nacc = p->pg ? 512 / bn
+                         : (mblocks > 1 ? std::min(16, 512 / acc_cols)
+                                        : (bn <= 16 ? 16 : (bn <= 32 ? 8 : (bn <= 128 ? 4 : 2))));
+        int cols = 32;
+        while (cols < nacc * (p->pg ? bn : acc_cols)) cols *= 2;
+        p->mblocks = mblocks;
+        p->nacc = nacc;
+        p->tmem_cols = cols;
         p->bn = bn;
         p->n_tiles = n_tiles;
         p->oc_alloc = oc_alloc;
@@ -374,7 +350,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
         p->stages = st;
         p->smem = halo_smem_plan(p->halo_rows, boxes, st, w_tile, p->oc_alloc).total_bytes;
         p->tiles_w = (static_cast<int>(d.out_w) + tw - 1) / tw;
-        p->tiles_h = (static_cast<int>(d.out_h) + th - 1) / th;
+        p->tiles_h = (static_cast<int>(d.out_h) + mblocks * th - 1) / (mblocks * th);
         p->m_tiles = static_cast<int>(d.batch) * p->tiles_h * p->tiles_w;
         p->total_tiles = p->m_tiles * p->n_tiles;
         if (p->pg) {
@@ -520,7 +496,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
     // the attribute is a per-kernel cap shared by every plan of this instance: set it to the
     // largest dynamic shared memory any plan may request, never to this plan's size
     ok = p->smem <= kMaxConvSmem &&
-         cuda_ok(p->halo ? set_halo_smem(f16, p->bn, kind == AEXRT_B200_KIND_CONV_SILU, p->pg)
+         cuda_ok(p->halo ? set_halo_smem(f16, p->bn, kind == AEXRT_B200_KIND_CONV_SILU, p->pg, p->mblocks > 1)
                          : cudaFuncSetAttribute(kernel_for(f16, p->pg, p->bn),
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxConvSmem),
                  "cudaFuncSetAttribute");
@@ -636,12 +612,15 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     h.status = p->d_status;
     h.silu = p->kind == AEXRT_B200_KIND_CONV_SILU;
     if (p->f16 && res) return fail("fp16 convs take no residual");
+    h.mblocks = p->mblocks;
+    h.nacc = p->nacc;
+    h.tmem_cols = p->tmem_cols;
     h.tap_pairs = p->tap_pairs;
     for (int m = 0; m < 5; ++m) {
       h.tap_a[m] = p->tap_a[m];
       h.tap_b[m] = p->tap_b[m];
     }
-    const HaloKernel k = halo_kernel_for(p->f16, p->bn, h.silu != 0, res != nullptr, p->pg);
+    const HaloKernel k = halo_kernel_for(p->f16, p->bn, h.silu != 0, res != nullptr, p->pg, p->mblocks > 1);
     k.fn<<<p->grid, k.threads, p->smem, static_cast<cudaStream_t>(stream)>>>(act_map, h);
     return cuda_ok(cudaGetLastError(), "conv launch") ? 1 : 0;
   }
@@ -962,26 +941,9 @@ int aexrt_b200_conv_f16_image(const AexrtB200ConvPlan* p, const void* images, ui
   const bool silu = p->kind == AEXRT_B200_KIND_CONV_SILU;
   auto* o = static_cast<__half*>(out);
   const int h = static_cast<int>(p->desc.in_h), w = static_cast<int>(p->desc.in_w), s = p->stride;
-#define AEXRT_STEM_LAUNCH_T(OC, T)                                                                                   \
-  (silu ? stem_conv_kernel<OC, true, T><<<grid, 256, 0, st>>>(static_cast<const T*>(images), h, w, oh, ow, s, o,        \
-                                                              out_ldc, out_coff, amax_out, amax_stride, amax_goff,    \
-                                                              p->stem)                                                \
-        : stem_conv_kernel<OC, false, T><<<grid, 256, 0, st>>>(static_cast<const T*>(images), h, w, oh, ow, s, o,       \
-                                                               out_ldc, out_coff, amax_out, amax_stride, amax_goff,   \
-                                                               p->stem))
-#define AEXRT_STEM_LAUNCH(OC)                      \
-  if (layout == AEXRT_B200_LAYOUT_NCHW_F16)        \
-    AEXRT_STEM_LAUNCH_T(OC, __half);               \
-  else                                             \
-    AEXRT_STEM_LAUNCH_T(OC, float)
-  switch (oc) {
-    case 16: AEXRT_STEM_LAUNCH(16); break;
-    case 32: AEXRT_STEM_LAUNCH(32); break;
-    case 48: AEXRT_STEM_LAUNCH(48); break;
-    default: AEXRT_STEM_LAUNCH(64); break;
-  }
-#undef AEXRT_STEM_LAUNCH_T
-#undef AEXRT_STEM_LAUNCH
+launch_stem(static_cast<int>(oc), silu, layout == AEXRT_B200_LAYOUT_NCHW_F16, images, h, w, oh, ow, s, o,
+              static_cast<int>(out_ldc), static_cast<int>(out_coff), amax_out, static_cast<int>(amax_stride),
+              static_cast<int>(amax_goff), p->stem, grid, st);
   return cuda_ok(cudaGetLastError(), "stem conv launch") ? 1 : 0;
 }
 

@@ -58,6 +58,9 @@ struct ConvHaloParams {
   // one slab (tap_a[m], tap_b[m] < 0: the second half of K has zero weights)
   int tap_pairs;
   int tap_a[5], tap_b[5];
+  // super-tiles (per tensor): a tile is mblocks M blocks of th rows stacked vertically, sharing one
+  // halo box per slab and one pipeline step; nacc TMEM buffers of mblocks*BN columns each
+  int mblocks, nacc, tmem_cols;
 };
 
 struct HaloSmemPlan {
@@ -348,9 +351,10 @@ __device__ __forceinline__ float halo_pg_finish8(const ConvHaloParams& p, const 
   return valid ? fmaxf(__low2float(m), __high2float(m)) : 0.0f;
 }
 
-template <bool kF16, int BN, bool kSilu, bool kRes, bool kPG = false>
+template <bool kF16, int BN, bool kSilu, bool kRes, bool kPG = false, bool kMB = false>
 __global__ void __launch_bounds__(halo_threads<BN>(), 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap act_map, const ConvHaloParams p) {
+  static_assert(!kMB || (!kPG && BN <= 64), "super-tiles: per tensor, BN <= 64");
   static_assert(!kPG || (!kF16 && (BN == 64 || BN == 128)), "pg16 halo: int8, BN 64 or 128 (no epilogue tile groups)");
   constexpr int kEpiWarps = halo_epi_warps<BN>();
   constexpr int kColBlocks = halo_col_blocks<BN>();
@@ -358,11 +362,16 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
   constexpr int kCols = BN / kColBlocks;        // columns per epilogue warp
   constexpr int CW = (kCols >= 32 && !kPG) ? 32 : 16;  // columns per TMEM load (pg16 keeps fp32 sums live)
   constexpr int kChunks = kCols / CW;
-  // accumulator buffers in TMEM (256-512 columns): the MMA runs up to kAcc tiles ahead of the epilogue
-  // (pg16: accumulation units are (tile, slab); 512 columns in units of BN)
-  constexpr int kAcc = kPG ? 512 / BN : (BN <= 16 ? 16 : (BN <= 32 ? 8 : (BN <= 128 ? 4 : 2)));
-  static_assert(kAcc <= kMaxAcc && kAcc % (4 / halo_col_blocks<BN>()) == 0, "accumulator buffers per tile group");
-  constexpr uint32_t kTmemCols = (kAcc * BN <= 32) ? 32 : (kAcc * BN <= 64) ? 64 : (kAcc * BN <= 128) ? 128 : (kAcc * BN <= 256) ? 256 : 512;
+  // accumulator buffers in TMEM, p.nacc of p.mblocks*BN columns each (the host keeps nacc a
+  // multiple of the issuers and of the epilogue tile groups): the MMA runs up to nacc tiles ahead
+  // of the epilogue.  pg16: accumulation units are (tile, slab), 512 / BN buffers of BN columns.
+  // super-tile instances (kMB) stack up to kMaxMB M blocks; the others keep compile-time counts
+  constexpr int kMaxMB = kMB ? (BN <= 32 ? 4 : 2) : 1;
+  constexpr int kAccFixed = kPG ? 512 / BN : (BN <= 16 ? 16 : (BN <= 32 ? 8 : (BN <= 128 ? 4 : 2)));
+  constexpr int kAcc = kPG ? kAccFixed : kMaxAcc;  // pg16 count; bound of nacc otherwise
+  const int nacc = kMaxMB == 1 ? kAccFixed : p.nacc;
+  const int acc_cols = kMaxMB == 1 ? BN : p.mblocks * BN;
+  const uint32_t tmem_cols = static_cast<uint32_t>(p.tmem_cols);
   constexpr int kCS = kF16 ? 8 : 16;  // tensor-map elements per 16-byte chunk
 
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -383,7 +392,7 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < kAcc; ++b) {
+    for (int b = 0; b < nacc; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4 * kColBlocks);  // the warps of the tile group that drains buffer b
     }
@@ -395,7 +404,7 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
   for (int i = threadIdx.x; i < kAmaxRing * (16 + 4); i += blockDim.x) reinterpret_cast<uint32_t*>(smem + sp.am_offset)[i] = 0u;
   if (warp == 0 && lane == 0) tma_prefetch_desc(&act_map);
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -443,7 +452,7 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
       const int m_tile = t - n_tile * p.m_tiles;
       const int img = m_tile / per_img;
       const int r = m_tile - img * per_img;
-      const int oh0 = (r / p.tiles_w) * p.th, ow0 = (r % p.tiles_w) * p.tw;
+      const int oh0 = (r / p.tiles_w) * p.th * p.mblocks, ow0 = (r % p.tiles_w) * p.tw;
       const int n_first = __shfl_sync(0xffffffffu, n_tile, 0);
       // n-tiles never decrease along q: the stages of this group form a prefix of the lanes
       const bool mine = lane < group && q < total_q && n_tile == n_first;
@@ -503,6 +512,7 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
       const uint64_t b_desc0 = smem_desc_kmajor_noswizzle(smem_u32(smem + sp.b_offset), BN * kSlotBytes, 128);
       const uint32_t b_step = (2 * BN * kSlotBytes) >> 4;  // one (pair, tap) of resident B
       const uint32_t stage_step = sp.stage_bytes >> 4;
+      const uint32_t mb_step = (p.th * p.pitch * kSlotBytes) >> 4;  // one M block of halo rows
       uint32_t tap_off[9];
 #pragma unroll
       for (int tap = 0; tap < 9; ++tap) {
@@ -604,16 +614,15 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
             continue;
           }
           const int u = i;
-          const int buf = u % kAcc;
-          if (u >= kAcc) {
-            if (!mbar_wait_bounded(&acc_empty[buf], ((u / kAcc) - 1) & 1, p.status, kStatusTimeoutAccEmpty)) {
+          const int buf = u % nacc;
+          if (u >= nacc) {
+            if (!mbar_wait_bounded(&acc_empty[buf], ((u / nacc) - 1) & 1, p.status, kStatusTimeoutAccEmpty)) {
               ok = false;
               break;
             }
             tc_fence_after();
           }
-          const uint32_t d = tmem_base + buf * BN;
-          uint64_t bd = b_desc0;
+          const uint32_t d = tmem_base + buf * acc_cols;
           for (int pr = 0; pr < p.slab_pairs; ++pr) {
             if (!mbar_wait_bounded(&full[s], ph, p.status, kStatusTimeoutFull)) {
               ok = false;
@@ -621,15 +630,23 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
             }
             tc_fence_after();
             const uint64_t ad = a_desc0 + s * stage_step;
-            if (p.taps == 9) {
+            const uint64_t bpr = b_desc0 + static_cast<uint32_t>(pr * p.taps) * b_step;
 #pragma unroll
-              for (int tap = 0; tap < 9; ++tap) {
-                tc_mma<kF16>(d, ad + tap_off[tap], bd, idesc, (pr | tap) ? 1u : 0u);
-                bd += b_step;
+            for (int mb = 0; mb < kMaxMB; ++mb) {
+              if (mb >= p.mblocks) break;
+              // M block mb starts mb*th rows down the (shared) halo of every box
+              const uint64_t amb = ad + mb * mb_step;
+              const uint32_t dmb = d + mb * BN;
+              uint64_t bd = bpr;
+              if (p.taps == 9) {
+#pragma unroll
+                for (int tap = 0; tap < 9; ++tap) {
+                  tc_mma<kF16>(dmb, amb + tap_off[tap], bd, idesc, (pr | tap) ? 1u : 0u);
+                  bd += b_step;
+                }
+              } else {
+                tc_mma<kF16>(dmb, amb, bd, idesc, pr ? 1u : 0u);
               }
-            } else {
-              tc_mma<kF16>(d, ad, bd, idesc, pr ? 1u : 0u);
-              bd += b_step;
             }
             tc_commit(&empty[s]);
             if (++s == (me + 1) * H) {
@@ -681,7 +698,7 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
       const int m_tile = t - n_tile * p.m_tiles;
       const int img = m_tile / per_img;
       const int r = m_tile - img * per_img;
-      const int oy = (r / p.tiles_w) * p.th + r_h, ox = (r % p.tiles_w) * p.tw + r_w;
+      const int oy = (r / p.tiles_w) * p.th * p.mblocks + r_h, ox = (r % p.tiles_w) * p.tw + r_w;
       const bool valid = r_h < p.th && r_w < p.tw && oy < p.oh && ox < p.ow;
       const size_t pix = (static_cast<size_t>(img) * p.oh + (valid ? oy : 0)) * p.ow + (valid ? ox : 0);
       __half* out_row = p.out + pix * p.out_ldc + p.out_coff;
@@ -758,53 +775,62 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
           }
         }
       } else {
-      const int buf = u % kAcc;
+      const int buf = u % nacc;
       // the scale record is ready before the launch: read it while the accumulator fills
       const float amax_in = kF16 ? 0.0f : __ldg(p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs));
-      if (!mbar_wait_bounded(&acc_full[buf], (u / kAcc) & 1, p.status, kStatusTimeoutAccFull)) break;
+      if (!mbar_wait_bounded(&acc_full[buf], (u / nacc) & 1, p.status, kStatusTimeoutAccFull)) break;
       tc_fence_after();
       const float in_scale = kF16 ? 1.0f : __fdiv_rn(amax_in, 127.0f);
+      const int oy0 = (r / p.tiles_w) * p.th * p.mblocks + r_h;
+      for (int mb = 0; mb < kMaxMB; ++mb) {
+        if (mb >= p.mblocks) break;
+        // M block mb of the super-tile: rows mb*th.. of the tile, columns mb*BN.. of the buffer
+        const int oyb = oy0 + mb * p.th;
+        const bool vb = r_h < p.th && r_w < p.tw && oyb < p.oh && ox < p.ow;
+        const size_t pixb = (static_cast<size_t>(img) * p.oh + (vb ? oyb : 0)) * p.ow + (vb ? ox : 0);
+        __half* outb = p.out + pixb * p.out_ldc + p.out_coff;
+        const __half* resb = kRes ? p.res + pixb * p.res_ldc + p.res_coff : nullptr;
 #pragma unroll
-      for (int c = 0; c < kChunks; ++c) {
-        uint32_t v[CW];
-        const uint32_t taddr = lane_addr + buf * BN + col0 + c * CW;
-        if constexpr (CW == 32) {
-          tmem_ld_32x32(taddr, v);
-        } else {
-          tmem_ld<16>(taddr, v);
-        }
-        tmem_ld_wait();
-        if (c == kChunks - 1) {
-          // every column of this accumulator has been read: hand it back to the MMA warp
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[buf]);
-        }
-        const int oc_c = n0 + col0 + c * CW;
-        if (!kF16 && p.acc_dump != nullptr && valid) {
-#pragma unroll
-          for (int i = 0; i < CW; ++i)
-            if (oc_c + i < p.oc) p.acc_dump[pix * p.oc + oc_c + i] = static_cast<int32_t>(v[i]);
-        }
-        // the whole chunk exists and its rows allow 16-byte accesses: packed path (warp-uniform)
-        const bool packed = oc_c + CW <= p.oc && p.out_vec && (!kRes || p.res_vec);
-#pragma unroll
-        for (int g = 0; g < CW / 16; ++g) {
-          const int lc = oc_c + 16 * g;  // output channel (the vectors are zero-padded to oc_alloc)
-          float mg;
-          if (packed) {
-            const __half2 m2 = halo_epilogue16_packed<kF16, kSilu, kRes>(
-                v + 16 * g, in_scale, s_scale + lc, s_bias + lc, valid, out_row + lc,
-                kRes ? res_row + lc : nullptr);
-            mg = fmaxf(__low2float(m2), __high2float(m2));
+        for (int c = 0; c < kChunks; ++c) {
+          uint32_t v[CW];
+          const uint32_t taddr = lane_addr + buf * acc_cols + mb * BN + col0 + c * CW;
+          if constexpr (CW == 32) {
+            tmem_ld_32x32(taddr, v);
           } else {
-            const float m0 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g, in_scale, lc, s_scale + lc, s_bias + lc,
-                                                               valid, out_row, res_row);
-            const float m1 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g + 8, in_scale, lc + 8, s_scale + lc + 8,
-                                                               s_bias + lc + 8, valid, out_row, res_row);
-            mg = fmaxf(m0, m1);
+            tmem_ld<16>(taddr, v);
           }
-          run_max[c * (CW / 16) + g] = fmaxf(run_max[c * (CW / 16) + g], mg);
+          tmem_ld_wait();
+          if (c == kChunks - 1 && (kMaxMB == 1 || mb == p.mblocks - 1)) {
+            // every column of this accumulator has been read: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          }
+          const int oc_c = n0 + col0 + c * CW;
+          if (!kF16 && p.acc_dump != nullptr && vb) {
+#pragma unroll
+            for (int i = 0; i < CW; ++i)
+              if (oc_c + i < p.oc) p.acc_dump[pixb * p.oc + oc_c + i] = static_cast<int32_t>(v[i]);
+          }
+          // the whole chunk exists and its rows allow 16-byte accesses: packed path (warp-uniform)
+          const bool packed = oc_c + CW <= p.oc && p.out_vec && (!kRes || p.res_vec);
+#pragma unroll
+          for (int g = 0; g < CW / 16; ++g) {
+            const int lc = oc_c + 16 * g;  // output channel (the vectors are zero-padded to oc_alloc)
+            float mg;
+            if (packed) {
+              const __half2 m2 = halo_epilogue16_packed<kF16, kSilu, kRes>(
+                  v + 16 * g, in_scale, s_scale + lc, s_bias + lc, vb, outb + lc, kRes ? resb + lc : nullptr);
+              mg = fmaxf(__low2float(m2), __high2float(m2));
+            } else {
+              const float m0 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g, in_scale, lc, s_scale + lc,
+                                                                 s_bias + lc, vb, outb, resb);
+              const float m1 = halo_epilogue8<kF16, kSilu, kRes>(p, v + 16 * g + 8, in_scale, lc + 8,
+                                                                 s_scale + lc + 8, s_bias + lc + 8, vb, outb, resb);
+              mg = fmaxf(m0, m1);
+            }
+            run_max[c * (CW / 16) + g] = fmaxf(run_max[c * (CW / 16) + g], mg);
+          }
         }
       }
       }  // per-tensor
@@ -844,7 +870,7 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc(tmem_base, tmem_cols);
   }
 }
 

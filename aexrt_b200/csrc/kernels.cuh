@@ -1,0 +1,59 @@
+// Kernel selection across the translation units that instantiate the conv
+// kernels (kernels_slot.cu, kernels_halo_*.cu): each unit compiles one family
+// of template instances, so the library builds in parallel.
+#pragma once
+#include <cuda.h>
+
+#include "conv_halo.cuh"
+#include "conv_tc.cuh"
+#include "stem.cuh"
+
+namespace aexrt {
+
+using KernelFn = void (*)(const CUtensorMap, const ConvTcParams);
+using HaloFn = void (*)(const CUtensorMap, const ConvHaloParams);
+
+struct HaloKernel {
+  HaloFn fn;
+  int threads;
+};
+
+// Slot-streaming kernel for (fp16, pg16, BN); nullptr when not instantiated.
+KernelFn kernel_for(bool f16, bool pg, int bn);
+
+// Halo kernel families: per tensor (int8 SiLU / linear, fp16), super-tiles (BN <= 64) and
+// pg16 (BN 64/128).
+HaloKernel halo_kernel_i8_silu(int bn, bool res);
+HaloKernel halo_kernel_i8_linear(int bn, bool res);
+HaloKernel halo_kernel_f16(int bn, bool silu);
+HaloKernel halo_kernel_mb(bool f16, int bn, bool silu, bool res);
+HaloKernel halo_kernel_pg(int bn, bool silu, bool res);
+
+// fp16 convs (stem, detect head) never carry a residual; the int8 convs do (C2f tail).
+inline HaloKernel halo_kernel_for(bool f16, int bn, bool silu, bool res, bool pg = false, bool mb = false) {
+  if (mb) return halo_kernel_mb(f16, bn, silu, res);
+  if (pg) return f16 ? HaloKernel{nullptr, 0} : halo_kernel_pg(bn, silu, res);
+  if (f16) return halo_kernel_f16(bn, silu);
+  return silu ? halo_kernel_i8_silu(bn, res) : halo_kernel_i8_linear(bn, res);
+}
+
+// The image stem (stem.cuh): one unit per output width (16, 32, 48, 64), fp16 or fp32 images.
+#define AEXRT_STEM_DECL(OC)                                                                                     \
+  void launch_stem_##OC(bool silu, bool f16_images, const void* images, int h, int w, int oh, int ow, int stride, \
+                        __half* out, int out_ldc, int out_coff, uint32_t* amax, int amax_stride, int amax_goff,   \
+                        const StemWeights& wt, dim3 grid, cudaStream_t st);
+AEXRT_STEM_DECL(16)
+AEXRT_STEM_DECL(32)
+AEXRT_STEM_DECL(48)
+AEXRT_STEM_DECL(64)
+#undef AEXRT_STEM_DECL
+
+inline void launch_stem(int oc, bool silu, bool f16_images, const void* images, int h, int w, int oh, int ow,
+                        int stride, __half* out, int out_ldc, int out_coff, uint32_t* amax, int amax_stride,
+                        int amax_goff, const StemWeights& wt, dim3 grid, cudaStream_t st) {
+  auto* fn = oc == 16 ? launch_stem_16 : oc == 32 ? launch_stem_32 : oc == 48 ? launch_stem_48 : launch_stem_64;
+  fn(silu, f16_images, images, h, w, oh, ow, stride, out, out_ldc, out_coff, amax, amax_stride, amax_goff, wt, grid,
+     st);
+}
+
+}  // namespace aexrt

@@ -1,0 +1,24 @@
+// Instances of the direct image-stem conv (stem.cuh) for 32 output channels.
+#include "kernels.cuh"
+
+namespace aexrt {
+namespace {
+template <bool SILU, typename T>
+void go(const void* images, int h, int w, int oh, int ow, int stride, __half* out, int out_ldc, int out_coff,
+        uint32_t* amax, int amax_stride, int amax_goff, const StemWeights& wt, dim3 grid, cudaStream_t st) {
+  stem_conv_kernel<32, SILU, T><<<grid, 256, 0, st>>>(static_cast<const T*>(images), h, w, oh, ow, stride, out,
+                                                       out_ldc, out_coff, amax, amax_stride, amax_goff, wt);
+}
+}  // namespace
+
+void launch_stem_32(bool silu, bool f16_images, const void* images, int h, int w, int oh, int ow, int stride,
+                    __half* out, int out_ldc, int out_coff, uint32_t* amax, int amax_stride, int amax_goff,
+                    const StemWeights& wt, dim3 grid, cudaStream_t st) {
+  if (f16_images)
+    (silu ? go<true, __half> : go<false, __half>)(images, h, w, oh, ow, stride, out, out_ldc, out_coff, amax,
+                                                 amax_stride, amax_goff, wt, grid, st);
+  else
+    (silu ? go<true, float> : go<false, float>)(images, h, w, oh, ow, stride, out, out_ldc, out_coff, amax,
+                                               amax_stride, amax_goff, wt, grid, st);
+}
+}  // namespace aexrt

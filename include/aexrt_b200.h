@@ -148,7 +148,8 @@ int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t 
  * block_n = 0 picks the output-channel tile automatically.  Tuning bits above
  * the tile (bits 0-15): bits 16-19 kernel variant (0 auto, 1 slot streaming,
  * 2 halo tile), bits 20-23 halo tile order (0 auto, 1 strided over CTAs,
- * 2 one contiguous run per CTA); results are identical for every choice.
+ * 2 one contiguous run per CTA), bits 24-27 the most M blocks stacked in one
+ * halo super-tile (0 auto, 1 none); results are identical for every choice.
  * Allocates device memory (set-up time only).  Returns NULL on error. */
 AexrtB200ConvPlan* aexrt_b200_conv_plan_create(const AexrtConv2DDesc* desc, uint32_t kind, uint32_t kernel_id,
                                                uint32_t flags, const int8_t* codes, const float* w_scale,

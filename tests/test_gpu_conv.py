@@ -370,3 +370,24 @@ def test_pg16_halo_residual_and_linear():
     res = seeded_act(rng, (2, 64, 12, 12))
     check_against_oracle(x, weight, bias, 3, 1, 1, silu=True, residual=res, variant=2)
     check_against_oracle(x, weight, bias, 3, 1, 1, silu=False, variant=2)
+
+
+@pytest.mark.parametrize("n,ic,h,w,oc,k,s", [
+    (16, 16, 80, 80, 16, 3, 1),    # narrow 3x3: 4 M blocks per super-tile
+    (16, 16, 81, 77, 32, 3, 2),    # stride 2, ragged map: partial super-tiles at the bottom
+    (16, 32, 80, 80, 32, 1, 1),    # 1x1
+    (16, 64, 40, 40, 64, 3, 1),    # 2 M blocks
+])
+def test_super_tiles_match_single_blocks(n, ic, h, w, oc, k, s):
+    """Halo super-tiles (several M blocks per pipeline step) give the same accumulators, outputs and
+    epilogue amax as one block per tile (block_n bits 24-27 = 1), and both match the oracle."""
+    rng = np.random.default_rng(ic * 3 + oc + h + s)
+    x = seeded_act(rng, (n, ic, h, w))
+    weight = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    g_auto, _, _ = check_against_oracle(x, weight, bias, k, s, 0, variant=2)
+    g_one, _, _ = check_against_oracle(x, weight, bias, k, s, 0, variant=2 | (1 << 8))
+    assert np.array_equal(g_auto["acc"], g_one["acc"])
+    assert np.array_equal(g_auto["out_full"], g_one["out_full"])
+    assert np.array_equal(g_auto["amax_out"], g_one["amax_out"])
+    assert g_auto["plan"].info.tile_h == g_one["plan"].info.tile_h
