@@ -679,7 +679,7 @@ bool rows_ok(const QuantParams& q, bool i8) {
 
 // Picks the quantize kernel: NHWC sources (16-byte aligned slices, enforced by
 // the entry points) go through the coalesced row kernel, stride-1 NCHW fp16
-// with H*W % 8 == 0 through the register-transpose kernel, anything else
+// with H*W % 4 == 0 through the register-transpose kernel, anything else
 // (more than 1024 channels, NCHW with ragged planes) through the per-slab
 // generic kernel.
 void launch_quantize(const QuantParams& q, cudaStream_t st) {
@@ -687,8 +687,8 @@ void launch_quantize(const QuantParams& q, cudaStream_t st) {
     const int pw = rows_pixels_per_warp(q, true);
     const dim3 grid((q.hp * q.wp + 8 * pw - 1) / (8 * pw), q.n);
     quant_rows_kernel<true><<<grid, 256, 0, st>>>(q, pw);
-  } else if (q.nsrc == 1 && q.src[0].layout == 1 && !q.split && (q.h * q.w) % 8 == 0 && q.slabs <= kMaxSlabs) {
-    const dim3 grid((q.h * q.w / 8 + 255) / 256, q.slabs, q.n);
+  } else if (q.nsrc == 1 && q.src[0].layout == 1 && !q.split && (q.h * q.w) % 4 == 0 && q.slabs <= kMaxSlabs) {
+    const dim3 grid((q.h * q.w / 4 + 255) / 256, q.slabs, q.n);
     quantize_nchw_kernel<<<grid, 256, 0, st>>>(q);
   } else {
     const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, q.n);
@@ -794,18 +794,24 @@ int aexrt_b200_act_amax_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, u
   if (group_offset + groups > groups_total) return fail("amax group range exceeds groups_total");
   if (n == 0 || c == 0 || h == 0 || w == 0) return 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (zero_first) {
+  const int hw = static_cast<int>(h * w);
+  if (reinterpret_cast<uintptr_t>(x) % 16) return fail("x must be 16-byte aligned");
+  // NCHW with enough (image, group) strips to fill the GPU: one block per strip stores its
+  // maximum, so zero_first needs no clearing pass
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const bool one_block = layout == AEXRT_B200_LAYOUT_NCHW_F16 && zero_first &&
+                         static_cast<long>(n) * groups >= static_cast<long>(sms);
+  if (zero_first && !one_block) {
     if (!cuda_ok(cudaMemset2DAsync(amax_groups + group_offset, groups_total * 4, 0, groups * 4, n, st), "memset amax"))
       return 0;
   }
-  const int hw = static_cast<int>(h * w);
-  if (reinterpret_cast<uintptr_t>(x) % 16) return fail("x must be 16-byte aligned");
   if (layout == AEXRT_B200_LAYOUT_NCHW_F16) {
-    const int chunk = 32768;  // halves per block: 64 KB, 16 loads of 16 bytes per thread
+    const int chunk = one_block ? 16 * hw : 32768;  // halves per block (chunked: 64 KB)
     const int blocks = static_cast<int>((16ull * hw + chunk - 1) / chunk);
-    amax_nchw_f16_kernel<<<dim3(blocks, groups, n), 256, 0, st>>>(static_cast<const __half*>(x), static_cast<int>(c),
-                                                                   hw, static_cast<int>(groups_total), chunk,
-                                                                   amax_groups + group_offset);
+    amax_nchw_f16_kernel<<<dim3(blocks, groups, n), one_block ? 512 : 256, 0, st>>>(
+        static_cast<const __half*>(x), static_cast<int>(c), hw, static_cast<int>(groups_total), chunk,
+        amax_groups + group_offset, one_block ? 1 : 0);
   } else if (layout == AEXRT_B200_LAYOUT_NHWC_F16) {
     if (ldc < coff + c || ldc % 8 || coff % 8 || reinterpret_cast<uintptr_t>(x) % 16)
       return fail("NHWC slice must be 16-byte aligned (ldc, coff multiples of 8)");

@@ -194,30 +194,6 @@ __device__ __forceinline__ float halo_epilogue8(const ConvHaloParams& p, const u
   return valid ? fmaxf(__low2float(m), __high2float(m)) : 0.0f;
 }
 
-__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-}
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
 // The epilogue of 16 consecutive output channels of one pixel when all 16
 // exist and the output (and residual) rows allow 16-byte accesses: the same
 // arithmetic as halo_epilogue8, element for element, with the affine, SiLU
@@ -286,7 +262,7 @@ __device__ __forceinline__ __half2 halo_epilogue16_packed(const uint32_t* v, flo
 }
 
 // pg16 final epilogue of 8 consecutive channels from the fp32 group sums `fp2` (packed pairs):
-// y = fp * w_scale + bias (two roundings, as the reference's LTS kernels), then
+// y = fma(fp, w_scale, bias) (the reference's `fp * scale + bias`, which its shader compiler may contract), then
 // SiLU (halved vectors, as above), residual, fp16 store.  Packed when all 8
 // channels exist and the rows allow 16-byte accesses.  Returns max |fp16 y|.
 template <bool kSilu, bool kRes>
@@ -302,7 +278,7 @@ __device__ __forceinline__ float halo_pg_finish8(const ConvHaloParams& p, const 
   float y[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    uint64_t v = f2_add(f2_mul(fp2[i], ss[i]), bb[i]);
+    uint64_t v = f2_fma(fp2[i], ss[i], bb[i]);
     if constexpr (kSilu) {
       float h0, h1;
       f2_unpack(v, h0, h1);
@@ -753,11 +729,12 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
             }
 #pragma unroll
             for (int j = 0; j < CW / 2; ++j) {
-              // fl32(S) * gs, then added in ascending group order (no fused multiply-add)
-              const uint64_t term = f2_mul(f2_pack(static_cast<float>(static_cast<int32_t>(v[2 * j])),
-                                                   static_cast<float>(static_cast<int32_t>(v[2 * j + 1]))),
-                                           gs2);
-              fp2[c * (CW / 2) + j] = g == 0 ? term : f2_add(fp2[c * (CW / 2) + j], term);
+              // fp += fl32(S) * gs in ascending group order, one fused multiply-add per group (the
+              // slot kernel's `fp + S * gs` contracts the same way; ptxas also fuses a packed
+              // mul.rn + add.rn pair, so the fma is written out)
+              const uint64_t s2 = f2_pack(static_cast<float>(static_cast<int32_t>(v[2 * j])),
+                                          static_cast<float>(static_cast<int32_t>(v[2 * j + 1])));
+              fp2[c * (CW / 2) + j] = g == 0 ? f2_mul(s2, gs2) : f2_fma(s2, gs2, fp2[c * (CW / 2) + j]);
             }
           }
         }

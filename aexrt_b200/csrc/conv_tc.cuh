@@ -485,8 +485,9 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < CW; ++i) {
-              const float term = static_cast<float>(static_cast<int32_t>(v[i])) * gs;
-              fp[c * CW + i] = g == 0 ? term : fp[c * CW + i] + term;
+              // fp += fl32(S) * gs, one fused multiply-add per group in ascending order
+              const float sv = static_cast<float>(static_cast<int32_t>(v[i]));
+              fp[c * CW + i] = g == 0 ? __fmul_rn(sv, gs) : fmaf(sv, gs, fp[c * CW + i]);
             }
             if (p.acc_dump != nullptr && valid) {
               const int oc_c = n0 + col0 + c * CW;

@@ -18,9 +18,10 @@ namespace aexrt {
 // Per (image, 16-channel group) amax of an NCHW fp16 tensor.  The 16 channel
 // planes of one group are one contiguous strip of 16*H*W halves; grid.x splits
 // each strip into chunks so small-channel / large-plane tensors still fill the
-// GPU.  Result: float bits, atomically max-ed into amax_g[n * G + g].
+// GPU.  Result: float bits, atomically max-ed into amax_g[n * G + g], or stored
+// (`store`, one block per strip) so that no clearing pass is needed.
 __global__ void amax_nchw_f16_kernel(const __half* __restrict__ x, int c, int hw, int groups, int chunk,
-                                     uint32_t* __restrict__ amax_g) {
+                                     uint32_t* __restrict__ amax_g, int store) {
   const int g = blockIdx.y;
   const int n = blockIdx.z;
   const int c0 = g * 16;
@@ -38,14 +39,14 @@ __global__ void amax_nchw_f16_kernel(const __half* __restrict__ x, int c, int hw
       const size_t vend = begin + ((end - begin) / 8) * 8;
       const size_t step = static_cast<size_t>(blockDim.x) * 8;
       size_t i = begin + static_cast<size_t>(threadIdx.x) * 8;
-      // four independent 16-byte loads in flight per thread, then the max
+      // eight independent 16-byte loads in flight per thread, then the max
       __half2 hm = __float2half2_rn(0.0f);
-      for (; i + 3 * step < vend; i += 4 * step) {
-        uint4 v[4];
+      for (; i + 7 * step < vend; i += 8 * step) {
+        uint4 v[8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const uint4*>(s + i + u * step);
+        for (int u = 0; u < 8; ++u) v[u] = *reinterpret_cast<const uint4*>(s + i + u * step);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 8; ++u) {
           const __half2* h2 = reinterpret_cast<const __half2*>(&v[u]);
 #pragma unroll
           for (int k = 0; k < 4; ++k) hm = __hmax2(hm, __habs2(h2[k]));
@@ -71,7 +72,12 @@ __global__ void amax_nchw_f16_kernel(const __half* __restrict__ x, int c, int hw
   if (warp == 0) {
     bits = lane < (blockDim.x >> 5) ? warp_max[lane] : 0u;
     bits = __reduce_max_sync(0xffffffffu, bits);
-    if (lane == 0 && begin < end) atomicMax(&amax_g[static_cast<size_t>(n) * groups + g], bits);
+    if (lane == 0 && begin < end) {
+      if (store)
+        amax_g[static_cast<size_t>(n) * groups + g] = bits;
+      else
+        atomicMax(&amax_g[static_cast<size_t>(n) * groups + g], bits);
+    }
   }
 }
 
@@ -308,6 +314,41 @@ __device__ __forceinline__ void slab_multipliers(const QuantParams& p, int n, fl
 // per-warp table computed once (no divisions in the copy loops).  A warp's
 // pixel count pw = 32 * 8 / (widest source's L), so the widest source keeps
 // 8 loads per lane in flight in one batch and narrower ones as many or more.
+// Adds 1.5*2^23 to both halves of a packed fl32 product: the low byte of each sum's bits is
+// round_half_even(product) & 0xFF for |product| < 2^22.  Scalar __fadd_rn, which is never
+// merged into a multiply-add, keeps the product rounded on its own (a fused x * mult + 1.5*2^23
+// rounds once and differs from the two-step result near .5).
+__device__ __forceinline__ void magic_round2(uint64_t vq, uint32_t& a, uint32_t& b) {
+  float x, y;
+  f2_unpack(vq, x, y);
+  a = __float_as_uint(__fadd_rn(x, 12582912.0f));
+  b = __float_as_uint(__fadd_rn(y, 12582912.0f));
+}
+
+// int8 codes of 8 fp16 values, q = low byte of round_half_even(fl32(x * mult)), four per word.
+// kMagic: the rounding comes from adding 1.5*2^23 (exact for |x * mult| < 2^22); else float-to-int.
+template <bool kMagic>
+__device__ __forceinline__ void codes8(const uint4& v, float mult, uint32_t& q0, uint32_t& q1) {
+  const __half2* h2 = reinterpret_cast<const __half2*>(&v);
+  const uint64_t m2 = f2_pack(mult, mult);
+  uint32_t b[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __half22float2(h2[e]);
+    const uint64_t vq = f2_mul(f2_pack(f.x, f.y), m2);
+    if (kMagic) {
+      magic_round2(vq, b[2 * e], b[2 * e + 1]);
+    } else {
+      float a, c;
+      f2_unpack(vq, a, c);
+      b[2 * e] = static_cast<uint32_t>(__float2int_rn(a));
+      b[2 * e + 1] = static_cast<uint32_t>(__float2int_rn(c));
+    }
+  }
+  q0 = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+  q1 = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
+}
+
 constexpr int kRowsMaxPixPerWarp = 256;
 
 inline int rows_pixels_per_warp(const QuantParams& q, bool i8) {
@@ -371,22 +412,28 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p,
             v[it] = *reinterpret_cast<const uint4*>(
                 base + (static_cast<size_t>(h >> ush) * s.src_w + (w >> ush)) * s.ldc + cidx * 8);
         }
+        // rounding by the 1.5*2^23 addend (see quantize_nchw_kernel) when every lane's inputs stay in
+        // its exact range, else float-to-int; the choice is warp-uniform
+        bool magic = true;
+        if (kI8) {
+          __half2 hm = __float2half2_rn(0.0f);
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const __half2* h2 = reinterpret_cast<const __half2*>(&v[it]);
+            hm = __hmax2(hm, __hmax2(__hmax2(__habs2(h2[0]), __habs2(h2[1])), __hmax2(__habs2(h2[2]), __habs2(h2[3]))));
+          }
+          magic = __all_sync(0xffffffffu, fmaxf(__low2float(hm), __high2float(hm)) * mult < 4194304.0f);
+        }
 #pragma unroll
         for (int it = 0; it < 8; ++it) {
           if (b * 8 + it >= per_lane) break;  // warp-uniform
           const int dpix = s_pix[warp][(b * 8 + it) * P + pl].y;
           if (kI8) {
-            const __half2* h2 = reinterpret_cast<const __half2*>(&v[it]);
-            int q[8];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = __half22float2(h2[e]);
-              q[2 * e] = __float2int_rn(__fmul_rn(f.x, mult));
-              q[2 * e + 1] = __float2int_rn(__fmul_rn(f.y, mult));
-            }
-            // low byte of each code (two's complement wrap, no clamp), four per word
-            const uint32_t q0 = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
-            const uint32_t q1 = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
+            uint32_t q0, q1;
+            if (magic)
+              codes8<true>(v[it], mult, q0, q1);
+            else
+              codes8<false>(v[it], mult, q0, q1);
             const uint32_t r0 = __shfl_down_sync(0xffffffffu, q0, 1);
             const uint32_t r1 = __shfl_down_sync(0xffffffffu, q1, 1);
             if ((cl & 1) == 0 && cact && dpix >= 0)
@@ -444,10 +491,46 @@ __global__ void __launch_bounds__(256) pack_nchw_f32_kernel(const float* __restr
   }
 }
 
-// NCHW fp16 single source -> int8 slab16, stride-1 layout, H*W % 8 == 0: each
-// thread quantizes 8 consecutive pixels of the 16 channels of one slab (16
-// coalesced 16-byte loads) and transposes in registers into eight 16-byte
-// pixel rows (128 contiguous bytes per thread).
+// NCHW fp16 single source -> int8 slab16, stride-1 layout, H*W % 4 == 0: each
+// thread quantizes 4 consecutive pixels of the 16 channels of one slab (16
+// coalesced 8-byte loads) and transposes in registers into four 16-byte pixel
+// rows (64 contiguous bytes per thread).  Rounding: v = fl32(x * mult), then
+// fl32(v + 1.5*2^23) holds rint(v) (round half even) in its low mantissa bits,
+// so the code's byte is the low byte of that float; exact for |v| < 2^22, which
+// a consistent amax guarantees (|v| <= 127).  A thread whose inputs could leave
+// that range (|x| * mult >= 2^22: an amax below the data) takes the
+// float-to-int conversion instead, with the same two's-complement low byte.
+// Codes of 4 pixels x 16 channels (v[c] = 4 halves of channel c) packed as
+// q[pixel][word], word k = channels 4k..4k+3 in byte order.
+template <bool kMagic>
+__device__ __forceinline__ void quantize_nchw_words(const uint2 (&v)[16], float mult, uint32_t (&q)[4][4]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint32_t b[4][4];  // [channel][pixel]: low byte = code
+    const uint64_t m2 = f2_pack(mult, mult);
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const __half2* h2 = reinterpret_cast<const __half2*>(&v[4 * k + cc]);
+#pragma unroll
+      for (int hp = 0; hp < 2; ++hp) {
+        const float2 f = __half22float2(h2[hp]);
+        const uint64_t vq = f2_mul(f2_pack(f.x, f.y), m2);  // fl32(x * mult), two at a time
+        if (kMagic) {
+          magic_round2(vq, b[cc][2 * hp], b[cc][2 * hp + 1]);
+        } else {
+          float a, c;
+          f2_unpack(vq, a, c);
+          b[cc][2 * hp] = static_cast<uint32_t>(__float2int_rn(a));
+          b[cc][2 * hp + 1] = static_cast<uint32_t>(__float2int_rn(c));
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      q[j][k] = __byte_perm(__byte_perm(b[0][j], b[1][j], 0x0040), __byte_perm(b[2][j], b[3][j], 0x0040), 0x5410);
+  }
+}
+
 __global__ void __launch_bounds__(256) quantize_nchw_kernel(const QuantParams p) {
   __shared__ float s_mult[kMaxSlabs];
   __shared__ float s_red[2];
@@ -455,33 +538,34 @@ __global__ void __launch_bounds__(256) quantize_nchw_kernel(const QuantParams p)
   const int n = blockIdx.z;
   slab_multipliers(p, n, s_mult, s_red);
   const int hw = p.h * p.w;
-  const int px0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const int px0 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (px0 >= hw) return;
   const QuantSrc& s = p.src[0];
   const float mult = s_mult[slab];
-  uint32_t q[8][4];
-#pragma unroll
-  for (int j = 0; j < 8; ++j)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) q[j][k] = 0u;
   const __half* base = static_cast<const __half*>(s.ptr) + (static_cast<size_t>(n) * s.ch + slab * 16) * hw + px0;
-  uint4 v[16];
+  uint2 v[16];
   const int nch = min(16, s.ch - slab * 16);
 #pragma unroll
   for (int c = 0; c < 16; ++c)  // all 16 loads issued before any is used
-    v[c] = c < nch ? *reinterpret_cast<const uint4*>(base + static_cast<size_t>(c) * hw) : make_uint4(0, 0, 0, 0);
+    v[c] = c < nch ? *reinterpret_cast<const uint2*>(base + static_cast<size_t>(c) * hw) : make_uint2(0u, 0u);
+  // range guard: max |x| of the thread's 64 inputs
+  __half2 hm = __float2half2_rn(0.0f);
 #pragma unroll
   for (int c = 0; c < 16; ++c) {
-    const __half* hv = reinterpret_cast<const __half*>(&v[c]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint32_t b = mult != 0.0f ? static_cast<uint32_t>(__float2int_rn(__fmul_rn(__half2float(hv[j]), mult))) & 0xFFu : 0u;
-      q[j][c >> 2] |= b << (8 * (c & 3));
-    }
+    const __half2* h2 = reinterpret_cast<const __half2*>(&v[c]);
+    hm = __hmax2(hm, __hmax2(__habs2(h2[0]), __habs2(h2[1])));
+  }
+  const bool fast = fmaxf(__low2float(hm), __high2float(hm)) * mult < 4194304.0f;
+  uint32_t q[4][4];
+  // warp-uniform choice (over the lanes still active past the tail), so only one rounding runs
+  if (__all_sync(__activemask(), fast)) {
+    quantize_nchw_words<true>(v, mult, q);
+  } else {
+    quantize_nchw_words<false>(v, mult, q);
   }
   uint4* out = reinterpret_cast<uint4*>(static_cast<int8_t*>(p.out) + ((static_cast<size_t>(n) * p.slabs + slab) * hw + px0) * 16);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) out[j] = make_uint4(q[j][0], q[j][1], q[j][2], q[j][3]);
+  for (int j = 0; j < 4; ++j) out[j] = make_uint4(q[j][0], q[j][1], q[j][2], q[j][3]);
 }
 
 }  // namespace aexrt

@@ -245,7 +245,11 @@ def pg16_sum(acc_g: np.ndarray, gscale: np.ndarray) -> np.ndarray:
 
     ``acc_g`` is ``[N, G, OC, ...]`` int32, ``gscale`` ``[N, G]`` fp32.  This is
     the float part of the pg16 kernels (runtime.cpp:3466-3468, 3616-3618) and of
-    the reference's known-answer check (mobile/hal/vk_hal.c:238-245).
+    the reference's known-answer check (mobile/hal/vk_hal.c:238-245).  The
+    shader source's ``fp += float(sub) * gs`` leaves contraction to its
+    compiler; the CUDA kernels fuse each step into one FMA, so their fp32 sums
+    may differ from these two-rounding sums in the last bit, which the fp16
+    output tolerance absorbs.
     """
     n, g, oc = acc_g.shape[:3]
     gs = np.asarray(gscale, dtype=F32).reshape(n, g)
