@@ -44,6 +44,12 @@ class AexrtB200DecodeLevel(ctypes.Structure):
                 ("cls_ldc", c_uint32), ("cls_coff", c_uint32), ("h", c_uint32), ("w", c_uint32), ("stride", c_float)]
 
 
+class AexrtYoloDetection(ctypes.Structure):
+    """Same layout as the reference's AexrtYoloDetection (native/aexrt.h:25-32, cpp_runtime.py:43-51)."""
+
+    _fields_ = [(name, c_float) for name in ("x1", "y1", "x2", "y2", "score", "class_id")]
+
+
 class AexrtError(RuntimeError):
     """A C-ABI call returned failure; the message is the library's last error."""
 
@@ -79,6 +85,8 @@ _SIGNATURES = {
                                                                    c_uint32, c_void_p]),
     "aexrt_b200_yolo_decode": (c_int, [POINTER(AexrtB200DecodeLevel), c_uint32, c_uint32, c_uint32, c_uint32, c_void_p,
                                        c_void_p]),
+    "aexrt_b200_yolo_nms_topk": (c_int, [c_void_p] + [c_uint32] * 6 + [c_float, c_float] + [c_uint32] * 3
+                                 + [c_void_p, c_void_p, c_void_p]),
     "aexrt_b200_zero": (c_int, [c_void_p, c_uint64, c_void_p]),
     "aexrt_b200_act_quantize_f16_noalloc": (c_int, [c_void_p] + [c_uint32] * 9 + [c_void_p, c_void_p, c_void_p]),
 }

@@ -21,6 +21,7 @@
 #include "../../include/aexrt_b200.h"
 #include "conv_halo.cuh"
 #include "kernels.cuh"
+#include "nms.cuh"
 #include "quant.cuh"
 #include "stem.cuh"
 #include "yolo_ops.cuh"
@@ -1151,6 +1152,58 @@ int aexrt_b200_yolo_decode(const AexrtB200DecodeLevel* levels, uint32_t nlevels,
   if (total == 0) return 1;
   yolo_decode_kernel<<<static_cast<unsigned>((total + 127) / 128), 128, 0, static_cast<cudaStream_t>(stream)>>>(d);
   return cuda_ok(cudaGetLastError(), "decode launch") ? 1 : 0;
+}
+
+int aexrt_b200_yolo_nms_topk(const float* output0, uint32_t n, uint32_t channels, uint32_t anchors, uint32_t nc,
+                             uint32_t has_objectness, uint32_t layout, float conf_threshold, float iou_threshold,
+                             uint32_t max_candidates, uint32_t max_detections, uint32_t mode,
+                             AexrtYoloDetection* detections, uint32_t* counts, void* stream) {
+  if (!output0 || !detections || !counts) return fail("yolo_nms_topk: null pointer");
+  if (nc == 0 || channels != (has_objectness ? 5u : 4u) + nc)
+    return fail("yolo_nms_topk: channels %u do not match nc %u (objectness %u)", channels, nc, has_objectness);
+  if (layout > 2) return fail("yolo_nms_topk: bad layout %u", layout);
+  if (mode > 1) return fail("yolo_nms_topk: bad mode %u", mode);
+  if (max_candidates == 0 || max_candidates > aexrt::kNmsMaxCandidates)
+    return fail("yolo_nms_topk: max_candidates %u outside 1..%d", max_candidates, aexrt::kNmsMaxCandidates);
+  if (max_detections == 0) return fail("yolo_nms_topk: max_detections must be >= 1");
+  if (static_cast<uint64_t>(channels) * anchors > (1ull << 31)) return fail("yolo_nms_topk: output0 too large");
+  if (n == 0) return 1;
+  aexrt::NmsParams p;
+  p.y = output0;
+  p.anchors = static_cast<int>(anchors);
+  p.channels = static_cast<int>(channels);
+  p.nc = static_cast<int>(nc);
+  p.has_obj = has_objectness ? 1 : 0;
+  p.channels_last = layout == 2 ? 1 : 0;
+  p.conf = conf_threshold;
+  p.iou = iou_threshold;
+  p.max_cand = static_cast<int>(max_candidates);
+  p.max_det = static_cast<int>(max_detections);
+  p.mode = static_cast<int>(mode);
+  p.pow2 = 1;
+  while (p.pow2 < p.max_cand) p.pow2 <<= 1;
+  p.dets = reinterpret_cast<float*>(detections);
+  p.counts = counts;
+  const size_t smem = aexrt::nms_smem_bytes(p.max_cand, p.pow2, p.mode);
+  if (smem > 48 * 1024) {
+    // raised once per device to the largest size seen, so a launch inside a stream capture
+    // that an earlier launch prepared makes no attribute call
+    static std::mutex mu;
+    static size_t raised[128] = {};
+    int dev = 0;
+    if (!cuda_ok(cudaGetDevice(&dev), "cudaGetDevice")) return 0;
+    if (dev < 0 || dev >= 128) return fail("device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (smem > raised[dev]) {
+      if (!cuda_ok(cudaFuncSetAttribute(aexrt::yolo_nms_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)),
+                   "nms smem attribute"))
+        return 0;
+      raised[dev] = smem;
+    }
+  }
+  aexrt::yolo_nms_kernel<<<n, aexrt::kNmsThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  return cuda_ok(cudaGetLastError(), "nms launch") ? 1 : 0;
 }
 
 int aexrt_b200_zero(void* ptr, uint64_t bytes, void* stream) {

@@ -17,10 +17,16 @@ start of each replay.
 Kernel plan: int8 convs become W8A8 plans with the reference's kernel ids
 (51 1x1, 52 3x3 s1, 53 3x3 s2) and INT8_PERGROUP flag; the rest (stem with 3
 input channels, detect head) become fp16 plans.
+
+Post-process: with an :class:`NmsConfig`, the replay ends with the GPU
+confidence filter + NMS + top-k (the reference's record_yolo_decode_nms_topk,
+runtime.cpp:27104-27219), and :meth:`CompiledYolo.detections` holds each
+image's AexrtYoloDetection rows and count, the output of ``aexrt_yolo_run``.
 """
 from __future__ import annotations
 
 import ctypes
+from dataclasses import dataclass
 from typing import Dict, List, Optional
 
 import numpy as np
@@ -36,11 +42,22 @@ def _torch():
     return torch
 
 
+@dataclass
+class NmsConfig:
+    """Post-process settings; the defaults are the reference model's (runtime.cpp:551-561)."""
+
+    conf: float = 0.25
+    iou: float = 0.45
+    max_candidates: int = 512
+    max_detections: int = 100
+    mode: int = ops.NMS_MARK  # the reference GPU path's rule; ops.NMS_GREEDY = yolo_postprocess's
+
+
 class CompiledYolo:
     """One program compiled for one batch size on the current CUDA device."""
 
     def __init__(self, program: YoloProgram, batch: int, device=None, block_n: Optional[Dict[str, int]] = None,
-                 image_dtype=None):
+                 image_dtype=None, nms: Optional[NmsConfig] = None):
         torch = _torch()
         self.program = program
         self.batch = batch
@@ -71,6 +88,8 @@ class CompiledYolo:
         self.image_dtype = torch.float16 if image_dtype is None else image_dtype
         self.images = torch.zeros((n, p.in_channels, p.imgsz, p.imgsz), dtype=self.image_dtype, device=self.device)
         self.output = torch.zeros((n, 4 + p.nc, p.anchors), dtype=torch.float32, device=self.device)
+        self.nms = nms
+        self.det_buf = self._new_det_buf()
         # ---- plans and per-command scratch
         self.steps: List[tuple] = []
         self.plans: Dict[str, ops.ConvPlan] = {}
@@ -81,10 +100,33 @@ class CompiledYolo:
                 self.steps.append(("sppf", c))
             elif isinstance(c, DecodeCmd):
                 self.steps.append(("decode", c))
+                if nms is not None:
+                    self.steps.append(("nms", c))
         self.graph = None
         self.launches_per_run = self._count_launches()
 
     # ------------------------------------------------------------------ compile
+    def _new_det_buf(self):
+        """One byte buffer per output slot: int32 counts [batch], then AexrtYoloDetection [batch][max_det]
+        (a single device->host copy reads both)."""
+        if self.nms is None:
+            return None
+        torch = _torch()
+        n, md = self.batch, self.nms.max_detections
+        return torch.zeros(n * 4 + n * md * 24, dtype=torch.uint8, device=self.device)
+
+    def split_detections(self, buf):
+        """(counts int32 [batch], detections fp32 [batch, max_det, 6]) views of a detection buffer
+        (device or host)."""
+        import torch
+
+        n, md = self.batch, self.nms.max_detections
+        return buf[:n * 4].view(torch.int32), buf[n * 4:].view(torch.float32).view(n, md, 6)
+
+    def detections(self):
+        """(counts, detections) of the last forward."""
+        return self.split_detections(self.det_buf)
+
     def _amax_view(self, value: str):
         g = self.amax_groups[value]
         o = self.amax_off[value]
@@ -204,6 +246,12 @@ class CompiledYolo:
                     lv[i].h, lv[i].w, lv[i].stride = v.h, v.w, stride
                 check(lib.aexrt_b200_yolo_decode(lv, len(c.levels), n, c.nc, c.reg_max, self.output.data_ptr(), stream),
                       "decode")
+            elif kind == "nms":
+                c, cfg = st[1], self.nms
+                counts, dets = self.split_detections(self.det_buf)
+                check(lib.aexrt_b200_yolo_nms_topk(self.output.data_ptr(), n, 4 + c.nc, self.program.anchors, c.nc, 0,
+                                                   1, cfg.conf, cfg.iou, cfg.max_candidates, cfg.max_detections,
+                                                   cfg.mode, dets.data_ptr(), counts.data_ptr(), stream), "nms")
 
     def capture(self) -> None:
         """Records one forward into a CUDA graph (warm-up run first, as graph capture requires)."""
@@ -238,17 +286,22 @@ class CompiledYolo:
         shared, since the graphs replay one after another on the compute stream."""
         torch = _torch()
         n, p = self.batch, self.program
-        self.slot_images, self.slot_outputs, self.slot_graphs = [], [], []
-        images, output, graph = self.images, self.output, self.graph
+        self.slot_images, self.slot_output0, self.slot_outputs, self.slot_graphs = [], [], [], []
+        images, output, graph, det_buf = self.images, self.output, self.graph, self.det_buf
         for _ in range(slots):
             self.images = torch.zeros((n, p.in_channels, p.imgsz, p.imgsz), dtype=self.image_dtype, device=self.device)
             self.output = torch.zeros((n, 4 + p.nc, p.anchors), dtype=torch.float32, device=self.device)
+            self.det_buf = self._new_det_buf()
             self.graph = None
             self.capture()
+            # every buffer a slot graph touches stays referenced as long as the graph: the next
+            # capture empties the allocator cache, which would unmap a released one
             self.slot_images.append(self.images)
-            self.slot_outputs.append(self.output)
+            self.slot_output0.append(self.output)
+            # with NMS the slot's read-back is its detection buffer, else its output0
+            self.slot_outputs.append(self.det_buf if self.nms is not None else self.output)
             self.slot_graphs.append(self.graph)
-        self.images, self.output, self.graph = images, output, graph
+        self.images, self.output, self.graph, self.det_buf = images, output, graph, det_buf
         self.compute_stream = torch.cuda.Stream(device=self.device)
         self.upload_stream = torch.cuda.Stream(device=self.device)
         self.download_stream = torch.cuda.Stream(device=self.device)
@@ -260,8 +313,10 @@ class CompiledYolo:
         reading host_outputs).
 
         host_inputs[k] (pinned, the engine's image dtype, [batch, 3, imgsz, imgsz]) is uploaded into slot k % slots,
-        its forward replays that slot's graph, and the detections are read back into
-        host_outputs[k % len(host_outputs)] (pinned fp32 [batch, 4 + nc, anchors])."""
+        its forward replays that slot's graph, and its result is read back into
+        host_outputs[k % len(host_outputs)]: with NMS a pinned uint8 buffer shaped like
+        ``det_buf`` (split it with :meth:`split_detections`), else pinned fp32 output0
+        [batch, 4 + nc, anchors]."""
         torch = _torch()
         slots = len(self.slot_graphs)
         cs, us, ds = self.compute_stream, self.upload_stream, self.download_stream
@@ -310,10 +365,11 @@ def main(argv=None) -> int:
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--imgsz", type=int, default=320)
     ap.add_argument("--forwards", type=int, default=2)
+    ap.add_argument("--no-nms", action="store_true", help="stop at output0 (no GPU filter + NMS + top-k)")
     a = ap.parse_args(argv)
     torch = _torch()
     program = yolo.build_yolov8n(nc=4, imgsz=a.imgsz, seed=0)
-    eng = CompiledYolo(program, a.batch)
+    eng = CompiledYolo(program, a.batch, nms=None if a.no_nms else NmsConfig())
     x = torch.from_numpy(np.random.default_rng(0).uniform(0, 1, (a.batch, 3, a.imgsz, a.imgsz)).astype(np.float16))
     x = x.to(eng.device)
     for _ in range(a.forwards):

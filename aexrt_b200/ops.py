@@ -8,6 +8,7 @@ The functions mirror the steps of the reference's int8 conv branch
 * :func:`act_quantize`               — aexrt_int8_quant_pack[_pg] (runtime.cpp:3277-3361)
 * :class:`ConvPlan` / :meth:`ConvPlan.run` — prequant conv kernels 51/52/53 (runtime.cpp:4614-4923)
 * :func:`conv_w8a8_layer`            — the whole branch: amax -> quantize -> conv
+* :func:`yolo_nms_topk`              — decode-filter + NMS + top-k (runtime.cpp:27104-27219)
 
 Every device call goes through ``libaexrt_b200.so``; there is no CPU or
 PyTorch fallback for any of them.
@@ -31,6 +32,8 @@ LAYOUT_NCHW_F16 = 1
 LAYOUT_NCHW_F32 = 2
 SCALE_PER_TENSOR = 0
 SCALE_PG16 = 1
+NMS_MARK = 0
+NMS_GREEDY = 1
 
 
 def _torch():
@@ -290,3 +293,26 @@ def conv_w8a8_layer(plan: ConvPlan, x_nhwc, mode: int = SCALE_PER_TENSOR, residu
     amax = act_amax(x_nhwc, LAYOUT_NHWC_F16, stream=stream)
     q, rec = act_quantize(x_nhwc, amax, mode, LAYOUT_NHWC_F16, consumer_stride=d.stride_h, stream=stream)
     return plan.run(q, rec, out=out, residual=residual, amax_out=amax_out, stream=stream)
+
+
+def yolo_nms_topk(output0, nc: int, conf: float = 0.25, iou: float = 0.45, max_candidates: int = 512,
+                  max_detections: int = 100, mode: int = NMS_MARK, has_objectness: bool = False,
+                  channels_last: bool = False, dets=None, counts=None, stream=None):
+    """Detections of a batch of fp32 output0 tensors ([n, 4 + nc, anchors], or [n, anchors, 4 + nc]
+    when `channels_last`): returns (dets [n, max_detections, 6] fp32 rows x1, y1, x2, y2, score,
+    class; counts [n] int32).  Rows at and beyond counts[i] are zero.
+
+    Defaults are the reference model's (runtime.cpp:551-561): 512 candidates, 100 detections,
+    conf 0.25, IoU 0.45, the GPU path's NMS rule; ``mode=NMS_GREEDY`` gives yolo_postprocess's."""
+    torch = _torch()
+    n = output0.shape[0]
+    channels = output0.shape[2] if channels_last else output0.shape[1]
+    anchors = output0.shape[1] if channels_last else output0.shape[2]
+    if dets is None:
+        dets = torch.zeros((n, max_detections, 6), dtype=torch.float32, device=output0.device)
+    if counts is None:
+        counts = torch.zeros((n,), dtype=torch.int32, device=output0.device)
+    check(_native.load().aexrt_b200_yolo_nms_topk(
+        output0.data_ptr(), n, channels, anchors, nc, int(has_objectness), 2 if channels_last else 1, conf, iou,
+        max_candidates, max_detections, mode, dets.data_ptr(), counts.data_ptr(), _stream(stream)), "yolo_nms_topk")
+    return dets, counts

@@ -263,6 +263,39 @@ typedef struct AexrtB200DecodeLevel {
 int aexrt_b200_yolo_decode(const AexrtB200DecodeLevel* levels, uint32_t nlevels, uint32_t n, uint32_t nc,
                            uint32_t reg_max, float* out, void* stream);
 
+/* One detection, layout-identical to the reference's AexrtYoloDetection
+ * (native/aexrt.h:25-32): box corners in input pixels, score, class index as float. */
+typedef struct AexrtYoloDetection {
+    float x1;
+    float y1;
+    float x2;
+    float y2;
+    float score;
+    float class_id;
+} AexrtYoloDetection;
+
+#define AEXRT_B200_NMS_MARK 0u   /* the reference GPU path's rule (runtime.cpp:15637-15691) */
+#define AEXRT_B200_NMS_GREEDY 1u /* yolo_postprocess's greedy rule (src/aexrt/yolo.py:996-1007) */
+#define AEXRT_B200_NMS_MAX_CANDIDATES 1024u
+
+/* Post-process of a batch of YOLO output0 tensors into detections: replaces the
+ * reference's decode-filter, NMS-mark and top-k dispatches
+ * (record_yolo_decode_nms_topk, runtime.cpp:27104-27219; shaders :15300-15355,
+ * :15637-15733) and, in greedy mode, yolo_postprocess (src/aexrt/yolo.py:92-138).
+ *   output0: fp32 [n][channels][anchors] (layout 0 or 1) or [n][anchors][channels]
+ *            (layout 2, the shader's channels-last case); channels = 4 (+1 with
+ *            objectness) + nc: cx, cy, w, h, [objectness], class scores.
+ *   Per image: best class = first maximum of (objectness *) class score, kept when
+ *   score >= conf_threshold; the first max_candidates such anchors in anchor order
+ *   are the candidates; NMS per class with IoU > iou_threshold; the kept boxes by
+ *   (score desc, anchor order) fill detections[img * max_detections ...] and
+ *   counts[img] = min(kept, max_detections); the rows after the count are zeroed.
+ *   max_candidates <= AEXRT_B200_NMS_MAX_CANDIDATES (the reference default is 512). */
+int aexrt_b200_yolo_nms_topk(const float* output0, uint32_t n, uint32_t channels, uint32_t anchors, uint32_t nc,
+                             uint32_t has_objectness, uint32_t layout, float conf_threshold, float iou_threshold,
+                             uint32_t max_candidates, uint32_t max_detections, uint32_t mode,
+                             AexrtYoloDetection* detections, uint32_t* counts, void* stream);
+
 /* cudaMemsetAsync(ptr, 0, bytes, stream): clears amax slots inside a captured graph. */
 int aexrt_b200_zero(void* ptr, uint64_t bytes, void* stream);
 

@@ -17,6 +17,10 @@ Two kinds of fixture are written:
    oracle (amax, int8 codes, int32 accumulators, fp32/fp16 outputs).  The
    reference has no W8A8 golden vectors of its own, so these are regression
    pins of the restatement, not of the reference.
+4. ``yolo_post.npz`` — synthetic YOLO output0 tensors (clustered boxes, so NMS
+   has work) and the detections that the REFERENCE'S OWN ``yolo_postprocess``
+   (src/aexrt/yolo.py:92-138) returns for them.  They pin the greedy mode of
+   the post-process oracle and kernel.
 
 Usage (needs the reference source tree, which only the build container has)::
 
@@ -148,18 +152,73 @@ def make_act_cases():
     np.savez_compressed(os.path.join(HERE, "act_cases.npz"), **out)
 
 
+def synthetic_head_output(rng, nc: int, anchors: int, objects: int, imgsz: float = 320.0) -> np.ndarray:
+    """One image's output0 [4 + nc][anchors] float32: anchors scattered around `objects` boxes
+    (jittered copies of each, so neighbours overlap) plus background anchors with low class
+    scores.  Scores are continuous, so ties (whose order the reference leaves to numpy's sort)
+    do not occur."""
+    sig = lambda z: 1.0 / (1.0 + np.exp(-z))  # noqa: E731
+    ctr = rng.uniform(0, imgsz, (objects, 2))
+    size = rng.uniform(8, 120, (objects, 2))
+    cls = rng.integers(0, nc, objects)
+    owner = rng.integers(-objects, objects, anchors)  # negative: background anchor
+    y = np.empty((4 + nc, anchors), dtype=np.float32)
+    fg = owner >= 0
+    o = np.where(fg, owner, 0)
+    y[0] = np.where(fg, ctr[o, 0] + rng.normal(0, 0.08, anchors) * size[o, 0], rng.uniform(0, imgsz, anchors))
+    y[1] = np.where(fg, ctr[o, 1] + rng.normal(0, 0.08, anchors) * size[o, 1], rng.uniform(0, imgsz, anchors))
+    y[2] = np.where(fg, size[o, 0] * np.exp(rng.normal(0, 0.15, anchors)), rng.uniform(4, 60, anchors))
+    y[3] = np.where(fg, size[o, 1] * np.exp(rng.normal(0, 0.15, anchors)), rng.uniform(4, 60, anchors))
+    logits = rng.normal(-4.0, 1.5, (nc, anchors))
+    logits[cls[o[fg]], np.nonzero(fg)[0]] = rng.normal(1.0, 1.5, int(fg.sum()))
+    y[4:] = sig(logits)
+    return y
+
+
+POST_CASES = [
+    # name, nc, anchors, objects, conf, iou, seed
+    ("nc4_a", 4, 1000, 12, 0.25, 0.45, 11),
+    ("nc4_b", 4, 1000, 30, 0.25, 0.45, 12),
+    ("nc4_iou07", 4, 1000, 20, 0.25, 0.7, 13),
+    ("nc20_conf01", 20, 600, 16, 0.1, 0.45, 14),
+    ("nc1", 1, 800, 25, 0.3, 0.5, 15),
+]
+
+
+def make_post_cases(ref_yolo):
+    out = {}
+    for name, nc, anchors, objects, conf, iou, seed in POST_CASES:
+        y = synthetic_head_output(np.random.default_rng(seed), nc, anchors, objects)
+        dets = ref_yolo.yolo_postprocess(y[None], conf, iou, layout="channels_first",
+                                         objectness=False)
+        rows = np.array([list(d.xyxy) + [d.score, d.class_id] for d in dets], dtype=np.float32).reshape(-1, 6)
+        out[name + ".y"] = y
+        out[name + ".meta"] = np.array([nc, conf, iou], dtype=np.float64)
+        out[name + ".dets"] = rows
+    out["names"] = np.array([c[0] for c in POST_CASES])
+    np.savez_compressed(os.path.join(HERE, "yolo_post.npz"), **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", default=None, help="path to the reference's src/ directory")
+    ap.add_argument("--only", default=None, choices=["weights", "engine", "act", "post"])
     args = ap.parse_args()
+    want = lambda k: args.only in (None, k)  # noqa: E731
     if args.reference_src:
         sys.path.insert(0, args.reference_src)
         import aexrt
         from aexrt import engine as ref_engine
+        from aexrt import yolo as ref_yolo
 
-        make_weights(ref_engine)
-        make_tiny_engine(aexrt)
-    make_act_cases()
+        if want("weights"):
+            make_weights(ref_engine)
+        if want("engine"):
+            make_tiny_engine(aexrt)
+        if want("post"):
+            make_post_cases(ref_yolo)
+    if want("act"):
+        make_act_cases()
 
 
 if __name__ == "__main__":

@@ -105,3 +105,29 @@ def test_unaligned_nhwc_slices_are_refused_before_any_launch():
     assert "aligned" in _native.last_error()
     assert lib.aexrt_b200_pack_f16(ctypes.c_void_p(4104), 1, 32, 4, 4, 0, 32, 0, 1, dummy, None) == 0
     assert "aligned" in _native.last_error()
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(channels=9), "do not match nc"),
+    (dict(max_candidates=0), "max_candidates"),
+    (dict(max_candidates=1025), "max_candidates"),
+    (dict(max_detections=0), "max_detections"),
+    (dict(mode=2), "bad mode"),
+    (dict(layout=3), "bad layout"),
+])
+def test_nms_arguments_fail_closed(kw, msg):
+    """Invalid post-process arguments are refused before any launch (no GPU needed)."""
+    lib = _native.load()
+    a = dict(channels=8, anchors=100, nc=4, has_obj=0, layout=1, max_candidates=512, max_detections=100, mode=0)
+    a.update(kw)
+    fake = ctypes.c_void_p(256)  # never dereferenced: validation fails first
+    ok = lib.aexrt_b200_yolo_nms_topk(fake, 1, a["channels"], a["anchors"], a["nc"], a["has_obj"], a["layout"], 0.25,
+                                      0.45, a["max_candidates"], a["max_detections"], a["mode"], fake, fake, None)
+    assert ok == 0
+    assert msg in _native.last_error()
+
+
+def test_detection_struct_matches_reference():
+    # native/aexrt.h:25-32: six floats
+    assert ctypes.sizeof(_native.AexrtYoloDetection) == 24
+    assert [f[0] for f in _native.AexrtYoloDetection._fields_] == ["x1", "y1", "x2", "y2", "score", "class_id"]

@@ -122,3 +122,47 @@ def test_streaming_slots_match_single_forwards(v8n):
     for k in range(len(batches)):
         assert torch.equal(host_out[k], want[k]), k
     assert eng.status() == 0
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_detections_match_oracle_postprocess(v8n, mode):
+    """The replay's post-process equals the oracle's on the device's own output0, bit for bit."""
+    from aexrt_b200 import engine
+    from oracle import yolo_post as op
+
+    torch = _torch()
+    cfg = engine.NmsConfig(conf=0.25, iou=0.45, max_candidates=512, max_detections=100, mode=mode)
+    eng = engine.CompiledYolo(v8n, 3, nms=cfg)
+    eng.capture()
+    out = eng.forward(torch.from_numpy(_images(3, seed=21)).cuda()).cpu().numpy()
+    counts, dets = (t.cpu().numpy() for t in eng.detections())
+    for i in range(3):
+        ref, cnt = op.postprocess(out[i], v8n.nc, cfg.conf, cfg.iou, cfg.max_candidates, cfg.max_detections, mode)
+        assert counts[i] == cnt
+        assert np.array_equal(dets[i, :cnt], ref), i
+    assert eng.status() == 0
+
+
+def test_streaming_detections_match_forwards(v8n):
+    """With NMS the streaming API reads back each batch's detection buffer (counts + rows)."""
+    from aexrt_b200 import engine
+
+    torch = _torch()
+    eng = engine.CompiledYolo(v8n, 2, nms=engine.NmsConfig())
+    batches = [_images(2, seed=30 + k) for k in range(4)]
+    want = []
+    for b in batches:
+        eng.forward(torch.from_numpy(b).cuda())
+        want.append(eng.det_buf.clone().cpu())
+    eng.capture_slots(2)
+    # each slot graph writes its own output0 before the post-process reads it: those buffers must
+    # outlive the capture (the next capture empties the allocator cache)
+    assert len(eng.slot_output0) == 2 and eng.slot_output0[0].data_ptr() != eng.slot_output0[1].data_ptr()
+    host_in = [torch.from_numpy(b).pin_memory() for b in batches]
+    host_out = [torch.empty_like(want[0]).pin_memory() for _ in batches]
+    eng.stream(host_in, host_out)
+    torch.cuda.synchronize()
+    for k in range(len(batches)):
+        counts, _ = eng.split_detections(host_out[k])
+        assert torch.equal(host_out[k], want[k]), k
+        assert int(counts.max()) <= 100

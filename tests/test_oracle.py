@@ -107,3 +107,58 @@ def test_tiny_engine_kernel_plan(golden_dir):
     convs = [r for r in plan if int(r[1]) in (1, 2)]
     assert [int(r[2]) for r in convs] == [52, 53, 51]
     assert [bool(int(r[5]) & 16) for r in convs] == [True, False, False]
+
+
+# ---------------------------------------------------------------- YOLO post-process
+def _post_cases(golden_dir):
+    d = np.load(f"{golden_dir}/yolo_post.npz")
+    for name in d["names"]:
+        nc, conf, iou = d[name + ".meta"]
+        yield str(name), d[name + ".y"], int(nc), float(conf), float(iou), d[name + ".dets"]
+
+
+def test_post_greedy_matches_reference_yolo_postprocess(golden_dir):
+    """Greedy mode reproduces the reference's own yolo_postprocess (src/aexrt/yolo.py:92-138) bit for bit."""
+    from oracle import yolo_post as op
+
+    for name, y, nc, conf, iou, ref in _post_cases(golden_dir):
+        dets, count = op.postprocess(y, nc, conf, iou, max_candidates=1 << 20, max_detections=1 << 20,
+                                     mode=op.MODE_GREEDY)
+        assert count == ref.shape[0], name
+        assert np.array_equal(dets, ref), name
+
+
+def test_post_mark_rule_matches_shader_loops(golden_dir):
+    """The vectorised mark rule equals the mark shader's loop (runtime.cpp:15664-15684) written out."""
+    from oracle import yolo_post as op
+
+    for name, y, nc, conf, iou, _ in _post_cases(golden_dir):
+        cand = op.decode_filter(y, nc, conf, 300)
+        assert np.array_equal(op.nms_keep(cand, iou, op.MODE_MARK), op.nms_mark_loops(cand, iou)), name
+    # ties: equal scores rank by candidate index, as the shader's `score_j == score_i && j < i`
+    cand = np.array([[0, 0, 10, 10, 0.5, 0], [1, 1, 11, 11, 0.5, 0], [2, 2, 12, 12, 0.5, 0],
+                     [50, 50, 60, 60, 0.5, 0], [0, 0, 10, 10, 0.9, 1]], np.float32)
+    keep = op.nms_keep(cand, 0.45, op.MODE_MARK)
+    assert list(keep) == [True, False, False, True, True]
+    assert np.array_equal(keep, op.nms_mark_loops(cand, 0.45))
+    # mark drops box 2 (suppressed by box 1, itself suppressed); greedy keeps it
+    cand = np.array([[0, 0, 10, 10, 0.9, 0], [4, 0, 14, 10, 0.8, 0], [8, 0, 18, 10, 0.7, 0]], np.float32)
+    assert list(op.nms_keep(cand, 0.3, op.MODE_MARK)) == [True, False, False]
+    assert list(op.nms_keep(cand, 0.3, op.MODE_GREEDY)) == [True, False, True]
+
+
+def test_post_candidate_cap_and_topk():
+    from oracle import yolo_post as op
+
+    rng = np.random.default_rng(3)
+    y = rng.uniform(0, 1, (6, 400)).astype(np.float32)
+    y[:2] *= 320
+    y[2:4] = y[2:4] * 20 + 2
+    cand = op.decode_filter(y, 2, 0.0, 100)
+    assert cand.shape[0] == 100  # the first 100 anchors in anchor order
+    assert np.array_equal(cand[:, 4], np.maximum(y[4], y[5])[:100])
+    dets, count = op.postprocess(y, 2, 0.0, 0.45, 100, 7)
+    assert count == 7 and dets.shape == (7, 6)
+    assert np.all(np.diff(dets[:, 4]) <= 0)
+    dets, count = op.postprocess(y, 2, 2.0, 0.45, 100, 7)
+    assert count == 0 and dets.shape == (0, 6)
