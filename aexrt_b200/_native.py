@@ -74,6 +74,8 @@ _SIGNATURES = {
                                     c_uint32, c_uint32, c_void_p]),
     "aexrt_b200_conv_f16_image": (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint32, c_uint32, c_void_p, c_uint32,
                                           c_uint32, c_void_p]),
+    "aexrt_b200_conv_f16_nhwc": (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_uint32, c_uint32,
+                                         c_void_p, c_uint32, c_uint32, c_void_p]),
     "aexrt_b200_conv_status": (c_int, [c_void_p, POINTER(c_uint32)]),
     "aexrt_b200_packed_f16_bytes": (c_uint64, [c_uint32] * 5),
     "aexrt_b200_pack_f16": (c_int, [c_void_p] + [c_uint32] * 8 + [c_void_p, c_void_p]),

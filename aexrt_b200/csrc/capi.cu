@@ -544,9 +544,11 @@ bool encode_act_map(const AexrtB200ConvPlan* p, const void* x, CUtensorMap* map)
   return encode_map(map, dt, 5, x, dims, strides, box);
 }
 
+// nhwc_map: an fp16 stride-1 halo plan reading the NHWC activation directly (see aexrt_b200_conv_f16_nhwc)
 int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_rec, const void* res, uint32_t res_ldc,
                 uint32_t res_coff, void* out, uint32_t out_ldc, uint32_t out_coff, uint32_t* amax_out,
-                uint32_t amax_stride, uint32_t amax_goff, int32_t* acc_dump, void* stream) {
+                uint32_t amax_stride, uint32_t amax_goff, int32_t* acc_dump, void* stream,
+                const CUtensorMap* nhwc_map = nullptr) {
   if (!p) return fail("null plan");
   if (!x || !out) return fail("null input/output pointer");
   if (!p->f16 && !scale_rec) return fail("null scale record");
@@ -559,7 +561,10 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     return fail("amax_out slots out of range (need amax_goff + ceil(oc/16) <= amax_stride, coff %% 16 == 0)");
   if (reinterpret_cast<uintptr_t>(x) % 16) return fail("packed input must be 16-byte aligned");
   CUtensorMap act_map;
-  if (!encode_act_map(p, x, &act_map)) return 0;
+  if (nhwc_map)
+    act_map = *nhwc_map;
+  else if (!encode_act_map(p, x, &act_map))
+    return 0;
   const int out_vec = (out_ldc % 8 == 0 && out_coff % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) ? 1 : 0;
   const int res_vec = (res && res_ldc % 8 == 0 && res_coff % 8 == 0 && reinterpret_cast<uintptr_t>(res) % 16 == 0) ? 1 : 0;
   if (p->halo) {
@@ -612,6 +617,7 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     h.acc_dump = acc_dump;
     h.status = p->d_status;
     h.silu = p->kind == AEXRT_B200_KIND_CONV_SILU;
+    h.nhwc = nhwc_map ? 1 : 0;
     if (p->f16 && res) return fail("fp16 convs take no residual");
     h.mblocks = p->mblocks;
     h.nacc = p->nacc;
@@ -1005,6 +1011,32 @@ int aexrt_b200_conv_f16(const AexrtB200ConvPlan* plan, const void* x_slab8, cons
   if (plan && !plan->f16) return fail("plan is int8; use aexrt_b200_conv_w8a8");
   return launch_conv(plan, x_slab8, nullptr, residual, res_ldc, res_coff, out, out_ldc, out_coff, amax_out,
                      amax_stride, amax_goff, nullptr, stream);
+}
+
+int aexrt_b200_conv_f16_nhwc(const AexrtB200ConvPlan* plan, const void* x, uint32_t ldc, uint32_t coff, void* out,
+                             uint32_t out_ldc, uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride,
+                             uint32_t amax_goff, void* stream) {
+  if (!plan) return fail("null plan");
+  if (!plan->f16) return fail("conv_f16_nhwc: plan is int8; use aexrt_b200_conv_w8a8");
+  if (!plan->halo || plan->stride != 1 || plan->image_input)
+    return fail("conv_f16_nhwc: needs a stride-1 halo plan (info.variant 2); pack with aexrt_b200_pack_f16 instead");
+  const uint32_t ic = plan->desc.in_channels;
+  if (!x) return fail("null input pointer");
+  if (ic % 8 || ldc % 8 || coff % 8 || coff + ic > ldc || reinterpret_cast<uintptr_t>(x) % 16)
+    return fail("conv_f16_nhwc: input slice needs in_channels, ldc and coff multiples of 8, coff + in_channels <= "
+                "ldc and a 16-byte aligned base");
+  // [image][H][W][ldc] fp16 viewed from channel coff: (channel, x, y, image); a halo box is 8 channels x
+  // pitch pixels x (halo rows / pitch) rows, which fills shared memory exactly as the slab8 box does
+  const uint64_t w = plan->desc.in_w, h = plan->desc.in_h;
+  const uint64_t dims[4] = {ic, w, h, plan->desc.batch};
+  const uint64_t strides[3] = {2ull * ldc, 2ull * ldc * w, 2ull * ldc * w * h};
+  const uint32_t box[4] = {8, static_cast<uint32_t>(plan->pitch), static_cast<uint32_t>(plan->halo_rows / plan->pitch),
+                           1};
+  CUtensorMap map;
+  if (!encode_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, static_cast<const __half*>(x) + coff, dims, strides, box))
+    return 0;
+  return launch_conv(plan, x, nullptr, nullptr, 0, 0, out, out_ldc, out_coff, amax_out, amax_stride, amax_goff,
+                     nullptr, stream, &map);
 }
 
 int aexrt_b200_conv_status(const AexrtB200ConvPlan* plan, uint32_t* status) {

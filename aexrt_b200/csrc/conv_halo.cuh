@@ -53,6 +53,7 @@ struct ConvHaloParams {
   uint32_t* status;
   int silu;
   int contiguous;           // tile order: 0 strided over CTAs, 1 one contiguous run per CTA
+  int nhwc;                 // fp16 stride 1: act_map is the NHWC activation (channel, x, y, image) itself
   int issuers;              // MMA issuing threads (1 or 2; 2 needs a half ring to hold a whole tile)
   // pg16 (INT8_PERGROUP): every slab is its own accumulation unit; a K step pairs two taps of
   // one slab (tap_a[m], tap_b[m] < 0: the second half of K has zero weights)
@@ -465,7 +466,12 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
             const int slab = 2 * pr + which;
             const int sn = slab < p.slabs ? img * p.slabs + slab : p.n_img * p.slabs;  // odd count: zero slab
             uint8_t* dst = smem + s * sp.stage_bytes + which * sp.slab_bytes + box * box_bytes;
-            if (p.stride == 2) {
+            if (p.nhwc) {
+              // 8 channels x pitch pixels x halo rows of the NHWC tensor land exactly as the slab8
+              // box would; a zero slab (odd slab count) reads channels past the extent: zero fill
+              const int o = p.ksize == 3 ? 1 : 0;
+              tma_load_4d(dst, &act_map, &full[s], 8 * slab, ow0 - o, oh0 - o, img);
+            } else if (p.stride == 2) {
               tma_load_5d(dst, &act_map, &full[s], kCS * (ow0 - 1), box & 1, box >> 1, oh0 - 1, sn);
             } else if (p.ksize == 3) {
               tma_load_3d(dst, &act_map, &full[s], kCS * (ow0 - 1), oh0 - 1, sn);

@@ -159,6 +159,14 @@ class CompiledYolo:
                 self.plans[c.name] = plan
                 self.steps.append(("stem", c, plan))
                 return
+            pt = c.inputs[0]
+            if (len(c.inputs) == 1 and pt.value != "images" and pt.upsample == 1 and c.s == 1
+                    and plan.info.variant == 2 and c.residual is None and c.ic % 8 == 0 and pt.coff % 8 == 0
+                    and self.values[pt.value].shape[-1] % 8 == 0):
+                # the conv's TMA reads the NHWC activation itself: no slab8 copy
+                self.plans[c.name] = plan
+                self.steps.append(("conv_nhwc", c, plan))
+                return
             hp = h + (h & 1 if c.s == 2 else 0)
             wp = w + (w & 1 if c.s == 2 else 0)
             x8 = torch.empty((n, (c.ic + 7) // 8, hp, wp, 8), dtype=torch.float16, device=self.device)
@@ -220,6 +228,12 @@ class CompiledYolo:
                           f"pack {c.name}")
                     plan.run(x8, out=out, out_coff=c.out[1], residual=res, res_coff=res_coff, amax_out=amax_out,
                              amax_goff=c.out[1] // 16, stream=stream)
+            elif kind == "conv_nhwc":
+                _, c, plan = st
+                out = self.values[c.out[0]]
+                amax_out = self._amax_view(c.out[0]) if c.out[0] in self.needs_amax else None
+                plan.run_nhwc(self.values[c.inputs[0].value], x_coff=c.inputs[0].coff, out=out, out_coff=c.out[1],
+                              amax_out=amax_out, amax_goff=c.out[1] // 16, stream=stream)
             elif kind == "stem":
                 _, c, plan = st
                 out = self.values[c.out[0]]

@@ -131,3 +131,10 @@ def test_detection_struct_matches_reference():
     # native/aexrt.h:25-32: six floats
     assert ctypes.sizeof(_native.AexrtYoloDetection) == 24
     assert [f[0] for f in _native.AexrtYoloDetection._fields_] == ["x1", "y1", "x2", "y2", "score", "class_id"]
+
+
+def test_conv_f16_nhwc_refuses_null_plan():
+    lib = _native.load()
+    assert lib.aexrt_b200_conv_f16_nhwc(None, ctypes.c_void_p(256), 64, 0, ctypes.c_void_p(256), 64, 0, None, 0, 0,
+                                        None) == 0
+    assert "null plan" in _native.last_error()

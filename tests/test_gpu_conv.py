@@ -391,3 +391,35 @@ def test_super_tiles_match_single_blocks(n, ic, h, w, oc, k, s):
     assert np.array_equal(g_auto["out_full"], g_one["out_full"])
     assert np.array_equal(g_auto["amax_out"], g_one["amax_out"])
     assert g_auto["plan"].info.tile_h == g_one["plan"].info.tile_h
+
+
+@pytest.mark.parametrize("n,ic,h,w,oc,k,ldc,coff,silu,block_n", [
+    (2, 64, 20, 20, 64, 3, 64, 0, True, 0),      # detect-head 3x3 shape
+    (2, 64, 40, 40, 64, 1, 64, 0, False, 0),     # detect-head 1x1 (box logits)
+    (3, 24, 13, 17, 16, 3, 72, 40, True, 0),     # odd slab count, channel slice of a wider buffer
+    (2, 32, 9, 30, 128, 3, 48, 8, True, 64),     # two weight tiles, ragged tiles
+    (1, 16, 80, 80, 16, 3, 16, 0, True, 16),     # narrow: stacked M blocks
+])
+def test_fp16_nhwc_input_matches_packed(n, ic, h, w, oc, k, ldc, coff, silu, block_n):
+    """aexrt_b200_conv_f16_nhwc (TMA boxes straight from the NHWC activation) equals pack_f16 +
+    conv_f16 bit for bit, including the epilogue amax."""
+    torch = _torch()
+    from aexrt_b200 import ops
+
+    rng = np.random.default_rng(ic * 7 + oc + ldc)
+    buf = rng.uniform(-1, 1, (n, h, w, ldc)).astype(np.float16)
+    weight = rng.normal(0, 1 / np.sqrt(ic * k * k), (oc, ic, k, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    plan = ops.ConvPlan.fp16(n, ic, h, w, oc, k, 1, weight, bias, silu=silu, block_n=block_n)
+    assert plan.info.variant == 2
+    xt = torch.from_numpy(buf).cuda()
+    groups = (oc + 15) // 16
+    am0 = torch.zeros((n, groups), dtype=torch.int32, device="cuda")
+    am1 = torch.zeros((n, groups), dtype=torch.int32, device="cuda")
+    packed = ops.pack_f16(xt, ops.LAYOUT_NHWC_F16, c=ic, ldc=ldc, coff=coff)
+    ref = plan.run(packed, amax_out=am0)
+    got = plan.run_nhwc(xt, x_coff=coff, amax_out=am1)
+    torch.cuda.synchronize()
+    assert plan.status() == 0
+    assert torch.equal(ref, got)
+    assert torch.equal(am0, am1)

@@ -54,7 +54,7 @@ def test_per_layer_teacher_forced(v8n):
     vals["images"] = imgs
     worst = {}
     for st in eng.steps:
-        if st[0] in ("conv", "stem"):
+        if st[0] in ("conv", "stem", "conv_nhwc"):
             c = st[1]
             x = om._gather(vals, c.inputs)
             res = vals[c.residual[0]][:, c.residual[1]:c.residual[1] + c.oc] if c.residual else None
