@@ -692,8 +692,10 @@ bool rows_ok(const QuantParams& q, bool i8) {
 void launch_quantize(const QuantParams& q, cudaStream_t st) {
   if (rows_ok(q, true)) {
     const int pw = rows_pixels_per_warp(q, true);
-    const dim3 grid((q.hp * q.wp + 8 * pw - 1) / (8 * pw), q.n);
-    quant_rows_kernel<true><<<grid, 256, 0, st>>>(q, pw);
+    const int groups = rows_channel_groups(q, true);
+    const long items = static_cast<long>((q.hp * q.wp + pw - 1) / pw) * groups;  // one warp each
+    const dim3 grid(static_cast<unsigned>((items + 7) / 8), q.n);
+    quant_rows_kernel<true><<<grid, 256, 0, st>>>(q, pw, groups);
   } else if (q.nsrc == 1 && q.src[0].layout == 1 && !q.split && (q.h * q.w) % 4 == 0 && q.slabs <= kMaxSlabs) {
     const dim3 grid((q.h * q.w / 4 + 255) / 256, q.slabs, q.n);
     quantize_nchw_kernel<<<grid, 256, 0, st>>>(q);
@@ -714,8 +716,10 @@ void launch_pack(const QuantParams& q, cudaStream_t st) {
   }
   if (rows_ok(q, false)) {
     const int pw = rows_pixels_per_warp(q, false);
-    const dim3 grid((q.hp * q.wp + 8 * pw - 1) / (8 * pw), q.n);
-    quant_rows_kernel<false><<<grid, 256, 0, st>>>(q, pw);
+    const int groups = rows_channel_groups(q, false);
+    const long items = static_cast<long>((q.hp * q.wp + pw - 1) / pw) * groups;
+    const dim3 grid(static_cast<unsigned>((items + 7) / 8), q.n);
+    quant_rows_kernel<false><<<grid, 256, 0, st>>>(q, pw, groups);
   } else {
     const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, q.n);
     pack_f16_kernel<<<grid, 256, 0, st>>>(q);

@@ -7,6 +7,7 @@
 #pragma once
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cstdint>
 
 namespace aexrt {
@@ -351,19 +352,35 @@ __device__ __forceinline__ void codes8(const uint4& v, float mult, uint32_t& q0,
 
 constexpr int kRowsMaxPixPerWarp = 256;
 
+// Lanes sharing one pixel in a load of source `ch` channels (see quant_rows_kernel).
+__host__ __device__ inline int rows_lanes_per_pixel(int ch, bool i8) {
+  const int nchunks = ch / 8;
+  int l = nchunks >= 8 ? 8 : (nchunks >= 4 ? 4 : (nchunks >= 2 ? 2 : 1));
+  return (i8 && l < 2) ? 2 : l;  // int8: a slab is two chunks, kept in neighbouring lanes
+}
+
 inline int rows_pixels_per_warp(const QuantParams& q, bool i8) {
   int lmax = 1;
-  for (int i = 0; i < q.nsrc; ++i) {
-    const int nchunks = q.src[i].ch / 8;
-    int l = nchunks >= 8 ? 8 : (nchunks >= 4 ? 4 : (nchunks >= 2 ? 2 : 1));
-    if (i8 && l < 2) l = 2;
-    lmax = l > lmax ? l : lmax;
-  }
+  for (int i = 0; i < q.nsrc; ++i) lmax = std::max(lmax, rows_lanes_per_pixel(q.src[i].ch, i8));
   return 32 * 8 / lmax;
 }
 
+// Channel groups of all sources: a group is the L_k chunks one load instruction covers.
+inline int rows_channel_groups(const QuantParams& q, bool i8) {
+  int g = 0;
+  for (int i = 0; i < q.nsrc; ++i) {
+    const int l = rows_lanes_per_pixel(q.src[i].ch, i8);
+    g += (q.src[i].ch / 8 + l - 1) / l;
+  }
+  return g;
+}
+
+// Work item = (pixel group of pw pixels, channel group); one warp per item, items numbered
+// pixel group major (the warps of a block read neighbouring channel ranges of the same pixels),
+// blockIdx.y = image.  Small maps thereby spread their channels over warps and blocks instead of
+// walking them in one warp.
 template <bool kI8>
-__global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p, int pw) {
+__global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p, int pw, int groups) {
   __shared__ float s_mult[kMaxSlabs];
   __shared__ float s_red[2];
   __shared__ int2 s_pix[8][kRowsMaxPixPerWarp];  // per pixel: (row << 16 | column), destination pixel (-1: none)
@@ -371,8 +388,11 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p,
   if (kI8) slab_multipliers(p, n, s_mult, s_red);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int npix = p.hp * p.wp;
-  const int pix0 = (blockIdx.x * 8 + warp) * pw;
+  const int item = blockIdx.x * 8 + warp;
+  const int pg = item / groups;
+  const int pix0 = pg * pw;
   if (pix0 >= npix) return;  // no barrier follows
+  int g = item - pg * groups;
   for (int j = 0; j < pw / 32; ++j) {
     const int pix = pix0 + j * 32 + lane;
     const int h = pix / p.wp, w = pix - (pix / p.wp) * p.wp;
@@ -380,71 +400,73 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p,
     s_pix[warp][j * 32 + lane] = make_int2((h << 16) | w, pix < npix ? dpix : -1);
   }
   __syncwarp();
+  // the item's source k and first chunk j0 within it
+  int k = 0, chunk_base = 0;  // chunk_base: 8-channel chunks of the sources before k
+  for (; k < p.nsrc - 1; ++k) {
+    const int gk = (p.src[k].ch / 8 + rows_lanes_per_pixel(p.src[k].ch, kI8) - 1) / rows_lanes_per_pixel(p.src[k].ch, kI8);
+    if (g < gk) break;
+    g -= gk;
+    chunk_base += p.src[k].ch / 8;
+  }
   const size_t plane = static_cast<size_t>(npix);
   uint8_t* out = static_cast<uint8_t*>(p.out) + static_cast<size_t>(n) * p.slabs * plane * 16;
-  int chunk_base = 0;  // 8-channel chunks of the sources before this one
-  for (int k = 0; k < p.nsrc; ++k) {
-    const QuantSrc& s = p.src[k];
-    const int nchunks = s.ch / 8;
-    int L = nchunks >= 8 ? 8 : (nchunks >= 4 ? 4 : (nchunks >= 2 ? 2 : 1));
-    if (kI8 && L < 2) L = 2;  // a slab is two chunks: keep the pair in neighbouring lanes
-    const int P = 32 / L;
-    const int cl = lane & (L - 1), pl = lane / L;
-    const int ush = s.up == 2 ? 1 : 0;
-    const __half* base = static_cast<const __half*>(s.ptr) + static_cast<size_t>(n) * s.src_h * s.src_w * s.ldc + s.coff;
-    const int per_lane = pw / P;                   // loads per lane covering the warp's pixels
-    const int batches = (per_lane + 7) / 8;        // in groups of up to 8
-    for (int j0 = 0; j0 < nchunks; j0 += L) {
-      const int cidx = j0 + cl;  // chunk of this lane within the source
-      const bool cact = cidx < nchunks;
-      const int slab = kI8 ? (chunk_base + cidx) >> 1 : chunk_base + cidx;
-      const float mult = kI8 && cact ? s_mult[slab] : 0.0f;
-      uint8_t* dst = out + static_cast<size_t>(slab) * plane * 16;
-      for (int b = 0; b < batches; ++b) {
-        uint4 v[8];
+  const QuantSrc& s = p.src[k];
+  const int nchunks = s.ch / 8;
+  const int L = rows_lanes_per_pixel(s.ch, kI8);
+  const int P = 32 / L;
+  const int cl = lane & (L - 1), pl = lane / L;
+  const int ush = s.up == 2 ? 1 : 0;
+  const __half* base = static_cast<const __half*>(s.ptr) + static_cast<size_t>(n) * s.src_h * s.src_w * s.ldc + s.coff;
+  const int per_lane = pw / P;                   // loads per lane covering the warp's pixels
+  const int batches = (per_lane + 7) / 8;        // in groups of up to 8
+  const int j0 = g * L;
+  const int cidx = j0 + cl;  // chunk of this lane within the source
+  const bool cact = cidx < nchunks;
+  const int slab = kI8 ? (chunk_base + cidx) >> 1 : chunk_base + cidx;
+  const float mult = kI8 && cact ? s_mult[slab] : 0.0f;
+  uint8_t* dst = out + static_cast<size_t>(slab) * plane * 16;
+  for (int b = 0; b < batches; ++b) {
+    uint4 v[8];
 #pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          v[it] = make_uint4(0u, 0u, 0u, 0u);
-          if (b * 8 + it >= per_lane) continue;
-          const int2 px = s_pix[warp][(b * 8 + it) * P + pl];
-          const int h = px.x >> 16, w = px.x & 0xFFFF;
-          if (cact && px.y >= 0 && h < p.h && w < p.w)
-            v[it] = *reinterpret_cast<const uint4*>(
-                base + (static_cast<size_t>(h >> ush) * s.src_w + (w >> ush)) * s.ldc + cidx * 8);
-        }
-        // rounding by the 1.5*2^23 addend (see quantize_nchw_kernel) when every lane's inputs stay in
-        // its exact range, else float-to-int; the choice is warp-uniform
-        bool magic = true;
-        if (kI8) {
-          __half2 hm = __float2half2_rn(0.0f);
+    for (int it = 0; it < 8; ++it) {
+      v[it] = make_uint4(0u, 0u, 0u, 0u);
+      if (b * 8 + it >= per_lane) continue;
+      const int2 px = s_pix[warp][(b * 8 + it) * P + pl];
+      const int h = px.x >> 16, w = px.x & 0xFFFF;
+      if (cact && px.y >= 0 && h < p.h && w < p.w)
+        v[it] = *reinterpret_cast<const uint4*>(
+            base + (static_cast<size_t>(h >> ush) * s.src_w + (w >> ush)) * s.ldc + cidx * 8);
+    }
+    // rounding by the 1.5*2^23 addend (see quantize_nchw_kernel) when every lane's inputs stay in
+    // its exact range, else float-to-int; the choice is warp-uniform
+    bool magic = true;
+    if (kI8) {
+      __half2 hm = __float2half2_rn(0.0f);
 #pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const __half2* h2 = reinterpret_cast<const __half2*>(&v[it]);
-            hm = __hmax2(hm, __hmax2(__hmax2(__habs2(h2[0]), __habs2(h2[1])), __hmax2(__habs2(h2[2]), __habs2(h2[3]))));
-          }
-          magic = __all_sync(0xffffffffu, fmaxf(__low2float(hm), __high2float(hm)) * mult < 4194304.0f);
-        }
+      for (int it = 0; it < 8; ++it) {
+        const __half2* h2 = reinterpret_cast<const __half2*>(&v[it]);
+        hm = __hmax2(hm, __hmax2(__hmax2(__habs2(h2[0]), __habs2(h2[1])), __hmax2(__habs2(h2[2]), __habs2(h2[3]))));
+      }
+      magic = __all_sync(0xffffffffu, fmaxf(__low2float(hm), __high2float(hm)) * mult < 4194304.0f);
+    }
 #pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          if (b * 8 + it >= per_lane) break;  // warp-uniform
-          const int dpix = s_pix[warp][(b * 8 + it) * P + pl].y;
-          if (kI8) {
-            uint32_t q0, q1;
-            if (magic)
-              codes8<true>(v[it], mult, q0, q1);
-            else
-              codes8<false>(v[it], mult, q0, q1);
-            const uint32_t r0 = __shfl_down_sync(0xffffffffu, q0, 1);
-            const uint32_t r1 = __shfl_down_sync(0xffffffffu, q1, 1);
-            if ((cl & 1) == 0 && cact && dpix >= 0)
-              *reinterpret_cast<uint4*>(dst + static_cast<size_t>(dpix) * 16) = make_uint4(q0, q1, r0, r1);
-          } else {
-            if (cact && dpix >= 0) *reinterpret_cast<uint4*>(dst + static_cast<size_t>(dpix) * 16) = v[it];
-          }
-        }
+    for (int it = 0; it < 8; ++it) {
+      if (b * 8 + it >= per_lane) break;  // warp-uniform
+      const int dpix = s_pix[warp][(b * 8 + it) * P + pl].y;
+      if (kI8) {
+        uint32_t q0, q1;
+        if (magic)
+          codes8<true>(v[it], mult, q0, q1);
+        else
+          codes8<false>(v[it], mult, q0, q1);
+        const uint32_t r0 = __shfl_down_sync(0xffffffffu, q0, 1);
+        const uint32_t r1 = __shfl_down_sync(0xffffffffu, q1, 1);
+        if ((cl & 1) == 0 && cact && dpix >= 0)
+          *reinterpret_cast<uint4*>(dst + static_cast<size_t>(dpix) * 16) = make_uint4(q0, q1, r0, r1);
+      } else {
+        if (cact && dpix >= 0) *reinterpret_cast<uint4*>(dst + static_cast<size_t>(dpix) * 16) = v[it];
       }
     }
-    chunk_base += nchunks;
   }
 }
 
