@@ -36,6 +36,9 @@ if ROOT not in sys.path:
 METRIC = "W8A8 YOLOv8n-320 images/s"
 WORKLOAD = "yolov8n-320 W8A8 forward (int8 backbone+neck, fp16 head, DFL decode, NMS + top-k)"
 L2_BYTES = 126 * 1024 * 1024
+# DRAM read + write bytes of the 44 W8A8 conv launches of one forward, per image, from one ncu
+# capture at batch 256 (profiles/conv_family_dram_b256.md); valid for that batch only
+CONV_DRAM_BYTES_PER_IMAGE_B256 = 1495.3e6 / 256
 
 
 def parse_args():
@@ -426,7 +429,10 @@ def run_ours(args):
             "e2e": e2e,
             "gpu_launches": eng.launches_per_run * args.steps,
             "roofline": {"bound": "hbm", "achieved": rf["bytes"] / rf["time_s"] / 1e9, "peak": hbm, "unit": "GB/s",
-                         "frac": rf["bytes"] / rf["time_s"] / 1e9 / hbm, "traffic": None,
+                         "frac": rf["bytes"] / rf["time_s"] / 1e9 / hbm,
+                         "traffic": CONV_DRAM_BYTES_PER_IMAGE_B256 * B if B == 256 else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum over the step's W8A8 "
+                                           "conv launches at batch 256 (profiles/conv_family_dram_b256.md)",
                          "kernel": "conv_halo_kernel / conv_tc_kernel: all W8A8 conv launches of one step "
                                    "(algorithmic bytes: int8 input + fp16 output + weights per launch)",
                          "peak_source": f"{src} hbm_gbs from MEASURED_PEAKS.json",
