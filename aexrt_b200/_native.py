@@ -89,6 +89,9 @@ _SIGNATURES = {
                                        c_void_p]),
     "aexrt_b200_yolo_nms_topk": (c_int, [c_void_p] + [c_uint32] * 6 + [c_float, c_float] + [c_uint32] * 3
                                  + [c_void_p, c_void_p, c_void_p]),
+    "aexrt_b200_act_amax_quantize_f16": (c_int, [c_void_p] + [c_uint32] * 5 + [c_void_p, c_uint32, c_uint32, c_void_p,
+                                                                             c_void_p, c_void_p]),
+    "aexrt_b200_act_status": (c_int, [POINTER(c_uint32)]),
     "aexrt_b200_zero": (c_int, [c_void_p, c_uint64, c_void_p]),
     "aexrt_b200_act_quantize_f16_noalloc": (c_int, [c_void_p] + [c_uint32] * 9 + [c_void_p, c_void_p, c_void_p]),
 }

@@ -23,7 +23,7 @@ LIB = os.path.join(HERE, "libaexrt_b200.so")
 SOURCES = ["capi.cu", "kernels_slot.cu", "kernels_halo_i8_silu.cu", "kernels_halo_i8_linear.cu",
            "kernels_halo_f16.cu", "kernels_halo_mb.cu", "kernels_halo_pg.cu",
            "kernels_stem16.cu", "kernels_stem32.cu", "kernels_stem48.cu", "kernels_stem64.cu"]
-HEADERS = ["conv_halo.cuh", "conv_tc.cuh", "kernels.cuh", "nms.cuh", "ptx.cuh", "quant.cuh", "stem.cuh", "yolo_ops.cuh"]
+HEADERS = ["conv_halo.cuh", "conv_tc.cuh", "kernels.cuh", "nms.cuh", "ptx.cuh", "quant.cuh", "quant_cluster.cuh", "stem.cuh", "yolo_ops.cuh"]
 OBJ_DIR = os.path.join(HERE, "_build")
 
 NVCC_FLAGS = [

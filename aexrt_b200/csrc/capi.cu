@@ -23,6 +23,7 @@
 #include "kernels.cuh"
 #include "nms.cuh"
 #include "quant.cuh"
+#include "quant_cluster.cuh"
 #include "stem.cuh"
 #include "yolo_ops.cuh"
 
@@ -873,6 +874,138 @@ int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t 
   q.rec = scale_rec;
   launch_quantize(q, static_cast<cudaStream_t>(stream));
   return cuda_ok(cudaGetLastError(), "quantize launch") ? 1 : 0;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Status word of the activation kernels that wait on their own copies (one per device, resolved
+// once per device like the allocation-free scratch below).
+static __device__ uint32_t g_act_status;
+std::mutex g_act_mutex;
+uint32_t* g_act_status_ptr[128] = {};
+size_t g_cluster_smem_raised[128] = {};
+int g_cluster_fits[128][kClusterQuantMaxCtas + 1] = {};  // per cluster size: 0 unknown, 1 schedulable, -1 not
+
+uint32_t* act_status_word(int dev) {
+  std::lock_guard<std::mutex> lock(g_act_mutex);
+  if (!g_act_status_ptr[dev]) {
+    void* ptr = nullptr;
+    if (!cuda_ok(cudaGetSymbolAddress(&ptr, g_act_status), "cudaGetSymbolAddress")) return nullptr;
+    g_act_status_ptr[dev] = static_cast<uint32_t*>(ptr);
+  }
+  return g_act_status_ptr[dev];
+}
+
+// Pixel slices per 16-channel strip for the single-pass cluster kernel, or 0 when it does not apply:
+// stride-1 consumers of NCHW fp16 tensors with whole 16-channel groups, strips x slices within one
+// cluster, slices of whole 16-byte plane segments that fit one CTA's shared memory.
+int cluster_quant_slices(uint32_t c, uint32_t hw, const void* x, const void* q) {
+  if (c % 16 || reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(q) % 16) return 0;
+  const uint32_t groups = c / 16;
+  for (uint32_t s = 1; s <= 4 && groups * s <= static_cast<uint32_t>(kClusterQuantMaxCtas); s *= 2) {
+    if (hw % (8 * s)) break;
+    if (32ull * (hw / s) <= static_cast<uint64_t>(kClusterQuantMaxSliceBytes)) return static_cast<int>(s);
+  }
+  return 0;
+}
+
+cudaLaunchConfig_t cluster_quant_config(unsigned ctas, unsigned n, size_t smem, cudaStream_t st,
+                                        cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(ctas, n, 1);
+  cfg.blockDim = dim3(kClusterQuantThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  attr->id = cudaLaunchAttributeClusterDimension;
+  attr->val.clusterDim.x = ctas;
+  attr->val.clusterDim.y = 1;
+  attr->val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// Prepares the kernel on the current device (smem attribute, cluster occupancy at the largest
+// slice), once per device and cluster size: returns 1 ready, 0 not schedulable (use the two-kernel
+// path), -1 error.
+int cluster_quant_prepare(int dev, int ctas) {
+  std::lock_guard<std::mutex> lock(g_act_mutex);
+  if (!g_cluster_smem_raised[dev]) {
+    if (!cuda_ok(cudaFuncSetAttribute(amax_quant_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kClusterQuantMaxSliceBytes),
+                 "cluster quantize smem attribute"))
+      return -1;
+    g_cluster_smem_raised[dev] = kClusterQuantMaxSliceBytes;
+  }
+  int& fits = g_cluster_fits[dev][ctas];
+  if (fits == 0) {
+    cudaLaunchAttribute attr{};
+    const cudaLaunchConfig_t cfg = cluster_quant_config(static_cast<unsigned>(ctas), 1, kClusterQuantMaxSliceBytes,
+                                                        nullptr, &attr);
+    int clusters = 0;
+    if (!cuda_ok(cudaOccupancyMaxActiveClusters(&clusters, amax_quant_cluster_kernel, &cfg), "cluster occupancy"))
+      return -1;
+    fits = clusters > 0 ? 1 : -1;
+  }
+  return fits > 0 ? 1 : 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int aexrt_b200_act_amax_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t mode,
+                                     uint32_t* amax_groups, uint32_t groups_total, uint32_t group_offset,
+                                     void* q_out, float* scale_rec, void* stream) {
+  if (!x || !amax_groups || !q_out || !scale_rec) return fail("null pointer");
+  if (mode > 1) return fail("mode must be 0 (per tensor) or 1 (pg16)");
+  if (mode == 1 && c % 16) return fail("pg16 needs c %% 16 == 0");
+  const uint32_t groups = (c + 15) / 16;
+  if (group_offset + groups > groups_total) return fail("amax group range exceeds groups_total");
+  if (n == 0 || c == 0 || h == 0 || w == 0) return 1;
+  const uint32_t hw = h * w;
+  int dev = 0;
+  if (!cuda_ok(cudaGetDevice(&dev), "cudaGetDevice")) return 0;
+  if (dev < 0 || dev >= 128) return fail("device index %d out of range", dev);
+  const int slices = n <= 65535u ? cluster_quant_slices(c, hw, x, q_out) : 0;
+  if (slices) {
+    const int ctas = static_cast<int>(groups) * slices;
+    const int ready = cluster_quant_prepare(dev, ctas);
+    if (ready < 0) return 0;
+    uint32_t* status = act_status_word(dev);
+    if (!status) return 0;
+    if (ready > 0) {
+      cudaLaunchAttribute attr{};
+      const cudaLaunchConfig_t cfg = cluster_quant_config(static_cast<unsigned>(ctas), n, 32ull * (hw / slices),
+                                                          static_cast<cudaStream_t>(stream), &attr);
+      return cuda_ok(cudaLaunchKernelEx(&cfg, amax_quant_cluster_kernel, static_cast<const __half*>(x),
+                                        static_cast<int>(c), static_cast<int>(hw), slices, static_cast<int>(mode),
+                                        static_cast<uint8_t*>(q_out), scale_rec, amax_groups,
+                                        static_cast<int>(groups_total), static_cast<int>(group_offset), status),
+                     "cluster quantize launch")
+                 ? 1
+                 : 0;
+    }
+  }
+  // two passes: amax into the caller's slots, then quantize
+  if (!aexrt_b200_act_amax_f16(x, n, c, h, w, AEXRT_B200_LAYOUT_NCHW_F16, c, 0, amax_groups, groups_total,
+                               group_offset, 1, stream))
+    return 0;
+  return aexrt_b200_act_quantize_f16(x, n, c, h, w, AEXRT_B200_LAYOUT_NCHW_F16, c, 0, amax_groups, groups_total,
+                                     group_offset, mode, 1, q_out, scale_rec, stream);
+}
+
+int aexrt_b200_act_status(uint32_t* status) {
+  if (!status) return fail("null pointer");
+  int dev = 0;
+  if (!cuda_ok(cudaGetDevice(&dev), "cudaGetDevice")) return 0;
+  if (dev < 0 || dev >= 128) return fail("device index %d out of range", dev);
+  uint32_t* word = act_status_word(dev);
+  if (!word) return 0;
+  if (!cuda_ok(cudaMemcpy(status, word, sizeof(uint32_t), cudaMemcpyDeviceToHost), "read status")) return 0;
+  return cuda_ok(cudaMemset(word, 0, sizeof(uint32_t)), "clear status") ? 1 : 0;
 }
 
 int aexrt_b200_pack_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t layout, uint32_t ldc,

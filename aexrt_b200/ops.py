@@ -137,6 +137,31 @@ def act_quantize(x, amax_groups, mode: int = SCALE_PER_TENSOR, layout: int = LAY
     return q_out, rec_out
 
 
+def act_amax_quantize(x, mode: int = SCALE_PER_TENSOR, amax_out=None, q_out=None, rec_out=None, stream=None):
+    """Standalone amax + quantize of an fp16 NCHW tensor for a stride-1 consumer in one call:
+    returns (codes slab16, scale record, amax slots [n, ceil(c/16)])."""
+    torch = _torch()
+    n, c, h, w = x.shape
+    groups = (c + 15) // 16
+    if amax_out is None:
+        amax_out = torch.empty((n, groups), dtype=torch.int32, device=x.device)
+    if q_out is None:
+        q_out = torch.empty(packed_act_shape(n, c, h, w, 1), dtype=torch.int8, device=x.device)
+    if rec_out is None:
+        rec_out = torch.empty((n, 1 + groups), dtype=torch.float32, device=x.device)
+    check(_native.load().aexrt_b200_act_amax_quantize_f16(x.data_ptr(), n, c, h, w, mode, amax_out.data_ptr(),
+                                                          amax_out.shape[1], 0, q_out.data_ptr(), rec_out.data_ptr(),
+                                                          _stream(stream)), "act_amax_quantize")
+    return q_out, rec_out, amax_out
+
+
+def act_status() -> int:
+    """Reads and clears the activation kernels' status word of the current device."""
+    v = ctypes.c_uint32(0)
+    check(_native.load().aexrt_b200_act_status(ctypes.byref(v)), "act_status")
+    return v.value
+
+
 def pack_f16(x, layout: int = LAYOUT_NHWC_F16, consumer_stride: int = 1, c: Optional[int] = None,
              ldc: Optional[int] = None, coff: int = 0, out=None, stream=None):
     """fp16 slab8 repack [N, ceil(C/8), Hp, Wp, 8] for the fp16 convs."""

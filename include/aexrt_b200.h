@@ -310,6 +310,26 @@ int aexrt_b200_yolo_nms_topk(const float* output0, uint32_t n, uint32_t channels
 /* cudaMemsetAsync(ptr, 0, bytes, stream): clears amax slots inside a captured graph. */
 int aexrt_b200_zero(void* ptr, uint64_t bytes, void* stream);
 
+/* Standalone amax + quantize of an fp16 NCHW tensor for a stride-1 consumer (the
+ * activation prequant of record_int8_prequant_activation,
+ * native/aexrt_d3d12_runtime.cpp:21466-21665, amax + pack shaders :3212-3361):
+ * writes q_out (slab16), scale_rec ([n][1 + ceil(c/16)]) and the per-(image, group)
+ * amax bits into amax_groups[n][groups_total] at group_offset (caller memory, no
+ * clearing needed).  Same results as aexrt_b200_act_amax_f16 (zero_first) +
+ * aexrt_b200_act_quantize_f16, bit for bit.  When c % 16 == 0 and each
+ * 16-channel strip splits into 1, 2 or 4 pixel slices (h * w a multiple of 8 per
+ * slice, at most 112 KB each, at most 8 slices per image), one thread-block
+ * cluster per image reads the tensor once (slices in shared memory, amax
+ * exchanged between the CTAs); otherwise it runs those two kernels. */
+int aexrt_b200_act_amax_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t mode,
+                                     uint32_t* amax_groups, uint32_t groups_total, uint32_t group_offset,
+                                     void* q_out, float* scale_rec, void* stream);
+
+/* Reads and clears this device's activation-kernel status word (synchronises):
+ * non-zero means a strip copy of aexrt_b200_act_amax_quantize_f16 did not land
+ * within the wait limit and that image's outputs were not written. */
+int aexrt_b200_act_status(uint32_t* status);
+
 /* ---------------------------------------------------------------- allocation-free variant
  * amax + quantize in one call for callers that cannot call cudaMalloc (a host
  * capturing a CUDA graph, a real-time loop that allocates nothing after

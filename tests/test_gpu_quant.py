@@ -194,3 +194,50 @@ def test_pack_f16_concat_sources_exact(specs, h, w, stride):
     got = o.transpose(0, 1, 4, 2, 3).reshape(n, -1, hp, wp)
     assert np.array_equal(got[:, :c, :h, :w], cat)
     assert (got[:, c:] == 0).all() and (got[:, :, h:] == 0).all() and (got[:, :, :, w:] == 0).all()
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("shape", [
+    (64, 64, 80, 80),    # one 4-CTA cluster per image, strips of 200 KB in shared memory
+    (3, 16, 13, 17),     # one strip per image, odd plane
+    (2, 128, 20, 20),    # eight strips: the largest cluster
+    (2, 48, 7, 9),
+    (2, 24, 10, 12),     # channels not a multiple of 16: the two-kernel path
+    (1, 256, 10, 10),    # sixteen strips: the two-kernel path
+    (1, 32, 96, 96),     # strip larger than shared memory: the two-kernel path
+])
+def test_single_pass_amax_quantize_equals_two_kernels(shape, mode):
+    """aexrt_b200_act_amax_quantize_f16 equals act_amax + act_quantize bit for bit (codes, scale
+    record, amax slots), and the oracle's codes."""
+    torch = _torch()
+    from aexrt_b200 import ops
+
+    rng = np.random.default_rng(sum(shape) + mode)
+    x = seeded_act(rng, shape) * np.float16(3)
+    if shape[0] > 1:
+        x[1] = 0  # an all-zero image: amax 0, codes 0
+    xt = torch.from_numpy(x).cuda()
+    amax_ref = ops.act_amax(xt, ops.LAYOUT_NCHW_F16)
+    if mode == 1 and shape[1] % 16:
+        # pg16 needs whole 16-channel groups: both entry points refuse, before any launch
+        from aexrt_b200._native import AexrtError
+
+        with pytest.raises(AexrtError, match="pg16"):
+            ops.act_quantize(xt, amax_ref, mode, ops.LAYOUT_NCHW_F16)
+        with pytest.raises(AexrtError, match="pg16"):
+            ops.act_amax_quantize(xt, mode)
+        return
+    q_ref, rec_ref = ops.act_quantize(xt, amax_ref, mode, ops.LAYOUT_NCHW_F16)
+    amax = torch.full_like(amax_ref, -1)
+    q = torch.full_like(q_ref, 55)
+    rec = torch.full_like(rec_ref, -2.0)
+    for _ in range(2):  # twice: nothing from the first call leaks into the second
+        ops.act_amax_quantize(xt, mode, amax_out=amax, q_out=q, rec_out=rec)
+        torch.cuda.synchronize()
+        assert ops.act_status() == 0
+        assert torch.equal(q, q_ref)
+        assert torch.equal(rec, rec_ref)
+        assert torch.equal(amax, amax_ref)
+    n, c, h, w = shape
+    at, ag = ow.act_amax(x)
+    assert np.array_equal(slab16_to_nchw(q.cpu().numpy(), c, h, w), ow.quantize_act(x, at, ag, mode))
