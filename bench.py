@@ -35,6 +35,14 @@ if ROOT not in sys.path:
 
 METRIC = "W8A8 YOLOv8n-320 images/s"
 WORKLOAD = "yolov8n-320 W8A8 forward (int8 backbone+neck, fp16 head, DFL decode, NMS + top-k)"
+# whole-model workloads: builder, metric, description, imgsz, nc, per-GPU batch (None: global batch / ranks), scaling
+MODELS = {
+    "yolov8n-320": ("build_yolov8n", METRIC, WORKLOAD, 320, 4, None, "weak"),
+    # global batch 512 split evenly over the GPUs
+    "yolov8s-640": ("build_yolov8s", "W8A8 YOLOv8s-640 images/s",
+                    "yolov8s-640 W8A8 forward (int8 backbone+neck, fp16 head, nc=80, DFL decode, NMS + top-k)",
+                    640, 80, 512, "strong"),
+}
 L2_BYTES = 126 * 1024 * 1024
 # DRAM read + write bytes of the 44 W8A8 conv launches of one forward, per image, from one ncu
 # capture at batch 256 (profiles/conv_family_dram_b256.md); valid for that batch only
@@ -46,12 +54,17 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--batch", type=int, default=256, help="images per GPU per step")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="images per GPU per step (default: 256 for yolov8n-320, 512 / GPUs for yolov8s-640, "
+                         "64 for the layer workloads)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--cpu-sample", type=int, default=160, help="images in the CPU baseline sample (about 12 s)")
+    ap.add_argument("--cpu-sample", type=int, default=None,
+                    help="images in the CPU baseline sample (default 160 for yolov8n-320, 8 for yolov8s-640: "
+                         "about 12-25 s)")
     ap.add_argument("--workload", default="yolov8n-320",
-                    help="yolov8n-320 (the metric), or a BASELINE layer: " + ", ".join(LAYERS)
+                    help="yolov8n-320 (the metric), yolov8s-640 (BASELINE config 5), or a BASELINE layer: "
+                         + ", ".join(LAYERS)
                     + ", or amax-quant, " + ", ".join(QUANTS))
     ap.add_argument("--mode", type=int, default=0, help="layer workloads: 0 per-tensor, 1 pg16 scales")
     ap.add_argument("--order", type=int, default=0,
@@ -85,7 +98,7 @@ def run_layer(args):
 
     torch.cuda.set_device(0)
     rng = np.random.default_rng(0)
-    n = args.batch
+    n = args.batch or 64
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
     hbm, bf16, src = measured_peaks()
     if args.workload == "amax-quant":
@@ -305,7 +318,8 @@ def run_reference(args):
         return 0
     from aexrt_b200 import yolo
 
-    program = yolo.build_yolov8n(nc=4, imgsz=320, seed=0)
+    builder, metric, workload, imgsz, nc, _, scaling = MODELS[args.workload]
+    program = getattr(yolo, builder)(nc=nc, imgsz=imgsz, seed=0)
     cores = host_cores()
     os.environ.setdefault("OMP_NUM_THREADS", str(cores))
     per_step = 4
@@ -316,10 +330,10 @@ def run_reference(args):
         dt += cpu_reference(program, per_step, seed=3 + k, warm=False)[1]
     ips = args.steps * per_step / dt
     line = {
-        "impl": "reference", "metric": METRIC, "value": ips, "unit": "images/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": metric, "value": ips, "unit": "images/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": WORKLOAD + " on the host CPU", "global_batch": per_step, "imgsz": 320, "nc": 4,
+        "scaling": scaling, "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": workload + " on the host CPU", "global_batch": per_step, "imgsz": imgsz, "nc": nc,
                    "parallelism": "host cores"},
         "cpu_baseline": {"value": ips, "unit": "images/s", "cores": cores, "kind": "port",
                          "sample": f"{per_step} images per step x {args.steps} steps through the CPU restatement "
@@ -345,12 +359,13 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local))
     from aexrt_b200 import engine, yolo
 
-    program = yolo.build_yolov8n(nc=4, imgsz=320, seed=0)
-    B = args.batch
+    builder, metric, workload, imgsz, nc, global_batch, scaling = MODELS[args.workload]
+    program = getattr(yolo, builder)(nc=nc, imgsz=imgsz, seed=0)
+    B = args.batch or (global_batch // world if global_batch else 256)
     eng = engine.CompiledYolo(program, B, nms=engine.NmsConfig())
     rng = np.random.default_rng(1000 + rank)
     # fp16 images, as BASELINE's config feeds them (uniform[0,1])
-    host_in = torch.from_numpy(rng.uniform(0, 1, (B, 3, 320, 320)).astype(np.float16)).pin_memory()
+    host_in = torch.from_numpy(rng.uniform(0, 1, (B, 3, imgsz, imgsz)).astype(np.float16)).pin_memory()
     # the read-back is the detection buffer: per image a count and up to 100 AexrtYoloDetection rows
     host_out = torch.empty(tuple(eng.det_buf.shape), dtype=torch.uint8).pin_memory()
     eng.images.copy_(host_in)
@@ -414,23 +429,26 @@ def run_ours(args):
         cpu = None
         if world == 1:
             os.environ["OMP_NUM_THREADS"] = str(host_cores())  # every host thread for the CPU baseline
-            ips, dt = cpu_reference(program, args.cpu_sample)
+            sample = args.cpu_sample or (160 if args.workload == "yolov8n-320" else 8)
+            ips, dt = cpu_reference(program, sample)
             cpu = {"value": ips, "unit": "images/s", "cores": host_cores(), "kind": "port",
-                   "sample": f"{args.cpu_sample} images through the CPU restatement of the reference's W8A8 "
+                   "sample": f"{sample} images through the CPU restatement of the reference's W8A8 "
                              f"arithmetic (oracle/, C/OpenMP int32 convolutions), {dt:.1f} s"}
         line = {
-            "metric": METRIC, "value": world * B * args.steps / t_dev, "unit": "images/s", "n_gpus": world,
+            "metric": metric, "value": world * B * args.steps / t_dev, "unit": "images/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_dev / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic (uniform[0,1] fp16 images, seeded random-init YOLOv8n weights)",
-            "config": {"workload": WORKLOAD, "global_batch": world * B, "per_gpu_batch": B, "imgsz": 320, "nc": 4,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "int8",
+            "data": f"synthetic (uniform[0,1] fp16 images, seeded random-init {builder[6:]} weights)",
+            "config": {"workload": workload, "global_batch": world * B, "per_gpu_batch": B, "imgsz": imgsz, "nc": nc,
                        "parallelism": f"dp{world} (independent replicas)",
-                       "l2": f"inputs larger than L2 ({B * 3 * 320 * 320 * 2 / 1e6:.0f} MB of fp16 images per step)"},
+                       "l2": f"inputs larger than L2 ({B * 3 * imgsz * imgsz * 2 / 1e6:.0f} MB of fp16 images "
+                             "per step)"},
             "e2e": e2e,
             "gpu_launches": eng.launches_per_run * args.steps,
             "roofline": {"bound": "hbm", "achieved": rf["bytes"] / rf["time_s"] / 1e9, "peak": hbm, "unit": "GB/s",
                          "frac": rf["bytes"] / rf["time_s"] / 1e9 / hbm,
-                         "traffic": CONV_DRAM_BYTES_PER_IMAGE_B256 * B if B == 256 else None,
+                         "traffic": (CONV_DRAM_BYTES_PER_IMAGE_B256 * B
+                                     if B == 256 and args.workload == "yolov8n-320" else None),
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum over the step's W8A8 "
                                            "conv launches at batch 256 (profiles/conv_family_dram_b256.md)",
                          "kernel": "conv_halo_kernel / conv_tc_kernel: all W8A8 conv launches of one step "
@@ -454,7 +472,7 @@ def run_ours(args):
 
 def main():
     args = parse_args()
-    if args.workload != "yolov8n-320":
+    if args.workload not in MODELS:
         return run_layer(args)
     if args.impl == "reference":
         # rank 0 alone runs the CPU reference: give it every host thread (torchrun exports

@@ -166,3 +166,26 @@ def test_streaming_detections_match_forwards(v8n):
         counts, _ = eng.split_detections(host_out[k])
         assert torch.equal(host_out[k], want[k]), k
         assert int(counts.max()) <= 100
+
+
+def test_yolov8s_end_to_end_against_oracle():
+    """BASELINE config 5's architecture (YOLOv8s: width 0.5, depth 0.33, nc=80) at a small input size:
+    class scores within the reference's 0.02 gate, boxes within a few pixels, detections as the
+    oracle's post-process of the device's own output0."""
+    from aexrt_b200 import engine, yolo
+    from oracle import yolo_post as op
+
+    torch = _torch()
+    prog = yolo.build_yolov8s(nc=80, imgsz=128, seed=1)
+    eng = engine.CompiledYolo(prog, 2, nms=engine.NmsConfig())
+    eng.capture()
+    imgs = _images(2, seed=8, size=128)
+    out = eng.forward(torch.from_numpy(imgs).cuda()).cpu().numpy()
+    ref = om.run_program(prog, imgs)["output0"]
+    assert np.abs(out[:, 4:] - ref[:, 4:]).max() <= 0.02
+    assert np.percentile(np.abs(out[:, :4] - ref[:, :4]), 99) <= 4.0
+    counts, dets = (t.cpu().numpy() for t in eng.detections())
+    for i in range(2):
+        want, cnt = op.postprocess(out[i], 80)
+        assert counts[i] == cnt and np.array_equal(dets[i, :cnt], want)
+    assert eng.status() == 0
