@@ -386,8 +386,11 @@ def main(argv=None) -> int:
     eng = CompiledYolo(program, a.batch, nms=None if a.no_nms else NmsConfig())
     x = torch.from_numpy(np.random.default_rng(0).uniform(0, 1, (a.batch, 3, a.imgsz, a.imgsz)).astype(np.float16))
     x = x.to(eng.device)
-    for _ in range(a.forwards):
+    for i in range(a.forwards):
+        # one NVTX range per forward, so a profiler can select exactly one (ncu --nvtx --nvtx-include "forward1/")
+        torch.cuda.nvtx.range_push(f"forward{i}")
         eng.forward(x)
+        torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(eng.device)
     print(f"{a.forwards} forwards of batch {a.batch}: {eng.launches_per_run - 1} kernels each, status {eng.status()}")
     return 0 if eng.status() == 0 else 1
