@@ -685,6 +685,13 @@ bool rows_ok(const QuantParams& q, bool i8) {
   return q.slabs <= kMaxSlabs;
 }
 
+// One source at full resolution for a stride-1 consumer (no padding rows or columns): source and
+// destination pixel are the linear pixel index.
+bool rows_linear(const QuantParams& q) {
+  return q.nsrc == 1 && q.src[0].up == 1 && !q.split && q.hp == q.h && q.wp == q.w && q.src[0].src_h == q.h &&
+         q.src[0].src_w == q.w;
+}
+
 // Picks the quantize kernel: NHWC sources (16-byte aligned slices, enforced by
 // the entry points) go through the coalesced row kernel, stride-1 NCHW fp16
 // with H*W % 4 == 0 through the register-transpose kernel, anything else
@@ -696,7 +703,10 @@ void launch_quantize(const QuantParams& q, cudaStream_t st) {
     const int groups = rows_channel_groups(q, true);
     const long items = static_cast<long>((q.hp * q.wp + pw - 1) / pw) * groups;  // one warp each
     const dim3 grid(static_cast<unsigned>((items + 7) / 8), q.n);
-    quant_rows_kernel<true><<<grid, 256, 0, st>>>(q, pw, groups);
+    if (rows_linear(q))
+      quant_rows_kernel<true, true><<<grid, 256, 0, st>>>(q, pw, groups);
+    else
+      quant_rows_kernel<true, false><<<grid, 256, 0, st>>>(q, pw, groups);
   } else if (q.nsrc == 1 && q.src[0].layout == 1 && !q.split && (q.h * q.w) % 4 == 0 && q.slabs <= kMaxSlabs) {
     const dim3 grid((q.h * q.w / 4 + 255) / 256, q.slabs, q.n);
     quantize_nchw_kernel<<<grid, 256, 0, st>>>(q);
@@ -720,7 +730,10 @@ void launch_pack(const QuantParams& q, cudaStream_t st) {
     const int groups = rows_channel_groups(q, false);
     const long items = static_cast<long>((q.hp * q.wp + pw - 1) / pw) * groups;
     const dim3 grid(static_cast<unsigned>((items + 7) / 8), q.n);
-    quant_rows_kernel<false><<<grid, 256, 0, st>>>(q, pw, groups);
+    if (rows_linear(q))
+      quant_rows_kernel<false, true><<<grid, 256, 0, st>>>(q, pw, groups);
+    else
+      quant_rows_kernel<false, false><<<grid, 256, 0, st>>>(q, pw, groups);
   } else {
     const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, q.n);
     pack_f16_kernel<<<grid, 256, 0, st>>>(q);

@@ -379,11 +379,13 @@ inline int rows_channel_groups(const QuantParams& q, bool i8) {
 // pixel group major (the warps of a block read neighbouring channel ranges of the same pixels),
 // blockIdx.y = image.  Small maps thereby spread their channels over warps and blocks instead of
 // walking them in one warp.
-template <bool kI8>
+// kLinear: one source, no upsample, stride-1 consumer with hp = h and wp = w, so source and
+// destination pixel are both the linear pixel index (no per-warp coordinate table).
+template <bool kI8, bool kLinear>
 __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p, int pw, int groups) {
   __shared__ float s_mult[kMaxSlabs];
   __shared__ float s_red[2];
-  __shared__ int2 s_pix[8][kRowsMaxPixPerWarp];  // per pixel: (row << 16 | column), destination pixel (-1: none)
+  __shared__ int2 s_pix[kLinear ? 1 : 8][kLinear ? 1 : kRowsMaxPixPerWarp];  // (row << 16 | column), destination (-1: none)
   const int n = blockIdx.y;
   if (kI8) slab_multipliers(p, n, s_mult, s_red);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -393,13 +395,15 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p,
   const int pix0 = pg * pw;
   if (pix0 >= npix) return;  // no barrier follows
   int g = item - pg * groups;
-  for (int j = 0; j < pw / 32; ++j) {
-    const int pix = pix0 + j * 32 + lane;
-    const int h = pix / p.wp, w = pix - (pix / p.wp) * p.wp;
-    const int dpix = p.split ? h * p.wp + (w & 1) * (p.wp >> 1) + (w >> 1) : pix;
-    s_pix[warp][j * 32 + lane] = make_int2((h << 16) | w, pix < npix ? dpix : -1);
+  if constexpr (!kLinear) {
+    for (int j = 0; j < pw / 32; ++j) {
+      const int pix = pix0 + j * 32 + lane;
+      const int h = pix / p.wp, w = pix - (pix / p.wp) * p.wp;
+      const int dpix = p.split ? h * p.wp + (w & 1) * (p.wp >> 1) + (w >> 1) : pix;
+      s_pix[warp][j * 32 + lane] = make_int2((h << 16) | w, pix < npix ? dpix : -1);
+    }
+    __syncwarp();
   }
-  __syncwarp();
   // the item's source k and first chunk j0 within it
   int k = 0, chunk_base = 0;  // chunk_base: 8-channel chunks of the sources before k
   for (; k < p.nsrc - 1; ++k) {
@@ -431,11 +435,17 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p,
     for (int it = 0; it < 8; ++it) {
       v[it] = make_uint4(0u, 0u, 0u, 0u);
       if (b * 8 + it >= per_lane) continue;
-      const int2 px = s_pix[warp][(b * 8 + it) * P + pl];
-      const int h = px.x >> 16, w = px.x & 0xFFFF;
-      if (cact && px.y >= 0 && h < p.h && w < p.w)
-        v[it] = *reinterpret_cast<const uint4*>(
-            base + (static_cast<size_t>(h >> ush) * s.src_w + (w >> ush)) * s.ldc + cidx * 8);
+      if constexpr (kLinear) {
+        const int pix = pix0 + (b * 8 + it) * P + pl;
+        if (cact && pix < npix)
+          v[it] = *reinterpret_cast<const uint4*>(base + static_cast<size_t>(pix) * s.ldc + cidx * 8);
+      } else {
+        const int2 px = s_pix[warp][(b * 8 + it) * P + pl];
+        const int h = px.x >> 16, w = px.x & 0xFFFF;
+        if (cact && px.y >= 0 && h < p.h && w < p.w)
+          v[it] = *reinterpret_cast<const uint4*>(
+              base + (static_cast<size_t>(h >> ush) * s.src_w + (w >> ush)) * s.ldc + cidx * 8);
+      }
     }
     // rounding by the 1.5*2^23 addend (see quantize_nchw_kernel) when every lane's inputs stay in
     // its exact range, else float-to-int; the choice is warp-uniform
@@ -452,7 +462,13 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p,
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
       if (b * 8 + it >= per_lane) break;  // warp-uniform
-      const int dpix = s_pix[warp][(b * 8 + it) * P + pl].y;
+      int dpix;
+      if constexpr (kLinear) {
+        dpix = pix0 + (b * 8 + it) * P + pl;
+        dpix = dpix < npix ? dpix : -1;
+      } else {
+        dpix = s_pix[warp][(b * 8 + it) * P + pl].y;
+      }
       if (kI8) {
         uint32_t q0, q1;
         if (magic)
