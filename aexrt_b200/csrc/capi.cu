@@ -685,10 +685,10 @@ bool rows_ok(const QuantParams& q, bool i8) {
   return q.slabs <= kMaxSlabs;
 }
 
-// One source at full resolution for a stride-1 consumer (no padding rows or columns): source and
-// destination pixel are the linear pixel index.
+// One source at full resolution with no padding rows or columns: the source pixel is the linear
+// pixel index (the destination too, unless a stride-2 consumer splits the columns by parity).
 bool rows_linear(const QuantParams& q) {
-  return q.nsrc == 1 && q.src[0].up == 1 && !q.split && q.hp == q.h && q.wp == q.w && q.src[0].src_h == q.h &&
+  return q.nsrc == 1 && q.src[0].up == 1 && q.hp == q.h && q.wp == q.w && q.src[0].src_h == q.h &&
          q.src[0].src_w == q.w;
 }
 

@@ -379,13 +379,14 @@ inline int rows_channel_groups(const QuantParams& q, bool i8) {
 // pixel group major (the warps of a block read neighbouring channel ranges of the same pixels),
 // blockIdx.y = image.  Small maps thereby spread their channels over warps and blocks instead of
 // walking them in one warp.
-// kLinear: one source, no upsample, stride-1 consumer with hp = h and wp = w, so source and
-// destination pixel are both the linear pixel index (no per-warp coordinate table).
+// kLinear: one source, no upsample, hp = h and wp = w, so the source pixel is the linear pixel
+// index (no per-warp coordinate table); the destination is that index too, or for a stride-2
+// consumer the column-parity-split position from the table.
 template <bool kI8, bool kLinear>
 __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p, int pw, int groups) {
   __shared__ float s_mult[kMaxSlabs];
   __shared__ float s_red[2];
-  __shared__ int2 s_pix[kLinear ? 1 : 8][kLinear ? 1 : kRowsMaxPixPerWarp];  // (row << 16 | column), destination (-1: none)
+  __shared__ int2 s_pix[8][kRowsMaxPixPerWarp];  // per pixel: (row << 16 | column), destination pixel (-1: none)
   const int n = blockIdx.y;
   if (kI8) slab_multipliers(p, n, s_mult, s_red);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -395,7 +396,7 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p,
   const int pix0 = pg * pw;
   if (pix0 >= npix) return;  // no barrier follows
   int g = item - pg * groups;
-  if constexpr (!kLinear) {
+  if (!kLinear || p.split) {
     for (int j = 0; j < pw / 32; ++j) {
       const int pix = pix0 + j * 32 + lane;
       const int h = pix / p.wp, w = pix - (pix / p.wp) * p.wp;
@@ -463,7 +464,7 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p,
     for (int it = 0; it < 8; ++it) {
       if (b * 8 + it >= per_lane) break;  // warp-uniform
       int dpix;
-      if constexpr (kLinear) {
+      if (kLinear && !p.split) {
         dpix = pix0 + (b * 8 + it) * P + pl;
         dpix = dpix < npix ? dpix : -1;
       } else {
