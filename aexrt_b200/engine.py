@@ -95,7 +95,7 @@ class CompiledYolo:
         self.plans: Dict[str, ops.ConvPlan] = {}
         for c in p.commands:
             if isinstance(c, ConvCmd):
-                self._compile_conv(c, (block_n or {}).get(c.name, 0))
+                self._compile_conv(c, (block_n or {}).get(c.name, c.block_n))
             elif isinstance(c, SppfCmd):
                 self.steps.append(("sppf", c))
             elif isinstance(c, DecodeCmd):

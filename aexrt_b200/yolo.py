@@ -54,6 +54,7 @@ class ConvCmd:
     precision: str = "int8"       # "int8" (W8A8 kernel 51/52/53) or "fp16"
     residual: Optional[Tuple[str, int]] = None  # (value, channel offset), added after SiLU
     pg16: bool = False            # INT8_PERGROUP plan flag
+    block_n: int = 0              # preferred output-channel tile of the plan (0: the plan's choice)
 
     @property
     def kind(self) -> str:
@@ -192,9 +193,22 @@ class _Builder:
             self.conv(f"{name}.{i}.cv23_0", [Part(f, 0, chs[i])], (h0, 0), c2 + c3, 3, 1, precision="fp16")
             self.conv(f"{name}.{i}.cv2_1", [Part(h0, 0, c2)], (h1, 0), c2, 3, 1, precision="fp16")
             self.conv(f"{name}.{i}.cv3_1", [Part(h0, c2, c3)], (h1, c2), c3, 3, 1, precision="fp16")
-            self.conv(f"{name}.{i}.cv2_2", [Part(h1, 0, c2)], (o, 0), 4 * reg_max, 1, 1, silu=False, precision="fp16")
-            self.conv(f"{name}.{i}.cv3_2", [Part(h1, c2, c3)], (o, 4 * reg_max), nc, 1, 1, silu=False,
-                      precision="fp16")
+            # cv2[i][2] (box logits from h1[:c2]) and cv3[i][2] (class logits from h1[c2:]) as one 1x1
+            # conv over all of h1 with block-diagonal weights: one launch instead of two small,
+            # latency-bound ones; the zero blocks add exact zeros
+            w2, b2 = self._weights(4 * reg_max, c2, 1)
+            w3, b3 = self._weights(nc, c3, 1)
+            oc = o_ch = self.p.values[o].channels
+            wf = np.zeros((oc, c2 + c3, 1, 1), np.float32)
+            wf[:4 * reg_max, :c2] = w2
+            wf[4 * reg_max:4 * reg_max + nc, c2:] = w3
+            bf = np.zeros(oc, np.float32)
+            bf[:4 * reg_max], bf[4 * reg_max:4 * reg_max + nc] = b2, b3
+            bn = 16
+            while bn < min(o_ch, 256):
+                bn *= 2
+            self.p.commands.append(ConvCmd(f"{name}.{i}.cv23_2", [Part(h1, 0, c2 + c3)], (o, 0), c2 + c3, oc, 1, 1,
+                                           False, wf, bf, "fp16", block_n=bn))
             levels.append((Part(o, 0, 4 * reg_max), Part(o, 4 * reg_max, nc), float(st)))
         self.p.commands.append(DecodeCmd(name + ".decode", levels, nc, reg_max))
 
