@@ -29,7 +29,7 @@ from __future__ import annotations
 
 import struct
 import zlib
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from typing import Dict, List, Optional, Tuple
 
 import numpy as np
@@ -48,7 +48,6 @@ KIND_NAME = {v: k for k, v in KIND.items()}
 PLAN_FLAG_INT8_PERGROUP = 1 << 4
 PACKED_LAYOUT_CONV_INT8 = 8
 INT8_KERNELS = (51, 52, 53)
-VALUE_INPUT, VALUE_CONSTANT = 1, 2
 PRECISION_FP32, PRECISION_FP16 = 1, 2
 
 

@@ -25,7 +25,6 @@ image's AexrtYoloDetection rows and count, the output of ``aexrt_yolo_run``.
 """
 from __future__ import annotations
 
-import ctypes
 from dataclasses import dataclass
 from typing import Dict, List, Optional
 

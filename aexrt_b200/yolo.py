@@ -198,14 +198,14 @@ class _Builder:
             # latency-bound ones; the zero blocks add exact zeros
             w2, b2 = self._weights(4 * reg_max, c2, 1)
             w3, b3 = self._weights(nc, c3, 1)
-            oc = o_ch = self.p.values[o].channels
+            oc = self.p.values[o].channels
             wf = np.zeros((oc, c2 + c3, 1, 1), np.float32)
             wf[:4 * reg_max, :c2] = w2
             wf[4 * reg_max:4 * reg_max + nc, c2:] = w3
             bf = np.zeros(oc, np.float32)
             bf[:4 * reg_max], bf[4 * reg_max:4 * reg_max + nc] = b2, b3
             bn = 16
-            while bn < min(o_ch, 256):
+            while bn < min(oc, 256):
                 bn *= 2
             self.p.commands.append(ConvCmd(f"{name}.{i}.cv23_2", [Part(h1, 0, c2 + c3)], (o, 0), c2 + c3, oc, 1, 1,
                                            False, wf, bf, "fp16", block_n=bn))
