@@ -134,9 +134,10 @@ struct AexrtB200ConvPlan {
   float* d_half_sb = nullptr;
   uint32_t* d_status = nullptr;
   int device = 0;
-  // image stem (fp16, 3 input channels, 3x3): direct kernel reading fp32 NCHW images
+  // image stem (fp16, 3 input channels, 3x3): direct kernel reading fp16 or fp32 NCHW images
   bool image_input = false;
   StemWeights stem{};
+  StemPairWeights stem_pair{};  // oc <= 32: the two-pixel kernel's copy of the same weights
 };
 
 namespace {
@@ -1080,6 +1081,14 @@ AexrtB200ConvPlan* aexrt_b200_conv_plan_create_f16(const AexrtConv2DDesc* desc, 
     p->image_input = true;
     for (uint32_t i = 0; i < oc * kStemIC * 9; ++i) p->stem.w[i] = __half2float(__float2half_rn(weight[i]));
     for (uint32_t i = 0; i < oc; ++i) p->stem.b[i] = bias[i];
+    if (oc <= static_cast<uint32_t>(kStemPairMaxOC)) {
+      for (uint32_t i = 0; i < oc * kStemIC * 9; ++i) {
+        uint32_t u;
+        std::memcpy(&u, &p->stem.w[i], sizeof(u));
+        p->stem_pair.w2[i] = (static_cast<uint64_t>(u) << 32) | u;
+      }
+      for (uint32_t i = 0; i < oc; ++i) p->stem_pair.b[i] = bias[i];
+    }
   }
   return p;
 }
@@ -1098,15 +1107,13 @@ int aexrt_b200_conv_f16_image(const AexrtB200ConvPlan* p, const void* images, ui
   if (amax_out && (amax_goff * 16 + oc > amax_stride * 16 || out_coff % 16))
     return fail("amax_out slots out of range (need amax_goff + ceil(oc/16) <= amax_stride, coff %% 16 == 0)");
   const int oh = static_cast<int>(p->desc.out_h), ow = static_cast<int>(p->desc.out_w);
-  const int per_img = oh * ow;
-  const dim3 grid((per_img + 255) / 256, p->desc.batch);
   auto* st = static_cast<cudaStream_t>(stream);
   const bool silu = p->kind == AEXRT_B200_KIND_CONV_SILU;
   auto* o = static_cast<__half*>(out);
   const int h = static_cast<int>(p->desc.in_h), w = static_cast<int>(p->desc.in_w), s = p->stride;
-launch_stem(static_cast<int>(oc), silu, layout == AEXRT_B200_LAYOUT_NCHW_F16, images, h, w, oh, ow, s, o,
-              static_cast<int>(out_ldc), static_cast<int>(out_coff), amax_out, static_cast<int>(amax_stride),
-              static_cast<int>(amax_goff), p->stem, grid, st);
+  launch_stem(static_cast<int>(oc), silu, layout == AEXRT_B200_LAYOUT_NCHW_F16, images, static_cast<int>(p->desc.batch),
+              h, w, oh, ow, s, o, static_cast<int>(out_ldc), static_cast<int>(out_coff), amax_out,
+              static_cast<int>(amax_stride), static_cast<int>(amax_goff), p->stem, p->stem_pair, st);
   return cuda_ok(cudaGetLastError(), "stem conv launch") ? 1 : 0;
 }
 

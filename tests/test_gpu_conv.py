@@ -266,6 +266,9 @@ def test_fp16_halo_vs_slot_streaming(n, ic, h, w, oc, k, s, silu):
     (3, 33, 47, 32, 2, True),    # odd sizes: clipped windows on the right/bottom
     (2, 20, 20, 64, 1, False),
     (1, 17, 16, 48, 2, True),
+    (2, 21, 19, 16, 1, True),    # two-pixel form: odd output width (last pair has one pixel)
+    (1, 18, 17, 32, 2, False),   # two-pixel form, stride 2, odd output width
+    (2, 40, 36, 32, 1, True),
 ])
 def test_stem_image_input(n, h, w, oc, s, silu, dtype):
     """The direct stem (fp32 or fp16 NCHW images in) against torch fp32 and the packed fp16 path; amax_out exact."""
