@@ -46,7 +46,8 @@ struct StemPairWeights {
   float b[kStemPairMaxOC];
 };
 
-__device__ __forceinline__ float stem_load(const float* p) { return __ldg(p); }
+// One tap as the conv consumes it: the image value rounded to fp16 (fp16 images already are).
+__device__ __forceinline__ float stem_load(const float* p) { return __half2float(__float2half_rn(__ldg(p))); }
 __device__ __forceinline__ float stem_load(const __half* p) { return __half2float(__ldg(p)); }
 
 // grid (ceil(oh*ow / 256), n); block 256, one output pixel per thread.  TIn: float or
@@ -82,8 +83,7 @@ __global__ void __launch_bounds__(256) stem_conv_kernel(const TIn* __restrict__ 
         for (int kw = 0; kw < 3; ++kw) {
           const int iy = iy0 + kh, ix = ix0 + kw;
           const bool in = iy >= 0 && iy < h && ix >= 0 && ix < w;
-          const float v = in ? stem_load(img + ic * plane + static_cast<size_t>(iy) * w + ix) : 0.0f;
-          xv[(ic * 3 + kh) * 3 + kw] = __half2float(__float2half_rn(v));
+          xv[(ic * 3 + kh) * 3 + kw] = in ? stem_load(img + ic * plane + static_cast<size_t>(iy) * w + ix) : 0.0f;
         }
     __half* orow = out + (static_cast<size_t>(n) * npix + pix) * out_ldc + out_coff;
 #pragma unroll
@@ -156,8 +156,7 @@ __global__ void __launch_bounds__(256, 3) stem_pair_kernel(const TIn* __restrict
         for (int j = 0; j < kCols; ++j) {
           const int ix = ix0 + j;
           const bool in = row_in && ix >= 0 && ix < w;
-          const float v = in ? stem_load(img + ic * plane + static_cast<size_t>(iy) * w + ix) : 0.0f;
-          col[j] = __half2float(__float2half_rn(v));
+          col[j] = in ? stem_load(img + ic * plane + static_cast<size_t>(iy) * w + ix) : 0.0f;
         }
 #pragma unroll
         for (int kw = 0; kw < 3; ++kw) xp[(ic * 3 + kh) * 3 + kw] = f2_pack(col[kw], col[kw + S]);
