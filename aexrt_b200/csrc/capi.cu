@@ -137,7 +137,6 @@ struct AexrtB200ConvPlan {
   // image stem (fp16, 3 input channels, 3x3): direct kernel reading fp16 or fp32 NCHW images
   bool image_input = false;
   StemWeights stem{};
-  StemPairWeights stem_pair{};  // oc <= 32: the two-pixel kernel's copy of the same weights
 };
 
 namespace {
@@ -1081,14 +1080,6 @@ AexrtB200ConvPlan* aexrt_b200_conv_plan_create_f16(const AexrtConv2DDesc* desc, 
     p->image_input = true;
     for (uint32_t i = 0; i < oc * kStemIC * 9; ++i) p->stem.w[i] = __half2float(__float2half_rn(weight[i]));
     for (uint32_t i = 0; i < oc; ++i) p->stem.b[i] = bias[i];
-    if (oc <= static_cast<uint32_t>(kStemPairMaxOC)) {
-      for (uint32_t i = 0; i < oc * kStemIC * 9; ++i) {
-        uint32_t u;
-        std::memcpy(&u, &p->stem.w[i], sizeof(u));
-        p->stem_pair.w2[i] = (static_cast<uint64_t>(u) << 32) | u;
-      }
-      for (uint32_t i = 0; i < oc; ++i) p->stem_pair.b[i] = bias[i];
-    }
   }
   return p;
 }
@@ -1113,7 +1104,7 @@ int aexrt_b200_conv_f16_image(const AexrtB200ConvPlan* p, const void* images, ui
   const int h = static_cast<int>(p->desc.in_h), w = static_cast<int>(p->desc.in_w), s = p->stride;
   launch_stem(static_cast<int>(oc), silu, layout == AEXRT_B200_LAYOUT_NCHW_F16, images, static_cast<int>(p->desc.batch),
               h, w, oh, ow, s, o, static_cast<int>(out_ldc), static_cast<int>(out_coff), amax_out,
-              static_cast<int>(amax_stride), static_cast<int>(amax_goff), p->stem, p->stem_pair, st);
+              static_cast<int>(amax_stride), static_cast<int>(amax_goff), p->stem, st);
   return cuda_ok(cudaGetLastError(), "stem conv launch") ? 1 : 0;
 }
 

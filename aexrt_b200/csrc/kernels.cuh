@@ -38,12 +38,11 @@ inline HaloKernel halo_kernel_for(bool f16, int bn, bool silu, bool res, bool pg
 }
 
 // The image stem (stem.cuh): one unit per output width (16, 32, 48, 64), fp16 or fp32 images.
-// Widths 16 and 32 run stem_pair_kernel (weights `wp`), 48 and 64 stem_conv_kernel (weights `wt`);
-// each launcher sizes its own grid.
+// Widths 16 and 32 run stem_pair_kernel, 48 and 64 stem_conv_kernel; each launcher sizes its own grid.
 #define AEXRT_STEM_DECL(OC)                                                                                        \
   void launch_stem_##OC(bool silu, bool f16_images, const void* images, int n, int h, int w, int oh, int ow,      \
                         int stride, __half* out, int out_ldc, int out_coff, uint32_t* amax, int amax_stride,      \
-                        int amax_goff, const StemWeights& wt, const StemPairWeights& wp, cudaStream_t st);
+                        int amax_goff, const StemWeights& wt, cudaStream_t st);
 AEXRT_STEM_DECL(16)
 AEXRT_STEM_DECL(32)
 AEXRT_STEM_DECL(48)
@@ -52,10 +51,9 @@ AEXRT_STEM_DECL(64)
 
 inline void launch_stem(int oc, bool silu, bool f16_images, const void* images, int n, int h, int w, int oh, int ow,
                         int stride, __half* out, int out_ldc, int out_coff, uint32_t* amax, int amax_stride,
-                        int amax_goff, const StemWeights& wt, const StemPairWeights& wp, cudaStream_t st) {
+                        int amax_goff, const StemWeights& wt, cudaStream_t st) {
   auto* fn = oc == 16 ? launch_stem_16 : oc == 32 ? launch_stem_32 : oc == 48 ? launch_stem_48 : launch_stem_64;
-  fn(silu, f16_images, images, n, h, w, oh, ow, stride, out, out_ldc, out_coff, amax, amax_stride, amax_goff, wt, wp,
-     st);
+  fn(silu, f16_images, images, n, h, w, oh, ow, stride, out, out_ldc, out_coff, amax, amax_stride, amax_goff, wt, st);
 }
 
 }  // namespace aexrt

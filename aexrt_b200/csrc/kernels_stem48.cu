@@ -14,7 +14,7 @@ void go(const void* images, int n, int h, int w, int oh, int ow, int stride, __h
 
 void launch_stem_48(bool silu, bool f16_images, const void* images, int n, int h, int w, int oh, int ow, int stride,
                     __half* out, int out_ldc, int out_coff, uint32_t* amax, int amax_stride, int amax_goff,
-                    const StemWeights& wt, const StemPairWeights&, cudaStream_t st) {
+                    const StemWeights& wt, cudaStream_t st) {
   if (f16_images)
     (silu ? go<true, __half> : go<false, __half>)(images, n, h, w, oh, ow, stride, out, out_ldc, out_coff, amax,
                                                  amax_stride, amax_goff, wt, st);

@@ -15,7 +15,8 @@
 // k = 0..26 from 0, then + bias), so their outputs are bit-identical:
 //   * stem_pair_kernel (OC <= 32): two horizontally adjacent output pixels per
 //     thread, the two fma chains run as one packed f32x2 fma per tap and
-//     channel; the weight operand is the tap's weight in both halves.  The
+//     channel; the weight operand is the tap's fp32 weight in both halves
+//     (packed in the kernel: faster than a pre-duplicated 64-bit parameter).  The
 //     kernel is issue-bound (about 1170 instructions per pixel in the
 //     one-pixel form), and the pair form halves the fma instructions and
 //     shares the overlapping window columns;
@@ -33,17 +34,11 @@ namespace aexrt {
 
 constexpr int kStemIC = 3;
 constexpr int kStemMaxOC = 64;
-constexpr int kStemPairMaxOC = 32;
+constexpr int kStemPairMaxOC = 32;  // widths that run stem_pair_kernel
 
 struct StemWeights {
   float w[kStemMaxOC * kStemIC * 9];  // [oc][ic][kh][kw], fp16-rounded
   float b[kStemMaxOC];
-};
-
-// the same weights for stem_pair_kernel: each fp32 weight in both halves of a 64-bit word
-struct StemPairWeights {
-  uint64_t w2[kStemPairMaxOC * kStemIC * 9];  // [oc][ic][kh][kw]
-  float b[kStemPairMaxOC];
 };
 
 // One tap as the conv consumes it: the image value rounded to fp16 (fp16 images already are).
@@ -125,7 +120,7 @@ template <int OC, bool kSilu, typename TIn, int S>
 __global__ void __launch_bounds__(256, 3) stem_pair_kernel(const TIn* __restrict__ x, int h, int w, int oh, int ow,
                                                            __half* __restrict__ out, int out_ldc, int out_coff,
                                                            uint32_t* __restrict__ amax, int amax_stride, int amax_goff,
-                                                           const __grid_constant__ StemPairWeights wt) {
+                                                           const __grid_constant__ StemWeights wt) {
   static_assert(OC % 16 == 0 && OC <= kStemPairMaxOC, "OC must be 16 or 32");
   constexpr int kGroups = OC / 16;
   constexpr int kCols = S + 3;
@@ -170,7 +165,10 @@ __global__ void __launch_bounds__(256, 3) stem_pair_kernel(const TIn* __restrict
         const int oc = o8 * 8 + i;
         uint64_t acc = 0ull;
 #pragma unroll
-        for (int k = 0; k < kStemIC * 9; ++k) acc = f2_fma(xp[k], wt.w2[oc * kStemIC * 9 + k], acc);
+        for (int k = 0; k < kStemIC * 9; ++k) {
+          const float wv = wt.w[oc * kStemIC * 9 + k];
+          acc = f2_fma(xp[k], f2_pack(wv, wv), acc);
+        }
         f2_unpack(acc, ya[i], yb[i]);
         ya[i] = ya[i] + wt.b[oc];
         yb[i] = yb[i] + wt.b[oc];
