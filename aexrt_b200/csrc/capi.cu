@@ -1279,8 +1279,9 @@ int aexrt_b200_sppf_pool(const void* x, uint32_t n, uint32_t h, uint32_t w, uint
   const long total = static_cast<long>(n) * h * w * (c / 8);
   if (total == 0) return 1;
   {
-    // whole map per (image, channel block) in shared memory when it fits
-    int cb = 64;
+    // whole map per (image, channel block) in shared memory when it fits; blocks of at most 32
+    // channels, so that small maps still give every SM several blocks (the passes are latency-bound)
+    int cb = 32;
     while (cb > 16 && (c % cb || 4L * h * w * cb * 2 > 160 * 1024)) cb /= 2;
     const long smem = 4L * h * w * cb * 2;
     if (c % cb == 0 && smem <= 160 * 1024) {
