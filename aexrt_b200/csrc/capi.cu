@@ -1397,10 +1397,10 @@ int aexrt_b200_zero(void* ptr, uint64_t bytes, void* stream) {
 // ----------------------------------------------------------------------------
 // Allocation-free amax + quantize
 //
-// Some callers cannot call cudaMalloc: a host that runs this step while it is
-// capturing a CUDA graph (allocation is not capturable), a real-time loop that
-// forbids allocation after start-up, or a plugin host whose memory is owned by
-// its own allocator.  For them the per-(image, group) amax slots, which are
+// Some callers cannot call cudaMalloc: a real-time loop that forbids allocation
+// after start-up (an allocation can stall on the driver), a plugin whose device
+// memory is owned by its host's allocator or budget, or an embedded caller with
+// no allocator of its own.  For them the per-(image, group) amax slots, which are
 // scratch between the amax and the quantize kernels, live in a fixed device
 // array owned by the library instead of in caller memory.
 // ----------------------------------------------------------------------------

@@ -331,9 +331,9 @@ int aexrt_b200_act_amax_quantize_f16(const void* x, uint32_t n, uint32_t c, uint
 int aexrt_b200_act_status(uint32_t* status);
 
 /* ---------------------------------------------------------------- allocation-free variant
- * amax + quantize in one call for callers that cannot call cudaMalloc (a host
- * capturing a CUDA graph, a real-time loop that allocates nothing after
- * start-up, a plugin whose memory belongs to its host's allocator): the
+ * amax + quantize in one call for callers that cannot call cudaMalloc (a
+ * real-time loop that allocates nothing after start-up, a plugin whose memory
+ * belongs to its host's allocator, an embedded caller with no allocator): the
  * per-(image, 16-channel group) amax scratch lives in a fixed device array
  * inside the library instead of caller memory.  No counterpart in the
  * reference (there the amax buffer is allocated by the recorder).

@@ -1,8 +1,8 @@
 """The allocation-free amax + quantize entry point.
 
-Callers that cannot allocate device memory (a host in the middle of a CUDA
-graph capture, a real-time loop that allocates nothing after start-up, a
-plugin whose memory belongs to its host) call
+Callers that cannot allocate device memory (a real-time loop that allocates
+nothing after start-up, a plugin whose memory belongs to its host's
+allocator, an embedded caller with no allocator of its own) call
 aexrt_b200_act_quantize_f16_noalloc, which keeps the amax scratch in a fixed
 array inside the library.  Its results must equal those of the two ordinary
 entry points (aexrt_b200_act_amax_f16 + aexrt_b200_act_quantize_f16, caller
