@@ -276,7 +276,6 @@ def conv_roofline(eng, torch, stream):
 
     Algorithmic ops per launch = 2*N*OH*OW*OC*IC*KH*KW (benchmarks/roofline_report.py:94 convention);
     achieved = sum(ops) / sum(kernel time) over all W8A8 conv launches of one step."""
-    from aexrt_b200 import _native
     from aexrt_b200._native import check
 
     lib = eng.lib

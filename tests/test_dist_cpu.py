@@ -6,7 +6,6 @@ ranks of the elapsed time.  This checks that logic with two gloo ranks.
 """
 import os
 
-import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp

@@ -10,7 +10,6 @@
 import numpy as np
 import pytest
 
-from oracle import w8a8 as ow
 from oracle import yolo_model as om
 from tests._util import nhwc_to_nchw, slab16_to_nchw
 
@@ -43,7 +42,6 @@ def _engine(program, batch):
 
 def test_per_layer_teacher_forced(v8n):
     torch = _torch()
-    from aexrt_b200.yolo import ConvCmd, SppfCmd
 
     eng = _engine(v8n, 2)
     imgs = _images(2)
