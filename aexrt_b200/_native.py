@@ -91,6 +91,9 @@ _SIGNATURES = {
                                  + [c_void_p, c_void_p, c_void_p]),
     "aexrt_b200_act_amax_quantize_f16": (c_int, [c_void_p] + [c_uint32] * 5 + [c_void_p, c_uint32, c_uint32, c_void_p,
                                                                              c_void_p, c_void_p]),
+    "aexrt_b200_act_amax_quantize_f16_wait_limit": (c_int, [c_void_p] + [c_uint32] * 5 + [c_void_p, c_uint32, c_uint32,
+                                                                                        c_void_p, c_void_p, c_uint64,
+                                                                                        c_void_p]),
     "aexrt_b200_act_status": (c_int, [POINTER(c_uint32)]),
     "aexrt_b200_zero": (c_int, [c_void_p, c_uint64, c_void_p]),
     "aexrt_b200_act_quantize_f16_noalloc": (c_int, [c_void_p] + [c_uint32] * 9 + [c_void_p, c_void_p, c_void_p]),

@@ -40,7 +40,7 @@ TOC_ENTRY = 32
 BASE_SECTIONS = tuple(range(1, 10))
 SECTION_NAMES = {1: "manifest", 2: "values", 3: "commands", 4: "raw constants", 5: "kernel plan",
                  6: "packed weights", 7: "memory plan", 8: "fusion plan", 9: "pipeline cache",
-                 10: "physical dispatch plan", 11: "arena barrier plan"}
+                 10: "physical dispatch plan", 11: "arena barrier plan", 12: "parallel plan"}
 # command kinds and flags: src/aexrt/engine.py:85-118
 KIND = {"CONV": 1, "CONV_SILU": 2, "CONCAT_CONV1X1": 3, "VIEW": 4, "ALIAS": 5, "SLICE": 6, "CONCAT": 7,
         "RESIZE": 8, "MAXPOOL": 9, "UNARY": 10, "BINARY": 11, "MATMUL": 12, "TRANSPOSE": 13, "SOFTMAX": 14}
@@ -95,7 +95,7 @@ def _u(fmt: str, buf: bytes, off: int, what: str):
 def load_engine(src) -> Engine:
     """Parses and validates an ``.aexrt`` engine (path or bytes)."""
     data = bytes(src) if isinstance(src, (bytes, bytearray, memoryview)) else open(src, "rb").read()
-    magic, version, hsize, count, flags, fsize, toc, toc_size = _u("<8sIIIIQQQ", data, 0, "header")
+    magic, version, hsize, count, flags, fsize, toc, toc_size, reserved = _u("<8sIIIIQQQ16s", data, 0, "header")
     if magic != MAGIC:
         raise EngineError("not an .aexrt engine (bad magic)")
     if version != 1 or hsize != HEADER_SIZE:
@@ -106,9 +106,17 @@ def load_engine(src) -> Engine:
         raise EngineError(f"file size {len(data)} does not match the header's {fsize}")
     if toc != HEADER_SIZE or toc_size != count * TOC_ENTRY or toc + toc_size > len(data):
         raise EngineError("bad section table")
+    if any(reserved):
+        raise EngineError("reserved header bytes are not zero")
+    if not len(BASE_SECTIONS) <= count <= max(SECTION_NAMES):
+        raise EngineError(f"section count {count} outside {len(BASE_SECTIONS)}..{max(SECTION_NAMES)}")
     sections: Dict[int, Tuple[int, int, int, int]] = {}
     for i in range(count):
-        sid, sflags, off, size, crc, _ = _u("<IIQQII", data, toc + TOC_ENTRY * i, "section table")
+        sid, sflags, off, size, crc, rsv = _u("<IIQQII", data, toc + TOC_ENTRY * i, "section table")
+        if sid not in SECTION_NAMES:
+            raise EngineError(f"unknown section id {sid}")
+        if rsv != 0:
+            raise EngineError(f"section {sid}: reserved table field is not zero")
         if sid in sections:
             raise EngineError(f"duplicate section {sid}")
         if off < toc + toc_size or off + size > len(data):
@@ -119,6 +127,8 @@ def load_engine(src) -> Engine:
     missing = [s for s in BASE_SECTIONS if s not in sections]
     if missing:
         raise EngineError(f"missing sections {missing}")
+    if 11 in sections and 10 not in sections:
+        raise EngineError("section 11 (arena barrier plan) requires section 10 (physical dispatch plan)")
     body = lambda sid: data[sections[sid][1]:sections[sid][1] + sections[sid][2]]  # noqa: E731
 
     m = body(1)
@@ -129,6 +139,11 @@ def load_engine(src) -> Engine:
     conf, iou = _u("<ff", m, 84, "manifest")
     if u[0] != 1:
         raise EngineError(f"unsupported manifest version {u[0]}")
+    # the manifest rules of the reference loader (parse_aexrt_engine, runtime.cpp:17613-17618)
+    if (u[1] != 1 or u[2] not in (1, 2) or u[3] != 2 or u[4] not in (1, 2) or u[5] > 1 or 0 in (u[6], u[7], u[8])
+            or u[12] == 0 or u[14] == 0 or u[15] >= u[12] or u[16] >= u[12] or input_elements == 0
+            or arena_nbytes == 0):
+        raise EngineError("manifest fields out of range (target, precision, mode, layout, counts or value ids)")
     manifest = dict(runtime_target=u[1], precision=u[2], mode=u[3], output_layout=u[4], objectness=u[5],
                     channels=u[6], anchors=u[7], classes=u[8], max_candidates=u[9], max_detections=u[10],
                     nodes=u[11], value_count=u[12], constant_count=u[13], command_count=u[14],

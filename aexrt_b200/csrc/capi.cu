@@ -143,6 +143,8 @@ namespace {
 
 // Kernel instances live in their own translation units (kernels_*.cu), compiled in parallel.
 constexpr int kMaxConvSmem = 200 * 1024;
+// The activation kernels put the image index in a grid's y or z dimension.
+constexpr uint32_t kMaxImagesPerLaunch = 65535;
 // Halo tile: output tw x th on an M grid of pitch = tw + (2 for 3x3 s1, 1 for 3x3 s2, 0 for 1x1)
 // <= max_pitch (one TMA box row of pitch pixels within the 256-element limit), th*pitch <= 128.
 bool pick_halo_tile(int oh, int ow, int k, int s, int max_pitch, int& tw, int& th, int& pitch) {
@@ -817,6 +819,7 @@ int aexrt_b200_act_amax_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, u
   if (!x || !amax_groups) return fail("null pointer");
   const uint32_t groups = (c + 15) / 16;
   if (group_offset + groups > groups_total) return fail("amax group range exceeds groups_total");
+  if (n > kMaxImagesPerLaunch) return fail("at most %u images per call (grid dimension limit)", kMaxImagesPerLaunch);
   if (n == 0 || c == 0 || h == 0 || w == 0) return 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int hw = static_cast<int>(h * w);
@@ -875,6 +878,7 @@ int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t 
     return fail("NHWC slice must be 16-byte aligned (ldc, coff multiples of 8)");
   if (group_offset + (c + 15) / 16 > groups_total) return fail("amax group range exceeds groups_total");
   if (reinterpret_cast<uintptr_t>(q_out) % 16) return fail("q_out must be 16-byte aligned");
+  if (n > kMaxImagesPerLaunch) return fail("at most %u images per call (grid dimension limit)", kMaxImagesPerLaunch);
   if (n == 0 || c == 0 || h == 0 || w == 0) return 1;
   QuantParams q;
   quant_params_common(q, x, n, c, h, w, layout, ldc, coff, amax_groups, groups_total, group_offset);
@@ -965,14 +969,14 @@ int cluster_quant_prepare(int dev, int ctas) {
   return fits > 0 ? 1 : 0;
 }
 
-}  // namespace
-
-extern "C" {
-
-int aexrt_b200_act_amax_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t mode,
-                                     uint32_t* amax_groups, uint32_t groups_total, uint32_t group_offset,
-                                     void* q_out, float* scale_rec, void* stream) {
+// aexrt_b200_act_amax_quantize_f16 with the cluster kernel's first copy wait limited to
+// wait_limit cycles (the second, which keeps a CTA from exiting under its own copies, always
+// has the full limit).
+int amax_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t mode,
+                      uint32_t* amax_groups, uint32_t groups_total, uint32_t group_offset, void* q_out,
+                      float* scale_rec, void* stream, long long wait_limit) {
   if (!x || !amax_groups || !q_out || !scale_rec) return fail("null pointer");
+  if (n > kMaxImagesPerLaunch) return fail("at most %u images per call (grid dimension limit)", kMaxImagesPerLaunch);
   if (mode > 1) return fail("mode must be 0 (per tensor) or 1 (pg16)");
   if (mode == 1 && c % 16) return fail("pg16 needs c %% 16 == 0");
   const uint32_t groups = (c + 15) / 16;
@@ -982,7 +986,7 @@ int aexrt_b200_act_amax_quantize_f16(const void* x, uint32_t n, uint32_t c, uint
   int dev = 0;
   if (!cuda_ok(cudaGetDevice(&dev), "cudaGetDevice")) return 0;
   if (dev < 0 || dev >= 128) return fail("device index %d out of range", dev);
-  const int slices = n <= 65535u ? cluster_quant_slices(c, hw, x, q_out) : 0;
+  const int slices = cluster_quant_slices(c, hw, x, q_out);
   if (slices) {
     const int ctas = static_cast<int>(groups) * slices;
     const int ready = cluster_quant_prepare(dev, ctas);
@@ -996,7 +1000,8 @@ int aexrt_b200_act_amax_quantize_f16(const void* x, uint32_t n, uint32_t c, uint
       return cuda_ok(cudaLaunchKernelEx(&cfg, amax_quant_cluster_kernel, static_cast<const __half*>(x),
                                         static_cast<int>(c), static_cast<int>(hw), slices, static_cast<int>(mode),
                                         static_cast<uint8_t*>(q_out), scale_rec, amax_groups,
-                                        static_cast<int>(groups_total), static_cast<int>(group_offset), status),
+                                        static_cast<int>(groups_total), static_cast<int>(group_offset), status,
+                                        wait_limit),
                      "cluster quantize launch")
                  ? 1
                  : 0;
@@ -1008,6 +1013,27 @@ int aexrt_b200_act_amax_quantize_f16(const void* x, uint32_t n, uint32_t c, uint
     return 0;
   return aexrt_b200_act_quantize_f16(x, n, c, h, w, AEXRT_B200_LAYOUT_NCHW_F16, c, 0, amax_groups, groups_total,
                                      group_offset, mode, 1, q_out, scale_rec, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int aexrt_b200_act_amax_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w, uint32_t mode,
+                                     uint32_t* amax_groups, uint32_t groups_total, uint32_t group_offset,
+                                     void* q_out, float* scale_rec, void* stream) {
+  return amax_quantize_f16(x, n, c, h, w, mode, amax_groups, groups_total, group_offset, q_out, scale_rec, stream,
+                           kWaitLimitCycles);
+}
+
+int aexrt_b200_act_amax_quantize_f16_wait_limit(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w,
+                                                uint32_t mode, uint32_t* amax_groups, uint32_t groups_total,
+                                                uint32_t group_offset, void* q_out, float* scale_rec,
+                                                uint64_t wait_limit_cycles, void* stream) {
+  const long long lim = wait_limit_cycles > static_cast<uint64_t>(kWaitLimitCycles)
+                            ? kWaitLimitCycles
+                            : static_cast<long long>(wait_limit_cycles);
+  return amax_quantize_f16(x, n, c, h, w, mode, amax_groups, groups_total, group_offset, q_out, scale_rec, stream, lim);
 }
 
 int aexrt_b200_act_status(uint32_t* status) {
@@ -1029,6 +1055,7 @@ int aexrt_b200_pack_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint3
   if (layout == AEXRT_B200_LAYOUT_NHWC_F16 && (ldc < coff + c || ldc % 8 || coff % 8))
     return fail("NHWC slice must be 16-byte aligned (ldc, coff multiples of 8)");
   if (reinterpret_cast<uintptr_t>(out) % 16) return fail("out must be 16-byte aligned");
+  if (n > kMaxImagesPerLaunch) return fail("at most %u images per call (grid dimension limit)", kMaxImagesPerLaunch);
   if (n == 0 || c == 0 || h == 0 || w == 0) return 1;
   QuantParams q;
   quant_params_common(q, x, n, c, h, w, layout, ldc, coff, nullptr, 0, 0);
@@ -1092,6 +1119,7 @@ int aexrt_b200_conv_f16_image(const AexrtB200ConvPlan* p, const void* images, ui
     return fail("images must be NCHW fp16 or fp32");
   if (!p->image_input) return fail("plan does not take images directly (need fp16, 3 input channels, 3x3, oc %% 16 == 0 <= 64)");
   if (!images || !out) return fail("null input/output pointer");
+  if (p->desc.batch > kMaxImagesPerLaunch) return fail("stem: at most %u images per launch", kMaxImagesPerLaunch);
   const uint32_t oc = p->desc.out_channels;
   if (out_ldc < out_coff + oc || out_ldc % 8 || out_coff % 8 || reinterpret_cast<uintptr_t>(out) % 16)
     return fail("output slice must fit (coff + oc <= ldc) with ldc, coff multiples of 8 and a 16-byte aligned base");
@@ -1197,6 +1225,7 @@ static bool fill_sources(QuantParams& q, const AexrtB200ActSource* srcs, uint32_
                          uint32_t w, int cps, bool need_amax) {
   if (!srcs || nsrc == 0 || nsrc > static_cast<uint32_t>(kMaxQuantSrc))
     return fail("between 1 and %d sources", kMaxQuantSrc) != 0;
+  if (n > kMaxImagesPerLaunch) return fail("at most %u images per call (grid dimension limit)", kMaxImagesPerLaunch) != 0;
   std::memset(&q, 0, sizeof(q));
   q.nsrc = static_cast<int>(nsrc);
   q.n = static_cast<int>(n);
@@ -1276,6 +1305,7 @@ int aexrt_b200_sppf_pool(const void* x, uint32_t n, uint32_t h, uint32_t w, uint
       reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
     return fail("sppf: c %% 16 == 0 and 16-byte aligned slices required");
   if (amax && amax_goff * 16 + 3 * c > amax_stride * 16) return fail("sppf: amax slots out of range");
+  if (n > kMaxImagesPerLaunch) return fail("sppf: at most %u images per call", kMaxImagesPerLaunch);
   const long total = static_cast<long>(n) * h * w * (c / 8);
   if (total == 0) return 1;
   {
@@ -1437,6 +1467,9 @@ extern "C" int aexrt_b200_act_quantize_f16_noalloc(const void* x, uint32_t n, ui
                                                    uint32_t layout, uint32_t ldc, uint32_t coff, uint32_t mode,
                                                    uint32_t consumer_stride, void* q_out, float* scale_rec,
                                                    void* stream) {
+  // the image index is a grid dimension of the amax and quantize launches
+  if (n > kMaxImagesPerLaunch)
+    return fail("act_quantize_noalloc: %u images exceed the %u a call takes", n, kMaxImagesPerLaunch);
   const uint64_t slots = static_cast<uint64_t>(n) * ((c + 15) / 16);
   if (slots > kNoAllocAmaxSlots)
     return fail("act_quantize_noalloc: %llu amax slots (images x ceil(channels/16)) exceed the fixed %u",

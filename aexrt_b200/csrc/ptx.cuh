@@ -79,19 +79,29 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Returns false (and
-// sets `flag` in *status) when the cycle limit passes first.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t flag) {
+// sets `flag` in *status) when `limit` cycles pass first; a limit of 0 is one
+// non-blocking test.
+__device__ __forceinline__ bool mbar_wait_bounded_limit(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t flag,
+                                                        long long limit) {
   if (mbar_test_wait(bar, parity)) return true;
+  if (limit <= 0) {
+    atomicOr(status, flag);
+    return false;
+  }
   const long long t0 = clock64();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 4; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit) {
       atomicOr(status, flag);
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t flag) {
+  return mbar_wait_bounded_limit(bar, parity, status, flag, kWaitLimitCycles);
 }
 
 // ---------------------------------------------------------------- packed fp32 pairs (sm_100 f32x2)

@@ -34,6 +34,7 @@ constexpr int kClusterQuantChunks = 8;      // mbarriers: two channel planes eac
 constexpr int kClusterQuantMaxCtas = 8;     // portable cluster size
 // dynamic shared memory of one CTA's strip slice: at most two CTAs per SM
 constexpr int kClusterQuantMaxSliceBytes = 112 * 1024;
+constexpr uint32_t kSliceFailed = 0x80000000u;
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -62,17 +63,20 @@ __device__ __forceinline__ void codes_pair(__half2 h, uint64_t m2, uint32_t& a, 
 // owns pixels [s * hw_s, (s + 1) * hw_s) of 16-channel strip g = r / slices, s = r % slices;
 // dynamic smem = 32 * hw_s bytes ([16 channels][hw_s] fp16).
 // amax_g: [n][groups_total] uint32 float bits (stored: no clearing pass), or null.
-// status: bit kStatusTimeoutFull when a copy did not land within the wait limit.
+// status: bit kStatusTimeoutFull when a copy did not land within wait_limit cycles; then no CTA of
+// that image's cluster writes q, rec or amax_g (the maxima would be incomplete).
 __global__ void __launch_bounds__(kClusterQuantThreads, 2)
     amax_quant_cluster_kernel(const __half* __restrict__ x, int c, int hw, int slices, int mode,
                               uint8_t* __restrict__ q, float* __restrict__ rec, uint32_t* __restrict__ amax_g,
-                              int groups_total, int group_offset, uint32_t* status) {
+                              int groups_total, int group_offset, uint32_t* status, long long wait_limit) {
   extern __shared__ __align__(128) unsigned char strip_smem[];
   __shared__ __align__(8) uint64_t bar[kClusterQuantChunks];
   __shared__ uint32_t s_warp[32];
-  __shared__ uint32_t s_slice_amax;  // read by the peer CTAs
+  // this slice's amax bits, read by the peer CTAs; bit 31 (never set in the bits of an |x| maximum)
+  // marks a slice whose copies did not all land in time
+  __shared__ uint32_t s_slice_amax;
   __shared__ float s_amax_t, s_amax_grp;
-  __shared__ int s_ok;
+  __shared__ int s_ok, s_cluster_ok;
   const int ctas = gridDim.x, n = blockIdx.y;
   const int g = blockIdx.x / slices, sl = blockIdx.x - g * slices;
   const int groups = ctas / slices;
@@ -98,7 +102,7 @@ __global__ void __launch_bounds__(kClusterQuantThreads, 2)
   __half2 hm = __float2half2_rn(0.0f);
   bool ok = true;
   for (int k = 0; k < kClusterQuantChunks; ++k) {
-    if (!mbar_wait_bounded(&bar[k], 0, status, kStatusTimeoutFull)) {
+    if (!mbar_wait_bounded_limit(&bar[k], 0, status, kStatusTimeoutFull, wait_limit)) {
       ok = false;
       break;
     }
@@ -115,26 +119,29 @@ __global__ void __launch_bounds__(kClusterQuantThreads, 2)
   __syncthreads();
   if (warp == 0) {
     m = __reduce_max_sync(0xffffffffu, lane < kClusterQuantThreads / 32 ? s_warp[lane] : 0u);
-    if (lane == 0) s_slice_amax = m;
+    if (lane == 0) s_slice_amax = m | (s_ok ? 0u : kSliceFailed);
   }
   // ---- 2. group and per-tensor amax over the cluster's slices (distributed shared memory)
   cluster_sync_all();
   if (tid == 0) {
-    uint32_t t = 0, gm = 0;
+    uint32_t t = 0, gm = 0, failed = 0;
     for (int r = 0; r < ctas; ++r) {
       const uint32_t v = ld_peer_u32(&s_slice_amax, static_cast<uint32_t>(r));
-      t = max(t, v);
-      if (r / slices == g) gm = max(gm, v);
+      failed |= v & kSliceFailed;
+      t = max(t, v & ~kSliceFailed);
+      if (r / slices == g) gm = max(gm, v & ~kSliceFailed);
     }
     s_amax_t = __uint_as_float(t);
     s_amax_grp = __uint_as_float(gm);
+    // one slice short of data makes the image's maxima wrong: then no CTA of the cluster writes
+    s_cluster_ok = failed ? 0 : 1;
   }
   __syncthreads();
   const float amax_grp = s_amax_grp, amax_t = s_amax_t;
   const float a = mode == 1 ? amax_grp : amax_t;
   const float mult = a > 0.0f ? __fdiv_rn(127.0f, a) : 0.0f;
   // ---- 3. quantize from shared memory: two pixels per thread, one 16-byte slab row each
-  if (s_ok) {
+  if (s_cluster_ok) {
     const uint64_t m2 = f2_pack(mult, mult);
     uint8_t* dst = q + ((static_cast<size_t>(n) * groups + g) * hw + static_cast<size_t>(sl) * hw_s) * 16;
     for (int p = 2 * tid; p < hw_s; p += 2 * kClusterQuantThreads) {
@@ -162,11 +169,14 @@ __global__ void __launch_bounds__(kClusterQuantThreads, 2)
       if (g == 0) r[0] = amax_t;
       if (amax_g) amax_g[static_cast<size_t>(n) * groups_total + group_offset + g] = __float_as_uint(amax_grp);
     }
-  } else if (tid == 0) {
-    // a copy that has not landed may still write this CTA's shared memory: wait for it (bounded)
+  } else if (tid == 0 && !s_ok) {
+    // a copy that has not landed may still write this CTA's shared memory: wait for it with the
+    // full limit (whatever limit the first wait had), so the CTA does not exit under its copies
     for (int k = 0; k < kClusterQuantChunks; ++k) mbar_wait_bounded(&bar[k], 0, status, kStatusTimeoutFull);
   }
-  // peers may still be reading s_slice_amax: leave the cluster together
+  // peers may still be reading s_slice_amax: leave the cluster together (the CTA's threads converge
+  // first: thread 0 may come from the wait above, and the cluster barrier is warp-aligned)
+  __syncthreads();
   cluster_sync_all();
 }
 

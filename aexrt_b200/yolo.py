@@ -114,9 +114,13 @@ def _make_divisible(x: float, d: int = 8) -> int:
 
 
 class _Builder:
-    def __init__(self, name: str, imgsz: int, nc: int, seed: int, reg_max: int = 16):
+    def __init__(self, name: str, imgsz: int, nc: int, seed: int, reg_max: int = 16, gain: float = 1.0,
+                 cls_gain: float = 1.0, cls_bias: float = 0.0):
         self.p = YoloProgram(name=name, in_channels=3, imgsz=imgsz, nc=nc, reg_max=reg_max)
         self.rng = np.random.default_rng(seed)
+        self.gain = gain
+        self.cls_gain = cls_gain
+        self.cls_bias = cls_bias
         self.p.values["images"] = ValueSpec(3, imgsz, imgsz)
 
     def value(self, name: str, channels: int, h: int, w: int) -> str:
@@ -124,7 +128,7 @@ class _Builder:
         return name
 
     def _weights(self, oc: int, ic: int, k: int) -> Tuple[np.ndarray, np.ndarray]:
-        w = self.rng.normal(0.0, 1.0 / math.sqrt(ic * k * k), (oc, ic, k, k)).astype(np.float32)
+        w = self.rng.normal(0.0, self.gain / math.sqrt(ic * k * k), (oc, ic, k, k)).astype(np.float32)
         b = self.rng.normal(0.0, 0.1, (oc,)).astype(np.float32)
         return w, b
 
@@ -201,9 +205,9 @@ class _Builder:
             oc = self.p.values[o].channels
             wf = np.zeros((oc, c2 + c3, 1, 1), np.float32)
             wf[:4 * reg_max, :c2] = w2
-            wf[4 * reg_max:4 * reg_max + nc, c2:] = w3
+            wf[4 * reg_max:4 * reg_max + nc, c2:] = w3 * np.float32(self.cls_gain)
             bf = np.zeros(oc, np.float32)
-            bf[:4 * reg_max], bf[4 * reg_max:4 * reg_max + nc] = b2, b3
+            bf[:4 * reg_max], bf[4 * reg_max:4 * reg_max + nc] = b2, b3 + np.float32(self.cls_bias)
             bn = 16
             while bn < min(oc, 256):
                 bn *= 2
@@ -214,15 +218,22 @@ class _Builder:
 
 
 def build_yolov8(width: float = 0.25, depth: float = 0.33, nc: int = 4, imgsz: int = 320, seed: int = 0,
-                 max_channels: int = 1024, name: Optional[str] = None) -> YoloProgram:
-    """YOLOv8 command stream (n: width 0.25 depth 0.33; s: width 0.5 depth 0.33)."""
+                 max_channels: int = 1024, name: Optional[str] = None, gain: float = 1.0,
+                 cls_gain: float = 1.0, cls_bias: float = 0.0) -> YoloProgram:
+    """YOLOv8 command stream (n: width 0.25 depth 0.33; s: width 0.5 depth 0.33).
+
+    ``gain`` scales the random weights' standard deviation (1.0: N(0, 1/sqrt(fan_in)), under which
+    activations shrink through the SiLU layers); ``cls_gain`` scales the class-logit weights and
+    ``cls_bias`` is added to the class-logit biases, which spreads the class scores and moves them
+    away from 0.5 so that only some anchors pass a confidence threshold."""
     def ch(c):
         return _make_divisible(min(c, max_channels) * width, 8)
 
     def dep(n):
         return max(round(n * depth), 1) if n > 1 else n
 
-    b = _Builder(name or f"yolov8_w{width}_d{depth}_{imgsz}", imgsz, nc, seed)
+    b = _Builder(name or f"yolov8_w{width}_d{depth}_{imgsz}", imgsz, nc, seed, gain=gain, cls_gain=cls_gain,
+                 cls_bias=cls_bias)
     img = [Part("images", 0, 3)]
     x = b.conv_block("l0", img, ch(64), 3, 2, precision="fp16")  # stem: 3 input channels fail IC % 4
     x = b.conv_block("l1", [Part(x, 0, ch(64))], ch(128), 3, 2)
@@ -245,9 +256,11 @@ def build_yolov8(width: float = 0.25, depth: float = 0.33, nc: int = 4, imgsz: i
     return b.p
 
 
-def build_yolov8n(nc: int = 4, imgsz: int = 320, seed: int = 0) -> YoloProgram:
+def build_yolov8n(nc: int = 4, imgsz: int = 320, seed: int = 0, gain: float = 1.0, cls_gain: float = 1.0,
+                  cls_bias: float = 0.0) -> YoloProgram:
     """YOLOv8n (width 0.25, depth 0.33), nc=4, 320x320."""
-    return build_yolov8(0.25, 0.33, nc, imgsz, seed, name=f"yolov8n_{imgsz}")
+    return build_yolov8(0.25, 0.33, nc, imgsz, seed, name=f"yolov8n_{imgsz}", gain=gain, cls_gain=cls_gain,
+                        cls_bias=cls_bias)
 
 
 def build_yolov8s(nc: int = 80, imgsz: int = 640, seed: int = 0) -> YoloProgram:

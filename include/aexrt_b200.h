@@ -226,7 +226,8 @@ int aexrt_b200_pack_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint3
  * and/or as a channel slice of a wider NHWC buffer (SLICE / C2f split).  The
  * quantizer reads the parts in place, so the concatenated fp16 tensor is never
  * materialised: the reference instead runs CONCAT, then quantizes the
- * concatenated value (runtime.cpp:21466-21665). */
+ * concatenated value (its compiler un-fuses concat + conv for the int8 path,
+ * src/aexrt/yolo.py:473-487; quantizer recorder runtime.cpp:21466-21665). */
 typedef struct AexrtB200ActSource {
     const void* ptr;
     uint32_t layout;              /* AEXRT_B200_LAYOUT_* */
@@ -325,9 +326,20 @@ int aexrt_b200_act_amax_quantize_f16(const void* x, uint32_t n, uint32_t c, uint
                                      uint32_t* amax_groups, uint32_t groups_total, uint32_t group_offset,
                                      void* q_out, float* scale_rec, void* stream);
 
+/* The same call with the wait for the strip copies limited to wait_limit_cycles
+ * SM clock cycles (capped at the default of 2^30).  For failure-detection tests:
+ * a limit of 0 makes the first wait give up unless the data has landed, which
+ * sets the status word and leaves that image's outputs unwritten; the kernel
+ * still waits, with the full limit, for its own copies before it exits. */
+int aexrt_b200_act_amax_quantize_f16_wait_limit(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_t w,
+                                                uint32_t mode, uint32_t* amax_groups, uint32_t groups_total,
+                                                uint32_t group_offset, void* q_out, float* scale_rec,
+                                                uint64_t wait_limit_cycles, void* stream);
+
 /* Reads and clears this device's activation-kernel status word (synchronises):
  * non-zero means a strip copy of aexrt_b200_act_amax_quantize_f16 did not land
- * within the wait limit and that image's outputs were not written. */
+ * within the wait limit; then no output of that image (codes, scale record,
+ * amax slots) was written. */
 int aexrt_b200_act_status(uint32_t* status);
 
 /* ---------------------------------------------------------------- allocation-free variant
@@ -344,6 +356,10 @@ int aexrt_b200_act_status(uint32_t* status);
  *   - The first call on a device resolves the array's device address
  *     (cudaGetSymbolAddress) with that device current: make it before any
  *     stream capture.  Each call clears its slots first.
+ *   - The address is cached per device for the life of the process: do not
+ *     use the library across a cudaDeviceReset (or any teardown of the
+ *     device's primary context) on that device.
+ *   - At most 65535 images per call (a grid dimension of the launches).
  *   - Every call shares the one array, so calls that overlap on the GPU (other
  *     streams, other host threads) race; serialize them.
  *   - Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */

@@ -85,6 +85,23 @@ def test_fails_closed_on_malformed_engines(raw):
     bad = _fix_crc(_patch(raw, off + 8 + 8, struct.pack("<I", 53)), 5)
     with pytest.raises(ae.EngineError, match="disagrees"):
         ae.load_engine(bad)
+    # reserved header bytes and TOC fields must be zero; section ids are 1..12; section 11 needs 10
+    with pytest.raises(ae.EngineError, match="reserved header"):
+        ae.load_engine(_patch(raw, 50, b"\x01"))
+    with pytest.raises(ae.EngineError, match="reserved table"):
+        ae.load_engine(_patch(raw, 64 + 28, struct.pack("<I", 7)))
+    with pytest.raises(ae.EngineError, match="unknown section id"):
+        ae.load_engine(_patch(raw, 64, struct.pack("<I", 40)))
+    count = struct.unpack_from("<I", raw, 16)[0]
+    for i in range(count):
+        if struct.unpack_from("<I", raw, 64 + 32 * i)[0] == 10:
+            with pytest.raises(ae.EngineError, match="requires section 10"):
+                ae.load_engine(_patch(raw, 64 + 32 * i, struct.pack("<I", 12)))
+    # manifest fields out of the reference loader's ranges (output value id past the value table)
+    off, _ = _section(raw, 1)
+    bad = _fix_crc(_patch(raw, off + 64, struct.pack("<I", 10 ** 6)), 1)
+    with pytest.raises(ae.EngineError, match="manifest fields"):
+        ae.load_engine(bad)
     # the same change applied to command and plan alike loads, but the runner-side check refuses
     # a layout-8 payload of the wrong size
     e = ae.load_engine(raw)

@@ -161,19 +161,21 @@ def test_baseline_pg16_output_channel_variant():
     assert np.abs(g["y"].astype(np.float32) - o["y32"]).max() <= TOL
 
 
+@pytest.mark.parametrize("mode", [0, 1])
 @pytest.mark.parametrize("n,ic,h,w,oc,k,s", [
     (64, 128, 40, 40, 128, 1, 1),
     (64, 64, 80, 80, 64, 3, 1),
     (64, 32, 160, 160, 64, 3, 2),
     (64, 128, 20, 20, 256, 3, 2),
 ])
-def test_conv_parity_batch64(n, ic, h, w, oc, k, s):
-    """BASELINE config 2 at batch 64: per-image scales, exact accumulators."""
+def test_conv_parity_batch64(n, ic, h, w, oc, k, s, mode):
+    """BASELINE config 2 at batch 64, per-tensor and pg16 (the INT8_PERGROUP scheme): per-image
+    scales, exact codes, accumulators and (pg16) per-group sub-sums."""
     rng = np.random.default_rng(64 + ic + oc)
     x = seeded_act(rng, (n, ic, h, w))
     weight = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
     bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
-    check_against_oracle(x, weight, bias, k, s, 0)
+    check_against_oracle(x, weight, bias, k, s, mode)
 
 
 @pytest.mark.parametrize("n,ic,h,w,oc,k,s,silu", [

@@ -1,9 +1,11 @@
 """GPU parity of the whole YOLOv8n-320 W8A8 program against the CPU oracle.
 
 * per layer, fed the device's own inputs ("teacher forcing"): int8 codes
-  bit-exact, fp16 outputs within max-abs 1e-2 (relative for large values);
+  bit-exact, fp16 outputs within max-abs 1e-2, with per-tensor scales and with
+  INT8_PERGROUP (pg16) on every int8 conv;
 * end to end from the same images: class scores within 0.02 (the reference's
-  detection-score gate, README.md:62-63) and boxes within a few pixels;
+  detection-score gate, README.md:62-63) and boxes within a few pixels, and the
+  detections of the GPU pipeline against the oracle pipeline's;
 * CUDA-graph replay equals eager launches bit-for-bit, and every image's
   result is independent of the batch it runs in (per-image scales).
 """
@@ -29,6 +31,21 @@ def v8n():
     return yolo.build_yolov8n(nc=4, imgsz=320, seed=0)
 
 
+def _v8n_pg16():
+    """YOLOv8n-320 with the INT8_PERGROUP flag on every int8 conv (all have 16k input channels)."""
+    from aexrt_b200 import yolo
+
+    prog = yolo.build_yolov8n(nc=4, imgsz=320, seed=0)
+    names = {c.name for c in prog.commands if isinstance(c, yolo.ConvCmd) and c.precision == "int8"}
+    assert all(c.ic % 16 == 0 for c in prog.commands if isinstance(c, yolo.ConvCmd) and c.name in names)
+    yolo.apply_algo_map(prog, pergroup=names)
+    return prog
+
+
+def _program(pg16, v8n):
+    return _v8n_pg16() if pg16 else v8n
+
+
 def _images(n, seed=0, size=320):
     rng = np.random.default_rng(seed)
     return rng.uniform(0, 1, (n, 3, size, size)).astype(np.float16).astype(np.float32)
@@ -40,9 +57,11 @@ def _engine(program, batch):
     return engine.CompiledYolo(program, batch)
 
 
-def test_per_layer_teacher_forced(v8n):
+@pytest.mark.parametrize("pg16", [False, True])
+def test_per_layer_teacher_forced(v8n, pg16):
     torch = _torch()
 
+    v8n = _program(pg16, v8n)
     eng = _engine(v8n, 2)
     imgs = _images(2)
     eng.forward(torch.from_numpy(imgs).cuda())
@@ -61,7 +80,10 @@ def test_per_layer_teacher_forced(v8n):
             if c.precision == "int8":
                 q = st[4][0].cpu().numpy()
                 assert np.array_equal(slab16_to_nchw(q, c.ic, x.shape[2], x.shape[3], c.s), r["xq"]), c.name
-            err = np.abs(got - r["y32"]) / np.maximum(1.0, np.abs(r["y32"]))
+            # max-abs 1e-2 on the fp16 outputs (every layer of this model stays below 8 in magnitude,
+            # where half an fp16 ulp is at most 2^-9, so the absolute gate applies to all of them)
+            assert np.abs(r["y32"]).max() < 8.0, c.name
+            err = np.abs(got - r["y32"])
             worst[c.name] = float(err.max())
             assert err.max() <= 1e-2, (c.name, float(err.max()))
         elif st[0] == "sppf":
@@ -77,8 +99,10 @@ def test_per_layer_teacher_forced(v8n):
     assert np.abs(out[:, :4] - ref[:, :4]).max() <= 1e-2 * 32
 
 
-def test_end_to_end_against_oracle(v8n):
+@pytest.mark.parametrize("pg16", [False, True])
+def test_end_to_end_against_oracle(v8n, pg16):
     torch = _torch()
+    v8n = _program(pg16, v8n)
     eng = _engine(v8n, 2)
     imgs = _images(2, seed=3)
     out = eng.forward(torch.from_numpy(imgs).cuda()).cpu().numpy()
@@ -164,6 +188,70 @@ def test_streaming_detections_match_forwards(v8n):
         counts, _ = eng.split_detections(host_out[k])
         assert torch.equal(host_out[k], want[k]), k
         assert int(counts.max()) <= 100
+
+
+def _match_detections(want, got, score_tol=0.02, box_tol=0.02):
+    """The reference's detection gate (tests/test_runtime.py:1277-1279, README.md:62-63): the same
+    count, and every oracle detection paired with a GPU detection of the same class whose score is
+    within score_tol and whose corners agree within np.allclose(atol=box_tol, rtol=box_tol)."""
+    assert len(want) == len(got), (len(want), len(got))
+    free = list(range(len(got)))
+    for w in want:
+        best = None
+        for j in free:
+            g = got[j]
+            if g[5] == w[5] and abs(g[4] - w[4]) <= score_tol and np.allclose(g[:4], w[:4], atol=box_tol,
+                                                                             rtol=box_tol):
+                best = j
+                break
+        assert best is not None, ("no GPU detection matches", w.tolist())
+        free.remove(best)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("pg16", [False, True])
+def test_detections_from_images_match_oracle_pipeline(v8n, pg16, mode):
+    """The GPU pipeline (W8A8 forward, decode, filter + NMS + top-k) against the oracle pipeline
+    (the reference's W8A8 arithmetic restated, then its post-process) on the same four images."""
+    from aexrt_b200 import engine
+    from oracle import yolo_post as op
+
+    torch = _torch()
+    prog = _program(pg16, v8n)
+    cfg = engine.NmsConfig(mode=mode)
+    eng = engine.CompiledYolo(prog, 4, nms=cfg)
+    eng.capture()
+    imgs = _images(4, seed=40)
+    eng.forward(torch.from_numpy(imgs).cuda())
+    counts, dets = (t.cpu().numpy() for t in eng.detections())
+    ref = om.run_program(prog, imgs)["output0"]
+    for i in range(4):
+        want, cnt = op.postprocess(ref[i], prog.nc, cfg.conf, cfg.iou, cfg.max_candidates, cfg.max_detections, mode)
+        _match_detections(want[:cnt], dets[i, :counts[i]])
+    assert eng.status() == 0
+
+
+def test_yolov8s_640_end_to_end_against_oracle():
+    """BASELINE config 5's model at its own size (YOLOv8s, nc=80, 640x640), batch 2: class scores
+    within 0.02, boxes within a few pixels, detections as the oracle's post-process of the device's
+    own output0."""
+    from aexrt_b200 import engine, yolo
+    from oracle import yolo_post as op
+
+    torch = _torch()
+    prog = yolo.build_yolov8s(nc=80, imgsz=640, seed=0)
+    eng = engine.CompiledYolo(prog, 2, nms=engine.NmsConfig())
+    eng.capture()
+    imgs = _images(2, seed=9, size=640)
+    out = eng.forward(torch.from_numpy(imgs).cuda()).cpu().numpy()
+    ref = om.run_program(prog, imgs)["output0"]
+    assert np.abs(out[:, 4:] - ref[:, 4:]).max() <= 0.02
+    assert np.percentile(np.abs(out[:, :4] - ref[:, :4]), 99) <= 4.0
+    counts, dets = (t.cpu().numpy() for t in eng.detections())
+    for i in range(2):
+        want, cnt = op.postprocess(out[i], 80)
+        assert counts[i] == cnt and np.array_equal(dets[i, :cnt], want)
+    assert eng.status() == 0
 
 
 def test_yolov8s_end_to_end_against_oracle():

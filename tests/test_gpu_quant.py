@@ -241,3 +241,41 @@ def test_single_pass_amax_quantize_equals_two_kernels(shape, mode):
     n, c, h, w = shape
     at, ag = ow.act_amax(x)
     assert np.array_equal(slab16_to_nchw(q.cpu().numpy(), c, h, w), ow.quantize_act(x, at, ag, mode))
+
+
+def test_single_pass_wait_timeout_reports_and_writes_nothing():
+    """Failure detection without a fault: with the copy wait limited to 0 cycles the cluster kernel
+    gives up, sets its status bit and writes nothing of an image whose slices did not all land (every
+    CTA still waits, with the full limit, for its own copies before it exits); the context stays
+    usable and the next normal call is exact."""
+    torch = _torch()
+    from aexrt_b200 import _native, ops
+
+    rng = np.random.default_rng(77)
+    x = seeded_act(rng, (64, 64, 80, 80))
+    xt = torch.from_numpy(x).cuda()
+    amax_ref = ops.act_amax(xt, ops.LAYOUT_NCHW_F16)
+    q_ref, rec_ref = ops.act_quantize(xt, amax_ref, 0, ops.LAYOUT_NCHW_F16)
+    torch.cuda.synchronize()
+    assert ops.act_status() == 0
+    amax = torch.full_like(amax_ref, -1)
+    q = torch.full_like(q_ref, 55)
+    rec = torch.full_like(rec_ref, -2.0)
+    lib = _native.load()
+    assert lib.aexrt_b200_act_amax_quantize_f16_wait_limit(xt.data_ptr(), 64, 64, 80, 80, 0, amax.data_ptr(), 4, 0,
+                                                           q.data_ptr(), rec.data_ptr(), 0, None) == 1
+    torch.cuda.synchronize()
+    assert ops.act_status() & 1  # the timeout bit
+    written = 0
+    for i in range(64):
+        # all of an image's outputs, or none of them
+        if torch.equal(q[i], q_ref[i]):
+            assert torch.equal(rec[i], rec_ref[i]) and torch.equal(amax[i], amax_ref[i])
+            written += 1
+        else:
+            assert (q[i] == 55).all() and (rec[i] == -2.0).all() and (amax[i] == -1).all(), i
+    assert written < 64
+    ops.act_amax_quantize(xt, 0, amax_out=amax, q_out=q, rec_out=rec)
+    torch.cuda.synchronize()
+    assert ops.act_status() == 0
+    assert torch.equal(q, q_ref) and torch.equal(rec, rec_ref) and torch.equal(amax, amax_ref)

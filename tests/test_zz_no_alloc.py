@@ -42,6 +42,11 @@ def test_noalloc_matches_caller_scratch_on_consecutive_calls():
         (ops.LAYOUT_NCHW_F16, (3, 48, 10, 12), 48, 10, 12, 0, 1, 4.0),
         (ops.LAYOUT_NHWC_F16, (2, 9, 11, 32), 32, 9, 11, 1, 2, 0.25),  # smaller values: stale maxima would show
         (ops.LAYOUT_NCHW_F16, (3, 48, 10, 12), 48, 10, 12, 0, 1, 0.5),
+        # 20 x 8 = 160 (image, group) strips >= the SM count: the NCHW amax stores one block's maximum
+        # per strip instead of clearing and max-ing; after a call with larger values, a stale slot
+        # would show
+        (ops.LAYOUT_NCHW_F16, (20, 128, 6, 5), 128, 6, 5, 0, 1, 8.0),
+        (ops.LAYOUT_NCHW_F16, (20, 128, 6, 5), 128, 6, 5, 1, 1, 0.125),
     ]
     for layout, shape, c, h, w, mode, stride, scale in cases:
         x = torch.from_numpy(_act(rng, shape, scale)).cuda()
@@ -68,3 +73,14 @@ def test_noalloc_rejects_more_slots_than_the_fixed_array():
     assert lib.aexrt_b200_act_quantize_f16_noalloc(dummy, 2048, 1024, 4, 4, 1, 1024, 0, 0, 1, dummy, dummy,
                                                    None) == 0
     assert "exceed" in _native.last_error()
+
+
+def test_noalloc_rejects_more_images_than_a_launch_takes():
+    from aexrt_b200 import _native
+
+    lib = _native.load()
+    # 65536 images of 16 channels fit the 65536 slots but not a grid dimension: refused with a message
+    dummy = ctypes.c_void_p(16)
+    assert lib.aexrt_b200_act_quantize_f16_noalloc(dummy, 65536, 16, 1, 1, 1, 16, 0, 0, 1, dummy, dummy,
+                                                   None) == 0
+    assert "65535" in _native.last_error()
