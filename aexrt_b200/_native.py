@@ -75,7 +75,7 @@ _SIGNATURES = {
     "aexrt_b200_conv_f16_image": (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint32, c_uint32, c_void_p, c_uint32,
                                           c_uint32, c_void_p]),
     "aexrt_b200_conv_f16_nhwc": (c_int, [c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_uint32, c_uint32,
-                                         c_void_p, c_uint32, c_uint32, c_void_p]),
+                                         c_void_p, c_uint32, c_uint32, c_void_p, c_uint32, c_uint32, c_void_p]),
     "aexrt_b200_conv_status": (c_int, [c_void_p, POINTER(c_uint32)]),
     "aexrt_b200_packed_f16_bytes": (c_uint64, [c_uint32] * 5),
     "aexrt_b200_pack_f16": (c_int, [c_void_p] + [c_uint32] * 8 + [c_void_p, c_void_p]),
@@ -129,8 +129,13 @@ def check(status: int, what: str) -> None:
 
 
 def header_functions() -> list:
-    """Names of the functions declared in include/aexrt_b200.h (for the ABI test)."""
+    """Names of the functions declared in include/*.h (for the ABI test): the kernel-level ABI
+    (aexrt_b200.h) and the reference runtime ABI (aexrt_yolo.h)."""
+    import glob
     import re
 
-    text = open(HEADER_PATH, encoding="utf-8").read()
-    return sorted(set(re.findall(r"\b(aexrt_b200_[a-z0-9_]+)\s*\(", text)))
+    names = set()
+    for path in glob.glob(os.path.join(os.path.dirname(HEADER_PATH), "*.h")):
+        text = re.sub(r"/\*.*?\*/", "", open(path, encoding="utf-8").read(), flags=re.S)
+        names.update(re.findall(r"\b(aexrt_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)

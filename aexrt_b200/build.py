@@ -20,10 +20,11 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libaexrt_b200.so")
 # capi.cu holds the C ABI and the memory-bound kernels; the conv kernel instances are split over
 # translation units that compile in parallel
-SOURCES = ["capi.cu", "kernels_slot.cu", "kernels_halo_i8_silu.cu", "kernels_halo_i8_linear.cu",
+SOURCES = ["capi.cu", "engine_file.cu", "yolo_runtime.cu", "kernels_slot.cu", "kernels_halo_i8_silu.cu", "kernels_halo_i8_linear.cu",
            "kernels_halo_f16.cu", "kernels_halo_mb.cu", "kernels_halo_pg.cu",
            "kernels_stem16.cu", "kernels_stem32.cu", "kernels_stem48.cu", "kernels_stem64.cu"]
-HEADERS = ["conv_halo.cuh", "conv_tc.cuh", "kernels.cuh", "nms.cuh", "ptx.cuh", "quant.cuh", "quant_cluster.cuh", "stem.cuh", "yolo_ops.cuh"]
+HEADERS = ["conv_halo.cuh", "conv_tc.cuh", "engine_file.h", "graph_ops.cuh", "kernels.cuh", "nms.cuh", "ptx.cuh",
+           "quant.cuh", "quant_cluster.cuh", "stem.cuh", "yolo_ops.cuh"]
 OBJ_DIR = os.path.join(HERE, "_build")
 
 NVCC_FLAGS = [
@@ -51,7 +52,8 @@ def needs_build() -> bool:
     if not os.path.exists(LIB):
         return True
     t = os.path.getmtime(LIB)
-    deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS] + [os.path.join(ROOT, "include", "aexrt_b200.h")]
+    deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS] + [
+        os.path.join(ROOT, "include", h) for h in ("aexrt_b200.h", "aexrt_yolo.h")]
     return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
 
 
@@ -64,6 +66,25 @@ def _run(cmd: list, what: str, verbose: bool) -> None:
         sys.stderr.write(res.stderr)
 
 
+def _includes(path: str, seen: set) -> set:
+    """The quoted #include files a source reaches (transitively), as absolute paths."""
+    import re
+
+    if path in seen or not os.path.exists(path):
+        return seen
+    seen.add(path)
+    for inc in re.findall(r'^#include "([^"]+)"', open(path, encoding="utf-8").read(), re.M):
+        _includes(os.path.normpath(os.path.join(os.path.dirname(path), inc)), seen)
+    return seen
+
+
+def _stale(src: str, obj: str) -> bool:
+    if not os.path.exists(obj):
+        return True
+    t = os.path.getmtime(obj)
+    return any(os.path.getmtime(d) > t for d in _includes(os.path.join(CSRC, src), set()))
+
+
 def build(verbose: bool = False, force: bool = False) -> str:
     if not force and not needs_build():
         return LIB
@@ -74,9 +95,11 @@ def build(verbose: bool = False, force: bool = False) -> str:
     objs = [os.path.join(OBJ_DIR, os.path.splitext(f)[0] + ".o") for f in SOURCES]
     jobs = []
     for src, obj in zip(SOURCES, objs):
+        if not (force or verbose) and not _stale(src, obj):
+            continue  # object newer than its source and every header it includes
         cmd = base + (["-Xptxas", "-v"] if verbose else []) + ["-c", os.path.join(CSRC, src), "-o", obj]
         jobs.append((cmd, src))
-    with ThreadPoolExecutor(max_workers=len(jobs)) as ex:
+    with ThreadPoolExecutor(max_workers=max(1, len(jobs))) as ex:
         for f in [ex.submit(_run, cmd, src, verbose) for cmd, src in jobs]:
             f.result()
     _run(base + ["-shared"] + objs + ["-o", LIB + ".tmp"], "link", verbose)

@@ -108,6 +108,11 @@ void pick_tile(int oh, int ow, int max_tw, int& tw, int& th) {
 
 }  // namespace
 
+namespace aexrt {
+// The library's one thread-local error message, shared by the runtime translation units.
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace aexrt
+
 struct AexrtB200ConvPlan {
   AexrtConv2DDesc desc{};
   uint32_t kind = 0, kernel_id = 0, flags = 0;
@@ -214,9 +219,10 @@ bool check_desc_int8(const AexrtConv2DDesc& d, uint32_t kernel_id, bool pg) {
 }
 
 cudaError_t set_halo_smem(bool f16, int bn, bool silu, bool pg, bool mb) {
-  for (int res = 0; res < (f16 ? 1 : 2); ++res) {
-    const cudaError_t e = cudaFuncSetAttribute(halo_kernel_for(f16, bn, silu, res, pg, mb).fn,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxConvSmem);
+  for (int res = 0; res < 2; ++res) {
+    const HaloFn fn = halo_kernel_for(f16, bn, silu, res, pg, mb).fn;
+    if (!fn) continue;  // no residual instance for this combination
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxConvSmem);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -621,7 +627,6 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     h.status = p->d_status;
     h.silu = p->kind == AEXRT_B200_KIND_CONV_SILU;
     h.nhwc = nhwc_map ? 1 : 0;
-    if (p->f16 && res) return fail("fp16 convs take no residual");
     h.mblocks = p->mblocks;
     h.nacc = p->nacc;
     h.tmem_cols = p->tmem_cols;
@@ -631,6 +636,7 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
       h.tap_b[m] = p->tap_b[m];
     }
     const HaloKernel k = halo_kernel_for(p->f16, p->bn, h.silu != 0, res != nullptr, p->pg, p->mblocks > 1);
+    if (!k.fn) return fail("no conv kernel instance with a residual for a linear fp16 conv");
     k.fn<<<p->grid, k.threads, p->smem, static_cast<cudaStream_t>(stream)>>>(act_map, h);
     return cuda_ok(cudaGetLastError(), "conv launch") ? 1 : 0;
   }
@@ -1189,9 +1195,10 @@ int aexrt_b200_conv_f16(const AexrtB200ConvPlan* plan, const void* x_slab8, cons
                      amax_stride, amax_goff, nullptr, stream);
 }
 
-int aexrt_b200_conv_f16_nhwc(const AexrtB200ConvPlan* plan, const void* x, uint32_t ldc, uint32_t coff, void* out,
-                             uint32_t out_ldc, uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride,
-                             uint32_t amax_goff, void* stream) {
+int aexrt_b200_conv_f16_nhwc(const AexrtB200ConvPlan* plan, const void* x, uint32_t ldc, uint32_t coff,
+                             const void* residual, uint32_t res_ldc, uint32_t res_coff, void* out, uint32_t out_ldc,
+                             uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride, uint32_t amax_goff,
+                             void* stream) {
   if (!plan) return fail("null plan");
   if (!plan->f16) return fail("conv_f16_nhwc: plan is int8; use aexrt_b200_conv_w8a8");
   if (!plan->halo || plan->stride != 1 || plan->image_input)
@@ -1211,8 +1218,8 @@ int aexrt_b200_conv_f16_nhwc(const AexrtB200ConvPlan* plan, const void* x, uint3
   CUtensorMap map;
   if (!encode_map(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, static_cast<const __half*>(x) + coff, dims, strides, box))
     return 0;
-  return launch_conv(plan, x, nullptr, nullptr, 0, 0, out, out_ldc, out_coff, amax_out, amax_stride, amax_goff,
-                     nullptr, stream, &map);
+  return launch_conv(plan, x, nullptr, residual, res_ldc, res_coff, out, out_ldc, out_coff, amax_out, amax_stride,
+                     amax_goff, nullptr, stream, &map);
 }
 
 int aexrt_b200_conv_status(const AexrtB200ConvPlan* plan, uint32_t* status) {

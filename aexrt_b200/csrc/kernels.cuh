@@ -25,15 +25,16 @@ KernelFn kernel_for(bool f16, bool pg, int bn);
 // pg16 (BN 64/128).
 HaloKernel halo_kernel_i8_silu(int bn, bool res);
 HaloKernel halo_kernel_i8_linear(int bn, bool res);
-HaloKernel halo_kernel_f16(int bn, bool silu);
+HaloKernel halo_kernel_f16(int bn, bool silu, bool res);
 HaloKernel halo_kernel_mb(bool f16, int bn, bool silu, bool res);
 HaloKernel halo_kernel_pg(int bn, bool silu, bool res);
 
-// fp16 convs (stem, detect head) never carry a residual; the int8 convs do (C2f tail).
+// Residuals (the C2f tail) are instantiated for every int8 conv and for fp16 SiLU convs; a
+// combination without an instance returns {nullptr, 0}.
 inline HaloKernel halo_kernel_for(bool f16, int bn, bool silu, bool res, bool pg = false, bool mb = false) {
   if (mb) return halo_kernel_mb(f16, bn, silu, res);
   if (pg) return f16 ? HaloKernel{nullptr, 0} : halo_kernel_pg(bn, silu, res);
-  if (f16) return halo_kernel_f16(bn, silu);
+  if (f16) return halo_kernel_f16(bn, silu, res);
   return silu ? halo_kernel_i8_silu(bn, res) : halo_kernel_i8_linear(bn, res);
 }
 

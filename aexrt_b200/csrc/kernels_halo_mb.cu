@@ -15,7 +15,10 @@ HaloKernel pick(int bn) {
 }  // namespace
 
 HaloKernel halo_kernel_mb(bool f16, int bn, bool silu, bool res) {
-  if (f16) return silu ? pick<true, true, false>(bn) : pick<true, false, false>(bn);
+  if (f16) {
+    if (res) return silu ? pick<true, true, true>(bn) : HaloKernel{nullptr, 0};
+    return silu ? pick<true, true, false>(bn) : pick<true, false, false>(bn);
+  }
   if (silu) return res ? pick<false, true, true>(bn) : pick<false, true, false>(bn);
   return res ? pick<false, false, true>(bn) : pick<false, false, false>(bn);
 }

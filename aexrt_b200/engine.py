@@ -160,7 +160,7 @@ class CompiledYolo:
                 return
             pt = c.inputs[0]
             if (len(c.inputs) == 1 and pt.value != "images" and pt.upsample == 1 and c.s == 1
-                    and plan.info.variant == 2 and c.residual is None and c.ic % 8 == 0 and pt.coff % 8 == 0
+                    and plan.info.variant == 2 and c.ic % 8 == 0 and pt.coff % 8 == 0
                     and self.values[pt.value].shape[-1] % 8 == 0):
                 # the conv's TMA reads the NHWC activation itself: no slab8 copy
                 self.plans[c.name] = plan
@@ -231,7 +231,9 @@ class CompiledYolo:
                 _, c, plan = st
                 out = self.values[c.out[0]]
                 amax_out = self._amax_view(c.out[0]) if c.out[0] in self.needs_amax else None
+                res = self.values[c.residual[0]] if c.residual is not None else None
                 plan.run_nhwc(self.values[c.inputs[0].value], x_coff=c.inputs[0].coff, out=out, out_coff=c.out[1],
+                              residual=res, res_coff=c.residual[1] if c.residual is not None else 0,
                               amax_out=amax_out, amax_goff=c.out[1] // 16, stream=stream)
             elif kind == "stem":
                 _, c, plan = st

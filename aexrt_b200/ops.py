@@ -281,17 +281,19 @@ class ConvPlan:
                                            _ptr(acc_dump), _stream(stream)), "conv_w8a8")
         return out
 
-    def run_nhwc(self, x, x_coff: int = 0, out=None, out_coff: int = 0, amax_out=None, amax_goff: int = 0,
-                 stream=None):
+    def run_nhwc(self, x, x_coff: int = 0, out=None, out_coff: int = 0, residual=None, res_coff: int = 0,
+                 amax_out=None, amax_goff: int = 0, stream=None):
         """fp16 stride-1 halo plans: the conv reads channels x_coff .. x_coff + in_channels of the fp16
         NHWC tensor ``x`` directly (no slab8 copy)."""
         torch = _torch()
         if out is None:
             out = torch.empty(self.out_shape, dtype=torch.float16, device=x.device)
         amax_stride = amax_out.shape[-1] if amax_out is not None else 0
-        check(_native.load().aexrt_b200_conv_f16_nhwc(self._h, x.data_ptr(), x.shape[-1], x_coff, out.data_ptr(),
-                                                      out.shape[-1], out_coff, _ptr(amax_out), amax_stride,
-                                                      amax_goff, _stream(stream)), "conv_f16_nhwc")
+        res_ldc = residual.shape[-1] if residual is not None else 0
+        check(_native.load().aexrt_b200_conv_f16_nhwc(self._h, x.data_ptr(), x.shape[-1], x_coff, _ptr(residual),
+                                                      res_ldc, res_coff, out.data_ptr(), out.shape[-1], out_coff,
+                                                      _ptr(amax_out), amax_stride, amax_goff, _stream(stream)),
+              "conv_f16_nhwc")
         return out
 
     def run_image(self, images, out=None, out_coff: int = 0, amax_out=None, amax_goff: int = 0, stream=None):

@@ -192,9 +192,10 @@ int aexrt_b200_conv_f16(const AexrtB200ConvPlan* plan, const void* x_slab8, cons
  * aexrt_b200_pack_f16 + aexrt_b200_conv_f16, bit for bit.  Replaces the
  * reference's fp16 CONV / CONV_SILU commands of the detect head
  * (record_replay_conv fp16 branch, native/aexrt_d3d12_runtime.cpp:23280). */
-int aexrt_b200_conv_f16_nhwc(const AexrtB200ConvPlan* plan, const void* x, uint32_t ldc, uint32_t coff, void* out,
-                             uint32_t out_ldc, uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride,
-                             uint32_t amax_goff, void* stream);
+int aexrt_b200_conv_f16_nhwc(const AexrtB200ConvPlan* plan, const void* x, uint32_t ldc, uint32_t coff,
+                             const void* residual, uint32_t res_ldc, uint32_t res_coff, void* out, uint32_t out_ldc,
+                             uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride, uint32_t amax_goff,
+                             void* stream);
 
 /* Reads and clears the plan's device status word (synchronises the device).
  * Non-zero bits mean a pipeline wait gave up (see the kernel sources). */

@@ -18,8 +18,10 @@ def test_library_exports_every_header_symbol():
     for name in names:
         assert hasattr(lib, name), name
     out = subprocess.run(["nm", "-D", "--defined-only", _native.LIB_PATH], capture_output=True, text=True).stdout
-    exported = {line.split()[-1] for line in out.splitlines() if line.split()[-1].startswith("aexrt_b200_")}
+    exported = {line.split()[-1] for line in out.splitlines() if line.split()[-1].startswith("aexrt_")}
     assert exported == set(names)
+    # both headers: the kernel-level ABI and the reference runtime ABI
+    assert "aexrt_b200_conv_w8a8" in names and "aexrt_yolo_run" in names and "aexrt_d3d12_create_device" in names
     assert lib.aexrt_b200_abi_version() == 1
 
 
@@ -135,6 +137,6 @@ def test_detection_struct_matches_reference():
 
 def test_conv_f16_nhwc_refuses_null_plan():
     lib = _native.load()
-    assert lib.aexrt_b200_conv_f16_nhwc(None, ctypes.c_void_p(256), 64, 0, ctypes.c_void_p(256), 64, 0, None, 0, 0,
-                                        None) == 0
+    assert lib.aexrt_b200_conv_f16_nhwc(None, ctypes.c_void_p(256), 64, 0, None, 0, 0, ctypes.c_void_p(256), 64, 0,
+                                        None, 0, 0, None) == 0
     assert "null plan" in _native.last_error()
