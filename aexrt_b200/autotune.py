@@ -1,0 +1,314 @@
+"""Per-device conv tuning of an ``.aexrt`` engine with a fail-closed numeric gate.
+
+The reference tunes its engines with ``conv_autotune`` (examples/cpp/conv_autotune.cpp), a C++ tool
+over the runtime ABI: per unique conv shape it tries every candidate algorithm the runtime lists
+(``aexrt_yolo_conv_plan_info``, :198-215), accepts a candidate only if the detections of a run with
+it match the baseline's (same count, |d score| <= 1e-3, |d corner| <= 0.05 px, :108-120), times the
+accepted ones by the per-command GPU profile events (:88-104), keeps a winner only when it is more
+than 5 % faster than the current algorithm (:336-345), applies all winners with incremental
+rejection if the combination fails (:398-445), re-checks the tuned engine against the baseline
+(final gate) and writes a report plus the ``{command: algorithm}`` map that ``aexrtc build
+--algo-map`` compiles into the engine (:493-503).
+
+This module runs the same procedure over the same ABI, served by ``libaexrt_b200.so``:
+
+* the candidates are the W8A8 kernel of the shape (51 / 52 / 53, where the int8 guard passes) and
+  the fp16 tensor-core conv, as the runtime lists them;
+* a second, B200-only stage sweeps the tile choice of every conv that keeps an int8 or fp16 plan
+  (output-channel tile, tile order, stacked M blocks: ``aexrt_b200_yolo_override_conv_variant``).
+  For int8 plans those choices never change a result (integer accumulation); an fp16 plan moved
+  between the halo and slot kernels sums K in another order.  Their gate is therefore stricter than
+  the detections gate: output0 must equal the baseline's bit for bit, which rejects such fp16
+  choices.  Winners go to a sidecar JSON (``--variants``) that
+  :func:`apply` (or ``bench.py --engine ... --variants``) loads next to the algo map.
+
+    python -m aexrt_b200.autotune ENGINE.aexrt [--images N] [--runs R] [--emit-map map.json]
+        [--variants variants.json] [--report report.md] [--shape-limit K]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+import time
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+
+SCORE_TOL = 1e-3  # conv_autotune.cpp:108-120
+BOX_TOL = 0.05
+SIGNIFICANCE = 0.95  # a winner must take < 95 % of the current time (> 5 % faster)
+
+
+def detections_match(a: Tuple[np.ndarray, np.ndarray], b: Tuple[np.ndarray, np.ndarray]) -> bool:
+    """The reference's gate, per image: the same count, and rows in rank order within 1e-3 in score
+    and 0.05 px in every corner."""
+    (ra, ca), (rb, cb) = a, b
+    if not np.array_equal(ca, cb):
+        return False
+    for i in range(len(ca)):
+        x, y = ra[i, :ca[i]], rb[i, :cb[i]]
+        if np.abs(x[:, 4] - y[:, 4]).max(initial=0) > SCORE_TOL or np.abs(x[:, :4] - y[:, :4]).max(initial=0) > BOX_TOL:
+            return False
+    return True
+
+
+def shape_key(p: dict) -> tuple:
+    d = p["desc"]  # AexrtConv2DDesc field order
+    return (p["silu"], d[1], d[2], d[3], d[4], d[5], d[6], d[7], d[9], d[15], d[13])
+
+
+def shape_str(key: tuple) -> str:
+    silu, ic, ih, iw, oc, oh, ow, k, s, g, dil = key
+    return f"{'silu' if silu else 'lin '} {ic}x{ih}x{iw} -> {oc}x{oh}x{ow} k{k}s{s} g{g} d{dil}"
+
+
+@dataclass
+class Row:
+    key: tuple
+    command: int
+    current: int
+    best: int
+    current_ms: float = -1.0
+    best_ms: float = -1.0
+    blocked: List[int] = field(default_factory=list)
+    variant: int = 0
+    variant_ms: float = -1.0
+
+
+class Tuner:
+    def __init__(self, engine: str, images: int = 1, runs: int = 10, warmup: int = 3, seed: int = 0xC2A11,
+                 log=print):
+        from .cpp_runtime import NativeCppYoloModel
+
+        self.engine, self.runs, self.warmup, self.log = engine, runs, warmup, log
+        self.model = NativeCppYoloModel(engine, 0, images=images)
+        self.model.set_profiling(True)
+        rng = np.random.default_rng(seed)
+        n = self.model.input_element_count // self.model.images
+        side = int(round((n // 3) ** 0.5))
+        self.input = rng.uniform(0, 1, (self.model.images, 3, side, side)).astype(np.float32)
+
+    # ------------------------------------------------------------------ runs
+    def run(self):
+        """One run: (detections, counts, output0, host ms)."""
+        t0 = time.perf_counter()
+        rows, counts = self.model.run_batch(self.input)
+        ms = (time.perf_counter() - t0) * 1e3
+        return (rows, counts), self.model.output0(), ms
+
+    def event_ms(self, command: int) -> float:
+        """Median over `runs` runs of the command's own profile event (GPU time)."""
+        prefix = f"cmd#{command} "
+        samples = []
+        for i in range(self.warmup + self.runs):
+            self.run()
+            if i < self.warmup:
+                continue
+            for label, ms in self.model.profile_events():
+                if label.startswith(prefix):
+                    samples.append(ms)
+                    break
+        return statistics.median(samples) if samples else -1.0
+
+    # ------------------------------------------------------------------ stages
+    def tune(self, shape_limit: int = 0, variants: bool = True):
+        m = self.model
+        for _ in range(self.warmup):
+            self.run()
+        self.base_dets, self.base_out, _ = self.run()
+        self.base_ms = statistics.median(self.run()[2] for _ in range(self.runs))
+        self.log(f"baseline e2e median {self.base_ms:.3f} ms, detections {int(self.base_dets[1].sum())}")
+        plans = m.conv_plans()
+        uniq: Dict[tuple, dict] = {}
+        for p in plans:
+            uniq.setdefault(shape_key(p), p)
+        shapes = list(uniq.items())
+        if shape_limit:
+            shapes = shapes[:shape_limit]
+        self.log(f"conv commands {len(plans)}, unique shapes {len(uniq)}, tuning {len(shapes)}")
+        self.rows: List[Row] = []
+        for key, p in shapes:
+            row = Row(key, p["command_index"], p["current_algorithm"], p["current_algorithm"])
+            if p["in_fusion_group"]:
+                self.log(f"  {shape_str(key)}: [in fusion group] keep alg={row.current}")
+                self.rows.append(row)
+                continue
+            row.current_ms = self.event_ms(row.command)
+            results = []
+            for alg in p["candidates"]:
+                if alg == row.current:
+                    continue
+                m.override_conv_algorithm(row.command, alg)
+                try:
+                    dets, _, _ = self.run()
+                    ok = detections_match(dets, self.base_dets)
+                except RuntimeError:
+                    ok = False
+                if ok:
+                    results.append((self.event_ms(row.command), alg))
+                else:
+                    row.blocked.append(alg)
+                m.override_conv_algorithm(row.command, p["planned_algorithm"])
+            best = min(results) if results else None
+            if best and row.current_ms > 0 and best[0] < row.current_ms * SIGNIFICANCE:
+                row.best, row.best_ms = best[1], best[0]
+            else:
+                row.best_ms = row.current_ms
+            self.log(f"  {shape_str(key)}: alg {row.current} -> {row.best} ({row.current_ms:.4f} -> "
+                     f"{row.best_ms:.4f} ms gpu), blocked {row.blocked}")
+            self.rows.append(row)
+        self.winners = self._winners(plans)
+        self._apply_with_rejection()
+        if variants:
+            self._tune_variants()
+        # final gate: the tuned engine against the baseline
+        for _ in range(self.warmup):
+            self.run()
+        self.tuned_dets, self.tuned_out, _ = self.run()
+        self.tuned_ms = statistics.median(self.run()[2] for _ in range(self.runs))
+        self.final_gate = detections_match(self.tuned_dets, self.base_dets)
+        self.log(f"tuned e2e median {self.tuned_ms:.3f} ms (baseline {self.base_ms:.3f}), final gate "
+                 f"{'PASS' if self.final_gate else 'FAIL'}")
+        return self.final_gate
+
+    def _winners(self, plans) -> Dict[int, int]:
+        best = {r.key: r.best for r in self.rows}
+        out = {}
+        for p in plans:
+            b = best.get(shape_key(p))
+            if b is not None and b != p["current_algorithm"] and not p["in_fusion_group"]:
+                out[p["command_index"]] = b
+        return out
+
+    def _apply_with_rejection(self):
+        """Applies every winner; while the combination fails to run or to pass the gate, drops the
+        first remaining winner (conv_autotune.cpp:398-445)."""
+        m = self.model
+        planned = {p["command_index"]: p["planned_algorithm"] for p in m.conv_plans() if not p["in_fusion_group"]}
+        live = dict(self.winners)
+        while True:
+            for cmd, alg in planned.items():
+                m.override_conv_algorithm(cmd, live.get(cmd, alg))
+            try:
+                dets, _, _ = self.run()
+                if detections_match(dets, self.base_dets):
+                    break
+            except RuntimeError as e:
+                self.log(f"  combination failed: {e}")
+            if not live:
+                break
+            cmd = next(iter(live))
+            self.log(f"  rejecting winner cmd#{cmd} alg={live.pop(cmd)}")
+        self.applied = live
+        self.log(f"overrides applied: {len(live)}")
+
+    def _variant_candidates(self, p: dict) -> List[int]:
+        d = p["desc"]
+        oc, k, s = d[4], d[7], d[9]
+        bns = [b for b in (32, 64, 128, 256) if b <= max(32, 2 * oc)]
+        cands = [bn for bn in bns] + [2 << 20, 1 << 20]
+        if k == 3 and s == 1:
+            cands.append(1 << 24)  # no stacked M blocks
+        return cands
+
+    def _tune_variants(self):
+        """Tile choices per conv (results identical by construction: the gate is bit equality)."""
+        m = self.model
+        _, ref_out, _ = self.run()
+        self.variants: Dict[int, int] = {}
+        plans = {p["command_index"]: p for p in m.conv_plans()}
+        seen = {}
+        for row in self.rows:
+            p = plans[row.command]
+            base = self.event_ms(row.command)
+            best = (base, 0)
+            for bits in self._variant_candidates(p):
+                try:
+                    m.override_conv_variant(row.command, bits)
+                    _, out, _ = self.run()
+                except RuntimeError:
+                    continue  # this tile does not fit the conv: the plan is refused
+                if not np.array_equal(out, ref_out):
+                    self.log(f"  cmd#{row.command} variant {bits:#x}: output differs, rejected")
+                    continue
+                t = self.event_ms(row.command)
+                if t > 0 and t < best[0] * SIGNIFICANCE:
+                    best = (t, bits)
+            m.override_conv_variant(row.command, best[1])
+            row.variant, row.variant_ms = best[1], best[0]
+            if best[1]:
+                seen[row.key] = best[1]
+        # every command of a tuned shape takes the shape's winning tile
+        for cmd, p in plans.items():
+            bits = seen.get(shape_key(p))
+            if bits:
+                m.override_conv_variant(cmd, bits)
+                self.variants[cmd] = bits
+        _, out, _ = self.run()
+        if not np.array_equal(out, ref_out):
+            self.log("  variant combination changed output0: dropped")
+            for cmd in self.variants:
+                m.override_conv_variant(cmd, 0)
+            self.variants = {}
+
+    # ------------------------------------------------------------------ outputs
+    def write(self, report: Optional[str] = None, algo_map: Optional[str] = None,
+              variants: Optional[str] = None) -> None:
+        if algo_map:
+            with open(algo_map, "w") as f:
+                json.dump({str(k): int(v) for k, v in sorted(self.winners.items())}, f, indent=4)
+        if variants:
+            with open(variants, "w") as f:
+                json.dump({str(k): int(v) for k, v in sorted(getattr(self, "variants", {}).items())}, f, indent=4)
+        if report:
+            lines = ["# conv autotune report", "", f"- engine: {self.engine}",
+                     f"- images per run: {self.model.images}",
+                     f"- unique shapes tuned: {len(self.rows)}, overrides applied: {len(self.applied)}, "
+                     f"tile variants: {len(getattr(self, 'variants', {}))}",
+                     f"- baseline e2e median: {self.base_ms:.3f} ms; tuned: {self.tuned_ms:.3f} ms",
+                     f"- final numeric gate: {'PASS' if self.final_gate else 'FAIL'}", "",
+                     "| shape | current alg | best alg | current ms | best ms | blocked | tile bits | tile ms |",
+                     "|---|---|---|---|---|---|---|---|"]
+            for r in self.rows:
+                lines.append(f"| {shape_str(r.key)} | {r.current} | {r.best} | {r.current_ms:.4f} | {r.best_ms:.4f} | "
+                             f"{' '.join(map(str, r.blocked))} | {r.variant:#x} | {r.variant_ms:.4f} |")
+            with open(report, "w") as f:
+                f.write("\n".join(lines) + "\n")
+
+    def close(self):
+        self.model.close()
+
+
+def apply(model, algo_map: Optional[str] = None, variants: Optional[str] = None) -> None:
+    """Loads a tuned map (and the tile sidecar) into a NativeCppYoloModel."""
+    if algo_map:
+        for cmd, alg in json.load(open(algo_map)).items():
+            model.override_conv_algorithm(int(cmd), int(alg))
+    if variants:
+        for cmd, bits in json.load(open(variants)).items():
+            model.override_conv_variant(int(cmd), int(bits))
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("engine")
+    ap.add_argument("--images", type=int, default=1)
+    ap.add_argument("--runs", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--shape-limit", type=int, default=0)
+    ap.add_argument("--no-variants", action="store_true")
+    ap.add_argument("--emit-map", default=None, help="JSON {command: algorithm} for aexrtc build --algo-map")
+    ap.add_argument("--variants", default=None, help="JSON {command: tile bits} of this backend")
+    ap.add_argument("--report", default=None)
+    a = ap.parse_args(argv)
+    t = Tuner(a.engine, a.images, a.runs, a.warmup)
+    ok = t.tune(a.shape_limit, variants=not a.no_variants)
+    t.write(a.report, a.emit_map, a.variants)
+    t.close()
+    return 0 if ok else 3
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

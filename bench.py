@@ -71,6 +71,11 @@ def parse_args():
                     help="layer workloads: halo tile order (0 auto, 1 strided, 2 contiguous)")
     ap.add_argument("--amax-out", action="store_true",
                     help="layer workloads: the conv also maxes |y| per 16-channel group for the next layer")
+    ap.add_argument("--engine", default=None,
+                    help="time an .aexrt engine compiled by the reference (e.g. tests/golden/yolov8n_w8a8.aexrt) "
+                         "through the reference runtime ABI (libaexrt_b200.so aexrt_yolo_*), batch --batch (256)")
+    ap.add_argument("--algo-map", default=None, help="--engine: a tuned {command: algorithm} map to apply")
+    ap.add_argument("--variants", default=None, help="--engine: a tuned {command: tile bits} sidecar to apply")
     return ap.parse_args()
 
 
@@ -489,8 +494,77 @@ def run_ours(args):
     return 0
 
 
+def run_engine(args):
+    """An engine compiled by the reference, loaded and run through the C++ runtime (the
+    NativeCppYoloModel interface): device-resident graph replays for `value`, and per step a
+    synchronous aexrt_b200_yolo_run_batch (fp16 host images in the model's pinned staging buffer,
+    detections read back) for `e2e`."""
+    import ctypes
+
+    import torch
+
+    from aexrt_b200 import cpp_runtime
+
+    torch.cuda.set_device(0)
+    B = args.batch or 256
+    m = cpp_runtime.NativeCppYoloModel(args.engine, 0, images=B)
+    if args.algo_map or args.variants:
+        from aexrt_b200 import autotune
+
+        autotune.apply(m, args.algo_map, args.variants)
+    m.set_input_dtype(True)
+    imgsz = 320
+    host = np.random.default_rng(1000).uniform(0, 1, (B, 3, imgsz, imgsz)).astype(np.float16)
+    ptr = m.lib.aexrt_yolo_input_ptr(m.model, None)
+    staging = np.ctypeslib.as_array(ctypes.cast(ptr, ctypes.POINTER(ctypes.c_uint16)), shape=(host.size,))
+    staging[:] = host.reshape(-1).view(np.uint16)
+    m.run_batch(host)  # uploads the images and warms up
+    stream = torch.cuda.Stream()  # a stream of its own (handle 0 would select the model's stream)
+    for _ in range(max(3, args.warmup)):
+        m.enqueue(stream.cuda_stream)
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            m.enqueue(stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t_dev = e0.elapsed_time(e1) / 1e3
+        # end to end: upload from pinned host memory, forward, detections back, per step
+        rows = np.zeros((B, 100, 6), np.float32)
+        counts = np.zeros(B, np.uint32)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            ok = m.lib.aexrt_b200_yolo_run_batch(m.model, ptr, 1,
+                                                 rows.ctypes.data_as(ctypes.POINTER(cpp_runtime.AexrtYoloDetection)),
+                                                 100, counts.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
+            assert ok, m.lib.aexrt_yolo_get_last_error(m.model)
+        t_e2e = time.perf_counter() - t0
+    _, det_bytes = m.device_detections()
+    line = {"metric": METRIC + " (reference-compiled engine)", "value": B * args.steps / t_dev, "unit": "images/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_dev / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (uniform[0,1] fp16 images)",
+            "config": {"workload": f"{os.path.basename(args.engine)} via the aexrt_yolo runtime ABI "
+                                   "(reference-compiled W8A8 engine, its own int8/fp16 kernel plan)",
+                       "algo_map": args.algo_map, "variants": args.variants,
+                       "per_gpu_batch": B, "l2": "inputs larger than L2"},
+            "e2e": {"value": B * args.steps / t_e2e, "unit": "images/s", "h2d_bytes_per_step": int(host.nbytes),
+                    "d2h_bytes_per_step": int(det_bytes), "pipeline": "synchronous per step (one frame in flight)"},
+            "gpu_launches": m.launch_count * args.steps, "arena_bytes": m.arena_bytes,
+            "int8_convs": sum(1 for p in m.conv_plans() if p["current_algorithm"] in (51, 52, 53)),
+            "status": m.status(), "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    m.close()
+    return 0
+
+
 def main():
     args = parse_args()
+    if args.engine:
+        return run_engine(args)
     if args.workload not in MODELS:
         return run_layer(args)
     if args.impl == "reference":

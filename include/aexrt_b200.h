@@ -149,7 +149,10 @@ int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t 
  * the tile (bits 0-15): bits 16-19 kernel variant (0 auto, 1 slot streaming,
  * 2 halo tile), bits 20-23 halo tile order (0 auto, 1 strided over CTAs,
  * 2 one contiguous run per CTA), bits 24-27 the most M blocks stacked in one
- * halo super-tile (0 auto, 1 none); results are identical for every choice.
+ * halo super-tile (0 auto, 1 none).  For int8 plans the results are identical
+ * for every choice (integer accumulation); an fp16 plan whose choice moves it
+ * between the halo and slot kernels sums K in another order, which can change
+ * the last bit of an fp16 output.
  * Allocates device memory (set-up time only).  Returns NULL on error. */
 AexrtB200ConvPlan* aexrt_b200_conv_plan_create(const AexrtConv2DDesc* desc, uint32_t kind, uint32_t kernel_id,
                                                uint32_t flags, const int8_t* codes, const float* w_scale,

@@ -200,7 +200,8 @@ uint32_t aexrt_b200_yolo_launch_count(AexrtYoloModel* model);
 uint64_t aexrt_b200_yolo_arena_bytes(AexrtYoloModel* model);
 /* B200 tile choice of one conv command (the block_n bits of
  * aexrt_b200_conv_plan_create: output-channel tile, variant, tile order,
- * stacked M blocks); results are identical for every choice. */
+ * stacked M blocks): int8 convs give identical results for every choice,
+ * fp16 ones can differ in the last bit (see aexrt_b200_conv_plan_create). */
 int aexrt_b200_yolo_override_conv_variant(AexrtYoloModel* model, uint32_t command_index, uint32_t block_n_bits);
 int aexrt_b200_yolo_set_profiling(AexrtYoloModel* model, uint32_t enabled);
 /* 0: every value keeps its own arena slot (so aexrt_yolo_debug_value can read

@@ -1,0 +1,36 @@
+"""GPU test of the autotuner (aexrt_b200.autotune, the reference's conv_autotune procedure over the
+runtime ABI) on the reference-compiled YOLOv8n-320 engine: it tunes a few conv shapes under the
+fail-closed gate, the final gate passes, the emitted algo map only names candidate algorithms of
+conv commands, and loading the map and the tile sidecar into a fresh model reproduces the tuned
+model's output0 bit for bit."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+ENGINE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "yolov8n_w8a8.aexrt")
+
+
+def test_autotune_gate_map_and_replay(tmp_path):
+    from aexrt_b200 import autotune, cpp_runtime
+
+    logs = []
+    t = autotune.Tuner(ENGINE, images=1, runs=3, warmup=1, log=logs.append)
+    assert t.tune(shape_limit=4)
+    paths = {k: str(tmp_path / f"{k}.json") for k in ("map", "variants")}
+    t.write(str(tmp_path / "report.md"), paths["map"], paths["variants"])
+    tuned_out = t.tuned_out.copy()
+    plans = {p["command_index"]: p for p in t.model.conv_plans()}
+    t.close()
+    amap = json.load(open(paths["map"]))
+    for cmd, alg in amap.items():
+        assert int(cmd) in plans and alg in plans[int(cmd)]["candidates"]
+    assert "final numeric gate: PASS" in open(tmp_path / "report.md").read()
+    m = cpp_runtime.NativeCppYoloModel(ENGINE, 0, images=1)
+    autotune.apply(m, paths["map"], paths["variants"])
+    m.run_batch(t.input)
+    assert np.array_equal(m.output0(), tuned_out)
+    assert m.status() == 0
+    m.close()
