@@ -205,3 +205,20 @@ def test_engine_zero_copy_input_and_fail_closed():
     assert b"input elements" in lib.aexrt_yolo_get_last_error(m.model)
     assert lib.aexrt_yolo_flush_pipeline(m.model, rows, 100, ctypes.byref(count)) == 1 and count.value == 0
     m.close()
+
+
+def test_session_backend_runs_the_engine():
+    """The reference InferenceSession's backend protocol (info / prepare / run) on the engine."""
+    from aexrt_b200.session_backend import B200Backend
+
+    be = B200Backend(0, images=2)
+    be.prepare(ENGINE)
+    imgs = _images(2, 11)
+    out = be.run({"images": imgs})["output0"]
+    m = _model(images=2)
+    rows, counts = m.run_batch(imgs)
+    assert np.array_equal(out, m.output0())
+    assert np.array_equal(be.last_detections[1], counts) and np.array_equal(be.last_detections[0], rows)
+    assert be.info().device == "cuda:0"
+    be.close()
+    m.close()

@@ -175,3 +175,30 @@ def test_reference_binding_loads_this_library():
     assert ctypes.sizeof(ref._YoloRunTiming) == ctypes.sizeof(cpp_runtime.AexrtYoloRunTiming)
     assert ctypes.sizeof(ref._D3D12Capabilities) == ctypes.sizeof(cpp_runtime.AexrtD3D12Capabilities)
     assert ctypes.sizeof(ref._YoloDetection) == ctypes.sizeof(_native.AexrtYoloDetection)
+
+
+@pytest.mark.skipif(not os.path.isdir(REFERENCE_SRC), reason="the reference source tree is not present")
+def test_session_backend_compiles_with_the_reference_compiler():
+    """B200Backend.compile: a reference Graph through the reference's build_aexrt_engine (with a W8A8
+    algo map), validated by this library's loader."""
+    sys.path.insert(0, REFERENCE_SRC)
+    try:
+        import aexrt
+
+        from aexrt_b200.session_backend import B200Backend
+
+        rng = np.random.default_rng(3)
+        g = aexrt.Graph("b200_backend")
+        g.input("images", aexrt.TensorSpec((1, 16, 16, 16), "float32"))
+        g.const("w", rng.normal(0, 0.05, (32, 16, 3, 3)).astype(np.float32))
+        g.const("b", rng.normal(0, 0.1, (32,)).astype(np.float32))
+        g.conv2d("c", "images", "w", "b", strides=(1, 1), pads=(1, 1, 1, 1))
+        g.sigmoid("s", "c")
+        g.mul("y", "c", "s")
+        g.reshape("out", "y", [1, 32, 256])
+        g.output("out")
+        data = B200Backend.compile(g, algo_overrides={0: 52}, precision="fp16")
+        cpp_runtime.validate_engine(data)
+        assert B200Backend().info().name == "b200"
+    finally:
+        sys.path.remove(REFERENCE_SRC)
