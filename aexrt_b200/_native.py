@@ -30,6 +30,7 @@ class AexrtB200ConvPlanInfo(ctypes.Structure):
     _fields_ = [(name, c_uint32) for name in (
         "struct_size", "kernel_id", "flags", "kind", "is_f16", "tile_w", "tile_h", "block_n", "k_slots", "stages",
         "smem_bytes", "grid_m", "grid_n", "in_hp", "in_wp", "grid", "variant", "pitch", "image_input",
+        "quant_on_load",
     )]
 
 
@@ -70,6 +71,9 @@ _SIGNATURES = {
     "aexrt_b200_conv_plan_destroy": (None, [c_void_p]),
     "aexrt_b200_conv_w8a8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_uint32, c_uint32,
                                      c_void_p, c_uint32, c_uint32, c_void_p, c_void_p]),
+    "aexrt_b200_conv_w8a8_sources": (c_int, [c_void_p, POINTER(AexrtB200ActSource), c_uint32, c_void_p, c_uint32,
+                                             c_uint32, c_void_p, c_uint32, c_uint32, c_void_p, c_uint32, c_uint32,
+                                             c_void_p, c_void_p]),
     "aexrt_b200_conv_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_void_p, c_uint32, c_uint32, c_void_p,
                                     c_uint32, c_uint32, c_void_p]),
     "aexrt_b200_conv_f16_image": (c_int, [c_void_p, c_void_p, c_uint32, c_void_p, c_uint32, c_uint32, c_void_p, c_uint32,

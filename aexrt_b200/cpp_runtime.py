@@ -115,6 +115,7 @@ SIGNATURES: Dict[str, tuple] = {
     "aexrt_b200_yolo_override_conv_variant": (c_int, [c_void_p, c_uint32, c_uint32]),
     "aexrt_b200_yolo_set_profiling": (c_int, [c_void_p, c_uint32]),
     "aexrt_b200_yolo_set_arena_reuse": (c_int, [c_void_p, c_uint32]),
+    "aexrt_b200_yolo_set_quant_on_load": (c_int, [c_void_p, c_uint32]),
     "aexrt_b200_yolo_status": (c_int, [c_void_p, POINTER(c_uint32)]),
     "aexrt_b200_arena_plan": (c_int, [c_uint32, POINTER(c_uint64), POINTER(c_uint32), POINTER(c_uint32), c_uint64,
                                       POINTER(c_uint64), POINTER(c_uint64)]),
@@ -303,6 +304,10 @@ class NativeCppYoloModel:
 
     def set_profiling(self, enabled: bool) -> None:
         _native.check(self.lib.aexrt_b200_yolo_set_profiling(self.model, int(bool(enabled))), "set_profiling")
+
+    def set_quant_on_load(self, enabled: bool) -> None:
+        _native.check(self.lib.aexrt_b200_yolo_set_quant_on_load(self.model, int(bool(enabled))),
+                      "set_quant_on_load")
 
     def set_arena_reuse(self, enabled: bool) -> None:
         _native.check(self.lib.aexrt_b200_yolo_set_arena_reuse(self.model, int(bool(enabled))), "set_arena_reuse")

@@ -127,6 +127,10 @@ struct AexrtB200ConvPlan {
   int total_tiles = 0;
   // halo variant (conv_halo.cuh): whole weight tile resident, one halo per slab and tile
   bool halo = false;
+  // quantize on load (AEXRT_B200_PLAN_FLAG_QUANT_ON_LOAD, int8 halo plans): fp16 NHWC sources are
+  // loaded into a raw ring of ql_raw slots of ql_raw_bytes and converted in shared memory
+  bool ql = false;
+  int ql_raw = 0, ql_raw_bytes = 0;
   int order = 0;  // halo tile order (see conv_halo.cuh): 0 auto, 1 strided, 2 contiguous
   // pg16 halo: K steps pair two taps of one slab, ordered by their shared-memory offset
   int tap_pairs = 0, tap_a[5] = {0, 0, 0, 0, 0}, tap_b[5] = {-1, -1, -1, -1, -1};
@@ -218,9 +222,9 @@ bool check_desc_int8(const AexrtConv2DDesc& d, uint32_t kernel_id, bool pg) {
   return true;
 }
 
-cudaError_t set_halo_smem(bool f16, int bn, bool silu, bool pg, bool mb) {
+cudaError_t set_halo_smem(bool f16, int bn, bool silu, bool pg, bool mb, bool ql) {
   for (int res = 0; res < 2; ++res) {
-    const HaloFn fn = halo_kernel_for(f16, bn, silu, res, pg, mb).fn;
+    const HaloFn fn = halo_kernel_for(f16, bn, silu, res, pg, mb, ql).fn;
     if (!fn) continue;  // no residual instance for this combination
     const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxConvSmem);
     if (e != cudaSuccess) return e;
@@ -324,12 +328,23 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
       }
       const int boxes = p->stride == 2 ? 4 : 1;
       const int budget = kMaxConvSmem - 1024;
-      int halo_h = 0, st = 0;
+      const bool want_ql = !f16 && (flags & AEXRT_B200_PLAN_FLAG_QUANT_ON_LOAD);
+      int halo_h = 0, st = 0, raw_slots = 0, raw_bytes = 0;
       for (;; mblocks /= 2) {
         // keep >= 4 stages (and a whole tile per issuer half ring) for a super-tile, else fewer blocks
         halo_h = mblocks * th + (p->k == 1 ? 0 : (p->stride == 1 ? 2 : 1));
         const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, oc_alloc);
-        st = std::min(16, (budget - one.total_bytes) / one.stage_bytes + 1);
+        // quantize on load: a raw ring of 3 (else 2) slots, each the fp16 boxes of one stage (twice
+        // its int8 bytes), while >= 4 stages remain
+        raw_slots = 0;
+        raw_bytes = want_ql ? 2 * one.stage_bytes : 0;
+        for (int rs = want_ql ? 3 : 0; rs >= 2; --rs) {
+          if ((budget - one.total_bytes - rs * raw_bytes) / one.stage_bytes + 1 >= 4) {
+            raw_slots = rs;
+            break;
+          }
+        }
+        st = std::min(16, (budget - one.total_bytes - raw_slots * raw_bytes) / one.stage_bytes + 1);
         if (mblocks == 1 || st >= std::max(4, 2 * pairs)) break;
       }
       if (st >= 2) {
@@ -348,6 +363,9 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
         p->n_tiles = n_tiles;
         p->oc_alloc = oc_alloc;
         p->halo = true;
+        p->ql = raw_slots > 0;
+        p->ql_raw = raw_slots;
+        p->ql_raw_bytes = raw_slots > 0 ? raw_bytes : 0;
         p->order = static_cast<int>(order);
         p->tw = tw;
         p->th = th;
@@ -358,7 +376,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
         p->taps = taps;
         p->w_tile_bytes = w_tile;
         p->stages = st;
-        p->smem = halo_smem_plan(p->halo_rows, boxes, st, w_tile, p->oc_alloc).total_bytes;
+        p->smem = halo_smem_plan(p->halo_rows, boxes, st, w_tile, p->oc_alloc, p->ql_raw * p->ql_raw_bytes).total_bytes;
         p->tiles_w = (static_cast<int>(d.out_w) + tw - 1) / tw;
         p->tiles_h = (static_cast<int>(d.out_h) + mblocks * th - 1) / (mblocks * th);
         p->m_tiles = static_cast<int>(d.batch) * p->tiles_h * p->tiles_w;
@@ -506,10 +524,13 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
     // the attribute is a per-kernel cap shared by every plan of this instance: set it to the
     // largest dynamic shared memory any plan may request, never to this plan's size
     ok = p->smem <= kMaxConvSmem &&
-         cuda_ok(p->halo ? set_halo_smem(f16, p->bn, kind == AEXRT_B200_KIND_CONV_SILU, p->pg, p->mblocks > 1)
+         cuda_ok(p->halo ? set_halo_smem(f16, p->bn, kind == AEXRT_B200_KIND_CONV_SILU, p->pg, p->mblocks > 1, false)
                          : cudaFuncSetAttribute(kernel_for(f16, p->pg, p->bn),
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxConvSmem),
                  "cudaFuncSetAttribute");
+    if (ok && p->ql)
+      ok = cuda_ok(set_halo_smem(false, p->bn, kind == AEXRT_B200_KIND_CONV_SILU, p->pg, p->mblocks > 1, true),
+                   "cudaFuncSetAttribute");
     if (p->smem > kMaxConvSmem) fail("conv plan needs %d bytes of shared memory", p->smem);
   }
   if (!ok) {
@@ -553,14 +574,24 @@ bool encode_act_map(const AexrtB200ConvPlan* p, const void* x, CUtensorMap* map)
   return encode_map(map, dt, 5, x, dims, strides, box);
 }
 
+// The quantize-on-load fields of a launch (aexrt_b200_conv_w8a8_sources): sources and their maps.
+struct QlLaunch {
+  int parts = 0, mode = 0;
+  int slab0[kQlMaxParts] = {}, up[kQlMaxParts] = {}, box_w[kQlMaxParts] = {}, box_h[kQlMaxParts] = {};
+  int groups[kQlMaxParts] = {}, amax_stride[kQlMaxParts] = {}, amax_goff[kQlMaxParts] = {};
+  const uint32_t* amax[kQlMaxParts] = {};
+  CUtensorMap map[kQlMaxParts];
+};
+
 // nhwc_map: an fp16 stride-1 halo plan reading the NHWC activation directly (see aexrt_b200_conv_f16_nhwc)
+// ql: an int8 plan converting fp16 NHWC sources on load (x and scale_rec unused)
 int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_rec, const void* res, uint32_t res_ldc,
                 uint32_t res_coff, void* out, uint32_t out_ldc, uint32_t out_coff, uint32_t* amax_out,
                 uint32_t amax_stride, uint32_t amax_goff, int32_t* acc_dump, void* stream,
-                const CUtensorMap* nhwc_map = nullptr) {
+                const CUtensorMap* nhwc_map = nullptr, const QlLaunch* ql = nullptr) {
   if (!p) return fail("null plan");
-  if (!x || !out) return fail("null input/output pointer");
-  if (!p->f16 && !scale_rec) return fail("null scale record");
+  if ((!x && !ql) || !out) return fail("null input/output pointer");
+  if (!p->f16 && !scale_rec && !ql) return fail("null scale record");
   const uint32_t oc = p->desc.out_channels;
   if (out_ldc < out_coff + oc || reinterpret_cast<uintptr_t>(out) % 2)
     return fail("output slice out of range (need coff + oc <= ldc)");
@@ -572,6 +603,8 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
   CUtensorMap act_map;
   if (nhwc_map)
     act_map = *nhwc_map;
+  else if (ql)
+    std::memset(&act_map, 0, sizeof(act_map));  // unused: the sources' maps travel in the params
   else if (!encode_act_map(p, x, &act_map))
     return 0;
   const int out_vec = (out_ldc % 8 == 0 && out_coff % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) ? 1 : 0;
@@ -635,8 +668,25 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
       h.tap_a[m] = p->tap_a[m];
       h.tap_b[m] = p->tap_b[m];
     }
-    const HaloKernel k = halo_kernel_for(p->f16, p->bn, h.silu != 0, res != nullptr, p->pg, p->mblocks > 1);
-    if (!k.fn) return fail("no conv kernel instance with a residual for a linear fp16 conv");
+    if (ql) {
+      h.ql_parts = ql->parts;
+      h.ql_raw_slots = p->ql_raw;
+      h.ql_raw_bytes = p->ql_raw_bytes;
+      h.ql_mode = ql->mode;
+      for (int k = 0; k < kQlMaxParts; ++k) {
+        h.ql_slab0[k] = ql->slab0[k];
+        h.ql_up[k] = ql->up[k];
+        h.ql_box_w[k] = ql->box_w[k];
+        h.ql_box_h[k] = ql->box_h[k];
+        h.ql_groups[k] = ql->groups[k];
+        h.ql_amax[k] = ql->amax[k];
+        h.ql_amax_stride[k] = ql->amax_stride[k];
+        h.ql_amax_goff[k] = ql->amax_goff[k];
+        if (k < ql->parts) h.ql_map[k] = ql->map[k];
+      }
+    }
+    const HaloKernel k = halo_kernel_for(p->f16, p->bn, h.silu != 0, res != nullptr, p->pg, p->mblocks > 1, ql != nullptr);
+    if (!k.fn) return fail("no conv kernel instance for this combination (linear fp16 residual, or quantize on load)");
     k.fn<<<p->grid, k.threads, p->smem, static_cast<cudaStream_t>(stream)>>>(act_map, h);
     return cuda_ok(cudaGetLastError(), "conv launch") ? 1 : 0;
   }
@@ -1162,6 +1212,7 @@ int aexrt_b200_conv_plan_info(const AexrtB200ConvPlan* p, AexrtB200ConvPlanInfo*
   i.variant = p->halo ? 2u : 1u;
   i.pitch = p->pitch;
   i.image_input = p->image_input ? 1u : 0u;
+  i.quant_on_load = p->ql ? 1u : 0u;
   i.in_hp = p->in_hp;
   i.in_wp = p->in_wp;
   *info = i;
@@ -1185,6 +1236,67 @@ int aexrt_b200_conv_w8a8(const AexrtB200ConvPlan* plan, const void* q_act, const
   if (plan && plan->f16) return fail("plan is fp16; use aexrt_b200_conv_f16");
   return launch_conv(plan, q_act, scale_rec, residual, res_ldc, res_coff, out, out_ldc, out_coff, amax_out,
                      amax_stride, amax_goff, acc_dump, stream);
+}
+
+int aexrt_b200_conv_w8a8_sources(const AexrtB200ConvPlan* plan, const AexrtB200ActSource* srcs, uint32_t nsrc,
+                                 const void* residual, uint32_t res_ldc, uint32_t res_coff, void* out,
+                                 uint32_t out_ldc, uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride,
+                                 uint32_t amax_goff, int32_t* acc_dump, void* stream) {
+  if (!plan) return fail("null plan");
+  if (plan->f16 || !plan->ql)
+    return fail("conv_w8a8_sources: needs an int8 plan created with AEXRT_B200_PLAN_FLAG_QUANT_ON_LOAD "
+                "(info.quant_on_load = 1)");
+  if (!srcs || nsrc == 0 || nsrc > static_cast<uint32_t>(kQlMaxParts))
+    return fail("conv_w8a8_sources: between 1 and %d sources", kQlMaxParts);
+  const AexrtConv2DDesc& d = plan->desc;
+  QlLaunch ql;
+  ql.parts = static_cast<int>(nsrc);
+  ql.mode = plan->pg ? 1 : 0;
+  const int halo_h = plan->halo_rows / plan->pitch;
+  uint32_t ch = 0;
+  for (uint32_t i = 0; i < nsrc; ++i) {
+    const AexrtB200ActSource& a = srcs[i];
+    if (!a.ptr || !a.amax_groups) return fail("source %u: null pointer", i);
+    if (a.layout != AEXRT_B200_LAYOUT_NHWC_F16) return fail("source %u: fp16 NHWC slices only", i);
+    if (a.channels < 16 || (i + 1 < nsrc && a.channels % 16) || a.coff % 16 || a.ldc % 8 ||
+        a.ldc < a.coff + a.channels || reinterpret_cast<uintptr_t>(a.ptr) % 16)
+      return fail("source %u: >= 16 channels (a multiple of 16 but for the last), coff %% 16 == 0, ldc %% 8 == 0, "
+                  "16-byte aligned", i);
+    if ((a.upsample != 1 && a.upsample != 2) || (a.upsample == 2 && plan->stride != 1))
+      return fail("source %u: upsample 1, or 2 for a stride-1 conv", i);
+    if (a.src_h * a.upsample != d.in_h || a.src_w * a.upsample != d.in_w)
+      return fail("source %u: spatial size does not match the conv input", i);
+    if (a.amax_goff * 16 + a.channels > a.amax_stride * 16) return fail("source %u: amax slots out of range", i);
+    ql.slab0[i] = static_cast<int>(ch / 16);
+    ql.up[i] = static_cast<int>(a.upsample);
+    if (plan->stride == 2) {
+      ql.box_w[i] = 2 * plan->pitch;
+      ql.box_h[i] = 2 * halo_h;
+    } else if (a.upsample == 2) {
+      ql.box_w[i] = plan->pitch / 2 + 2;
+      ql.box_h[i] = halo_h / 2 + 2;
+    } else {
+      ql.box_w[i] = plan->pitch;
+      ql.box_h[i] = halo_h;
+    }
+    if (32 * ql.box_w[i] * ql.box_h[i] > plan->ql_raw_bytes / 2)
+      return fail("source %u: staging box larger than the plan's raw slot", i);
+    ql.groups[i] = static_cast<int>((a.channels + 15) / 16);
+    ql.amax[i] = a.amax_groups;
+    ql.amax_stride[i] = static_cast<int>(a.amax_stride);
+    ql.amax_goff[i] = static_cast<int>(a.amax_goff);
+    // the slice viewed from its channel offset: (channel, x, y, image)
+    const uint64_t dims[4] = {a.channels, a.src_w, a.src_h, d.batch};
+    const uint64_t strides[3] = {2ull * a.ldc, 2ull * a.ldc * a.src_w, 2ull * a.ldc * a.src_w * a.src_h};
+    const uint32_t box[4] = {16, static_cast<uint32_t>(ql.box_w[i]), static_cast<uint32_t>(ql.box_h[i]), 1};
+    if (!encode_map(&ql.map[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, static_cast<const __half*>(a.ptr) + a.coff, dims,
+                    strides, box))
+      return 0;
+    ch += a.channels;
+  }
+  if (ch != d.in_channels) return fail("sources hold %u channels, the conv %u", ch, d.in_channels);
+  return launch_conv(plan, nullptr, nullptr, residual, res_ldc, res_coff, out, out_ldc, out_coff, amax_out, amax_stride,
+                     amax_goff, acc_dump, stream, nullptr, &ql);
 }
 
 int aexrt_b200_conv_f16(const AexrtB200ConvPlan* plan, const void* x_slab8, const void* residual, uint32_t res_ldc,

@@ -22,9 +22,21 @@
 // drops from 9x the input (one box per tap) to ~1.3x (one halo per tile), and
 // weight traffic to one copy per CTA.
 #pragma once
+#include "codes.cuh"
 #include "conv_tc.cuh"
 
 namespace aexrt {
+
+// Quantize on load: an int8 plan can read fp16 NHWC sources (the producers' outputs, a
+// concatenation of up to kQlMaxParts slices, each optionally read through a nearest 2x upsample)
+// instead of pre-quantized slab16 codes.  The producer warp loads each slab's fp16 box into a raw
+// ring; kQlWarps converter warps turn it into int8 codes in the A stage (the quantizer's arithmetic:
+// code = low byte of round_half_even(fl32(x * fl32(127 / amax))), 0 when amax <= 0) and hand the
+// stage to the MMA.  The activation scales come from the producers' amax slots, so the separate
+// quantize launch and its int8 write + read disappear.
+constexpr int kQlMaxParts = 4;
+constexpr int kQlMaxRaw = 4;
+constexpr int kQlWarps = 1;  // 20 warps: 5 per SM sub-partition keeps the 96-register budget of the 19-warp form
 
 struct ConvHaloParams {
   int n_img, slabs, slab_pairs;
@@ -62,12 +74,24 @@ struct ConvHaloParams {
   // super-tiles (per tensor): a tile is mblocks M blocks of th rows stacked vertically, sharing one
   // halo box per slab and one pipeline step; nacc TMEM buffers of mblocks*BN columns each
   int mblocks, nacc, tmem_cols;
+  // quantize on load (kQL instances): sources, raw ring, per-source staging boxes and amax slots
+  int ql_parts;
+  int ql_raw_slots, ql_raw_bytes;     // raw ring: slots, bytes of one slot (two slabs)
+  int ql_mode;                        // 0 per tensor, 1 pg16 (every slab its own group's scale)
+  int ql_slab0[kQlMaxParts];          // first slab of each source
+  int ql_up[kQlMaxParts];             // 1 or 2 (nearest 2x upsample)
+  int ql_box_w[kQlMaxParts], ql_box_h[kQlMaxParts];  // staging box of one slab, pixels
+  int ql_groups[kQlMaxParts];         // amax groups of each source (one per slab it fills)
+  const uint32_t* ql_amax[kQlMaxParts];
+  int ql_amax_stride[kQlMaxParts], ql_amax_goff[kQlMaxParts];
+  CUtensorMap ql_map[kQlMaxParts];    // (channel, x, y, image) maps of the fp16 NHWC slices
 };
 
 struct HaloSmemPlan {
   int slab_bytes;   // one slab's halo (all parity boxes), multiple of 128
   int stage_bytes;  // two slabs
   int a_bytes;      // all stages
+  int raw_offset;   // quantize on load: the fp16 raw ring
   int b_offset;
   int sb_offset;
   int am_offset;    // per-tile amax reduction ring (strided order): [8][16] maxima + [8][4] counters
@@ -79,19 +103,21 @@ constexpr int kMaxAcc = 16;                 // TMEM accumulator buffers (narrow 
 constexpr int kAmaxRing = 2 * kMaxAcc;      // >= 2 x accumulator buffers: a slot is reset before any warp reuses it
 
 __host__ __device__ inline HaloSmemPlan halo_smem_plan(int halo_rows, int boxes_per_slab, int stages,
-                                                       int w_tile_bytes, int oc_alloc) {
+                                                       int w_tile_bytes, int oc_alloc, int raw_total = 0) {
   HaloSmemPlan s;
   const int box_bytes = ((halo_rows * kSlotBytes + 127) / 128) * 128;
   s.slab_bytes = box_bytes * boxes_per_slab;
   s.stage_bytes = 2 * s.slab_bytes;
   // 4 KB of slack: a shifted 128-row window may run past the last halo row
   s.a_bytes = stages * s.stage_bytes + 4096;
-  s.b_offset = ((s.a_bytes + 1023) / 1024) * 1024;
+  s.raw_offset = ((s.a_bytes + 127) / 128) * 128;
+  s.b_offset = ((s.raw_offset + raw_total + 1023) / 1024) * 1024;
   s.sb_offset = s.b_offset + ((w_tile_bytes + 127) / 128) * 128;  // w_scale[oc_alloc], bias[oc_alloc]
   s.am_offset = s.sb_offset + ((8 * oc_alloc + 127) / 128) * 128;
   s.bar_offset = s.am_offset + kAmaxRing * (16 + 4) * 4;
-  // barriers: full[stages], empty[stages], acc_full[16], acc_empty[16], w_full[2], sb_full; then the TMEM address
-  s.total_bytes = s.bar_offset + (2 * stages + 2 * kMaxAcc + 3) * 8 + 16;
+  // barriers: full[stages], empty[stages], acc_full[16], acc_empty[16], w_full[2], sb_full, raw_full[4],
+  // raw_empty[4]; then the TMEM address
+  s.total_bytes = s.bar_offset + (2 * stages + 2 * kMaxAcc + 3 + 2 * kQlMaxRaw) * 8 + 16;
   return s;
 }
 
@@ -114,10 +140,58 @@ constexpr int halo_col_blocks() {
 // ring slot still has a single consumer taking its phases in order (mbarrier
 // parity waits are only unambiguous one phase ahead).
 constexpr int kMmaIssuers = 2;
-template <int BN>
+template <int BN, bool kQL = false>
 constexpr int halo_threads() {
-  return 32 * (1 + halo_epi_warps<BN>() + kMmaIssuers);  // producer, epilogue, issuers (warp 1 and the last)
+  // producer, epilogue, issuers (warp 1 and warp 2 + epilogue warps), then the converters
+  return 32 * (1 + halo_epi_warps<BN>() + kMmaIssuers + (kQL ? kQlWarps : 0));
 }
+
+// Sixteen fp16 values (two 16-byte chunks) -> sixteen int8 codes, the quantizer's arithmetic
+// (codes8 in quant.cuh): the 1.5*2^23 rounding when every |x * mult| < 2^22, else float-to-int.
+__device__ __forceinline__ uint4 ql_codes16(const uint4& a, const uint4& b, float mult) {
+  const __half2* ha = reinterpret_cast<const __half2*>(&a);
+  const __half2* hb = reinterpret_cast<const __half2*>(&b);
+  __half2 m = __habs2(ha[0]);
+#pragma unroll
+  for (int e = 1; e < 4; ++e) m = __hmax2(m, __habs2(ha[e]));
+#pragma unroll
+  for (int e = 0; e < 4; ++e) m = __hmax2(m, __habs2(hb[e]));
+  const bool magic = fmaxf(__low2float(m), __high2float(m)) * mult < 4194304.0f;
+  uint4 r;
+  if (magic) {
+    codes8<true>(a, mult, r.x, r.y);
+    codes8<true>(b, mult, r.z, r.w);
+  } else {
+    codes8<false>(a, mult, r.x, r.y);
+    codes8<false>(b, mult, r.z, r.w);
+  }
+  return r;
+}
+
+// Source (part) of slab `slab` of the concatenated input.
+__device__ __forceinline__ int ql_part_of(const ConvHaloParams& p, int slab) {
+  int k = 0;
+#pragma unroll
+  for (int j = 1; j < kQlMaxParts; ++j)
+    if (j < p.ql_parts && slab >= p.ql_slab0[j]) k = j;
+  return k;
+}
+
+// amax of 16-channel group g of source k for image img (float bits in the producers' slots).
+__device__ __forceinline__ float ql_group_amax(const ConvHaloParams& p, int k, int img, int g) {
+  return __uint_as_float(
+      __ldg(p.ql_amax[k] + static_cast<size_t>(img) * p.ql_amax_stride[k] + p.ql_amax_goff[k] + g));
+}
+
+// Per-tensor amax of image img: the max over every group of every source (the quantizer's `at`).
+__device__ __forceinline__ float ql_tensor_amax(const ConvHaloParams& p, int img) {
+  float at = 0.0f;
+  for (int k = 0; k < p.ql_parts; ++k)
+    for (int g = 0; g < p.ql_groups[k]; ++g) at = fmaxf(at, ql_group_amax(p, k, img, g));
+  return at;
+}
+
+__device__ __forceinline__ float ql_mult(float a) { return a > 0.0f ? __fdiv_rn(127.0f, a) : 0.0f; }
 
 // Epilogue of 8 consecutive output channels of one pixel (full-width fast path
 // when all 8 channels exist and the row is 16-byte aligned): scale, bias,
@@ -328,10 +402,11 @@ __device__ __forceinline__ float halo_pg_finish8(const ConvHaloParams& p, const 
   return valid ? fmaxf(__low2float(m), __high2float(m)) : 0.0f;
 }
 
-template <bool kF16, int BN, bool kSilu, bool kRes, bool kPG = false, bool kMB = false>
-__global__ void __launch_bounds__(halo_threads<BN>(), 1)
-    conv_halo_kernel(const __grid_constant__ CUtensorMap act_map, const ConvHaloParams p) {
+template <bool kF16, int BN, bool kSilu, bool kRes, bool kPG = false, bool kMB = false, bool kQL = false>
+__global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
+    conv_halo_kernel(const __grid_constant__ CUtensorMap act_map, const __grid_constant__ ConvHaloParams p) {
   static_assert(!kMB || (!kPG && BN <= 64), "super-tiles: per tensor, BN <= 64");
+  static_assert(!kQL || !kF16, "quantize on load: int8 plans");
   static_assert(!kPG || (!kF16 && (BN == 64 || BN == 128)), "pg16 halo: int8, BN 64 or 128 (no epilogue tile groups)");
   constexpr int kEpiWarps = halo_epi_warps<BN>();
   constexpr int kColBlocks = halo_col_blocks<BN>();
@@ -354,14 +429,17 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const HaloSmemPlan sp = halo_smem_plan(p.halo_rows, p.boxes_per_slab, p.stages, p.w_tile_bytes, p.oc_alloc);
+  const HaloSmemPlan sp = halo_smem_plan(p.halo_rows, p.boxes_per_slab, p.stages, p.w_tile_bytes, p.oc_alloc,
+                                         kQL ? p.ql_raw_slots * p.ql_raw_bytes : 0);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.bar_offset);
   uint64_t* empty = full + p.stages;
   uint64_t* acc_full = full + 2 * p.stages;  // [kAcc]
   uint64_t* acc_empty = acc_full + kMaxAcc;  // [kAcc]
   uint64_t* w_full = acc_empty + kMaxAcc;
   uint64_t* sb_full = w_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sb_full + 1);
+  uint64_t* raw_full = sb_full + 1;         // [kQlMaxRaw]: fp16 boxes of a stage landed
+  uint64_t* raw_empty = raw_full + kQlMaxRaw;  // [kQlMaxRaw]: the converters have read them
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(raw_empty + kQlMaxRaw);
   const int box_bytes = sp.slab_bytes / p.boxes_per_slab;
 
   if (threadIdx.x == 0) {
@@ -376,10 +454,22 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
     mbar_init(&w_full[0], 1);
     mbar_init(&w_full[1], p.issuers);  // every active issuer releases the old weights
     mbar_init(sb_full, 1);
+    if constexpr (kQL) {
+      for (int r = 0; r < p.ql_raw_slots; ++r) {
+        mbar_init(&raw_full[r], 1);
+        mbar_init(&raw_empty[r], 1);
+      }
+    }
     fence_mbar_init();
   }
   for (int i = threadIdx.x; i < kAmaxRing * (16 + 4); i += blockDim.x) reinterpret_cast<uint32_t*>(smem + sp.am_offset)[i] = 0u;
-  if (warp == 0 && lane == 0) tma_prefetch_desc(&act_map);
+  if (warp == 0 && lane == 0) {
+    if constexpr (kQL) {
+      for (int k = 0; k < p.ql_parts; ++k) tma_prefetch_desc(&p.ql_map[k]);
+    } else {
+      tma_prefetch_desc(&act_map);
+    }
+  }
   if (warp == 1) {
     tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
@@ -414,7 +504,9 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
                              : 0;
     const int total_q = my_tiles * p.slab_pairs;
     const int R = p.issuers, H = p.stages / p.issuers;  // rings and slots per ring
-    const int group = min(32, H);
+    // quantize on load: stages go to the raw ring (one slot per stage, in order); the converters
+    // fill the A stages
+    const int group = kQL ? min(32, p.ql_raw_slots) : min(32, H);
     const int per_img = p.tiles_w * p.tiles_h;
     const int nbox = 2 * p.boxes_per_slab;
     const uint32_t stage_tx = static_cast<uint32_t>(nbox * p.halo_rows * kSlotBytes);
@@ -452,7 +544,43 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
         ++wloads;
       }
       bool lane_ok = true;
-      if (mine) {
+      if (kQL && mine) {
+        const int rr = q % p.ql_raw_slots;
+        const uint32_t rph = static_cast<uint32_t>(q / p.ql_raw_slots) & 1u;
+        lane_ok = q < p.ql_raw_slots || mbar_wait_bounded(&raw_empty[rr], rph ^ 1u, p.status, kStatusTimeoutEmpty);
+        if (lane_ok) {
+          const int o = p.ksize == 3 ? 1 : 0;
+          int kp[2] = {-1, -1};
+          uint32_t tx = 0;
+#pragma unroll
+          for (int which = 0; which < 2; ++which) {
+            const int slab = 2 * pr + which;
+            if (slab < p.slabs) {
+              kp[which] = ql_part_of(p, slab);
+              tx += static_cast<uint32_t>(32 * p.ql_box_w[kp[which]] * p.ql_box_h[kp[which]]);
+            }
+          }
+          mbar_arrive_expect_tx(&raw_full[rr], tx);
+#pragma unroll
+          for (int which = 0; which < 2; ++which) {
+            const int k = kp[which];
+            if (k < 0) continue;  // odd slab count: the converters write zero codes
+            int x, y;
+            if (p.stride == 2) {
+              x = 2 * (ow0 - 1);
+              y = 2 * (oh0 - 1);
+            } else if (p.ql_up[k] == 2) {
+              x = (ow0 - o) >> 1;  // floor for negative coordinates too
+              y = (oh0 - o) >> 1;
+            } else {
+              x = ow0 - o;
+              y = oh0 - o;
+            }
+            uint8_t* dst = smem + sp.raw_offset + rr * p.ql_raw_bytes + which * (p.ql_raw_bytes / 2);
+            tma_load_4d(dst, &p.ql_map[k], &raw_full[rr], 16 * (2 * pr + which - p.ql_slab0[k]), x, y, img);
+          }
+        }
+      } else if (!kQL && mine) {
         // tile i's stages go to ring i % R, in that ring's own order
         const int qr = (i / R) * p.slab_pairs + pr;
         const int s = (i % R) * H + qr % H;
@@ -641,6 +769,94 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
         }
       }
     }
+  } else if (kQL && warp >= 3 + kEpiWarps) {
+    // ------------------------------------------------------------ converters (quantize on load)
+    // Every stage, in the producer's order: wait for its fp16 boxes in the raw ring and for its A
+    // slot (the stage ring of the tile's issuer), write the int8 codes of both slabs in the TMA
+    // layout the MMA descriptors expect, then release the raw slot and fill the A slot.
+    constexpr int kCT = 32 * kQlWarps;
+    const int ct = static_cast<int>(threadIdx.x) - 32 * (3 + kEpiWarps);
+    const int my_tiles = static_cast<int>(blockIdx.x) < p.total_tiles
+                             ? (p.total_tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                             : 0;
+    const int total_q = my_tiles * p.slab_pairs;
+    const int R = p.issuers, H = p.stages / p.issuers;
+    const int per_img = p.tiles_w * p.tiles_h;
+    const int o = p.ksize == 3 ? 1 : 0;
+    int cur_img = -1;
+    float mult_t = 0.0f;
+    for (int q = 0; q < total_q; ++q) {
+      const int i = q / p.slab_pairs;
+      const int pr = q - i * p.slab_pairs;
+      const int t = p.contiguous ? run_start + i : static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
+      const int m_tile = t % p.m_tiles;
+      const int img = m_tile / per_img;
+      const int r = m_tile - img * per_img;
+      const int oh0 = (r / p.tiles_w) * p.th * p.mblocks, ow0 = (r % p.tiles_w) * p.tw;
+      const int rr = q % p.ql_raw_slots;
+      const int qr = (i / R) * p.slab_pairs + pr;
+      const int s = (i % R) * H + qr % H;
+      bool ok = mbar_wait_bounded(&raw_full[rr], static_cast<uint32_t>(q / p.ql_raw_slots) & 1u, p.status,
+                                  kStatusTimeoutFull);
+      ok = ok && (qr < H || mbar_wait_bounded(&empty[s], (static_cast<uint32_t>(qr / H) & 1u) ^ 1u, p.status,
+                                              kStatusTimeoutEmpty));
+      // the converter threads leave together if any of them gave up (they share a named barrier)
+      uint32_t all_ok;
+      asm volatile(
+          "{\n\t.reg .pred pa, pb;\n\tsetp.ne.u32 pa, %1, 0;\n\tbar.red.and.pred pb, 1, %2, pa;\n\t"
+          "selp.u32 %0, 1, 0, pb;\n\t}"
+          : "=r"(all_ok)
+          : "r"(ok ? 1u : 0u), "r"(kCT)
+          : "memory");
+      if (!all_ok) break;
+      if (p.ql_mode == 0 && img != cur_img) {
+        mult_t = ql_mult(ql_tensor_amax(p, img));
+        cur_img = img;
+      }
+      const uint8_t* raw = smem + sp.raw_offset + rr * p.ql_raw_bytes;
+      uint8_t* stage = smem + s * sp.stage_bytes;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        const int slab = 2 * pr + which;
+        const int k = slab < p.slabs ? ql_part_of(p, slab) : 0;
+        const float mult = slab >= p.slabs ? 0.0f
+                           : (p.ql_mode == 0 ? mult_t
+                                             : ql_mult(ql_group_amax(p, k, img, slab - p.ql_slab0[k])));
+        const uint8_t* src = raw + which * (p.ql_raw_bytes / 2);
+        uint8_t* dst = stage + which * sp.slab_bytes;
+        const int bw = p.ql_box_w[k], up = p.ql_up[k];
+        const int units = p.halo_rows * p.boxes_per_slab;
+        for (int u = ct; u < units; u += kCT) {
+          const int box = u / p.halo_rows;
+          const int rem = u - box * p.halo_rows;
+          const int row = rem / p.pitch, col = rem - row * p.pitch;
+          uint4 code = make_uint4(0u, 0u, 0u, 0u);
+          if (mult != 0.0f) {
+            int sy, sx;
+            if (p.stride == 2) {  // parity box (row parity box >> 1, column parity box & 1)
+              sy = 2 * row + (box >> 1);
+              sx = 2 * col + (box & 1);
+            } else if (up == 2) {
+              sy = ((oh0 - o + row) >> 1) - ((oh0 - o) >> 1);
+              sx = ((ow0 - o + col) >> 1) - ((ow0 - o) >> 1);
+            } else {
+              sy = row;
+              sx = col;
+            }
+            const uint4* v = reinterpret_cast<const uint4*>(src + (sy * bw + sx) * 32);
+            code = ql_codes16(v[0], v[1], mult);
+          }
+          *reinterpret_cast<uint4*>(dst + box * (sp.slab_bytes / p.boxes_per_slab) + rem * kSlotBytes) = code;
+        }
+      }
+      // the codes are generic-proxy writes read by the tensor core (async proxy)
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"r"(kCT) : "memory");
+      if (ct == 0) {
+        mbar_arrive(&full[s]);
+        mbar_arrive(&raw_empty[rr]);
+      }
+    }
   } else {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;                   // TMEM lane quadrant this warp may access
@@ -672,6 +888,8 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
     };
     uint32_t* am_ring = reinterpret_cast<uint32_t*>(smem + sp.am_offset);  // [kAmaxRing][16] maxima
     uint32_t* am_count = am_ring + kAmaxRing * 16;                          // [kAmaxRing][4] arrivals
+    int ep_img = -1;  // quantize on load: the image whose per-tensor amax ep_at holds
+    float ep_at = 0.0f;
     for (int k = blockIdx.x, i = 0; k < p.total_tiles; k += gridDim.x, ++i) {
       if (kTileGroups > 1 && i % kTileGroups != tgroup) continue;
       const int u = i;  // the tile's place in this CTA's sequence: accumulator buffer and phase
@@ -695,7 +913,7 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
       if constexpr (kPG) {
         // pg16: drain the tile's slab units in ascending group order into fp32 sums,
         // fp = sum_g fl32(fl32(S_g) * fl32(amax_g / 127)), then the final epilogue
-        const float* rec = p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs);
+        const float* rec = kQL ? nullptr : p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs);
         const int Hh = kAcc / p.issuers;
         const int r_iss = i % p.issuers;
         const int ubase = (i / p.issuers) * p.slabs;
@@ -704,7 +922,14 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
         for (int g = 0; g < p.slabs; ++g) {
           const int uu = ubase + g;
           const int gbuf = r_iss * Hh + uu % Hh;
-          const float gs = __fdiv_rn(__ldg(rec + 1 + g), 127.0f);
+          float ag;
+          if constexpr (kQL) {
+            const int kq = ql_part_of(p, g);
+            ag = ql_group_amax(p, kq, img, g - p.ql_slab0[kq]);
+          } else {
+            ag = __ldg(rec + 1 + g);
+          }
+          const float gs = __fdiv_rn(ag, 127.0f);
           const uint64_t gs2 = f2_pack(gs, gs);
           if (!mbar_wait_bounded(&acc_full[gbuf], (uu / Hh) & 1, p.status, kStatusTimeoutAccFull)) {
             pg_ok = false;
@@ -760,7 +985,16 @@ __global__ void __launch_bounds__(halo_threads<BN>(), 1)
       } else {
       const int buf = u % nacc;
       // the scale record is ready before the launch: read it while the accumulator fills
-      const float amax_in = kF16 ? 0.0f : __ldg(p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs));
+      float amax_in = 0.0f;
+      if constexpr (kQL) {
+        if (img != ep_img) {
+          ep_at = ql_tensor_amax(p, img);
+          ep_img = img;
+        }
+        amax_in = ep_at;
+      } else if constexpr (!kF16) {
+        amax_in = __ldg(p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs));
+      }
       if (!mbar_wait_bounded(&acc_full[buf], (u / nacc) & 1, p.status, kStatusTimeoutAccFull)) break;
       tc_fence_after();
       const float in_scale = kF16 ? 1.0f : __fdiv_rn(amax_in, 127.0f);

@@ -28,10 +28,19 @@ HaloKernel halo_kernel_i8_linear(int bn, bool res);
 HaloKernel halo_kernel_f16(int bn, bool silu, bool res);
 HaloKernel halo_kernel_mb(bool f16, int bn, bool silu, bool res);
 HaloKernel halo_kernel_pg(int bn, bool silu, bool res);
+// quantize on load (int8 plans reading fp16 NHWC sources): per tensor, super-tiles, pg16
+HaloKernel halo_kernel_ql(int bn, bool silu, bool res);
+HaloKernel halo_kernel_ql_mb(int bn, bool silu, bool res);
+HaloKernel halo_kernel_ql_pg(int bn, bool silu, bool res);
 
 // Residuals (the C2f tail) are instantiated for every int8 conv and for fp16 SiLU convs; a
 // combination without an instance returns {nullptr, 0}.
-inline HaloKernel halo_kernel_for(bool f16, int bn, bool silu, bool res, bool pg = false, bool mb = false) {
+inline HaloKernel halo_kernel_for(bool f16, int bn, bool silu, bool res, bool pg = false, bool mb = false,
+                                  bool ql = false) {
+  if (ql) {
+    if (f16) return HaloKernel{nullptr, 0};
+    return mb ? halo_kernel_ql_mb(bn, silu, res) : (pg ? halo_kernel_ql_pg(bn, silu, res) : halo_kernel_ql(bn, silu, res));
+  }
   if (mb) return halo_kernel_mb(f16, bn, silu, res);
   if (pg) return f16 ? HaloKernel{nullptr, 0} : halo_kernel_pg(bn, silu, res);
   if (f16) return halo_kernel_f16(bn, silu, res);

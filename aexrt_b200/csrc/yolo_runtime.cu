@@ -99,7 +99,7 @@ struct Buffer {
 };
 
 enum OpKind { kOpConv, kOpSppf, kOpMaxPool, kOpAdd, kOpDecode, kOpNms };
-enum ConvPath { kPathInt8, kPathF16Pack, kPathF16Nhwc, kPathStem };
+enum ConvPath { kPathInt8, kPathInt8Ql, kPathF16Pack, kPathF16Nhwc, kPathStem };
 
 struct Op {
   OpKind kind = kOpConv;
@@ -144,6 +144,7 @@ struct AexrtYoloModel {
   uint32_t graph_batch = 1;  // the engine's batch
   uint32_t input_dtype = 0;  // 0 fp32, 1 fp16
   bool profiling = false, reuse = true, dirty = true, head_fusion = false;
+  bool quant_on_load = true;  // int8 convs quantize their fp16 inputs on load (else a quantize launch each)
   std::map<uint32_t, uint32_t> overrides, variants;
   // lowered state
   std::vector<Buffer> bufs;
@@ -453,12 +454,22 @@ struct Lowering {
                                                   codes.data(), scale.data()))
           return fail("conv %u: weight quantization failed", ci) != 0;
       }
-      op.plan = aexrt_b200_conv_plan_create(&d, kind, iid, pg ? AEXRT_B200_PLAN_FLAG_INT8_PERGROUP : 0u, codes.data(),
-                                            scale.data(), bias.data(), vbits);
+      // quantize on load when every part fits its rules: the conv reads the producers' fp16 slices
+      bool ql = m->quant_on_load && op.in.size() <= 4;
+      for (size_t k = 0; k < op.in.size(); ++k)
+        ql = ql && op.in[k].ch >= 16 && (op.in[k].up == 1 || op.s == 1);
+      uint32_t pflags = (pg ? AEXRT_B200_PLAN_FLAG_INT8_PERGROUP : 0u) | (ql ? AEXRT_B200_PLAN_FLAG_QUANT_ON_LOAD : 0u);
+      op.plan = aexrt_b200_conv_plan_create(&d, kind, iid, pflags, codes.data(), scale.data(), bias.data(), vbits);
       if (!op.plan) return fail("conv %u: %s", ci, aexrt_b200_get_last_error()) != 0;
-      op.path = kPathInt8;
-      op.q = new_scratch(aexrt_b200_packed_act_bytes(d.batch, d.in_channels, d.in_h, d.in_w, d.stride_h));
-      op.rec = new_scratch(uint64_t(d.batch) * (1 + (d.in_channels + 15) / 16) * 4);
+      AexrtB200ConvPlanInfo pi{};
+      aexrt_b200_conv_plan_info(op.plan, &pi);
+      if (ql && pi.quant_on_load) {
+        op.path = kPathInt8Ql;
+      } else {
+        op.path = kPathInt8;
+        op.q = new_scratch(aexrt_b200_packed_act_bytes(d.batch, d.in_channels, d.in_h, d.in_w, d.stride_h));
+        op.rec = new_scratch(uint64_t(d.batch) * (1 + (d.in_channels + 15) / 16) * 4);
+      }
     } else {
       if (!f16_ok(d)) return fail("conv %u: shape outside the fp16 conv (k 1 or 3, pad k/2, stride 1/2)", ci) != 0;
       op.plan = aexrt_b200_conv_plan_create_f16(&d, kind, weight.data(), bias.data(), vbits);
@@ -705,7 +716,8 @@ struct Lowering {
             if (oi < 0 || consumers[cv] != 1) continue;
             Op& op = m->ops[oi];
             // int8 convs take a residual; fp16 ones with SiLU too (the C2f bottleneck)
-            const bool res_ok = op.path == kPathInt8 || ((op.path == kPathF16Pack || op.path == kPathF16Nhwc) &&
+            const bool res_ok = op.path == kPathInt8 || op.path == kPathInt8Ql ||
+                                ((op.path == kPathF16Pack || op.path == kPathF16Nhwc) &&
                                                          e.commands[op.cmd].kind == kConvSilu);
             if (op.kind != kOpConv || !res_ok || op.has_res || other.size() != 1 || other[0].up != 1 ||
                 other[0].buf == kInput || other[0].ch != op.oc)
@@ -773,7 +785,7 @@ struct Lowering {
 
     // ---- amax slots: every buffer an int8 conv reads gets them, and its producer fills them
     for (const Op& op : m->ops)
-      if (op.kind == kOpConv && op.path == kPathInt8)
+      if (op.kind == kOpConv && (op.path == kPathInt8 || op.path == kPathInt8Ql))
         for (const Part& p : op.in) {
           if (p.buf == kInput) return fail("an int8 conv reads the graph input directly") != 0;
           m->bufs[p.buf].amax = true;
@@ -924,6 +936,13 @@ bool launch_forward(AexrtYoloModel* m, cudaStream_t st, std::vector<std::pair<cu
             ok = aexrt_b200_conv_w8a8(op.plan, q, rec, res, res_ldc, op.has_res ? op.res.coff : 0, out, ldc, 0, am,
                                       astride, 0, nullptr, sv);
           }
+        } else if (op.path == kPathInt8Ql) {
+          AexrtB200ActSource src[aexrt::kMaxGraphParts];
+          for (size_t i = 0; i < op.in.size(); ++i) fill_source(m, op.in[i], true, &src[i]);
+          const void* res = op.has_res ? static_cast<const void*>(buf_ptr(m, op.res.buf)) : nullptr;
+          const uint32_t res_ldc = op.has_res ? static_cast<uint32_t>(m->bufs[op.res.buf].c) : 0u;
+          ok = aexrt_b200_conv_w8a8_sources(op.plan, src, static_cast<uint32_t>(op.in.size()), res, res_ldc,
+                                            op.has_res ? op.res.coff : 0, out, ldc, 0, am, astride, 0, nullptr, sv);
         } else if (op.path == kPathStem) {
           ok = aexrt_b200_conv_f16_image(op.plan, m->d_input,
                                          m->input_dtype == 1 ? AEXRT_B200_LAYOUT_NCHW_F16 : AEXRT_B200_LAYOUT_NCHW_F32,
@@ -1470,6 +1489,15 @@ double aexrt_yolo_profile_event_ms(AexrtYoloModel* m, uint32_t i) {
 int aexrt_b200_yolo_set_profiling(AexrtYoloModel* m, uint32_t enabled) {
   if (!m) return set_error(nullptr, "null model");
   m->profiling = enabled != 0;
+  return 1;
+}
+
+int aexrt_b200_yolo_set_quant_on_load(AexrtYoloModel* m, uint32_t enabled) {
+  if (!m) return set_error(nullptr, "null model");
+  if (m->quant_on_load != (enabled != 0)) {
+    m->quant_on_load = enabled != 0;
+    m->dirty = true;
+  }
   return 1;
 }
 

@@ -56,7 +56,7 @@ class CompiledYolo:
     """One program compiled for one batch size on the current CUDA device."""
 
     def __init__(self, program: YoloProgram, batch: int, device=None, block_n: Optional[Dict[str, int]] = None,
-                 image_dtype=None, nms: Optional[NmsConfig] = None):
+                 image_dtype=None, nms: Optional[NmsConfig] = None, quant_on_load: bool = True):
         torch = _torch()
         self.program = program
         self.batch = batch
@@ -88,6 +88,7 @@ class CompiledYolo:
         self.images = torch.zeros((n, p.in_channels, p.imgsz, p.imgsz), dtype=self.image_dtype, device=self.device)
         self.output = torch.zeros((n, 4 + p.nc, p.anchors), dtype=torch.float32, device=self.device)
         self.nms = nms
+        self.quant_on_load = quant_on_load
         self.det_buf = self._new_det_buf()
         # ---- plans and per-command scratch
         self.steps: List[tuple] = []
@@ -144,8 +145,18 @@ class CompiledYolo:
         h, w = sh * c.inputs[0].upsample, sw * c.inputs[0].upsample
         if c.precision == "int8":
             codes, scale = ops.quantize_conv_weight_int8(c.weight)
+            # quantize on load: the conv reads the producers' fp16 slices and quantizes them itself,
+            # when the plan supports it and every part fits its rules (see conv_w8a8_sources)
+            ql = self.quant_on_load and all(
+                pt.value != "images" and pt.coff % 16 == 0 and pt.channels >= 16
+                and (pt.channels % 16 == 0 or i == len(c.inputs) - 1) and (pt.upsample == 1 or c.s == 1)
+                for i, pt in enumerate(c.inputs)) and len(c.inputs) <= 4
             plan = ops.ConvPlan.int8(n, c.ic, h, w, c.oc, c.k, c.s, codes, scale, c.bias, silu=c.silu, pg16=c.pg16,
-                                     block_n=block_n)
+                                     block_n=block_n, quant_on_load=ql)
+            if ql and plan.info.quant_on_load:
+                self.plans[c.name] = plan
+                self.steps.append(("conv_ql", c, plan, self._sources(c.inputs, True), (h, w)))
+                return
             shape = ops.packed_act_shape(n, c.ic, h, w, c.s)
             q = torch.empty(shape, dtype=torch.int8, device=self.device)
             rec = torch.empty((n, 1 + shape[1]), dtype=torch.float32, device=self.device)
@@ -171,8 +182,13 @@ class CompiledYolo:
             x8 = torch.empty((n, (c.ic + 7) // 8, hp, wp, 8), dtype=torch.float16, device=self.device)
             scratch = (x8,)
         self.plans[c.name] = plan
-        srcs = (AexrtB200ActSource * len(c.inputs))()
-        for i, pt in enumerate(c.inputs):
+        self.steps.append(("conv", c, plan, self._sources(c.inputs, c.precision == "int8"), scratch, (h, w)))
+
+    def _sources(self, inputs, int8: bool):
+        """AexrtB200ActSource array of a conv's input parts (with their amax slots for int8)."""
+        torch = _torch()
+        srcs = (AexrtB200ActSource * len(inputs))()
+        for i, pt in enumerate(inputs):
             ph, pw = self._spatial(pt)
             s = srcs[i]
             if pt.value == "images":
@@ -186,14 +202,14 @@ class CompiledYolo:
                 s.layout = ops.LAYOUT_NHWC_F16
                 s.ldc = buf.shape[-1]
                 s.coff = pt.coff
-                if c.precision == "int8":
+                if int8:
                     s.amax_groups = self._amax_view(pt.value).data_ptr()
                     s.amax_stride = self.amax_groups[pt.value]
                     s.amax_goff = pt.coff // 16
             s.channels = pt.channels
             s.upsample = pt.upsample
             s.src_h, s.src_w = ph, pw
-        self.steps.append(("conv", c, plan, srcs, scratch, (h, w)))
+        return srcs
 
     def _count_launches(self) -> int:
         k = 1  # amax arena clear
@@ -227,6 +243,14 @@ class CompiledYolo:
                           f"pack {c.name}")
                     plan.run(x8, out=out, out_coff=c.out[1], residual=res, res_coff=res_coff, amax_out=amax_out,
                              amax_goff=c.out[1] // 16, stream=stream)
+            elif kind == "conv_ql":
+                _, c, plan, srcs, _ = st
+                out = self.values[c.out[0]]
+                amax_out = self._amax_view(c.out[0]) if c.out[0] in self.needs_amax else None
+                res = self.values[c.residual[0]] if c.residual is not None else None
+                plan.run_sources(srcs, out=out, out_coff=c.out[1], residual=res,
+                                 res_coff=c.residual[1] if c.residual is not None else 0, amax_out=amax_out,
+                                 amax_goff=c.out[1] // 16, stream=stream)
             elif kind == "conv_nhwc":
                 _, c, plan = st
                 out = self.values[c.out[0]]

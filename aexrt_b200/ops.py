@@ -27,6 +27,7 @@ from ._native import AexrtB200ConvPlanInfo, AexrtConv2DDesc, check
 KIND_CONV = 1
 KIND_CONV_SILU = 2
 PLAN_FLAG_INT8_PERGROUP = 1 << 4
+PLAN_FLAG_QUANT_ON_LOAD = 1 << 8
 LAYOUT_NHWC_F16 = 0
 LAYOUT_NCHW_F16 = 1
 LAYOUT_NCHW_F32 = 2
@@ -202,12 +203,13 @@ class PlanInfo:
     variant: int = 0
     pitch: int = 0
     image_input: int = 0
+    quant_on_load: int = 0
 
     @staticmethod
     def from_c(i: AexrtB200ConvPlanInfo) -> "PlanInfo":
         return PlanInfo(i.kernel_id, i.flags, i.kind, bool(i.is_f16), i.tile_w, i.tile_h, i.block_n, i.k_slots,
                         i.stages, i.smem_bytes, i.grid_m, i.grid_n, i.in_hp, i.in_wp, i.grid, i.variant, i.pitch,
-                        i.image_input)
+                        i.image_input, i.quant_on_load)
 
 
 class ConvPlan:
@@ -225,13 +227,14 @@ class ConvPlan:
         self.info = self._info()
 
     @classmethod
-    def int8(cls, n, ic, h, w, oc, k, s, codes, w_scale, bias, silu=True, pg16=False, block_n=0):
+    def int8(cls, n, ic, h, w, oc, k, s, codes, w_scale, bias, silu=True, pg16=False, block_n=0,
+             quant_on_load=False):
         p = k // 2
         desc = conv_desc(n, ic, h, w, oc, k, s, p)
         codes = np.ascontiguousarray(codes, dtype=np.int8)
         w_scale = np.ascontiguousarray(w_scale, dtype=np.float32)
         bias = np.ascontiguousarray(bias, dtype=np.float32)
-        flags = PLAN_FLAG_INT8_PERGROUP if pg16 else 0
+        flags = (PLAN_FLAG_INT8_PERGROUP if pg16 else 0) | (PLAN_FLAG_QUANT_ON_LOAD if quant_on_load else 0)
         h_ = _native.load().aexrt_b200_conv_plan_create(
             ctypes.byref(desc), KIND_CONV_SILU if silu else KIND_CONV, kernel_id_for(k, s), flags, codes.ctypes.data,
             w_scale.ctypes.data, bias.ctypes.data, block_n)
@@ -279,6 +282,21 @@ class ConvPlan:
             check(lib.aexrt_b200_conv_w8a8(self._h, x.data_ptr(), rec.data_ptr(), _ptr(residual), res_ldc, res_coff,
                                            out.data_ptr(), out_ldc, out_coff, _ptr(amax_out), amax_stride, amax_goff,
                                            _ptr(acc_dump), _stream(stream)), "conv_w8a8")
+        return out
+
+    def run_sources(self, srcs, out=None, out_coff: int = 0, residual=None, res_coff: int = 0, amax_out=None,
+                    amax_goff: int = 0, acc_dump=None, stream=None, device=None):
+        """Quantize-on-load plans: the conv reads the fp16 NHWC sources (a ctypes array of
+        AexrtB200ActSource with their amax slots) and quantizes them in shared memory."""
+        torch = _torch()
+        if out is None:
+            out = torch.empty(self.out_shape, dtype=torch.float16, device=device or "cuda")
+        res_ldc = residual.shape[-1] if residual is not None else 0
+        amax_stride = amax_out.shape[-1] if amax_out is not None else 0
+        check(_native.load().aexrt_b200_conv_w8a8_sources(self._h, srcs, len(srcs), _ptr(residual), res_ldc, res_coff,
+                                                          out.data_ptr(), out.shape[-1], out_coff, _ptr(amax_out),
+                                                          amax_stride, amax_goff, _ptr(acc_dump), _stream(stream)),
+              "conv_w8a8_sources")
         return out
 
     def run_nhwc(self, x, x_coff: int = 0, out=None, out_coff: int = 0, residual=None, res_coff: int = 0,

@@ -298,26 +298,35 @@ def conv_roofline(eng, torch, stream):
     recs = []
     check(lib.aexrt_b200_zero(eng.amax_arena.data_ptr(), eng.amax_arena.numel() * 4, stream), "zero")
     for st in eng.steps:
-        if st[0] != "conv":
+        if st[0] not in ("conv", "conv_ql") or st[1].precision != "int8":
             continue
-        _, c, plan, srcs, scratch, (h, w) = st
-        if c.precision != "int8":
-            continue
-        q, rec = scratch
-        check(lib.aexrt_b200_act_quantize_concat(srcs, len(srcs), n, h, w, int(c.pg16), c.s, q.data_ptr(),
-                                                 rec.data_ptr(), stream), "quantize")
+        c = st[1]
         out = eng.values[c.out[0]]
         res = eng.values[c.residual[0]] if c.residual else None
+        amax_out = eng._amax_view(c.out[0]) if c.out[0] in eng.needs_amax else None
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(torch.cuda.current_stream())
-        amax_out = eng._amax_view(c.out[0]) if c.out[0] in eng.needs_amax else None
-        plan.run(q, rec, out=out, out_coff=c.out[1], residual=res, res_coff=c.residual[1] if c.residual else 0,
-                 amax_out=amax_out, amax_goff=c.out[1] // 16, stream=stream)
+        if st[0] == "conv_ql":
+            # quantize on load: the conv reads the fp16 sources (2 bytes per input element)
+            _, _, plan, srcs, (h, w) = st
+            in_bytes = 2
+            e0.record(torch.cuda.current_stream())
+            plan.run_sources(srcs, out=out, out_coff=c.out[1], residual=res,
+                             res_coff=c.residual[1] if c.residual else 0, amax_out=amax_out,
+                             amax_goff=c.out[1] // 16, stream=stream)
+        else:
+            _, _, plan, srcs, scratch, (h, w) = st
+            in_bytes = 1
+            q, rec = scratch
+            check(lib.aexrt_b200_act_quantize_concat(srcs, len(srcs), n, h, w, int(c.pg16), c.s, q.data_ptr(),
+                                                     rec.data_ptr(), stream), "quantize")
+            e0.record(torch.cuda.current_stream())
+            plan.run(q, rec, out=out, out_coff=c.out[1], residual=res, res_coff=c.residual[1] if c.residual else 0,
+                     amax_out=amax_out, amax_goff=c.out[1] // 16, stream=stream)
         e1.record(torch.cuda.current_stream())
         d = eng.program.values[c.out[0]]
         ops = 2.0 * n * d.h * d.w * c.oc * c.ic * c.k * c.k
-        byts = n * (c.ic * h * w + 2 * c.oc * d.h * d.w) + c.oc * c.ic * c.k * c.k
+        byts = n * (in_bytes * c.ic * h * w + 2 * c.oc * d.h * d.w) + c.oc * c.ic * c.k * c.k
         recs.append((e0, e1, ops, byts))
     torch.cuda.synchronize()
     t = sum(e0.elapsed_time(e1) for e0, e1, _, _ in recs) / 1e3

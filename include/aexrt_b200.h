@@ -62,6 +62,9 @@ typedef struct AexrtConv2DDesc {
 #define AEXRT_B200_KIND_CONV 1u
 #define AEXRT_B200_KIND_CONV_SILU 2u
 #define AEXRT_B200_PLAN_FLAG_INT8_PERGROUP (1u << 4)
+/* This backend's own plan flag (above the reference's bits 0-4): an int8 plan that
+ * reads fp16 NHWC sources and quantizes them on load (aexrt_b200_conv_w8a8_sources). */
+#define AEXRT_B200_PLAN_FLAG_QUANT_ON_LOAD (1u << 8)
 
 /* Activation layouts accepted by the amax / quantize entry points. */
 #define AEXRT_B200_LAYOUT_NHWC_F16 0u
@@ -93,6 +96,7 @@ typedef struct AexrtB200ConvPlanInfo {
     uint32_t variant;          /* 1 slot streaming, 2 halo tile */
     uint32_t pitch;            /* halo variant: M rows per tile row */
     uint32_t image_input;      /* 1: aexrt_b200_conv_f16_image accepts this plan */
+    uint32_t quant_on_load;    /* 1: aexrt_b200_conv_w8a8_sources accepts this plan */
 } AexrtB200ConvPlanInfo;
 
 /* ---------------------------------------------------------------- library */
@@ -251,6 +255,25 @@ int aexrt_b200_act_quantize_concat(const AexrtB200ActSource* srcs, uint32_t nsrc
 /* fp16 slab8 repack of a concatenation of parts (fp16 convs). */
 int aexrt_b200_pack_f16_concat(const AexrtB200ActSource* srcs, uint32_t nsrc, uint32_t n, uint32_t h, uint32_t w,
                                uint32_t consumer_stride, void* out, void* stream);
+
+/* The same W8A8 conv reading its input straight from fp16 NHWC sources (the
+ * producers' outputs: a concatenation of up to 4 slices, each optionally read
+ * through a nearest 2x upsample for stride-1 convs), for plans created with
+ * AEXRT_B200_PLAN_FLAG_QUANT_ON_LOAD whose info.quant_on_load is 1.  The conv
+ * quantizes each 16-channel slab in shared memory with the scales of the
+ * sources' amax slots (AexrtB200ActSource.amax_groups; per tensor or pg16 per the
+ * plan), with the arithmetic of aexrt_b200_act_quantize_concat, so codes,
+ * accumulators and outputs equal aexrt_b200_act_quantize_concat +
+ * aexrt_b200_conv_w8a8 bit for bit, without the int8 codes ever reaching
+ * memory: the reference's prequant pass (record_int8_prequant_activation,
+ * runtime.cpp:21466-21665) and its conv (:4614-4923) in one launch.  Sources:
+ * >= 16 channels each (a multiple of 16 but for the last), coff a multiple of
+ * 16, ldc of 8, 16-byte aligned. */
+int aexrt_b200_conv_w8a8_sources(const AexrtB200ConvPlan* plan, const AexrtB200ActSource* srcs, uint32_t nsrc,
+                                 const void* residual, uint32_t res_ldc, uint32_t res_coff, void* out,
+                                 uint32_t out_ldc, uint32_t out_coff, uint32_t* amax_out, uint32_t amax_stride,
+                                 uint32_t amax_goff, int32_t* acc_dump, void* stream);
+
 
 /* SPPF pooling (YOLOv8 SPPF: three cascaded MaxPool2d(5, 1, 2) whose outputs
  * are concatenated; reference kind MAXPOOL, engine.py:103-118): writes the 5x5,

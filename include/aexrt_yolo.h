@@ -204,6 +204,9 @@ uint64_t aexrt_b200_yolo_arena_bytes(AexrtYoloModel* model);
  * fp16 ones can differ in the last bit (see aexrt_b200_conv_plan_create). */
 int aexrt_b200_yolo_override_conv_variant(AexrtYoloModel* model, uint32_t command_index, uint32_t block_n_bits);
 int aexrt_b200_yolo_set_profiling(AexrtYoloModel* model, uint32_t enabled);
+/* 1 (default): int8 convs quantize their fp16 inputs on load (one launch each);
+ * 0: a separate quantize launch writes the int8 codes first.  Same results. */
+int aexrt_b200_yolo_set_quant_on_load(AexrtYoloModel* model, uint32_t enabled);
 /* 0: every value keeps its own arena slot (so aexrt_yolo_debug_value can read
  * any of them); 1 (default): slots are reused between values whose lifetimes
  * do not overlap. */

@@ -428,3 +428,85 @@ def test_fp16_nhwc_input_matches_packed(n, ic, h, w, oc, k, ldc, coff, silu, blo
     assert plan.status() == 0
     assert torch.equal(ref, got)
     assert torch.equal(am0, am1)
+
+
+def _ql_sources(parts):
+    """AexrtB200ActSource array of fp16 NHWC torch tensors [(tensor, coff, channels, upsample), ...] with
+    their amax slots (computed here, as a producer's epilogue would leave them)."""
+    from aexrt_b200 import ops
+    from aexrt_b200._native import AexrtB200ActSource
+
+    srcs = (AexrtB200ActSource * len(parts))()
+    keep = []
+    for i, (t, coff, ch, up) in enumerate(parts):
+        am = ops.act_amax(t, ops.LAYOUT_NHWC_F16)  # every group of the buffer
+        keep.append(am)
+        s = srcs[i]
+        s.ptr, s.layout, s.ldc, s.coff, s.channels, s.upsample = t.data_ptr(), ops.LAYOUT_NHWC_F16, t.shape[-1], coff, ch, up
+        s.src_h, s.src_w = t.shape[1], t.shape[2]
+        s.amax_groups, s.amax_stride, s.amax_goff = am.data_ptr(), am.shape[1], coff // 16
+    return srcs, keep
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("n,ic,h,w,oc,k,s,split", [
+    (2, 32, 12, 10, 64, 3, 1, None),
+    (2, 16, 13, 11, 32, 3, 1, None),       # narrow: stacked M blocks
+    (3, 32, 11, 9, 48, 3, 2, None),        # stride 2, odd input
+    (2, 48, 9, 7, 32, 1, 1, None),
+    (8, 64, 80, 80, 128, 3, 1, None),      # C1 at batch 8
+    (2, 48, 16, 16, 64, 1, 1, (32, 2)),    # concat: 32 channels upsampled 2x, then 16 at full size
+    (2, 48, 16, 16, 32, 3, 1, (32, 2)),
+    (2, 40, 10, 12, 32, 3, 1, (16, 1)),    # last part of 24 channels: a partial slab
+    (64, 64, 80, 80, 64, 3, 1, None),      # BASELINE config 2 layers at batch 64
+    (64, 32, 160, 160, 64, 3, 2, None),
+    (64, 128, 20, 20, 256, 3, 2, None),
+    (64, 128, 40, 40, 128, 1, 1, None),
+])
+def test_quantize_on_load_equals_quantize_then_conv(n, ic, h, w, oc, k, s, split, mode):
+    """aexrt_b200_conv_w8a8_sources (the conv quantizes its fp16 NHWC sources in shared memory) equals
+    aexrt_b200_act_quantize_concat + aexrt_b200_conv_w8a8 bit for bit: fp16 outputs, int32
+    accumulators (pg16: every group's sub-sum) and the next-layer amax."""
+    torch = _torch()
+    from aexrt_b200 import _native, ops
+
+    if mode == 1 and ic % 16:
+        pytest.skip("pg16 needs 16-channel groups")
+    rng = np.random.default_rng(n * 7 + ic + oc + k + s + mode)
+    weight = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    wq, ws = ops.quantize_conv_weight_int8(weight)
+    if split is None:
+        x = torch.from_numpy(nchw_to_nhwc(seeded_act(rng, (n, ic, h, w)) * np.float16(2))).cuda()
+        parts = [(x, 0, ic, 1)]
+    else:
+        c0, up = split
+        a = torch.from_numpy(nchw_to_nhwc(seeded_act(rng, (n, c0, h // up, w // up)))).cuda()
+        b = torch.from_numpy(nchw_to_nhwc(seeded_act(rng, (n, 48, h, w)) * np.float16(3))).cuda()
+        parts = [(a, 0, c0, up), (b, 16, ic - c0, 1)]
+    res = torch.from_numpy(nchw_to_nhwc(rng.standard_normal((n, oc, (h - 1) // s + 1 if k == 3 else h,
+                                                             (w - 1) // s + 1 if k == 3 else w)).astype(np.float16))).cuda()
+    results = []
+    for ql in (False, True):
+        plan = ops.ConvPlan.int8(n, ic, h, w, oc, k, s, wq, ws, bias, silu=True, pg16=bool(mode), quant_on_load=ql)
+        srcs, keep = _ql_sources(parts)
+        out = torch.zeros(plan.out_shape, dtype=torch.float16, device="cuda")
+        amax_out = torch.zeros((n, (oc + 15) // 16), dtype=torch.int32, device="cuda")
+        d = plan.desc
+        groups = (ic + 15) // 16
+        dump = torch.zeros((groups, n * d.out_h * d.out_w, oc) if mode else (n * d.out_h * d.out_w, oc),
+                           dtype=torch.int32, device="cuda")
+        if ql:
+            assert plan.info.quant_on_load == 1
+            plan.run_sources(srcs, out=out, residual=res, amax_out=amax_out, acc_dump=dump)
+        else:
+            q = torch.empty(ops.packed_act_shape(n, ic, h, w, s), dtype=torch.int8, device="cuda")
+            rec = torch.empty((n, 1 + groups), dtype=torch.float32, device="cuda")
+            _native.check(_native.load().aexrt_b200_act_quantize_concat(srcs, len(srcs), n, h, w, mode, s, q.data_ptr(),
+                                                                        rec.data_ptr(), None), "quantize")
+            plan.run(q, rec, out=out, residual=res, amax_out=amax_out, acc_dump=dump)
+        torch.cuda.synchronize()
+        assert plan.status() == 0
+        results.append((out.cpu(), dump.cpu(), amax_out.cpu()))
+    for a, b in zip(results[0], results[1]):
+        assert torch.equal(a, b)
