@@ -144,7 +144,7 @@ struct AexrtYoloModel {
   uint32_t graph_batch = 1;  // the engine's batch
   uint32_t input_dtype = 0;  // 0 fp32, 1 fp16
   bool profiling = false, reuse = true, dirty = true, head_fusion = false;
-  bool quant_on_load = true;  // int8 convs quantize their fp16 inputs on load (else a quantize launch each)
+  bool quant_on_load = false;  // int8 convs quantize their fp16 inputs on load (else a quantize launch each)
   std::map<uint32_t, uint32_t> overrides, variants;
   // lowered state
   std::vector<Buffer> bufs;

@@ -56,7 +56,7 @@ class CompiledYolo:
     """One program compiled for one batch size on the current CUDA device."""
 
     def __init__(self, program: YoloProgram, batch: int, device=None, block_n: Optional[Dict[str, int]] = None,
-                 image_dtype=None, nms: Optional[NmsConfig] = None, quant_on_load: bool = True):
+                 image_dtype=None, nms: Optional[NmsConfig] = None, quant_on_load: bool = False):
         torch = _torch()
         self.program = program
         self.batch = batch

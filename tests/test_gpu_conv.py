@@ -497,7 +497,15 @@ def test_quantize_on_load_equals_quantize_then_conv(n, ic, h, w, oc, k, s, split
         dump = torch.zeros((groups, n * d.out_h * d.out_w, oc) if mode else (n * d.out_h * d.out_w, oc),
                            dtype=torch.int32, device="cuda")
         if ql:
-            assert plan.info.quant_on_load == 1
+            if not plan.info.quant_on_load:
+                # the planner keeps quantize-then-conv where the raw ring does not fit: narrow pg16
+                # convs stream slots (pg16 halo tiles are 64 or 128 channels wide), and wide convs
+                # whose resident weights leave no room for the ring next to 4 stages; such a plan
+                # refuses sources
+                assert ic >= 128 or (plan.info.variant != 2 and mode == 1 and oc < 64)
+                with pytest.raises(_native.AexrtError):
+                    plan.run_sources(srcs, out=out, residual=res, amax_out=amax_out, acc_dump=dump)
+                return
             plan.run_sources(srcs, out=out, residual=res, amax_out=amax_out, acc_dump=dump)
         else:
             q = torch.empty(ops.packed_act_shape(n, ic, h, w, s), dtype=torch.int8, device="cuda")

@@ -190,6 +190,27 @@ def test_streaming_detections_match_forwards(v8n):
         assert int(counts.max()) <= 100
 
 
+@pytest.mark.parametrize("pg16", [False, True])
+def test_quantize_on_load_model_bitexact(pg16, v8n):
+    """The whole model with every int8 conv quantizing its fp16 inputs on load equals the separate
+    quantize launches bit for bit (output0 and the detection buffer)."""
+    from aexrt_b200 import engine
+
+    torch = _torch()
+    prog = _program(pg16, v8n)
+    x = torch.from_numpy(_images(3, seed=41)).cuda()
+    res = []
+    for ql in (False, True):
+        eng = engine.CompiledYolo(prog, 3, nms=engine.NmsConfig(), quant_on_load=ql)
+        out = eng.forward(x).clone()
+        torch.cuda.synchronize()
+        assert eng.status() == 0
+        res.append((out.cpu(), eng.det_buf.clone().cpu(), sum(1 for s in eng.steps if s[0] == "conv_ql")))
+    assert res[0][2] == 0 and res[1][2] > 0
+    assert torch.equal(res[0][0], res[1][0])
+    assert torch.equal(res[0][1], res[1][1])
+
+
 def _match_detections(want, got, score_tol=0.02, box_tol=0.02):
     """The reference's detection gate (tests/test_runtime.py:1277-1279, README.md:62-63): the same
     count, and every oracle detection paired with a GPU detection of the same class whose score is

@@ -164,11 +164,12 @@ def test_conv_plans_override_and_profile():
     assert np.array_equal(m.output0(), base)
     with pytest.raises(RuntimeError, match="not a candidate"):
         m.override_conv_algorithm(p["command_index"], 7)
-    # the int8 convs with a separate quantize launch instead of quantize on load: identical results
-    m.set_quant_on_load(False)
+    # the int8 convs quantizing their fp16 inputs on load instead of a separate quantize launch:
+    # identical results
+    m.set_quant_on_load(True)
     m.run(img)
     assert np.array_equal(m.output0(), base)
-    m.set_quant_on_load(True)
+    m.set_quant_on_load(False)
     # variants of the tile choice give identical results
     m.override_conv_variant(p["command_index"], 2 << 20)
     m.run(img)
