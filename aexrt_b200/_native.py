@@ -15,6 +15,7 @@ from ctypes import POINTER, c_char_p, c_float, c_int, c_uint32, c_uint64, c_void
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libaexrt_b200.so")
 HEADER_PATH = os.path.join(os.path.dirname(HERE), "include", "aexrt_b200.h")
+LAUNCH_PROGRAMMATIC = 1  # AEXRT_B200_LAUNCH_PROGRAMMATIC
 
 
 class AexrtConv2DDesc(ctypes.Structure):
@@ -30,7 +31,7 @@ class AexrtB200ConvPlanInfo(ctypes.Structure):
     _fields_ = [(name, c_uint32) for name in (
         "struct_size", "kernel_id", "flags", "kind", "is_f16", "tile_w", "tile_h", "block_n", "k_slots", "stages",
         "smem_bytes", "grid_m", "grid_n", "in_hp", "in_wp", "grid", "variant", "pitch", "image_input",
-        "quant_on_load",
+        "quant_on_load", "staged_out",
     )]
 
 
@@ -57,6 +58,8 @@ class AexrtError(RuntimeError):
 
 _SIGNATURES = {
     "aexrt_b200_abi_version": (c_uint32, []),
+    "aexrt_b200_set_launch_flags": (c_int, [c_uint32]),
+    "aexrt_b200_get_launch_flags": (c_uint32, []),
     "aexrt_b200_get_last_error": (c_char_p, []),
     "aexrt_b200_device_count": (c_int, []),
     "aexrt_b200_quantize_conv_weight_int8": (c_int, [c_void_p, c_uint32, c_uint32, c_uint32, c_uint32, c_void_p, c_void_p]),
@@ -91,6 +94,11 @@ _SIGNATURES = {
                                                                    c_uint32, c_void_p]),
     "aexrt_b200_yolo_decode": (c_int, [POINTER(AexrtB200DecodeLevel), c_uint32, c_uint32, c_uint32, c_uint32, c_void_p,
                                        c_void_p]),
+    "aexrt_b200_dwconv3x3_f16": (c_int, [c_void_p] + [c_uint32] * 9 + [c_void_p, c_void_p, c_uint32, c_uint32,
+                                                                        c_void_p, c_uint32, c_uint32, c_void_p]),
+    "aexrt_b200_psa_attention_f16": (c_int, [c_void_p] + [c_uint32] * 8 + [c_float, c_void_p, c_uint32, c_uint32,
+                                                                            c_void_p, c_uint32, c_uint32, c_void_p,
+                                                                            c_uint32, c_uint32, c_void_p]),
     "aexrt_b200_yolo_nms_topk": (c_int, [c_void_p] + [c_uint32] * 6 + [c_float, c_float] + [c_uint32] * 3
                                  + [c_void_p, c_void_p, c_void_p]),
     "aexrt_b200_act_amax_quantize_f16": (c_int, [c_void_p] + [c_uint32] * 5 + [c_void_p, c_uint32, c_uint32, c_void_p,

@@ -24,7 +24,8 @@ SOURCES = ["capi.cu", "engine_file.cu", "yolo_runtime.cu", "kernels_slot.cu", "k
            "kernels_halo_f16.cu", "kernels_halo_mb.cu", "kernels_halo_pg.cu", "kernels_halo_ql.cu",
            "kernels_halo_ql_mb.cu",
            "kernels_stem16.cu", "kernels_stem32.cu", "kernels_stem48.cu", "kernels_stem64.cu"]
-HEADERS = ["codes.cuh", "conv_halo.cuh", "conv_tc.cuh", "engine_file.h", "graph_ops.cuh", "kernels.cuh", "nms.cuh", "ptx.cuh",
+HEADERS = ["codes.cuh", "conv_halo.cuh", "conv_tc.cuh", "engine_file.h", "graph_ops.cuh", "kernels.cuh", "launch.cuh", "nms.cuh",
+           "psa.cuh", "ptx.cuh",
            "quant.cuh", "quant_cluster.cuh", "stem.cuh", "yolo_ops.cuh"]
 OBJ_DIR = os.path.join(HERE, "_build")
 

@@ -22,10 +22,12 @@
 #include "conv_halo.cuh"
 #include "kernels.cuh"
 #include "nms.cuh"
+#include "psa.cuh"
 #include "quant.cuh"
 #include "quant_cluster.cuh"
 #include "stem.cuh"
 #include "yolo_ops.cuh"
+#include "launch.cuh"
 
 using namespace aexrt;
 
@@ -69,7 +71,8 @@ EncodeTiledFn encode_fn() {
 }
 
 bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base, const uint64_t* dims,
-                const uint64_t* strides_bytes, const uint32_t* box) {
+                const uint64_t* strides_bytes, const uint32_t* box,
+                CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail("cuTensorMapEncodeTiled unavailable (no CUDA driver)") != 0;
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail("TMA base address must be 16-byte aligned") != 0;
@@ -82,7 +85,7 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* 
     if (i > 0) s[i - 1] = strides_bytes[i - 1];
   }
   const CUresult r = fn(map, dt, rank, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail("cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r)) != 0;
   return true;
@@ -111,6 +114,9 @@ void pick_tile(int oh, int ow, int max_tw, int& tw, int& th) {
 namespace aexrt {
 // The library's one thread-local error message, shared by the runtime translation units.
 void set_last_error(const char* msg) { g_last_error = msg; }
+// Launch flags of this thread (aexrt_b200_set_launch_flags), read by launch_kernel (launch.cuh).
+thread_local uint32_t g_launch_flags = 0;
+uint32_t launch_flags() { return g_launch_flags; }
 }  // namespace aexrt
 
 struct AexrtB200ConvPlan {
@@ -135,6 +141,10 @@ struct AexrtB200ConvPlan {
   // pg16 halo: K steps pair two taps of one slab, ordered by their shared-memory offset
   int tap_pairs = 0, tap_a[5] = {0, 0, 0, 0, 0}, tap_b[5] = {-1, -1, -1, -1, -1};
   int mblocks = 1, nacc = 4, tmem_cols = 512;  // super-tile M blocks, TMEM buffers and columns
+  // staged output (conv_halo.cuh): buffers per epilogue group (0: direct stores) and their bytes
+  int out_nbuf = 0, out_gbytes = 0;
+  // every |int32 accumulator| <= 2^22 (bounded from the weight codes): exact fast conversion
+  bool acc_small = false;
   int pitch = 0, halo_rows = 0, boxes_per_slab = 1, slab_pairs = 0, taps = 1, w_tile_bytes = 0, m_tiles = 0;
   void* d_w = nullptr;   // [n_tile][q_total][bn][16 bytes]
   float* d_scale = nullptr;
@@ -151,7 +161,10 @@ struct AexrtB200ConvPlan {
 namespace {
 
 // Kernel instances live in their own translation units (kernels_*.cu), compiled in parallel.
-constexpr int kMaxConvSmem = 200 * 1024;
+// Dynamic shared memory of a conv CTA: the B200's 227 KB.  Halo pipelines and weights take at
+// most kConvStageBudget of it; the rest goes first to the staged output buffers.
+constexpr int kMaxConvSmem = 227 * 1024;
+constexpr int kConvStageBudget = 200 * 1024;
 // The activation kernels put the image index in a grid's y or z dimension.
 constexpr uint32_t kMaxImagesPerLaunch = 65535;
 // Halo tile: output tw x th on an M grid of pitch = tw + (2 for 3x3 s1, 1 for 3x3 s2, 0 for 1x1)
@@ -264,6 +277,10 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   const uint32_t variant = (block_n >> 16) & 0xF;  // 0 auto, 1 slot streaming, 2 halo
   const uint32_t order = (block_n >> 20) & 0xF;    // halo tile order: 0 auto, 1 strided, 2 contiguous
   const int mblocks_cap = static_cast<int>((block_n >> 24) & 0xF);  // super-tile M blocks: 0 auto, else at most
+  // staged TMA-store epilogue: bit 28 forces direct stores, bit 29 forces staging; by default only
+  // 1x1 plans stage (measured at batch 64: 1x1 128->128 @40 24.6 against 26.7 us direct, while the
+  // 3x3 layers ran 4-9 % slower staged, their four epilogue warps held in step by the per-tile barrier)
+  const bool direct_store = ((block_n >> 28) & 1u) != 0 || (((block_n >> 29) & 1u) == 0 && d.kernel_h != 1);
   int sms = 148;
   {
     int dev = 0;
@@ -327,9 +344,9 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
           mblocks *= 2;
       }
       const int boxes = p->stride == 2 ? 4 : 1;
-      const int budget = kMaxConvSmem - 1024;
+      const int budget = kConvStageBudget - 1024;
       const bool want_ql = !f16 && (flags & AEXRT_B200_PLAN_FLAG_QUANT_ON_LOAD);
-      int halo_h = 0, st = 0, raw_slots = 0, raw_bytes = 0;
+      int halo_h = 0, st = 0, raw_slots = 0, raw_bytes = 0, out_nbuf = 0, out_gbytes = 0;
       for (;; mblocks /= 2) {
         // keep >= 4 stages (and a whole tile per issuer half ring) for a super-tile, else fewer blocks
         halo_h = mblocks * th + (p->k == 1 ? 0 : (p->stride == 1 ? 2 : 1));
@@ -346,6 +363,23 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
         }
         st = std::min(16, (budget - one.total_bytes - raw_slots * raw_bytes) / one.stage_bytes + 1);
         if (mblocks == 1 || st >= std::max(4, 2 * pairs)) break;
+      }
+      // staged output: two buffers per epilogue group (else one) from the whole 227 KB, while the
+      // pipeline keeps min(st, max(4, 2 * pairs)) stages; the TMA box holds <= 256 rows
+      if (st >= 2 && mblocks * th <= 256 && !direct_store) {
+        const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, oc_alloc);
+        const int gbytes = halo_out_gbytes(bn, mblocks * th * tw);
+        const int keep = std::min(st, std::max(4, 2 * pairs));
+        for (int nb = 2; nb >= 1; --nb) {
+          const int total = one.total_bytes + raw_slots * raw_bytes + 4 * nb * gbytes + 2048;  // + alignment
+          const int st_o = std::min(16, (kMaxConvSmem - 1024 - total) / one.stage_bytes + 1);
+          if (st_o >= keep) {
+            out_nbuf = nb;
+            out_gbytes = gbytes;
+            st = std::min(st, st_o);
+            break;
+          }
+        }
       }
       if (st >= 2) {
         // TMEM accumulators: nacc buffers of mblocks*bn columns (a multiple of the two issuers and of
@@ -376,7 +410,11 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
         p->taps = taps;
         p->w_tile_bytes = w_tile;
         p->stages = st;
-        p->smem = halo_smem_plan(p->halo_rows, boxes, st, w_tile, p->oc_alloc, p->ql_raw * p->ql_raw_bytes).total_bytes;
+        p->out_nbuf = out_nbuf;
+        p->out_gbytes = out_gbytes;
+        p->smem = halo_smem_plan(p->halo_rows, boxes, st, w_tile, p->oc_alloc, p->ql_raw * p->ql_raw_bytes,
+                                 4 * out_nbuf * out_gbytes)
+                      .total_bytes;
         p->tiles_w = (static_cast<int>(d.out_w) + tw - 1) / tw;
         p->tiles_h = (static_cast<int>(d.out_h) + mblocks * th - 1) / (mblocks * th);
         p->m_tiles = static_cast<int>(d.batch) * p->tiles_h * p->tiles_w;
@@ -408,6 +446,19 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
       delete p;
       return nullptr;
     }
+  }
+
+  // int8 accumulators are bounded by 128 * sum_k |w[o][k]| (|activation code| <= 127 when its scale
+  // comes from the tensor's amax): within 2^22 the epilogue converts them on full-rate pipes
+  if (!f16) {
+    long worst = 0;
+    const int8_t* wc = static_cast<const int8_t*>(host_w);
+    for (int o = 0; o < oc; ++o) {
+      long s = 0;
+      for (size_t j = 0; j < static_cast<size_t>(ic) * kk; ++j) s += std::abs(static_cast<int>(wc[static_cast<size_t>(o) * ic * kk + j]));
+      worst = std::max(worst, s);
+    }
+    p->acc_small = 128L * worst <= (1L << 22);
   }
 
   // ---- weight repack.  Slot streaming: [n_tile][slot][bn][16 bytes] (one stage of B is one
@@ -653,6 +704,24 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     h.out_coff = static_cast<int>(out_coff);
     h.out_vec = out_vec;
     h.res_vec = res_vec;
+    h.acc_small = p->acc_small ? 1 : 0;
+    if (p->out_nbuf > 0 && out_vec) {
+      // staged output: the output slice as (channel, x, y, image), one box per epilogue group's
+      // column block of a (super-)tile, swizzled by its row width (conv_halo.cuh halo_stage_off)
+      const int cols = halo_out_cols(p->bn);
+      const uint64_t ldc = out_ldc, ow = p->desc.out_w, oh = p->desc.out_h;
+      const uint64_t dims[4] = {oc, ow, oh, p->desc.batch};
+      const uint64_t strides[3] = {2 * ldc, 2 * ldc * ow, 2 * ldc * ow * oh};
+      const uint32_t box[4] = {static_cast<uint32_t>(cols), static_cast<uint32_t>(p->tw),
+                               static_cast<uint32_t>(p->th * p->mblocks), 1};
+      const CUtensorMapSwizzle sw = cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                               : (cols == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+      if (!encode_map(&h.out_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, static_cast<const __half*>(out) + out_coff, dims,
+                      strides, box, sw))
+        return 0;
+      h.out_nbuf = p->out_nbuf;
+      h.out_gbytes = p->out_gbytes;
+    }
     h.amax_out = amax_out;
     h.amax_stride = static_cast<int>(amax_stride);
     h.amax_goff = static_cast<int>(amax_goff);
@@ -687,7 +756,7 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     }
     const HaloKernel k = halo_kernel_for(p->f16, p->bn, h.silu != 0, res != nullptr, p->pg, p->mblocks > 1, ql != nullptr);
     if (!k.fn) return fail("no conv kernel instance for this combination (linear fp16 residual, or quantize on load)");
-    k.fn<<<p->grid, k.threads, p->smem, static_cast<cudaStream_t>(stream)>>>(act_map, h);
+    launch_kernel(k.fn, dim3(p->grid), dim3(k.threads), p->smem, static_cast<cudaStream_t>(stream), act_map, h);
     return cuda_ok(cudaGetLastError(), "conv launch") ? 1 : 0;
   }
   ConvTcParams prm{};
@@ -728,7 +797,7 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
   prm.acc_dump = acc_dump;
   prm.status = p->d_status;
   KernelFn fn = kernel_for(p->f16, p->pg, p->bn);
-  fn<<<p->grid, kConvThreads, p->smem, static_cast<cudaStream_t>(stream)>>>(act_map, prm);
+  launch_kernel(fn, dim3(p->grid), dim3(kConvThreads), p->smem, static_cast<cudaStream_t>(stream), act_map, prm);
   return cuda_ok(cudaGetLastError(), "conv launch") ? 1 : 0;
 }
 
@@ -762,15 +831,15 @@ void launch_quantize(const QuantParams& q, cudaStream_t st) {
     const long items = static_cast<long>((q.hp * q.wp + pw - 1) / pw) * groups;  // one warp each
     const dim3 grid(static_cast<unsigned>((items + 7) / 8), q.n);
     if (rows_linear(q))
-      quant_rows_kernel<true, true><<<grid, 256, 0, st>>>(q, pw, groups);
+      launch_kernel(quant_rows_kernel<true, true>, dim3(grid), dim3(256), 0, st, q, pw, groups);
     else
-      quant_rows_kernel<true, false><<<grid, 256, 0, st>>>(q, pw, groups);
+      launch_kernel(quant_rows_kernel<true, false>, dim3(grid), dim3(256), 0, st, q, pw, groups);
   } else if (q.nsrc == 1 && q.src[0].layout == 1 && !q.split && (q.h * q.w) % 4 == 0 && q.slabs <= kMaxSlabs) {
     const dim3 grid((q.h * q.w / 4 + 255) / 256, q.slabs, q.n);
-    quantize_nchw_kernel<<<grid, 256, 0, st>>>(q);
+    launch_kernel(quantize_nchw_kernel, dim3(grid), dim3(256), 0, st, q);
   } else {
     const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, q.n);
-    quantize_i8_kernel<<<grid, 256, 0, st>>>(q);
+    launch_kernel(quantize_i8_kernel, dim3(grid), dim3(256), 0, st, q);
   }
 }
 
@@ -779,8 +848,9 @@ void launch_pack(const QuantParams& q, cudaStream_t st) {
     // images (fp32 NCHW, <= 8 channels): one slab, four pixels per thread
     const int quads = q.hp * ((q.wp + 3) / 4);
     const dim3 grid((quads + 255) / 256, q.n);
-    pack_nchw_f32_kernel<<<grid, 256, 0, st>>>(static_cast<const float*>(q.src[0].ptr), q.src[0].ch, q.h, q.w, q.hp,
-                                               q.wp, q.split, static_cast<__half*>(q.out));
+    launch_kernel(pack_nchw_f32_kernel, dim3(grid), dim3(256), 0, st,
+        static_cast<const float*>(q.src[0].ptr), q.src[0].ch, q.h, q.w, q.hp, q.wp, q.split,
+        static_cast<__half*>(q.out));
     return;
   }
   if (rows_ok(q, false)) {
@@ -789,12 +859,12 @@ void launch_pack(const QuantParams& q, cudaStream_t st) {
     const long items = static_cast<long>((q.hp * q.wp + pw - 1) / pw) * groups;
     const dim3 grid(static_cast<unsigned>((items + 7) / 8), q.n);
     if (rows_linear(q))
-      quant_rows_kernel<false, true><<<grid, 256, 0, st>>>(q, pw, groups);
+      launch_kernel(quant_rows_kernel<false, true>, dim3(grid), dim3(256), 0, st, q, pw, groups);
     else
-      quant_rows_kernel<false, false><<<grid, 256, 0, st>>>(q, pw, groups);
+      launch_kernel(quant_rows_kernel<false, false>, dim3(grid), dim3(256), 0, st, q, pw, groups);
   } else {
     const dim3 grid((q.hp * q.wp + 255) / 256, q.slabs, q.n);
-    pack_f16_kernel<<<grid, 256, 0, st>>>(q);
+    launch_kernel(pack_f16_kernel, dim3(grid), dim3(256), 0, st, q);
   }
 }
 
@@ -826,6 +896,14 @@ void quant_params_common(QuantParams& q, const void* x, uint32_t n, uint32_t c, 
 extern "C" {
 
 uint32_t aexrt_b200_abi_version(void) { return AEXRT_B200_ABI_VERSION; }
+
+int aexrt_b200_set_launch_flags(uint32_t flags) {
+  if (flags & ~static_cast<uint32_t>(AEXRT_B200_LAUNCH_PROGRAMMATIC)) return fail("unknown launch flags 0x%x", flags);
+  aexrt::g_launch_flags = flags;
+  return 1;
+}
+
+uint32_t aexrt_b200_get_launch_flags(void) { return aexrt::g_launch_flags; }
 
 const char* aexrt_b200_get_last_error(void) { return g_last_error.c_str(); }
 
@@ -893,7 +971,7 @@ int aexrt_b200_act_amax_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, u
   if (layout == AEXRT_B200_LAYOUT_NCHW_F16) {
     const int chunk = one_block ? 16 * hw : 32768;  // halves per block (chunked: 64 KB)
     const int blocks = static_cast<int>((16ull * hw + chunk - 1) / chunk);
-    amax_nchw_f16_kernel<<<dim3(blocks, groups, n), one_block ? 512 : 256, 0, st>>>(
+    launch_kernel(amax_nchw_f16_kernel, dim3(blocks, groups, n), dim3(one_block ? 512 : 256), 0, st,
         static_cast<const __half*>(x), static_cast<int>(c), hw, static_cast<int>(groups_total), chunk,
         amax_groups + group_offset, one_block ? 1 : 0);
   } else if (layout == AEXRT_B200_LAYOUT_NHWC_F16) {
@@ -902,7 +980,7 @@ int aexrt_b200_act_amax_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, u
     const int vec = static_cast<int>((c + 7) / 8);
     const int ppb = std::max(1, 2048 / vec);
     const int blocks = (hw + ppb - 1) / ppb;
-    amax_nhwc_f16_kernel<<<dim3(blocks, n), 256, groups * 4, st>>>(
+    launch_kernel(amax_nhwc_f16_kernel, dim3(blocks, n), dim3(256), groups * 4, st,
         static_cast<const __half*>(x), hw, static_cast<int>(c), static_cast<int>(ldc), static_cast<int>(coff),
         static_cast<int>(groups), ppb, amax_groups + group_offset, static_cast<int>(groups_total));
   } else {
@@ -1213,6 +1291,7 @@ int aexrt_b200_conv_plan_info(const AexrtB200ConvPlan* p, AexrtB200ConvPlanInfo*
   i.pitch = p->pitch;
   i.image_input = p->image_input ? 1u : 0u;
   i.quant_on_load = p->ql ? 1u : 0u;
+  i.staged_out = static_cast<uint32_t>(p->out_nbuf);
   i.in_hp = p->in_hp;
   i.in_wp = p->in_wp;
   *info = i;
@@ -1438,16 +1517,69 @@ int aexrt_b200_sppf_pool(const void* x, uint32_t n, uint32_t h, uint32_t w, uint
       if (!cuda_ok(cudaFuncSetAttribute(sppf_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024),
                    "cudaFuncSetAttribute"))
         return 0;
-      sppf_smem_kernel<<<dim3(c / cb, n), 256, smem, static_cast<cudaStream_t>(stream)>>>(
+      launch_kernel(sppf_smem_kernel, dim3(c / cb, n), dim3(256), smem, static_cast<cudaStream_t>(stream),
           static_cast<const __half*>(x), h, w, c, ldc, coff, cb, static_cast<__half*>(out), out_ldc, out_coff, amax,
           amax_stride, amax_goff);
       return cuda_ok(cudaGetLastError(), "sppf launch") ? 1 : 0;
     }
   }
-  sppf_pool_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_kernel(sppf_pool_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0,
+      static_cast<cudaStream_t>(stream),
       static_cast<const __half*>(x), n, h, w, c, ldc, coff, static_cast<__half*>(out), out_ldc, out_coff, amax,
       amax_stride, amax_goff);
   return cuda_ok(cudaGetLastError(), "sppf launch") ? 1 : 0;
+}
+
+int aexrt_b200_dwconv3x3_f16(const void* x, uint32_t n, uint32_t h, uint32_t w, uint32_t c, uint32_t ldc,
+                             uint32_t coff, uint32_t grp, uint32_t grp_stride, uint32_t grp_off, const float* w9,
+                             const float* bias, uint32_t stride, uint32_t silu, void* out, uint32_t out_ldc,
+                             uint32_t out_coff, void* stream) {
+  if (!x || !out || !w9 || !bias) return fail("dwconv: null pointer");
+  if (stride != 1 && stride != 2) return fail("dwconv: stride must be 1 or 2");
+  if (grp == 0) grp = c;
+  if (grp_stride == 0) grp_stride = grp;
+  if (c % 8 || grp % 8 || grp_stride % 8 || grp_off % 8 || ldc % 8 || coff % 8 || out_ldc % 8 || out_coff % 8 ||
+      c % grp || reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16 ||
+      reinterpret_cast<uintptr_t>(w9) % 16 || reinterpret_cast<uintptr_t>(bias) % 16)
+    return fail("dwconv: channel counts, groups and slices must be multiples of 8 with 16-byte aligned buffers");
+  if (ldc < coff + (c / grp - 1) * grp_stride + grp_off + grp || out_ldc < out_coff + c)
+    return fail("dwconv: input or output slice out of range");
+  const uint32_t oh = (h + 2 - 3) / stride + 1, ow = (w + 2 - 3) / stride + 1;
+  const long total = static_cast<long>(n) * oh * ow * (c / 8);
+  if (total == 0) return 1;
+  launch_kernel(dwconv3x3_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0,
+      static_cast<cudaStream_t>(stream),
+      static_cast<const __half*>(x), n, h, w, c, ldc, coff, grp, grp_stride, grp_off, w9, bias, stride, silu ? 1 : 0,
+      oh, ow, static_cast<__half*>(out), out_ldc, out_coff);
+  return cuda_ok(cudaGetLastError(), "dwconv launch") ? 1 : 0;
+}
+
+int aexrt_b200_psa_attention_f16(const void* qkv, uint32_t n, uint32_t h, uint32_t w, uint32_t ldc, uint32_t coff,
+                                 uint32_t heads, uint32_t key_dim, uint32_t head_dim, float scale, const void* pe,
+                                 uint32_t pe_ldc, uint32_t pe_coff, void* out, uint32_t out_ldc, uint32_t out_coff,
+                                 uint32_t* amax, uint32_t amax_stride, uint32_t amax_goff, void* stream) {
+  if (!qkv || !pe || !out) return fail("psa attention: null pointer");
+  if (head_dim != static_cast<uint32_t>(kPsaHeadDim)) return fail("psa attention: head_dim must be 64");
+  if (heads == 0 || key_dim == 0 || key_dim % 8 || ldc % 8 || coff % 8 || pe_ldc % 2 || pe_coff % 2 ||
+      out_ldc % 2 || out_coff % 16 || reinterpret_cast<uintptr_t>(qkv) % 16)
+    return fail("psa attention: key_dim, ldc and coff multiples of 8, output slice at a 16-channel boundary");
+  const uint32_t per_head = 2 * key_dim + head_dim;
+  if (ldc < coff + heads * per_head || pe_ldc < pe_coff + heads * head_dim || out_ldc < out_coff + heads * head_dim)
+    return fail("psa attention: qkv, pe or output slice out of range");
+  if (amax && amax_goff * 16 + heads * head_dim > amax_stride * 16) return fail("psa attention: amax slots out of range");
+  if (n > kMaxImagesPerLaunch) return fail("psa attention: at most %u images per call", kMaxImagesPerLaunch);
+  const uint32_t l = h * w;
+  const size_t smem = psa_smem_bytes(static_cast<int>(l), static_cast<int>(key_dim));
+  if (smem > 200 * 1024) return fail("psa attention: a %ux%u map does not fit one CTA's shared memory", h, w);
+  if (n == 0 || l == 0) return 1;
+  if (!cuda_ok(cudaFuncSetAttribute(psa_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+               "cudaFuncSetAttribute"))
+    return 0;
+  launch_kernel(psa_attention_kernel, dim3(heads, n), dim3(kPsaThreads), smem, static_cast<cudaStream_t>(stream),
+      static_cast<const __half*>(qkv), static_cast<int>(l), ldc, coff, key_dim, scale,
+      static_cast<const __half*>(pe), pe_ldc, pe_coff, static_cast<__half*>(out), out_ldc, out_coff, amax,
+      amax_stride, amax_goff);
+  return cuda_ok(cudaGetLastError(), "psa attention launch") ? 1 : 0;
 }
 
 int aexrt_b200_yolo_decode(const AexrtB200DecodeLevel* levels, uint32_t nlevels, uint32_t n, uint32_t nc,
@@ -1480,7 +1612,8 @@ int aexrt_b200_yolo_decode(const AexrtB200DecodeLevel* levels, uint32_t nlevels,
   d.out = out;
   const long total = static_cast<long>(n) * anchors;
   if (total == 0) return 1;
-  yolo_decode_kernel<<<static_cast<unsigned>((total + 127) / 128), 128, 0, static_cast<cudaStream_t>(stream)>>>(d);
+  launch_kernel(yolo_decode_kernel, dim3(static_cast<unsigned>((total + 127) / 128)), dim3(128), 0,
+      static_cast<cudaStream_t>(stream), d);
   return cuda_ok(cudaGetLastError(), "decode launch") ? 1 : 0;
 }
 
@@ -1532,7 +1665,7 @@ int aexrt_b200_yolo_nms_topk(const float* output0, uint32_t n, uint32_t channels
       raised[dev] = smem;
     }
   }
-  aexrt::yolo_nms_kernel<<<n, aexrt::kNmsThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  launch_kernel(aexrt::yolo_nms_kernel, dim3(n), dim3(aexrt::kNmsThreads), smem, static_cast<cudaStream_t>(stream), p);
   return cuda_ok(cudaGetLastError(), "nms launch") ? 1 : 0;
 }
 

@@ -84,14 +84,30 @@ struct ConvHaloParams {
   int ql_groups[kQlMaxParts];         // amax groups of each source (one per slab it fills)
   const uint32_t* ql_amax[kQlMaxParts];
   int ql_amax_stride[kQlMaxParts], ql_amax_goff[kQlMaxParts];
+  // int32 accumulators convert through the exact small-integer path (the host bounds every
+  // |accumulator| <= 2^22 from the weight codes)
+  int acc_small;
+  // staged output (out_nbuf > 0): each epilogue group of four warps (one per TMEM lane quadrant)
+  // writes its column block of a tile into a swizzled shared-memory box and one thread stores
+  // the box with a TMA tensor store; out_nbuf buffers of out_gbytes per group
+  int out_nbuf, out_gbytes;
   CUtensorMap ql_map[kQlMaxParts];    // (channel, x, y, image) maps of the fp16 NHWC slices
+  CUtensorMap out_map;                // (channel, x, y, image) over the output slice; box = one group's block
 };
+
+// Shared-memory bytes of the staged output of one plan: 4 epilogue groups x nbuf buffers, each
+// one group's column block (kCols channels) of every pixel of a (super-)tile, 1024-aligned.
+__host__ __device__ constexpr int halo_out_cols(int bn) { return bn >= 64 ? bn / 4 : 16; }
+__host__ __device__ inline int halo_out_gbytes(int bn, int tile_px) {
+  return ((tile_px * halo_out_cols(bn) * 2 + 1023) / 1024) * 1024;
+}
 
 struct HaloSmemPlan {
   int slab_bytes;   // one slab's halo (all parity boxes), multiple of 128
   int stage_bytes;  // two slabs
   int a_bytes;      // all stages
   int raw_offset;   // quantize on load: the fp16 raw ring
+  int out_offset;   // staged output buffers (1024-aligned)
   int b_offset;
   int sb_offset;
   int am_offset;    // per-tile amax reduction ring (strided order): [8][16] maxima + [8][4] counters
@@ -103,7 +119,8 @@ constexpr int kMaxAcc = 16;                 // TMEM accumulator buffers (narrow 
 constexpr int kAmaxRing = 2 * kMaxAcc;      // >= 2 x accumulator buffers: a slot is reset before any warp reuses it
 
 __host__ __device__ inline HaloSmemPlan halo_smem_plan(int halo_rows, int boxes_per_slab, int stages,
-                                                       int w_tile_bytes, int oc_alloc, int raw_total = 0) {
+                                                       int w_tile_bytes, int oc_alloc, int raw_total = 0,
+                                                       int out_total = 0) {
   HaloSmemPlan s;
   const int box_bytes = ((halo_rows * kSlotBytes + 127) / 128) * 128;
   s.slab_bytes = box_bytes * boxes_per_slab;
@@ -111,7 +128,8 @@ __host__ __device__ inline HaloSmemPlan halo_smem_plan(int halo_rows, int boxes_
   // 4 KB of slack: a shifted 128-row window may run past the last halo row
   s.a_bytes = stages * s.stage_bytes + 4096;
   s.raw_offset = ((s.a_bytes + 127) / 128) * 128;
-  s.b_offset = ((s.raw_offset + raw_total + 1023) / 1024) * 1024;
+  s.out_offset = ((s.raw_offset + raw_total + 1023) / 1024) * 1024;
+  s.b_offset = ((s.out_offset + out_total + 1023) / 1024) * 1024;
   s.sb_offset = s.b_offset + ((w_tile_bytes + 127) / 128) * 128;  // w_scale[oc_alloc], bias[oc_alloc]
   s.am_offset = s.sb_offset + ((8 * oc_alloc + 127) / 128) * 128;
   s.bar_offset = s.am_offset + kAmaxRing * (16 + 4) * 4;
@@ -336,6 +354,95 @@ __device__ __forceinline__ __half2 halo_epilogue16_packed(const uint32_t* v, flo
   return valid ? m : __float2half2_rn(0.0f);
 }
 
+// The staged epilogue of 16 consecutive output channels of one pixel: the arithmetic of
+// halo_epilogue16_packed (scale, bias, SiLU, residual, fp16), with the results returned as two
+// 16-byte chunks `o` instead of stored.  `r` holds the 16 residual values (zero where absent);
+// the scale and bias vectors are zero-padded, so channels past the last one compute zeros.
+// kSmall: the accumulators convert through acc2_to_f2's exact small-integer path.
+template <bool kF16, bool kSilu, bool kRes, bool kSmall>
+__device__ __forceinline__ __half2 halo_epi16(const uint32_t* v, uint64_t s2, const float* sscale, const float* sbias,
+                                              const uint4* r, uint4* o) {
+  const uint64_t half2c = f2_pack(0.5f, 0.5f);
+  __half2 m = __float2half2_rn(0.0f);
+#pragma unroll
+  for (int h8 = 0; h8 < 2; ++h8) {
+    const float4 b0 = *reinterpret_cast<const float4*>(sbias + 8 * h8);
+    const float4 b1 = *reinterpret_cast<const float4*>(sbias + 8 * h8 + 4);
+    const uint64_t bb[4] = {f2_pack(b0.x, b0.y), f2_pack(b0.z, b0.w), f2_pack(b1.x, b1.y), f2_pack(b1.z, b1.w)};
+    uint64_t y[4];
+    if constexpr (kF16) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint64_t a = f2_pack(__uint_as_float(v[8 * h8 + 2 * i]), __uint_as_float(v[8 * h8 + 2 * i + 1]));
+        y[i] = kSilu ? f2_fma(a, half2c, bb[i]) : f2_add(a, bb[i]);
+      }
+    } else {
+      const float4 c0 = *reinterpret_cast<const float4*>(sscale + 8 * h8);
+      const float4 c1 = *reinterpret_cast<const float4*>(sscale + 8 * h8 + 4);
+      const uint64_t ss[4] = {f2_pack(c0.x, c0.y), f2_pack(c0.z, c0.w), f2_pack(c1.x, c1.y), f2_pack(c1.z, c1.w)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint64_t a = acc2_to_f2<kSmall>(v[8 * h8 + 2 * i], v[8 * h8 + 2 * i + 1]);
+        y[i] = f2_fma(f2_mul(a, s2), ss[i], bb[i]);
+      }
+    }
+    if constexpr (kSilu) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float h0, h1;
+        f2_unpack(y[i], h0, h1);
+        y[i] = f2_fma(y[i], f2_pack(tanh_approx(h0), tanh_approx(h1)), y[i]);
+      }
+    }
+    if constexpr (kRes) {
+      const __half2* rh = reinterpret_cast<const __half2*>(&r[h8]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(rh[i]);
+        y[i] = f2_add(y[i], f2_pack(f.x, f.y));
+      }
+    }
+    __half2* hv = reinterpret_cast<__half2*>(&o[h8]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float a, b;
+      f2_unpack(y[i], a, b);
+      hv[i] = __floats2half2_rn(a, b);
+      m = __hmax2(m, __habs2(hv[i]));
+    }
+  }
+  return m;
+}
+
+// The 16 residual values of channels [oc, oc + 16) of one pixel row (zero past the last channel
+// or for an invalid pixel): two 16-byte loads when the whole group exists and the row allows it.
+__device__ __forceinline__ void halo_load_res16(const ConvHaloParams& p, const __half* res_row, int oc, bool valid,
+                                                uint4* r) {
+  r[0] = r[1] = make_uint4(0u, 0u, 0u, 0u);
+  if (!valid) return;
+  const int n_valid = p.oc - oc;
+  if (n_valid >= 16 && p.res_vec) {
+    r[0] = *reinterpret_cast<const uint4*>(res_row + oc);
+    r[1] = *reinterpret_cast<const uint4*>(res_row + oc + 8);
+  } else {
+    __half* h = reinterpret_cast<__half*>(r);
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (i < n_valid) h[i] = res_row[oc + i];
+  }
+}
+
+// Byte offset of 16-byte chunk `c` of staging row `row` inside one group's output box: rows of
+// kCols fp16 channels, chunks permuted by the TMA swizzle of that row width (32, 64 or 128 bytes:
+// chunk bits XOR address bits 7.. of the row), so that eight consecutive rows written by eight
+// lanes land in eight distinct bank groups.
+template <int kCols>
+__device__ __forceinline__ uint32_t halo_stage_off(int row, int c) {
+  static_assert(kCols == 16 || kCols == 32 || kCols == 64, "staged output rows are 32, 64 or 128 bytes");
+  const int sw = kCols == 64 ? (row & 7) : (kCols == 32 ? ((row >> 1) & 3) : ((row >> 2) & 1));
+  return static_cast<uint32_t>(row * (2 * kCols) + ((c ^ sw) << 4));
+}
+
 // pg16 final epilogue of 8 consecutive channels from the fp32 group sums `fp2` (packed pairs):
 // y = fma(fp, w_scale, bias) (the reference's `fp * scale + bias`, which its shader compiler may contract), then
 // SiLU (halved vectors, as above), residual, fp16 store.  Packed when all 8
@@ -402,6 +509,39 @@ __device__ __forceinline__ float halo_pg_finish8(const ConvHaloParams& p, const 
   return valid ? fmaxf(__low2float(m), __high2float(m)) : 0.0f;
 }
 
+// pg16, staged: the arithmetic of halo_pg_finish8 for 8 channels with the residual values `r`
+// (zero where absent), returned as one 16-byte chunk.
+template <bool kSilu, bool kRes>
+__device__ __forceinline__ __half2 halo_pg_vals8(const uint64_t* fp2, const float* sscale, const float* sbias,
+                                                 const uint4& r, uint4& o) {
+  const float4 c0 = *reinterpret_cast<const float4*>(sscale), c1 = *reinterpret_cast<const float4*>(sscale + 4);
+  const float4 b0 = *reinterpret_cast<const float4*>(sbias), b1 = *reinterpret_cast<const float4*>(sbias + 4);
+  const uint64_t ss[4] = {f2_pack(c0.x, c0.y), f2_pack(c0.z, c0.w), f2_pack(c1.x, c1.y), f2_pack(c1.z, c1.w)};
+  const uint64_t bb[4] = {f2_pack(b0.x, b0.y), f2_pack(b0.z, b0.w), f2_pack(b1.x, b1.y), f2_pack(b1.z, b1.w)};
+  const __half2* rh = reinterpret_cast<const __half2*>(&r);
+  __half2* hv = reinterpret_cast<__half2*>(&o);
+  __half2 m = __float2half2_rn(0.0f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint64_t v = f2_fma(fp2[i], ss[i], bb[i]);
+    if constexpr (kSilu) {
+      float h0, h1;
+      f2_unpack(v, h0, h1);
+      v = f2_fma(v, f2_pack(tanh_approx(h0), tanh_approx(h1)), v);
+    }
+    float y0, y1;
+    f2_unpack(v, y0, y1);
+    if constexpr (kRes) {
+      const float2 f = __half22float2(rh[i]);
+      y0 += f.x;
+      y1 += f.y;
+    }
+    hv[i] = __floats2half2_rn(y0, y1);
+    m = __hmax2(m, __habs2(hv[i]));
+  }
+  return m;
+}
+
 template <bool kF16, int BN, bool kSilu, bool kRes, bool kPG = false, bool kMB = false, bool kQL = false>
 __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap act_map, const __grid_constant__ ConvHaloParams p) {
@@ -427,10 +567,16 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
   constexpr int kCS = kF16 ? 8 : 16;  // tensor-map elements per 16-byte chunk
 
   extern __shared__ __align__(1024) uint8_t smem[];
+  // programmatic dependent launch (ptx.cuh): the next kernel may be scheduled right away.  The set-up
+  // below and the loads of the plan's own weights, scales and biases touch no memory another kernel
+  // writes; every role that reads activations, scale records or amax slots, or writes outputs, first
+  // waits for the previous grid (the producer before its first activation box, the epilogue and the
+  // converters on entry; the MMA issuers only touch shared memory and TMEM).
+  grid_dep_launch();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const HaloSmemPlan sp = halo_smem_plan(p.halo_rows, p.boxes_per_slab, p.stages, p.w_tile_bytes, p.oc_alloc,
-                                         kQL ? p.ql_raw_slots * p.ql_raw_bytes : 0);
+                                         kQL ? p.ql_raw_slots * p.ql_raw_bytes : 0, 4 * p.out_nbuf * p.out_gbytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.bar_offset);
   uint64_t* empty = full + p.stages;
   uint64_t* acc_full = full + 2 * p.stages;  // [kAcc]
@@ -511,7 +657,7 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
     const int nbox = 2 * p.boxes_per_slab;
     const uint32_t stage_tx = static_cast<uint32_t>(nbox * p.halo_rows * kSlotBytes);
     int cur_n = -1, wloads = 0;
-    bool ok = true;
+    bool ok = true, deps = false;
     for (int q0 = 0; q0 < total_q && ok;) {
       const int q = q0 + lane;
       const int i = q / p.slab_pairs;
@@ -542,6 +688,10 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
         __syncwarp();
         cur_n = n_first;
         ++wloads;
+      }
+      if (!deps) {
+        grid_dep_wait();  // the first weight tile is on its way; activations come from the previous kernel
+        deps = true;
       }
       bool lane_ok = true;
       if (kQL && mine) {
@@ -775,6 +925,7 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
     // slot (the stage ring of the tile's issuer), write the int8 codes of both slabs in the TMA
     // layout the MMA descriptors expect, then release the raw slot and fill the A slot.
     constexpr int kCT = 32 * kQlWarps;
+    grid_dep_wait();  // the sources and their amax slots come from earlier kernels
     const int ct = static_cast<int>(threadIdx.x) - 32 * (3 + kEpiWarps);
     const int my_tiles = static_cast<int>(blockIdx.x) < p.total_tiles
                              ? (p.total_tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
@@ -859,6 +1010,7 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    grid_dep_wait();  // scale records and residuals come from earlier kernels; outputs may still be read
     const int quad = warp & 3;                   // TMEM lane quadrant this warp may access
     const int colq = ((warp - 2) >> 2) % kColBlocks;  // which kCols-wide column block
     const int tgroup = ((warp - 2) >> 2) / kColBlocks;  // which tiles: i % kTileGroups == tgroup
@@ -890,6 +1042,18 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
     uint32_t* am_count = am_ring + kAmaxRing * 16;                          // [kAmaxRing][4] arrivals
     int ep_img = -1;  // quantize on load: the image whose per-tensor amax ep_at holds
     float ep_at = 0.0f;
+    // Staged output: the four warps of this warp's group (one per TMEM lane quadrant, the same
+    // column block and tile group) write their column block of a tile into a swizzled box in
+    // shared memory; after a named barrier the group's first thread stores the box with one TMA
+    // store.  A thread whose wait gives up keeps walking its tiles (without waiting) so that the
+    // group's barriers always see all four warps.
+    const bool staged = p.out_nbuf > 0;
+    const int sgroup = (warp - 2) >> 2;
+    const bool st_issuer = staged && warp == 2 + 4 * sgroup && lane == 0;
+    uint8_t* const sbuf0 = smem + sp.out_offset + sgroup * p.out_nbuf * p.out_gbytes;
+    const int srow0 = (r_h < p.th && r_w < p.tw) ? r_h * p.tw + r_w : -1;  // staging row (M block 0)
+    int jj = 0;         // this group's tiles so far: staging buffer jj % out_nbuf
+    bool alive = true;  // every wait of this warp so far succeeded
     for (int k = blockIdx.x, i = 0; k < p.total_tiles; k += gridDim.x, ++i) {
       if (kTileGroups > 1 && i % kTileGroups != tgroup) continue;
       const int u = i;  // the tile's place in this CTA's sequence: accumulator buffer and phase
@@ -904,6 +1068,12 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
       __half* out_row = p.out + pix * p.out_ldc + p.out_coff;
       const __half* res_row = kRes ? p.res + pix * p.res_ldc + p.res_coff : nullptr;
       const int n0 = n_tile * BN;
+      uint8_t* const sbuf = sbuf0 + (staged ? (jj % p.out_nbuf) * p.out_gbytes : 0);
+      if (staged && p.out_nbuf == 1 && jj > 0) {
+        // one buffer: the previous tile's store must have read it before anyone writes it again
+        if (st_issuer) bulk_wait_read_all();
+        named_bar_sync(2 + sgroup, 128);
+      }
       if (p.amax_out != nullptr && p.contiguous && t / per_img != run_key) {
         if (run_key >= 0) flush_amax();
         run_key = t / per_img;
@@ -918,7 +1088,6 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
         const int r_iss = i % p.issuers;
         const int ubase = (i / p.issuers) * p.slabs;
         uint64_t fp2[kCols / 2];  // packed fp32 pairs of the group sums
-        bool pg_ok = true;
         for (int g = 0; g < p.slabs; ++g) {
           const int uu = ubase + g;
           const int gbuf = r_iss * Hh + uu % Hh;
@@ -931,10 +1100,8 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
           }
           const float gs = __fdiv_rn(ag, 127.0f);
           const uint64_t gs2 = f2_pack(gs, gs);
-          if (!mbar_wait_bounded(&acc_full[gbuf], (uu / Hh) & 1, p.status, kStatusTimeoutAccFull)) {
-            pg_ok = false;
-            break;
-          }
+          if (alive && !mbar_wait_bounded(&acc_full[gbuf], (uu / Hh) & 1, p.status, kStatusTimeoutAccFull))
+            alive = false;
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < kChunks; ++c) {
@@ -962,24 +1129,40 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
             for (int j = 0; j < CW / 2; ++j) {
               // fp += fl32(S) * gs in ascending group order, one fused multiply-add per group (the
               // slot kernel's `fp + S * gs` contracts the same way; ptxas also fuses a packed
-              // mul.rn + add.rn pair, so the fma is written out)
-              const uint64_t s2 = f2_pack(static_cast<float>(static_cast<int32_t>(v[2 * j])),
-                                          static_cast<float>(static_cast<int32_t>(v[2 * j + 1])));
+              // mul.rn + add.rn pair, so the fma is written out).  |S| <= 128 * 127 * 144 < 2^22:
+              // the exact small-integer conversion always applies to a group sub-sum.
+              const uint64_t s2 = acc2_to_f2<true>(v[2 * j], v[2 * j + 1]);
               fp2[c * (CW / 2) + j] = g == 0 ? f2_mul(s2, gs2) : f2_fma(s2, gs2, fp2[c * (CW / 2) + j]);
             }
           }
         }
-        if (!pg_ok) break;
 #pragma unroll
         for (int c = 0; c < kChunks; ++c) {
 #pragma unroll
           for (int g16 = 0; g16 < CW / 16; ++g16) {
             const int lc = n0 + col0 + c * CW + 16 * g16;
-            const float m0 = halo_pg_finish8<kSilu, kRes>(p, fp2 + (c * CW + 16 * g16) / 2, lc, s_scale + lc,
-                                                          s_bias + lc, valid, out_row, res_row);
-            const float m1 = halo_pg_finish8<kSilu, kRes>(p, fp2 + (c * CW + 16 * g16 + 8) / 2, lc + 8,
-                                                          s_scale + lc + 8, s_bias + lc + 8, valid, out_row, res_row);
-            run_max[c * (CW / 16) + g16] = fmaxf(run_max[c * (CW / 16) + g16], fmaxf(m0, m1));
+            float mg;
+            if (staged) {
+              uint4 rr[2], o[2];
+              if constexpr (kRes) halo_load_res16(p, res_row, lc, valid, rr);
+              const __half2 m2 = __hmax2(
+                  halo_pg_vals8<kSilu, kRes>(fp2 + (c * CW + 16 * g16) / 2, s_scale + lc, s_bias + lc, rr[0], o[0]),
+                  halo_pg_vals8<kSilu, kRes>(fp2 + (c * CW + 16 * g16 + 8) / 2, s_scale + lc + 8, s_bias + lc + 8,
+                                             rr[1], o[1]));
+              if (srow0 >= 0) {
+                const int cc = (c * CW + 16 * g16) >> 3;
+                *reinterpret_cast<uint4*>(sbuf + halo_stage_off<kCols>(srow0, cc)) = o[0];
+                *reinterpret_cast<uint4*>(sbuf + halo_stage_off<kCols>(srow0, cc + 1)) = o[1];
+              }
+              mg = valid ? fmaxf(__low2float(m2), __high2float(m2)) : 0.0f;
+            } else {
+              const float m0 = halo_pg_finish8<kSilu, kRes>(p, fp2 + (c * CW + 16 * g16) / 2, lc, s_scale + lc,
+                                                            s_bias + lc, valid, out_row, res_row);
+              const float m1 = halo_pg_finish8<kSilu, kRes>(p, fp2 + (c * CW + 16 * g16 + 8) / 2, lc + 8,
+                                                            s_scale + lc + 8, s_bias + lc + 8, valid, out_row, res_row);
+              mg = fmaxf(m0, m1);
+            }
+            run_max[c * (CW / 16) + g16] = fmaxf(run_max[c * (CW / 16) + g16], mg);
           }
         }
       } else {
@@ -995,9 +1178,10 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
       } else if constexpr (!kF16) {
         amax_in = __ldg(p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs));
       }
-      if (!mbar_wait_bounded(&acc_full[buf], (u / nacc) & 1, p.status, kStatusTimeoutAccFull)) break;
+      if (alive && !mbar_wait_bounded(&acc_full[buf], (u / nacc) & 1, p.status, kStatusTimeoutAccFull)) alive = false;
       tc_fence_after();
       const float in_scale = kF16 ? 1.0f : __fdiv_rn(amax_in, 127.0f);
+      const uint64_t s2 = f2_pack(in_scale, in_scale);
       const int oy0 = (r / p.tiles_w) * p.th * p.mblocks + r_h;
       for (int mb = 0; mb < kMaxMB; ++mb) {
         if (mb >= p.mblocks) break;
@@ -1007,6 +1191,7 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
         const size_t pixb = (static_cast<size_t>(img) * p.oh + (vb ? oyb : 0)) * p.ow + (vb ? ox : 0);
         __half* outb = p.out + pixb * p.out_ldc + p.out_coff;
         const __half* resb = kRes ? p.res + pixb * p.res_ldc + p.res_coff : nullptr;
+        const int srow = srow0 >= 0 ? srow0 + mb * p.th * p.tw : -1;
 #pragma unroll
         for (int c = 0; c < kChunks; ++c) {
           uint32_t v[CW];
@@ -1028,6 +1213,27 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
 #pragma unroll
             for (int i = 0; i < CW; ++i)
               if (oc_c + i < p.oc) p.acc_dump[pixb * p.oc + oc_c + i] = static_cast<int32_t>(v[i]);
+          }
+          if (staged) {
+#pragma unroll
+            for (int g = 0; g < CW / 16; ++g) {
+              const int lc = oc_c + 16 * g;  // output channel (the vectors are zero-padded to oc_alloc)
+              uint4 rr[2], o[2];
+              if constexpr (kRes) halo_load_res16(p, resb, lc, vb, rr);
+              __half2 m2;
+              if (kF16 || !p.acc_small)
+                m2 = halo_epi16<kF16, kSilu, kRes, false>(v + 16 * g, s2, s_scale + lc, s_bias + lc, rr, o);
+              else
+                m2 = halo_epi16<kF16, kSilu, kRes, !kF16>(v + 16 * g, s2, s_scale + lc, s_bias + lc, rr, o);
+              if (srow >= 0) {
+                const int cc = (c * CW + 16 * g) >> 3;
+                *reinterpret_cast<uint4*>(sbuf + halo_stage_off<kCols>(srow, cc)) = o[0];
+                *reinterpret_cast<uint4*>(sbuf + halo_stage_off<kCols>(srow, cc + 1)) = o[1];
+              }
+              const float mg = vb ? fmaxf(__low2float(m2), __high2float(m2)) : 0.0f;
+              run_max[c * (CW / 16) + g] = fmaxf(run_max[c * (CW / 16) + g], mg);
+            }
+            continue;
           }
           // the whole chunk exists and its rows allow 16-byte accesses: packed path (warp-uniform)
           const bool packed = oc_c + CW <= p.oc && p.out_vec && (!kRes || p.res_vec);
@@ -1051,6 +1257,18 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
         }
       }
       }  // per-tensor
+      if (staged) {
+        // the group's box is complete once all four warps pass the barrier; the issuer's wait
+        // before it guarantees that the previous tile's store has read the other buffer
+        fence_proxy_async_smem();
+        if (st_issuer) bulk_wait_read_all();
+        named_bar_sync(2 + sgroup, 128);
+        if (st_issuer && n0 + col0 < p.oc) {  // a column block past the last channel has nothing to store
+          tma_store_4d(&p.out_map, sbuf, n0 + col0, (r % p.tiles_w) * p.tw, (r / p.tiles_w) * p.th * p.mblocks, img);
+          bulk_commit_group();
+        }
+        ++jj;
+      }
       if (p.amax_out != nullptr && !p.contiguous) {
         // this tile's maxima: warp max, then shared max over the four lane quadrants; the last
         // quadrant to arrive at this (ring slot, column block) issues the global atomics
@@ -1081,6 +1299,7 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
       }
     }
     if (p.amax_out != nullptr && p.contiguous && run_key >= 0) flush_amax();
+    if (st_issuer) bulk_wait_all();  // the last boxes are written before the CTA's shared memory goes away
   }
 
   tc_fence_before();

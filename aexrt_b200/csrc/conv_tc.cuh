@@ -241,6 +241,8 @@ __device__ __forceinline__ void amax_commit(const ConvTcParams& p, float m, int 
 template <bool kF16, bool kPG, int BN>
 __global__ void __launch_bounds__(kConvThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap act_map, const ConvTcParams p) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   constexpr int kHalf = BN / 2;                  // columns per epilogue warp
   constexpr int CW = kHalf >= 16 ? 16 : 8;       // columns per TMEM load
   constexpr int kChunks = kHalf / CW;

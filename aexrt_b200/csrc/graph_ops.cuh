@@ -8,6 +8,7 @@
 // Both ops max |y| per (image, 16-channel group) into the output buffer's amax
 // slots when the output feeds an int8 conv.
 #pragma once
+#include "ptx.cuh"
 #include <cuda_fp16.h>
 
 #include <cstdint>
@@ -43,6 +44,8 @@ __device__ __forceinline__ void store_amax(uint32_t* amax, int amax_stride, int 
 __global__ void maxpool_nhwc_kernel(const GraphParts in, int n, int h, int w, int c, int k, int s, int pad, int oh,
                                     int ow, __half* __restrict__ out, int out_ldc, uint32_t* __restrict__ amax,
                                     int amax_stride) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   const long total = static_cast<long>(n) * oh * ow * c;
   const long idx = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= total) return;
@@ -68,6 +71,8 @@ __global__ void maxpool_nhwc_kernel(const GraphParts in, int n, int h, int w, in
 // out = a + b (fp32 sum of the fp16 operands, rounded to fp16), same n x h x w x c shape.
 __global__ void add_nhwc_kernel(const GraphParts a, const GraphParts b, int n, int h, int w, int c,
                                 __half* __restrict__ out, int out_ldc, uint32_t* __restrict__ amax, int amax_stride) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   const long total = static_cast<long>(n) * h * w * c;
   const long idx = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= total) return;

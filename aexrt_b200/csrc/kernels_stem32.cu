@@ -1,5 +1,6 @@
 // Instances of the image-stem conv (stem.cuh) for 32 output channels: the two-pixel form.
 #include "kernels.cuh"
+#include "launch.cuh"
 
 namespace aexrt {
 namespace {
@@ -7,8 +8,8 @@ template <bool SILU, typename T, int S>
 void go(const void* images, int n, int h, int w, int oh, int ow, __half* out, int out_ldc, int out_coff,
         uint32_t* amax, int amax_stride, int amax_goff, const StemWeights& wt, cudaStream_t st) {
   const dim3 grid((oh * ((ow + 1) / 2) + 255) / 256, n);
-  stem_pair_kernel<32, SILU, T, S><<<grid, 256, 0, st>>>(static_cast<const T*>(images), h, w, oh, ow, out, out_ldc,
-                                                         out_coff, amax, amax_stride, amax_goff, wt);
+  launch_kernel(stem_pair_kernel<32, SILU, T, S>, dim3(grid), dim3(256), 0, st,
+      static_cast<const T*>(images), h, w, oh, ow, out, out_ldc, out_coff, amax, amax_stride, amax_goff, wt);
 }
 
 template <bool SILU, typename T>

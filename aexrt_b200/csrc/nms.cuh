@@ -37,6 +37,7 @@
 // den * thr * (1 +- 2^-20) (each off by at most 2^-23 relative) already decide
 // fl(inter / den) > thr the same way.
 #pragma once
+#include "ptx.cuh"
 #include <cstdint>
 
 namespace aexrt {
@@ -89,6 +90,8 @@ __device__ __forceinline__ uint32_t nms_orderable(float f) {
 }
 
 __global__ void __launch_bounds__(kNmsThreads) yolo_nms_kernel(const NmsParams p) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   extern __shared__ __align__(16) unsigned char nms_smem[];
   const int MC = p.max_cand;
   const int MCe = (MC + 1) & ~1;  // array stride: keeps `key` 8-byte aligned

@@ -29,6 +29,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization (launch.cuh) may start while the
+// kernel before it on the stream still runs.  grid_dep_wait() blocks until that grid has
+// completed and its writes are visible; every kernel calls it before its first access to memory
+// another kernel writes or reads, and before it can exit, so that a grid's completion implies its
+// predecessors' (for an ordinary launch it returns at once).  grid_dep_launch() lets the next
+// kernel start once every CTA of this grid has issued it or exited.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -130,6 +140,20 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   return d;
 }
 
+// Two int32 accumulators -> an fp32 pair, exactly.  kSmall (every |v| <= 2^22): the float whose
+// bits are those of 1.5*2^23 plus v equals 1.5*2^23 + v (v only moves the low mantissa bits), and
+// subtracting 1.5*2^23 is exact; two integer adds and one packed add on full-rate pipes replace two
+// int-to-float conversions on the quarter-rate conversion pipe.  Otherwise plain conversions.
+template <bool kSmall>
+__device__ __forceinline__ uint64_t acc2_to_f2(uint32_t a, uint32_t b) {
+  if constexpr (kSmall) {
+    return f2_add(f2_pack(__uint_as_float(a + 0x4B400000u), __uint_as_float(b + 0x4B400000u)),
+                  f2_pack(-12582912.0f, -12582912.0f));
+  } else {
+    return f2_pack(static_cast<float>(static_cast<int32_t>(a)), static_cast<float>(static_cast<int32_t>(b)));
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -158,6 +182,27 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, u
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
       : "memory");
+}
+
+// Tiled TMA store shared -> global of a 4-D box (bulk-group completion).  The innermost
+// coordinate times the element size is a multiple of 16 bytes and no coordinate is negative;
+// elements outside the tensor are not written.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk group of this thread has finished reading its shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until every committed bulk group of this thread has completed (its global writes done).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) reads.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Named barrier `id` over `threads` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // Non-tensor bulk copy global -> shared (16-byte aligned addresses, size % 16 == 0).

@@ -5,6 +5,7 @@
 // whole tensor (never one block per channel group, which is the reference's
 // "grid collapse" the block-split amax fixed, runtime.cpp:3226-3231).
 #pragma once
+#include "ptx.cuh"
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -25,6 +26,8 @@ namespace aexrt {
 // (`store`, one block per strip) so that no clearing pass is needed.
 __global__ void amax_nchw_f16_kernel(const __half* __restrict__ x, int c, int hw, int groups, int chunk,
                                      uint32_t* __restrict__ amax_g, int store) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   const int g = blockIdx.y;
   const int n = blockIdx.z;
   const int c0 = g * 16;
@@ -89,6 +92,8 @@ __global__ void amax_nchw_f16_kernel(const __half* __restrict__ x, int c, int hw
 // memory so each block issues one global atomic per group it touched.
 __global__ void amax_nhwc_f16_kernel(const __half* __restrict__ x, int hw, int c, int ldc, int coff, int groups,
                                      int pix_per_block, uint32_t* __restrict__ amax_g, int amax_stride) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   extern __shared__ uint32_t gmax[];
   const int n = blockIdx.y;
   for (int i = threadIdx.x; i < groups; i += blockDim.x) gmax[i] = 0u;
@@ -165,6 +170,8 @@ __device__ __forceinline__ float load_src(const QuantSrc& s, int n, int h, int w
 // int8 codes of one 16-channel slab per thread: q = round_half_even(x * (127/amax)),
 // low byte kept with no clamp, zero when amax <= 0 (runtime.cpp:3333-3344).
 __global__ void quantize_i8_kernel(const QuantParams p) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   const int slab = blockIdx.y;
   const int n = blockIdx.z;
   __shared__ float s_mult;
@@ -234,6 +241,8 @@ __global__ void quantize_i8_kernel(const QuantParams p) {
 
 // fp16 repack into 8-channel slabs for the fp16 convs (no scaling).
 __global__ void pack_f16_kernel(const QuantParams p) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   const int slab = blockIdx.y;
   const int n = blockIdx.z;
   const int pix = blockIdx.x * blockDim.x + threadIdx.x;
@@ -351,6 +360,8 @@ inline int rows_channel_groups(const QuantParams& q, bool i8) {
 // consumer the column-parity-split position from the table.
 template <bool kI8, bool kLinear>
 __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p, int pw, int groups) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   __shared__ float s_mult[kMaxSlabs];
   __shared__ float s_red[2];
   __shared__ int2 s_pix[8][kRowsMaxPixPerWarp];  // per pixel: (row << 16 | column), destination pixel (-1: none)
@@ -459,6 +470,8 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p,
 // 16-byte pixel rows (stride-2 consumers: into the column-parity-split layout).
 __global__ void __launch_bounds__(256) pack_nchw_f32_kernel(const float* __restrict__ x, int c, int h, int w, int hp,
                                                           int wp, int split, __half* __restrict__ out) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   const int n = blockIdx.y;
   const int quads_per_row = (wp + 3) / 4;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
@@ -538,6 +551,8 @@ __device__ __forceinline__ void quantize_nchw_words(const uint2 (&v)[16], float 
 }
 
 __global__ void __launch_bounds__(256) quantize_nchw_kernel(const QuantParams p) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   __shared__ float s_mult[kMaxSlabs];
   __shared__ float s_red[2];
   const int slab = blockIdx.y;

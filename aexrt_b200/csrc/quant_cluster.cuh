@@ -69,6 +69,8 @@ __global__ void __launch_bounds__(kClusterQuantThreads, 2)
     amax_quant_cluster_kernel(const __half* __restrict__ x, int c, int hw, int slices, int mode,
                               uint8_t* __restrict__ q, float* __restrict__ rec, uint32_t* __restrict__ amax_g,
                               int groups_total, int group_offset, uint32_t* status, long long wait_limit) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   extern __shared__ __align__(128) unsigned char strip_smem[];
   __shared__ __align__(8) uint64_t bar[kClusterQuantChunks];
   __shared__ uint32_t s_warp[32];

@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(256) stem_conv_kernel(const TIn* __restrict__ 
                                                         int stride, __half* __restrict__ out, int out_ldc,
                                                         int out_coff, uint32_t* __restrict__ amax, int amax_stride,
                                                         int amax_goff, const __grid_constant__ StemWeights wt) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   static_assert(OC % 16 == 0 && OC <= kStemMaxOC, "OC must be a multiple of 16, at most 64");
   constexpr int kGroups = OC / 16;
   __shared__ uint32_t s_amax[kGroups];
@@ -121,6 +123,8 @@ __global__ void __launch_bounds__(256, 3) stem_pair_kernel(const TIn* __restrict
                                                            __half* __restrict__ out, int out_ldc, int out_coff,
                                                            uint32_t* __restrict__ amax, int amax_stride, int amax_goff,
                                                            const __grid_constant__ StemWeights wt) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   static_assert(OC % 16 == 0 && OC <= kStemPairMaxOC, "OC must be 16 or 32");
   constexpr int kGroups = OC / 16;
   constexpr int kCols = S + 3;

@@ -2,6 +2,7 @@
 // max-pool cascade and the detect-head decode (DFL softmax + anchor decode +
 // class sigmoid).  Both are small HBM-bound element passes.
 #pragma once
+#include "ptx.cuh"
 #include <cuda_fp16.h>
 
 #include <cstdint>
@@ -16,6 +17,8 @@ namespace aexrt {
 __global__ void sppf_pool_kernel(const __half* __restrict__ x, int n, int h, int w, int c, int ldc, int coff,
                                  __half* __restrict__ out, int out_ldc, int out_coff, uint32_t* __restrict__ amax,
                                  int amax_stride, int amax_goff) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   const int vec = c / 8;
   const long total = static_cast<long>(n) * h * w * vec;
   const long idx = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -72,6 +75,8 @@ __global__ void __launch_bounds__(256) sppf_smem_kernel(const __half* __restrict
                                                        int coff, int cb, __half* __restrict__ out, int out_ldc,
                                                        int out_coff, uint32_t* __restrict__ amax, int amax_stride,
                                                        int amax_goff) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   extern __shared__ __align__(16) __half sm[];  // [4][h*w][cb]: input, then row maxima for 5, 9, 13
   __shared__ uint32_t s_amax[3 * 16];           // cb <= 256 -> <= 16 groups per slice
   const int n = blockIdx.y;
@@ -163,6 +168,8 @@ struct DecodeParams {
 // (softmax over reg_max bins), distance -> box around the anchor centre, and a
 // sigmoid per class.  Matches the anchor-free YOLOv8 head (ultralytics Detect).
 __global__ void yolo_decode_kernel(const DecodeParams p) {
+  grid_dep_launch();
+  grid_dep_wait();  // programmatic dependent launch: see ptx.cuh
   const long idx = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= static_cast<long>(p.n) * p.anchors) return;
   const int img = static_cast<int>(idx / p.anchors);

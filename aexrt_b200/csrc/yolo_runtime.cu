@@ -46,6 +46,7 @@
 #include "../../include/aexrt_yolo.h"
 #include "engine_file.h"
 #include "graph_ops.cuh"
+#include "launch.cuh"
 
 using aexrt::engine::Command;
 using aexrt::engine::Engine;
@@ -979,7 +980,8 @@ bool launch_forward(AexrtYoloModel* m, cudaStream_t st, std::vector<std::pair<cu
         int astride = 0;
         uint32_t* am = amax_of(m, op.out, &astride);
         const long total = long(n) * op.out_h * op.out_w * op.c;
-        aexrt::maxpool_nhwc_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(
+        aexrt::launch_kernel(aexrt::maxpool_nhwc_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256),
+            0, st,
             graph_parts(m, op.a), n, op.in_h, op.in_w, op.c, op.pool_k, op.pool_s, op.pool_p, op.out_h, op.out_w,
             buf_ptr(m, op.out), op.c, am, astride);
         ok = cudaGetLastError() == cudaSuccess;
@@ -989,7 +991,8 @@ bool launch_forward(AexrtYoloModel* m, cudaStream_t st, std::vector<std::pair<cu
         int astride = 0;
         uint32_t* am = amax_of(m, op.out, &astride);
         const long total = long(n) * op.out_h * op.out_w * op.c;
-        aexrt::add_nhwc_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(
+        aexrt::launch_kernel(aexrt::add_nhwc_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0,
+            st,
             graph_parts(m, op.a), graph_parts(m, op.b), n, op.out_h, op.out_w, op.c, buf_ptr(m, op.out), op.c, am,
             astride);
         ok = cudaGetLastError() == cudaSuccess;

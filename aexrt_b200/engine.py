@@ -32,7 +32,7 @@ import numpy as np
 
 from . import _native, ops
 from ._native import AexrtB200ActSource, AexrtB200DecodeLevel, check
-from .yolo import ConvCmd, DecodeCmd, Part, SppfCmd, YoloProgram
+from .yolo import ConvCmd, DecodeCmd, DwConvCmd, Part, PsaAttnCmd, SppfCmd, YoloProgram
 
 
 def _torch():
@@ -56,7 +56,8 @@ class CompiledYolo:
     """One program compiled for one batch size on the current CUDA device."""
 
     def __init__(self, program: YoloProgram, batch: int, device=None, block_n: Optional[Dict[str, int]] = None,
-                 image_dtype=None, nms: Optional[NmsConfig] = None, quant_on_load: bool = False):
+                 image_dtype=None, nms: Optional[NmsConfig] = None, quant_on_load: bool = False,
+                 plan_bits: int = 0, programmatic: Optional[bool] = None):
         torch = _torch()
         self.program = program
         self.batch = batch
@@ -89,15 +90,26 @@ class CompiledYolo:
         self.output = torch.zeros((n, 4 + p.nc, p.anchors), dtype=torch.float32, device=self.device)
         self.nms = nms
         self.quant_on_load = quant_on_load
+        # programmatic dependent launch (aexrt_b200_set_launch_flags): each kernel's launch and set-up
+        # overlap the previous kernel; by default for small batches, whose grids leave most SMs idle
+        self.programmatic = batch <= 8 if programmatic is None else bool(programmatic)
         self.det_buf = self._new_det_buf()
         # ---- plans and per-command scratch
         self.steps: List[tuple] = []
         self.plans: Dict[str, ops.ConvPlan] = {}
         for c in p.commands:
             if isinstance(c, ConvCmd):
-                self._compile_conv(c, (block_n or {}).get(c.name, c.block_n))
+                # plan_bits: tuning bits above the tile (aexrt_b200_conv_plan_create) for every conv
+                self._compile_conv(c, (block_n or {}).get(c.name, c.block_n) | plan_bits)
             elif isinstance(c, SppfCmd):
                 self.steps.append(("sppf", c))
+            elif isinstance(c, DwConvCmd):
+                # fp16-rounded weights as [9][c] fp32 (kh-major taps), fp32 bias
+                w9 = c.weight.astype(np.float16).astype(np.float32).reshape(c.c, 9).T.copy()
+                self.steps.append(("dwconv", c, torch.from_numpy(w9).to(self.device),
+                                   torch.from_numpy(c.bias.astype(np.float32)).to(self.device)))
+            elif isinstance(c, PsaAttnCmd):
+                self.steps.append(("attn", c))
             elif isinstance(c, DecodeCmd):
                 self.steps.append(("decode", c))
                 if nms is not None:
@@ -221,6 +233,15 @@ class CompiledYolo:
     def launch(self, stream: int) -> None:
         """Issues every launch of one forward on `stream` (capturable)."""
         lib = self.lib
+        prev = lib.aexrt_b200_get_launch_flags()
+        check(lib.aexrt_b200_set_launch_flags(_native.LAUNCH_PROGRAMMATIC if self.programmatic else 0), "launch flags")
+        try:
+            self._launch(stream)
+        finally:
+            lib.aexrt_b200_set_launch_flags(prev)
+
+    def _launch(self, stream: int) -> None:
+        lib = self.lib
         n = self.batch
         check(lib.aexrt_b200_zero(self.amax_arena.data_ptr(), self.amax_arena.numel() * 4, stream), "zero amax")
         for st in self.steps:
@@ -274,6 +295,26 @@ class CompiledYolo:
                 check(lib.aexrt_b200_sppf_pool(x.data_ptr(), n, v.h, v.w, c.x.channels, x.shape[-1], c.x.coff,
                                                out.data_ptr(), out.shape[-1], c.out[1], am.data_ptr(), am.shape[1],
                                                c.out[1] // 16, stream), "sppf")
+            elif kind == "dwconv":
+                _, c, w9, bias = st
+                x = self.values[c.x.value]
+                out = self.values[c.out[0]]
+                v = self.program.values[c.x.value]
+                g = c.group or c.c
+                check(lib.aexrt_b200_dwconv3x3_f16(x.data_ptr(), n, v.h, v.w, c.c, x.shape[-1], c.x.coff, g,
+                                                   c.group_stride or g, c.group_off, w9.data_ptr(), bias.data_ptr(),
+                                                   c.s, int(c.silu), out.data_ptr(), out.shape[-1], c.out[1], stream),
+                      f"dwconv {c.name}")
+            elif kind == "attn":
+                c = st[1]
+                qkv, pe, out = self.values[c.qkv.value], self.values[c.pe.value], self.values[c.out[0]]
+                v = self.program.values[c.qkv.value]
+                am = self._amax_view(c.out[0]) if c.out[0] in self.needs_amax else None
+                check(lib.aexrt_b200_psa_attention_f16(
+                    qkv.data_ptr(), n, v.h, v.w, qkv.shape[-1], c.qkv.coff, c.heads, c.key_dim, c.head_dim, c.scale,
+                    pe.data_ptr(), pe.shape[-1], c.pe.coff, out.data_ptr(), out.shape[-1], c.out[1],
+                    am.data_ptr() if am is not None else None, am.shape[1] if am is not None else 0,
+                    c.out[1] // 16, stream), f"attention {c.name}")
             elif kind == "decode":
                 c = st[1]
                 lv = (AexrtB200DecodeLevel * len(c.levels))()

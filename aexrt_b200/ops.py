@@ -204,12 +204,13 @@ class PlanInfo:
     pitch: int = 0
     image_input: int = 0
     quant_on_load: int = 0
+    staged_out: int = 0
 
     @staticmethod
     def from_c(i: AexrtB200ConvPlanInfo) -> "PlanInfo":
         return PlanInfo(i.kernel_id, i.flags, i.kind, bool(i.is_f16), i.tile_w, i.tile_h, i.block_n, i.k_slots,
                         i.stages, i.smem_bytes, i.grid_m, i.grid_n, i.in_hp, i.in_wp, i.grid, i.variant, i.pitch,
-                        i.image_input, i.quant_on_load)
+                        i.image_input, i.quant_on_load, i.staged_out)
 
 
 class ConvPlan:

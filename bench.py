@@ -42,6 +42,11 @@ MODELS = {
     "yolov8s-640": ("build_yolov8s", "W8A8 YOLOv8s-640 images/s",
                     "yolov8s-640 W8A8 forward (int8 backbone+neck, fp16 head, nc=80, DFL decode, NMS + top-k)",
                     640, 80, 512, "strong"),
+    # YOLOv11s-320 (C3k2, SPPF, C2PSA; W8A8 except the head, the depthwise convs and the
+    # attention core), batch sweep 1 / 8 / 64 on one GPU (--batch)
+    "yolov11s-320": ("build_yolov11s", "W8A8 YOLOv11s-320 images/s",
+                     "yolov11s-320 W8A8 forward (int8 C3k2/SPPF/C2PSA convs, fp16 head + depthwise + attention, "
+                     "nc=80, DFL decode, NMS + top-k)", 320, 80, None, "weak"),
 }
 L2_BYTES = 126 * 1024 * 1024
 # DRAM read + write bytes of the 44 W8A8 conv launches of one forward, per image, from one ncu
@@ -59,6 +64,10 @@ def parse_args():
                          "64 for the layer workloads)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--programmatic", default="auto", choices=["auto", "on", "off"],
+                    help="model workloads: programmatic dependent launch (auto: the engine's choice by batch)")
+    ap.add_argument("--quant-on-load", action="store_true",
+                    help="model workloads: int8 convs quantize their fp16 sources on load (no separate quantize)")
     ap.add_argument("--cpu-sample", type=int, default=None,
                     help="images in the CPU baseline sample (default 160 for yolov8n-320, 8 for yolov8s-640: "
                          "about 12-25 s)")
@@ -69,6 +78,8 @@ def parse_args():
     ap.add_argument("--mode", type=int, default=0, help="layer workloads: 0 per-tensor, 1 pg16 scales")
     ap.add_argument("--order", type=int, default=0,
                     help="layer workloads: halo tile order (0 auto, 1 strided, 2 contiguous)")
+    ap.add_argument("--plan-bits", type=lambda s: int(s, 0), default=0,
+                    help="extra plan tuning bits for every conv (block_n bits 16-31, e.g. 0x10000000 direct stores)")
     ap.add_argument("--amax-out", action="store_true",
                     help="layer workloads: the conv also maxes |y| per 16-channel group for the next layer")
     ap.add_argument("--engine", default=None,
@@ -136,7 +147,7 @@ def run_layer(args):
         b = rng.normal(0, 0.1, oc).astype(np.float32)
         codes, scale = ops.quantize_conv_weight_int8(wt)
         plan = ops.ConvPlan.int8(n, ic, h, w, oc, k, s, codes, scale, b, pg16=bool(args.mode),
-                                 block_n=args.order << 20)
+                                 block_n=(args.order << 20) | args.plan_bits)
         x = torch.from_numpy((lambda z: z / (1 + np.exp(-z)))(rng.standard_normal((n, ic, h, w)).astype(np.float32))
                              .astype(np.float16)).cuda()
         amax = ops.act_amax(x, ops.LAYOUT_NCHW_F16)
@@ -395,7 +406,9 @@ def run_ours(args):
         tb = torch.tensor([B], device="cuda")
         dist.all_reduce(tb)
         total = int(tb.item())  # images of one step over all ranks
-    eng = engine.CompiledYolo(program, B, nms=engine.NmsConfig())
+    eng = engine.CompiledYolo(program, B, nms=engine.NmsConfig(), quant_on_load=args.quant_on_load,
+                              plan_bits=args.plan_bits,
+                              programmatic=None if args.programmatic == "auto" else args.programmatic == "on")
     # fp16 images, as BASELINE's config feeds them (uniform[0,1]); image k of the job from seed 1000 + k
     host_in = torch.from_numpy(np.stack([np.random.default_rng(1000 + start + k).uniform(0, 1, (3, imgsz, imgsz))
                                          for k in range(B)]).astype(np.float16)).pin_memory()
@@ -451,6 +464,30 @@ def run_ours(args):
                "h2d_bytes_per_step": int(host_in.numel() * host_in.element_size()),
                "d2h_bytes_per_step": int(host_out.numel() * host_out.element_size()),
                "pipeline": "double-buffered: upload k+1 and read-back k-1 overlap forward k"}
+    latency = None
+    if B <= 8:
+        # small batches: synchronous latency of one batch through the same graph, the upload of its
+        # images from pinned memory and the read-back of its detections inside each timed step
+        # (one batch in flight, as an interactive caller runs it)
+        dev_out = eng.det_buf
+
+        def one_batch():
+            eng.images.copy_(host_in, non_blocking=True)
+            eng.graph.replay()
+            host_out.copy_(dev_out, non_blocking=True)
+            stream.synchronize()
+
+        for _ in range(10):
+            one_batch()
+        ts = []
+        for _ in range(max(20, args.steps)):
+            t0 = time.perf_counter()
+            one_batch()
+            ts.append(time.perf_counter() - t0)
+        ts.sort()
+        latency = {"ms_per_batch_median": ts[len(ts) // 2] * 1e3, "ms_per_batch_p90": ts[int(len(ts) * 0.9)] * 1e3,
+                   "batch": B, "device_ms_per_step": t_dev / args.steps * 1e3,
+                   "how": "host wall clock around upload + graph replay + read-back + synchronize, one batch in flight"}
     status = eng.status()
     # roofline of the dominant kernel (W8A8 conv), measured per launch with CUDA events
     rf = conv_roofline(eng, torch, stream.cuda_stream)
@@ -475,7 +512,10 @@ def run_ours(args):
             "config": {"workload": workload, "global_batch": total, "per_gpu_batch": B, "imgsz": imgsz, "nc": nc,
                        "parallelism": f"dp{world} (independent replicas)",
                        "l2": f"inputs larger than L2 ({B * 3 * imgsz * imgsz * 2 / 1e6:.0f} MB of fp16 images "
-                             "per step)"},
+                             "per step)",
+                       **({"quant_on_load": True} if args.quant_on_load else {}),
+                       "programmatic_launch": eng.programmatic,
+                       **({"plan_bits": hex(args.plan_bits)} if args.plan_bits else {})},
             "e2e": e2e,
             "gpu_launches": eng.launches_per_run * args.steps,
             "roofline": {"bound": "hbm", "achieved": rf["bytes"] / rf["time_s"] / 1e9, "peak": hbm, "unit": "GB/s",
@@ -492,6 +532,7 @@ def run_ours(args):
                          "tensor_peak_source": f"2 x {src} bf16 dense ({bf16} TFLOP/s), MEASURED_PEAKS.json",
                          "conv_ms_per_step": rf["time_s"] * 1e3, "conv_launches": rf["launches"]},
             "cpu_baseline": cpu,
+            **({"latency": latency} if latency else {}),
             "clocks": clocks,
             "status": status,
         }

@@ -97,12 +97,25 @@ typedef struct AexrtB200ConvPlanInfo {
     uint32_t pitch;            /* halo variant: M rows per tile row */
     uint32_t image_input;      /* 1: aexrt_b200_conv_f16_image accepts this plan */
     uint32_t quant_on_load;    /* 1: aexrt_b200_conv_w8a8_sources accepts this plan */
+    uint32_t staged_out;       /* halo variant: output tiles staged in shared memory for a TMA store
+                                  (buffers per epilogue group; 0: direct stores) */
 } AexrtB200ConvPlanInfo;
 
 /* ---------------------------------------------------------------- library */
 uint32_t aexrt_b200_abi_version(void);
 /* Thread-local message of the last failed call on this thread ("" if none). */
 const char* aexrt_b200_get_last_error(void);
+/* Launch flags of the calling thread, applied to every later launch it makes
+ * through this library (the reference has no counterpart: D3D12 command lists
+ * have no dependent-launch overlap).  AEXRT_B200_LAUNCH_PROGRAMMATIC: kernels
+ * are launched with programmatic stream serialization, so that each one's
+ * launch and set-up (barrier init, TMEM allocation, weight loads) overlap the
+ * kernel before it; every kernel waits for its predecessor's grid before it
+ * touches activations.  Meant for small batches, where grids use few SMs; it
+ * also applies inside CUDA graph capture.  Returns 0 for unknown flags. */
+#define AEXRT_B200_LAUNCH_PROGRAMMATIC 1u
+int aexrt_b200_set_launch_flags(uint32_t flags);
+uint32_t aexrt_b200_get_launch_flags(void);
 /* Number of visible CUDA devices (0 when no driver or GPU is present). */
 int aexrt_b200_device_count(void);
 
@@ -153,7 +166,10 @@ int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t 
  * the tile (bits 0-15): bits 16-19 kernel variant (0 auto, 1 slot streaming,
  * 2 halo tile), bits 20-23 halo tile order (0 auto, 1 strided over CTAs,
  * 2 one contiguous run per CTA), bits 24-27 the most M blocks stacked in one
- * halo super-tile (0 auto, 1 none).  For int8 plans the results are identical
+ * halo super-tile (0 auto, 1 none), bit 28 halo epilogue stores each output
+ * pixel directly, bit 29 it stages every tile in shared memory for one TMA
+ * tensor store (default: staged for 1x1 convs only).  For int8 plans the
+ * results are identical
  * for every choice (integer accumulation); an fp16 plan whose choice moves it
  * between the halo and slot kernels sums K in another order, which can change
  * the last bit of an fp16 output.
@@ -283,6 +299,31 @@ int aexrt_b200_conv_w8a8_sources(const AexrtB200ConvPlan* plan, const AexrtB200A
 int aexrt_b200_sppf_pool(const void* x, uint32_t n, uint32_t h, uint32_t w, uint32_t c, uint32_t ldc, uint32_t coff,
                          void* out, uint32_t out_ldc, uint32_t out_coff, uint32_t* amax, uint32_t amax_stride,
                          uint32_t amax_goff, void* stream);
+
+/* ---------------------------------------------------------------- YOLOv11 fp16 ops
+ * Depthwise 3x3 conv (pad 1, stride 1 or 2) on an NHWC fp16 slice: fp32
+ * accumulation from the bias, optional SiLU, fp16 out.  The reference runs
+ * grouped convs on its generic fp16 conv path (its int8 guard refuses
+ * groups != 1, native/aexrt_d3d12_runtime.cpp:9404).  Output channel k reads
+ * input channel coff + (k / grp) * grp_stride + grp_off + k % grp (grp = 0:
+ * the plain slice).  w9: device [9][c] fp32 (kh-major taps), bias: device [c]
+ * fp32; c, grp, strides and offsets multiples of 8. */
+int aexrt_b200_dwconv3x3_f16(const void* x, uint32_t n, uint32_t h, uint32_t w, uint32_t c, uint32_t ldc,
+                             uint32_t coff, uint32_t grp, uint32_t grp_stride, uint32_t grp_off, const float* w9,
+                             const float* bias, uint32_t stride, uint32_t silu, void* out, uint32_t out_ldc,
+                             uint32_t out_coff, void* stream);
+
+/* C2PSA multi-head self-attention over an h x w map (the reference lowers it
+ * to MATMUL / SOFTMAX commands, runtime.cpp:17305-17307, 20195, 20305): per
+ * image and head, q, k (key_dim channels) and v (head_dim = 64) are that
+ * head's consecutive channels of the qkv slice; out = v @ softmax(q^T k *
+ * scale)^T + pe (the positional-encoding slice), fp16, with per-16-channel
+ * |out| maxima max-ed into amax slots (NULL: none) for an int8 consumer.
+ * h * w must fit one CTA's shared memory (up to 20 x 20 at key_dim 32). */
+int aexrt_b200_psa_attention_f16(const void* qkv, uint32_t n, uint32_t h, uint32_t w, uint32_t ldc, uint32_t coff,
+                                 uint32_t heads, uint32_t key_dim, uint32_t head_dim, float scale, const void* pe,
+                                 uint32_t pe_ldc, uint32_t pe_coff, void* out, uint32_t out_ldc, uint32_t out_coff,
+                                 uint32_t* amax, uint32_t amax_stride, uint32_t amax_goff, void* stream);
 
 /* One detect level: box-distribution logits (4*reg_max channels) and class
  * logits (nc channels), both fp16 NHWC slices, with the level's stride. */

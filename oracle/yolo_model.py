@@ -13,7 +13,13 @@ Ops restated here besides oracle.w8a8:
 * nearest 2x upsample (RESIZE) and channel concat (CONCAT);
 * detect decode: DFL softmax expectation over reg_max bins, distance -> box
   around the anchor centre, class sigmoid; the reference post-processes this
-  output0 layout in src/aexrt/yolo.py:92-138.
+  output0 layout in src/aexrt/yolo.py:92-138;
+* YOLOv11's fp16 ops: the depthwise 3x3 conv (a grouped CONV in the reference,
+  refused by its int8 guard, native/aexrt_d3d12_runtime.cpp:9404) and the C2PSA
+  attention core (MATMUL / SOFTMAX commands in the reference,
+  runtime.cpp:17305-17307): softmax(q^T k * key_dim^-0.5) applied to v, plus the
+  positional encoding, per head, as the public ultralytics Attention module
+  defines it.
 """
 from __future__ import annotations
 
@@ -50,6 +56,41 @@ def conv_cmd(c, x: np.ndarray, residual: Optional[np.ndarray]) -> dict:
     if residual is not None:
         y = (y + residual.astype(F32)).astype(F32)
     return {"y32": y, "y": y.astype(np.float16)}
+
+
+def dwconv3x3(c, x: np.ndarray) -> np.ndarray:
+    """Depthwise 3x3 conv (pad 1, stride c.s) of NCHW `x` (already gathered per c.in_channel) with
+    fp16-rounded operands, fp32 accumulation, optional SiLU; returns fp32."""
+    xf = x.astype(np.float16).astype(F32)
+    wf = c.weight.astype(np.float16).astype(F32).reshape(c.c, 3, 3)
+    n, ch, h, w = xf.shape
+    oh, owd = (h - 1) // c.s + 1, (w - 1) // c.s + 1
+    pad = np.zeros((n, ch, h + 2, w + 2), F32)
+    pad[:, :, 1:1 + h, 1:1 + w] = xf
+    y = np.broadcast_to(c.bias.astype(F32).reshape(1, ch, 1, 1), (n, ch, oh, owd)).copy()
+    for kh in range(3):
+        for kw in range(3):
+            tap = pad[:, :, kh:kh + (oh - 1) * c.s + 1:c.s, kw:kw + (owd - 1) * c.s + 1:c.s]
+            y = (y + tap * wf[:, kh, kw].reshape(1, ch, 1, 1)).astype(F32)
+    if c.silu:
+        y = ow.silu_f32(y)
+    return y
+
+
+def psa_attention(c, qkv: np.ndarray, pe: np.ndarray) -> np.ndarray:
+    """C2PSA attention core on NCHW fp16 tensors: per image and head, q, k, v are the head's
+    consecutive (key_dim, key_dim, head_dim) qkv channels over the N = H*W pixels;
+    out = v @ softmax(q^T k * scale)^T + pe, computed in fp32 (returns fp32)."""
+    n, _, h, w = qkv.shape
+    nh, kd, hd = c.heads, c.key_dim, c.head_dim
+    t = qkv.astype(F32).reshape(n, nh, 2 * kd + hd, h * w)
+    q, k, v = t[:, :, :kd], t[:, :, kd:2 * kd], t[:, :, 2 * kd:]
+    s = np.einsum("bhdi,bhdj->bhij", q, k).astype(F32) * F32(c.scale)
+    s = s - s.max(axis=-1, keepdims=True)
+    e = np.exp(s).astype(F32)
+    a = (e / e.sum(axis=-1, keepdims=True)).astype(F32)
+    o = np.einsum("bhcj,bhij->bhci", v, a).astype(F32).reshape(n, nh * hd, h, w)
+    return (o + pe.astype(F32)).astype(F32)
 
 
 def sppf_pool(x: np.ndarray) -> np.ndarray:
@@ -99,7 +140,7 @@ def run_program(program, images: np.ndarray, keep: bool = False) -> dict:
         if name != "images":
             values[name] = np.zeros((n, v.channels, v.h, v.w), np.float16)
     out0 = None
-    from aexrt_b200.yolo import ConvCmd, DecodeCmd, SppfCmd  # the program's command classes
+    from aexrt_b200.yolo import ConvCmd, DecodeCmd, DwConvCmd, PsaAttnCmd, SppfCmd  # the program's command classes
 
     for c in program.commands:
         if isinstance(c, ConvCmd):
@@ -112,6 +153,15 @@ def run_program(program, images: np.ndarray, keep: bool = False) -> dict:
         elif isinstance(c, SppfCmd):
             x = values[c.x.value][:, c.x.coff:c.x.coff + c.x.channels]
             values[c.out[0]][:, c.out[1]:c.out[1] + 3 * c.x.channels] = sppf_pool(x)
+        elif isinstance(c, DwConvCmd):
+            src = values[c.x.value]
+            idx = [c.in_channel(k) for k in range(c.c)]
+            values[c.out[0]][:, c.out[1]:c.out[1] + c.c] = dwconv3x3(c, src[:, idx]).astype(np.float16)
+        elif isinstance(c, PsaAttnCmd):
+            qkv = values[c.qkv.value][:, c.qkv.coff:c.qkv.coff + c.qkv.channels]
+            pe = values[c.pe.value][:, c.pe.coff:c.pe.coff + c.pe.channels]
+            values[c.out[0]][:, c.out[1]:c.out[1] + c.heads * c.head_dim] = \
+                psa_attention(c, qkv, pe).astype(np.float16)
         elif isinstance(c, DecodeCmd):
             out0 = decode(c.levels, values, c.nc, c.reg_max)
     res = {"output0": out0}

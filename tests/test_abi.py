@@ -32,14 +32,14 @@ def test_conv_desc_layout_matches_reference():
 
 
 def test_plan_info_struct_matches_header():
-    # 20 uint32 fields (struct_size .. quant_on_load); the Python view carries every one but struct_size
-    assert ctypes.sizeof(_native.AexrtB200ConvPlanInfo) == 20 * 4
+    # 21 uint32 fields (struct_size .. staged_out); the Python view carries every one but struct_size
+    assert ctypes.sizeof(_native.AexrtB200ConvPlanInfo) == 21 * 4
     i = _native.AexrtB200ConvPlanInfo()
     for k, (name, _) in enumerate(_native.AexrtB200ConvPlanInfo._fields_):
         setattr(i, name, k + 1)
     info = ops.PlanInfo.from_c(i)
     assert info.kernel_id == 2 and info.in_wp == 15 and info.grid == 16 and info.image_input == 19
-    assert info.quant_on_load == 20
+    assert info.quant_on_load == 20 and info.staged_out == 21
 
 
 def test_c_weight_quantizer_matches_reference_payloads(golden_dir):

@@ -518,3 +518,65 @@ def test_quantize_on_load_equals_quantize_then_conv(n, ic, h, w, oc, k, s, split
         results.append((out.cpu(), dump.cpu(), amax_out.cpu()))
     for a, b in zip(results[0], results[1]):
         assert torch.equal(a, b)
+
+
+STAGED, DIRECT = 0x20000000, 0x10000000  # plan bits: staged TMA-store epilogue / direct stores
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("n,ic,h,w,oc,k,s,block_n,res,ldc,coff", [
+    (2, 64, 20, 20, 128, 3, 1, 0, False, None, 0),
+    (2, 96, 10, 10, 32, 1, 1, 0, True, None, 0),      # 1x1 with the C2f residual
+    (2, 48, 17, 13, 48, 3, 1, 64, False, 80, 16),     # odd channel count: partial column blocks, slice
+    (2, 32, 20, 18, 64, 3, 2, 0, False, None, 0),     # stride 2
+    (1, 128, 10, 10, 256, 1, 1, 256, False, None, 0),  # BN 256: 128-byte rows (128B swizzle)
+    (2, 16, 80, 80, 16, 3, 1, 0, True, None, 0),      # narrow 3x3: stacked M blocks, tile groups
+    (1, 64, 40, 40, 32, 3, 1, 32, False, 96, 64),     # BN 32 written into a concat buffer
+])
+def test_staged_epilogue_equals_direct_stores(n, ic, h, w, oc, k, s, block_n, res, ldc, coff, mode):
+    """The staged epilogue (swizzled shared-memory boxes, one TMA tensor store per tile and column
+    block) writes exactly the bytes and amax of the direct-store epilogue, both equal to the oracle."""
+    if mode == 1 and (ic % 16 or block_n not in (0, 64, 128) or oc < 64):
+        pytest.skip("pg16 halo plans need 16k input channels and 64 / 128-wide output tiles")
+    rng = np.random.default_rng(ic * 3 + oc + k + s)
+    x = seeded_act(rng, (n, ic, h, w))
+    weight = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    oh, ow_ = (h + 2 * (k // 2) - k) // s + 1, (w + 2 * (k // 2) - k) // s + 1
+    residual = seeded_act(rng, (n, oc, oh, ow_)) if res else None
+    runs = {}
+    for bits in (STAGED, DIRECT):
+        runs[bits] = run_gpu_layer(x, weight, bias, k, s, mode, residual=residual, block_n=block_n | bits,
+                                   out_ldc=ldc, out_coff=coff)
+    st, di = runs[STAGED], runs[DIRECT]
+    assert st["plan"].info.staged_out > 0 and di["plan"].info.staged_out == 0
+    assert np.array_equal(st["out_full"], di["out_full"])
+    assert np.array_equal(st["amax_out"], di["amax_out"])
+    o = ow.conv_w8a8(x, weight, bias, k, s, k // 2, mode=mode, residual=residual)
+    assert np.array_equal(st["acc"], o["acc"])
+    assert np.abs(st["y"].astype(np.float32) - o["y32"]).max() <= TOL
+
+
+@pytest.mark.parametrize("n,ic,h,w,oc,k,silu,block_n", [
+    (2, 64, 20, 20, 64, 3, True, 0),
+    (2, 192, 40, 40, 144, 1, False, 128),   # the fused head logits conv (a partial second tile)
+    (1, 16, 80, 80, 16, 3, True, 16),
+])
+def test_fp16_staged_epilogue_equals_direct_stores(n, ic, h, w, oc, k, silu, block_n):
+    torch = _torch()
+    from aexrt_b200 import ops
+
+    rng = np.random.default_rng(ic + oc + k)
+    xt = torch.from_numpy(rng.uniform(-1, 1, (n, h, w, ic)).astype(np.float16)).cuda()
+    weight = rng.normal(0, 1 / np.sqrt(ic * k * k), (oc, ic, k, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, (oc,)).astype(np.float32)
+    outs = []
+    for bits in (STAGED, DIRECT):
+        plan = ops.ConvPlan.fp16(n, ic, h, w, oc, k, 1, weight, bias, silu=silu, block_n=block_n | bits)
+        am = torch.zeros((n, (oc + 15) // 16), dtype=torch.int32, device="cuda")
+        out = plan.run_nhwc(xt, amax_out=am)
+        torch.cuda.synchronize()
+        assert plan.status() == 0
+        outs.append((plan.info.staged_out, out, am))
+    assert outs[0][0] > 0 and outs[1][0] == 0
+    assert torch.equal(outs[0][1], outs[1][1]) and torch.equal(outs[0][2], outs[1][2])
