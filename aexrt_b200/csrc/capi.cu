@@ -277,10 +277,11 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   const uint32_t variant = (block_n >> 16) & 0xF;  // 0 auto, 1 slot streaming, 2 halo
   const uint32_t order = (block_n >> 20) & 0xF;    // halo tile order: 0 auto, 1 strided, 2 contiguous
   const int mblocks_cap = static_cast<int>((block_n >> 24) & 0xF);  // super-tile M blocks: 0 auto, else at most
-  // staged TMA-store epilogue: bit 28 forces direct stores, bit 29 forces staging; by default only
-  // 1x1 plans stage (measured at batch 64: 1x1 128->128 @40 24.6 against 26.7 us direct, while the
-  // 3x3 layers ran 4-9 % slower staged, their four epilogue warps held in step by the per-tile barrier)
-  const bool direct_store = ((block_n >> 28) & 1u) != 0 || (((block_n >> 29) & 1u) == 0 && d.kernel_h != 1);
+  // staged TMA-store epilogue: bit 29 asks for it, bit 28 forces direct stores (the default).  Measured
+  // at batch 64: 1x1 128->128 @40 24.6 us staged against 26.7 us direct, but the 3x3 layers ran 4-9 %
+  // slower staged (the per-tile barrier holds the four warps of a column block in step), and the
+  // YOLOv8n-320 step at batch 256 was 1.3 % slower even with only its 1x1 convs staged
+  const bool direct_store = ((block_n >> 28) & 1u) != 0 || ((block_n >> 29) & 1u) == 0;
   int sms = 148;
   {
     int dev = 0;
@@ -288,6 +289,13 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   }
   block_n &= 0xFFFF;
   p->bn = choose_bn(oc, p->pg, block_n);
+  if (!block_n) {
+    // small grids (one or a few images): narrower output-channel tiles until the conv spreads over at
+    // least a third of the SMs, so that each CTA loads and multiplies a smaller weight tile (the
+    // latency of a batch-1 layer is one CTA's weight load, MMAs and epilogue)
+    const long m_tiles = static_cast<long>(d.batch) * p->tiles_h * p->tiles_w;
+    while (p->bn > (p->pg ? 64 : 32) && m_tiles * ((oc + p->bn - 1) / p->bn) * 3 < sms) p->bn /= 2;
+  }
   if (!kernel_for(f16, p->pg, p->bn)) {
     fail("unsupported block_n %d", p->bn);
     delete p;
@@ -756,7 +764,12 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     }
     const HaloKernel k = halo_kernel_for(p->f16, p->bn, h.silu != 0, res != nullptr, p->pg, p->mblocks > 1, ql != nullptr);
     if (!k.fn) return fail("no conv kernel instance for this combination (linear fp16 residual, or quantize on load)");
-    launch_kernel(k.fn, dim3(p->grid), dim3(k.threads), p->smem, static_cast<cudaStream_t>(stream), act_map, h);
+    // with programmatic dependent launch, CTAs of this conv may be placed while the previous conv still
+    // runs: more than half of an SM's shared memory keeps two conv CTAs (each owning the SM's TMEM)
+    // off one SM, so that the persistent grid still spreads one CTA per SM
+    const int smem = (aexrt::launch_flags() & aexrt::kLaunchProgrammatic) ? std::max(p->smem, kMaxConvSmem / 2 + 1024)
+                                                                          : p->smem;
+    launch_kernel(k.fn, dim3(p->grid), dim3(k.threads), smem, static_cast<cudaStream_t>(stream), act_map, h);
     return cuda_ok(cudaGetLastError(), "conv launch") ? 1 : 0;
   }
   ConvTcParams prm{};

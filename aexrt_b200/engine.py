@@ -91,8 +91,10 @@ class CompiledYolo:
         self.nms = nms
         self.quant_on_load = quant_on_load
         # programmatic dependent launch (aexrt_b200_set_launch_flags): each kernel's launch and set-up
-        # overlap the previous kernel; by default for small batches, whose grids leave most SMs idle
-        self.programmatic = batch <= 8 if programmatic is None else bool(programmatic)
+        # overlap the previous kernel; by default at batch 1 (measured: YOLOv8n-320 0.626 against
+        # 0.690 ms per step at batch 1, 0.641 against 0.688 at batch 2, no gain at 4 and a loss at 8;
+        # YOLOv11s-320 even at batch 1, slower from batch 2)
+        self.programmatic = batch == 1 if programmatic is None else bool(programmatic)
         self.det_buf = self._new_det_buf()
         # ---- plans and per-command scratch
         self.steps: List[tuple] = []
@@ -436,7 +438,7 @@ class CompiledYolo:
 
 
 def main(argv=None) -> int:
-    """Runs eager forwards of the synthetic YOLOv8n model (profiling entry: one forward = one launch list)."""
+    """Runs eager forwards of a synthetic YOLO model (profiling entry: one forward = one launch list)."""
     import argparse
 
     from . import yolo
@@ -446,10 +448,16 @@ def main(argv=None) -> int:
     ap.add_argument("--imgsz", type=int, default=320)
     ap.add_argument("--forwards", type=int, default=2)
     ap.add_argument("--no-nms", action="store_true", help="stop at output0 (no GPU filter + NMS + top-k)")
+    ap.add_argument("--model", default="yolov8n", choices=["yolov8n", "yolov8s", "yolov11s"])
+    ap.add_argument("--programmatic", default="auto", choices=["auto", "on", "off"])
     a = ap.parse_args(argv)
     torch = _torch()
-    program = yolo.build_yolov8n(nc=4, imgsz=a.imgsz, seed=0)
-    eng = CompiledYolo(program, a.batch, nms=None if a.no_nms else NmsConfig())
+    if a.model == "yolov8n":
+        program = yolo.build_yolov8n(nc=4, imgsz=a.imgsz, seed=0)
+    else:
+        program = getattr(yolo, f"build_{a.model}")(nc=80, imgsz=a.imgsz, seed=0)
+    eng = CompiledYolo(program, a.batch, nms=None if a.no_nms else NmsConfig(),
+                       programmatic=None if a.programmatic == "auto" else a.programmatic == "on")
     x = torch.from_numpy(np.random.default_rng(0).uniform(0, 1, (a.batch, 3, a.imgsz, a.imgsz)).astype(np.float16))
     x = x.to(eng.device)
     for i in range(a.forwards):

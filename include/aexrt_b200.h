@@ -166,10 +166,11 @@ int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t 
  * the tile (bits 0-15): bits 16-19 kernel variant (0 auto, 1 slot streaming,
  * 2 halo tile), bits 20-23 halo tile order (0 auto, 1 strided over CTAs,
  * 2 one contiguous run per CTA), bits 24-27 the most M blocks stacked in one
- * halo super-tile (0 auto, 1 none), bit 28 halo epilogue stores each output
- * pixel directly, bit 29 it stages every tile in shared memory for one TMA
- * tensor store (default: staged for 1x1 convs only).  For int8 plans the
- * results are identical
+ * halo super-tile (0 auto, 1 none), bit 29 halo epilogue stages each tile in
+ * shared memory and writes it with one TMA tensor store per column block,
+ * bit 28 it stores each output pixel directly (the default).  Small grids (one
+ * or a few images) pick narrower automatic tiles so that the conv spreads over
+ * more SMs.  For int8 plans the results are identical
  * for every choice (integer accumulation); an fp16 plan whose choice moves it
  * between the halo and slot kernels sums K in another order, which can change
  * the last bit of an fp16 output.
