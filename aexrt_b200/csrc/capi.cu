@@ -329,8 +329,10 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
     const int taps = kk;
     const int pairs = (p->slabs + 1) / 2;
     const int tap_pairs = (kk + 1) / 2;
+    // (pg16: the epilogue's per-warp group-scale table holds kMaxSlabsPg slabs)
     const bool tile_ok = pick_halo_tile(static_cast<int>(d.out_h), static_cast<int>(d.out_w), p->k, p->stride,
-                                        f16 ? 32 : 16, tw, th, pitch);
+                                        f16 ? 32 : 16, tw, th, pitch) &&
+                         !(p->pg && p->slabs > kMaxSlabsPg);
     const int bn_min = p->pg ? 64 : 16;
     for (int bn = p->bn; tile_ok && !p->halo && bn >= bn_min; bn = block_n ? 0 : bn / 2) {
       if (p->pg && bn != 64 && bn != 128) continue;
@@ -358,7 +360,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
       for (;; mblocks /= 2) {
         // keep >= 4 stages (and a whole tile per issuer half ring) for a super-tile, else fewer blocks
         halo_h = mblocks * th + (p->k == 1 ? 0 : (p->stride == 1 ? 2 : 1));
-        const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, oc_alloc);
+        const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, oc_alloc, 0, 0, p->pg);
         // quantize on load: a raw ring of 3 (else 2) slots, each the fp16 boxes of one stage (twice
         // its int8 bytes), while >= 4 stages remain
         raw_slots = 0;
@@ -375,7 +377,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
       // staged output: two buffers per epilogue group (else one) from the whole 227 KB, while the
       // pipeline keeps min(st, max(4, 2 * pairs)) stages; the TMA box holds <= 256 rows
       if (st >= 2 && mblocks * th <= 256 && !direct_store) {
-        const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, oc_alloc);
+        const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, oc_alloc, 0, 0, p->pg);
         const int gbytes = halo_out_gbytes(bn, mblocks * th * tw);
         const int keep = std::min(st, std::max(4, 2 * pairs));
         for (int nb = 2; nb >= 1; --nb) {
@@ -421,7 +423,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
         p->out_nbuf = out_nbuf;
         p->out_gbytes = out_gbytes;
         p->smem = halo_smem_plan(p->halo_rows, boxes, st, w_tile, p->oc_alloc, p->ql_raw * p->ql_raw_bytes,
-                                 4 * out_nbuf * out_gbytes)
+                                 4 * out_nbuf * out_gbytes, p->pg)
                       .total_bytes;
         p->tiles_w = (static_cast<int>(d.out_w) + tw - 1) / tw;
         p->tiles_h = (static_cast<int>(d.out_h) + mblocks * th - 1) / (mblocks * th);
@@ -1558,11 +1560,11 @@ int aexrt_b200_dwconv3x3_f16(const void* x, uint32_t n, uint32_t h, uint32_t w, 
   if (ldc < coff + (c / grp - 1) * grp_stride + grp_off + grp || out_ldc < out_coff + c)
     return fail("dwconv: input or output slice out of range");
   const uint32_t oh = (h + 2 - 3) / stride + 1, ow = (w + 2 - 3) / stride + 1;
-  const long total = static_cast<long>(n) * oh * ow * (c / 8);
+  const long total = static_cast<long>(n) * oh * ((ow + kDwRun - 1) / kDwRun) * (c / 8);
   if (total == 0) return 1;
-  launch_kernel(dwconv3x3_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0,
-      static_cast<cudaStream_t>(stream),
-      static_cast<const __half*>(x), n, h, w, c, ldc, coff, grp, grp_stride, grp_off, w9, bias, stride, silu ? 1 : 0,
+  launch_kernel(stride == 1 ? dwconv3x3_kernel<1> : dwconv3x3_kernel<2>,
+      dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+      static_cast<const __half*>(x), n, h, w, c, ldc, coff, grp, grp_stride, grp_off, w9, bias, silu ? 1 : 0,
       oh, ow, static_cast<__half*>(out), out_ldc, out_coff);
   return cuda_ok(cudaGetLastError(), "dwconv launch") ? 1 : 0;
 }
@@ -1588,7 +1590,12 @@ int aexrt_b200_psa_attention_f16(const void* qkv, uint32_t n, uint32_t h, uint32
   if (!cuda_ok(cudaFuncSetAttribute(psa_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
                "cudaFuncSetAttribute"))
     return 0;
-  launch_kernel(psa_attention_kernel, dim3(heads, n), dim3(kPsaThreads), smem, static_cast<cudaStream_t>(stream),
+  // split each head's queries over up to 4 CTAs while the grid is below two CTAs per SM
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const uint32_t pairs = heads * n;
+  const uint32_t splits = std::min(4u, std::max(1u, (2u * static_cast<uint32_t>(sms) + pairs - 1) / pairs));
+  launch_kernel(psa_attention_kernel, dim3(heads, n, splits), dim3(kPsaThreads), smem, static_cast<cudaStream_t>(stream),
       static_cast<const __half*>(qkv), static_cast<int>(l), ldc, coff, key_dim, scale,
       static_cast<const __half*>(pe), pe_ldc, pe_coff, static_cast<__half*>(out), out_ldc, out_coff, amax,
       amax_stride, amax_goff);

@@ -36,7 +36,7 @@ namespace aexrt {
 // quantize launch and its int8 write + read disappear.
 constexpr int kQlMaxParts = 4;
 constexpr int kQlMaxRaw = 4;
-constexpr int kQlWarps = 1;  // 20 warps: 5 per SM sub-partition keeps the 96-register budget of the 19-warp form
+constexpr int kQlWarps = 4;
 
 struct ConvHaloParams {
   int n_img, slabs, slab_pairs;
@@ -111,16 +111,18 @@ struct HaloSmemPlan {
   int b_offset;
   int sb_offset;
   int am_offset;    // per-tile amax reduction ring (strided order): [8][16] maxima + [8][4] counters
+  int gs_offset;    // pg16: per epilogue warp, the current image's group scales [16][kMaxSlabsPg]
   int bar_offset;
   int total_bytes;
 };
 
 constexpr int kMaxAcc = 16;                 // TMEM accumulator buffers (narrow tiles keep more in flight)
+constexpr int kMaxSlabsPg = 64;             // pg16 group-scale table per epilogue warp (up to 1024 input channels)
 constexpr int kAmaxRing = 2 * kMaxAcc;      // >= 2 x accumulator buffers: a slot is reset before any warp reuses it
 
 __host__ __device__ inline HaloSmemPlan halo_smem_plan(int halo_rows, int boxes_per_slab, int stages,
                                                        int w_tile_bytes, int oc_alloc, int raw_total = 0,
-                                                       int out_total = 0) {
+                                                       int out_total = 0, bool pg = false) {
   HaloSmemPlan s;
   const int box_bytes = ((halo_rows * kSlotBytes + 127) / 128) * 128;
   s.slab_bytes = box_bytes * boxes_per_slab;
@@ -132,7 +134,8 @@ __host__ __device__ inline HaloSmemPlan halo_smem_plan(int halo_rows, int boxes_
   s.b_offset = ((s.out_offset + out_total + 1023) / 1024) * 1024;
   s.sb_offset = s.b_offset + ((w_tile_bytes + 127) / 128) * 128;  // w_scale[oc_alloc], bias[oc_alloc]
   s.am_offset = s.sb_offset + ((8 * oc_alloc + 127) / 128) * 128;
-  s.bar_offset = s.am_offset + kAmaxRing * (16 + 4) * 4;
+  s.gs_offset = s.am_offset + kAmaxRing * (16 + 4) * 4;
+  s.bar_offset = s.gs_offset + (pg ? 16 * kMaxSlabsPg * 4 : 0);
   // barriers: full[stages], empty[stages], acc_full[16], acc_empty[16], w_full[2], sb_full, raw_full[4],
   // raw_empty[4]; then the TMEM address
   s.total_bytes = s.bar_offset + (2 * stages + 2 * kMaxAcc + 3 + 2 * kQlMaxRaw) * 8 + 16;
@@ -542,6 +545,32 @@ __device__ __forceinline__ __half2 halo_pg_vals8(const uint64_t* fp2, const floa
   return m;
 }
 
+// A conv tile index t = ((nt * n_img + img) * tiles_h + row) * tiles_w + col as its digits.
+struct TileCursor {
+  int col, row, img, nt;
+  __device__ __forceinline__ void set(int t, const ConvHaloParams& p) {
+    col = t % p.tiles_w;
+    t /= p.tiles_w;
+    row = t % p.tiles_h;
+    t /= p.tiles_h;
+    img = t % p.n_img;
+    nt = t / p.n_img;
+  }
+  // this += d (every digit of d below its radix, so one carry per digit suffices)
+  __device__ __forceinline__ void advance(const TileCursor& d, const ConvHaloParams& p) {
+    col += d.col;
+    int c = col >= p.tiles_w;
+    col -= c ? p.tiles_w : 0;
+    row += d.row + c;
+    c = row >= p.tiles_h;
+    row -= c ? p.tiles_h : 0;
+    img += d.img + c;
+    c = img >= p.n_img;
+    img -= c ? p.n_img : 0;
+    nt += d.nt + c;
+  }
+};
+
 template <bool kF16, int BN, bool kSilu, bool kRes, bool kPG = false, bool kMB = false, bool kQL = false>
 __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap act_map, const __grid_constant__ ConvHaloParams p) {
@@ -576,7 +605,8 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const HaloSmemPlan sp = halo_smem_plan(p.halo_rows, p.boxes_per_slab, p.stages, p.w_tile_bytes, p.oc_alloc,
-                                         kQL ? p.ql_raw_slots * p.ql_raw_bytes : 0, 4 * p.out_nbuf * p.out_gbytes);
+                                         kQL ? p.ql_raw_slots * p.ql_raw_bytes : 0, 4 * p.out_nbuf * p.out_gbytes,
+                                         kPG);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + sp.bar_offset);
   uint64_t* empty = full + p.stages;
   uint64_t* acc_full = full + 2 * p.stages;  // [kAcc]
@@ -1040,8 +1070,9 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
     };
     uint32_t* am_ring = reinterpret_cast<uint32_t*>(smem + sp.am_offset);  // [kAmaxRing][16] maxima
     uint32_t* am_count = am_ring + kAmaxRing * 16;                          // [kAmaxRing][4] arrivals
-    int ep_img = -1;  // quantize on load: the image whose per-tensor amax ep_at holds
-    float ep_at = 0.0f;
+    int ep_img = -1;       // the image whose activation scale ep_scale holds (per tensor)
+    float ep_scale = 0.0f;
+    int gs_img = -1;       // pg16: the image whose group scales this warp's table holds
     // Staged output: the four warps of this warp's group (one per TMEM lane quadrant, the same
     // column block and tile group) write their column block of a tile into a swizzled box in
     // shared memory; after a named barrier the group's first thread stores the box with one TMA
@@ -1054,15 +1085,23 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
     const int srow0 = (r_h < p.th && r_w < p.tw) ? r_h * p.tw + r_w : -1;  // staging row (M block 0)
     int jj = 0;         // this group's tiles so far: staging buffer jj % out_nbuf
     bool alive = true;  // every wait of this warp so far succeeded
+    // This warp's tiles are t0, t0 + step, t0 + 2 step, ... (t0: its tile group's first tile; step:
+    // kTileGroups tiles in contiguous order, kTileGroups * gridDim.x in strided order).  A tile index is
+    // the mixed-radix number (n-tile, image, tile row, tile column); the cursor holds those digits and
+    // adds the step's digits with carries, so no tile needs an integer division.
+    TileCursor cur, stp;
+    {
+      const int t0 = p.contiguous ? run_start + tgroup : static_cast<int>(blockIdx.x) + tgroup * static_cast<int>(gridDim.x);
+      cur.set(t0, p);
+      stp.set(kTileGroups * (p.contiguous ? 1 : static_cast<int>(gridDim.x)), p);
+    }
     for (int k = blockIdx.x, i = 0; k < p.total_tiles; k += gridDim.x, ++i) {
       if (kTileGroups > 1 && i % kTileGroups != tgroup) continue;
+      if (i != tgroup) cur.advance(stp, p);
       const int u = i;  // the tile's place in this CTA's sequence: accumulator buffer and phase
-      const int t = p.contiguous ? run_start + i : k;
-      const int n_tile = t / p.m_tiles;
-      const int m_tile = t - n_tile * p.m_tiles;
-      const int img = m_tile / per_img;
-      const int r = m_tile - img * per_img;
-      const int oy = (r / p.tiles_w) * p.th * p.mblocks + r_h, ox = (r % p.tiles_w) * p.tw + r_w;
+      const int n_tile = cur.nt;
+      const int img = cur.img;
+      const int oy = cur.row * p.th * p.mblocks + r_h, ox = cur.col * p.tw + r_w;
       const bool valid = r_h < p.th && r_w < p.tw && oy < p.oh && ox < p.ow;
       const size_t pix = (static_cast<size_t>(img) * p.oh + (valid ? oy : 0)) * p.ow + (valid ? ox : 0);
       __half* out_row = p.out + pix * p.out_ldc + p.out_coff;
@@ -1074,16 +1113,33 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
         if (st_issuer) bulk_wait_read_all();
         named_bar_sync(2 + sgroup, 128);
       }
-      if (p.amax_out != nullptr && p.contiguous && t / per_img != run_key) {
+      if (p.amax_out != nullptr && p.contiguous && n_tile * p.n_img + img != run_key) {
         if (run_key >= 0) flush_amax();
-        run_key = t / per_img;
+        run_key = n_tile * p.n_img + img;
         run_img = img;
         run_oc = n0 + col0;
       }
       if constexpr (kPG) {
         // pg16: drain the tile's slab units in ascending group order into fp32 sums,
         // fp = sum_g fl32(fl32(S_g) * fl32(amax_g / 127)), then the final epilogue
-        const float* rec = kQL ? nullptr : p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs);
+        // the image's group scales fl32(amax_g / 127), computed once per image into this warp's table
+        float* gs_tab = reinterpret_cast<float*>(smem + sp.gs_offset) + (warp - 2) * kMaxSlabsPg;
+        if (img != gs_img) {
+          __syncwarp();
+          const float* rec = kQL ? nullptr : p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs);
+          for (int g = lane; g < p.slabs; g += 32) {
+            float ag;
+            if constexpr (kQL) {
+              const int kq = ql_part_of(p, g);
+              ag = ql_group_amax(p, kq, img, g - p.ql_slab0[kq]);
+            } else {
+              ag = __ldg(rec + 1 + g);
+            }
+            gs_tab[g] = __fdiv_rn(ag, 127.0f);
+          }
+          __syncwarp();
+          gs_img = img;
+        }
         const int Hh = kAcc / p.issuers;
         const int r_iss = i % p.issuers;
         const int ubase = (i / p.issuers) * p.slabs;
@@ -1091,14 +1147,7 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
         for (int g = 0; g < p.slabs; ++g) {
           const int uu = ubase + g;
           const int gbuf = r_iss * Hh + uu % Hh;
-          float ag;
-          if constexpr (kQL) {
-            const int kq = ql_part_of(p, g);
-            ag = ql_group_amax(p, kq, img, g - p.ql_slab0[kq]);
-          } else {
-            ag = __ldg(rec + 1 + g);
-          }
-          const float gs = __fdiv_rn(ag, 127.0f);
+          const float gs = gs_tab[g];
           const uint64_t gs2 = f2_pack(gs, gs);
           if (alive && !mbar_wait_bounded(&acc_full[gbuf], (uu / Hh) & 1, p.status, kStatusTimeoutAccFull))
             alive = false;
@@ -1129,9 +1178,10 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
             for (int j = 0; j < CW / 2; ++j) {
               // fp += fl32(S) * gs in ascending group order, one fused multiply-add per group (the
               // slot kernel's `fp + S * gs` contracts the same way; ptxas also fuses a packed
-              // mul.rn + add.rn pair, so the fma is written out).  |S| <= 128 * 127 * 144 < 2^22:
-              // the exact small-integer conversion always applies to a group sub-sum.
-              const uint64_t s2 = acc2_to_f2<true>(v[2 * j], v[2 * j + 1]);
+              // mul.rn + add.rn pair, so the fma is written out).  Plain conversions: the exact
+              // small-integer path (two integer adds and a packed add per pair) measured 9 % slower
+              // here, where the drain is issue-bound (C1 batch 64: 140.8 against 129.0 us)
+              const uint64_t s2 = acc2_to_f2<false>(v[2 * j], v[2 * j + 1]);
               fp2[c * (CW / 2) + j] = g == 0 ? f2_mul(s2, gs2) : f2_fma(s2, gs2, fp2[c * (CW / 2) + j]);
             }
           }
@@ -1167,22 +1217,23 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
         }
       } else {
       const int buf = u % nacc;
-      // the scale record is ready before the launch: read it while the accumulator fills
-      float amax_in = 0.0f;
-      if constexpr (kQL) {
-        if (img != ep_img) {
-          ep_at = ql_tensor_amax(p, img);
-          ep_img = img;
+      // the image's activation scale fl32(amax / 127), computed once per image (the scale record is
+      // ready before the launch: read it while the accumulator fills)
+      if (!kF16 && img != ep_img) {
+        float amax_in;
+        if constexpr (kQL) {
+          amax_in = ql_tensor_amax(p, img);
+        } else {
+          amax_in = __ldg(p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs));
         }
-        amax_in = ep_at;
-      } else if constexpr (!kF16) {
-        amax_in = __ldg(p.scale_rec + static_cast<size_t>(img) * (1 + p.slabs));
+        ep_scale = __fdiv_rn(amax_in, 127.0f);
+        ep_img = img;
       }
       if (alive && !mbar_wait_bounded(&acc_full[buf], (u / nacc) & 1, p.status, kStatusTimeoutAccFull)) alive = false;
       tc_fence_after();
-      const float in_scale = kF16 ? 1.0f : __fdiv_rn(amax_in, 127.0f);
+      const float in_scale = kF16 ? 1.0f : ep_scale;
       const uint64_t s2 = f2_pack(in_scale, in_scale);
-      const int oy0 = (r / p.tiles_w) * p.th * p.mblocks + r_h;
+      const int oy0 = cur.row * p.th * p.mblocks + r_h;
       for (int mb = 0; mb < kMaxMB; ++mb) {
         if (mb >= p.mblocks) break;
         // M block mb of the super-tile: rows mb*th.. of the tile, columns mb*BN.. of the buffer
@@ -1264,7 +1315,7 @@ __global__ void __launch_bounds__(halo_threads<BN, kQL>(), 1)
         if (st_issuer) bulk_wait_read_all();
         named_bar_sync(2 + sgroup, 128);
         if (st_issuer && n0 + col0 < p.oc) {  // a column block past the last channel has nothing to store
-          tma_store_4d(&p.out_map, sbuf, n0 + col0, (r % p.tiles_w) * p.tw, (r / p.tiles_w) * p.th * p.mblocks, img);
+          tma_store_4d(&p.out_map, sbuf, n0 + col0, cur.col * p.tw, cur.row * p.th * p.mblocks, img);
           bulk_commit_group();
         }
         ++jj;

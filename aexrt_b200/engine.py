@@ -160,8 +160,9 @@ class CompiledYolo:
         if c.precision == "int8":
             codes, scale = ops.quantize_conv_weight_int8(c.weight)
             # quantize on load: the conv reads the producers' fp16 slices and quantizes them itself,
-            # when the plan supports it and every part fits its rules (see conv_w8a8_sources)
-            ql = self.quant_on_load and all(
+            # when the plan supports it and every part fits its rules (see conv_w8a8_sources); SiLU
+            # convs only (the linear ones, with or without a residual, have no instance of every tile)
+            ql = self.quant_on_load and c.silu and all(
                 pt.value != "images" and pt.coff % 16 == 0 and pt.channels >= 16
                 and (pt.channels % 16 == 0 or i == len(c.inputs) - 1) and (pt.upsample == 1 or c.s == 1)
                 for i, pt in enumerate(c.inputs)) and len(c.inputs) <= 4
