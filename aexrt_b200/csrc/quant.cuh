@@ -366,15 +366,15 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p,
   __shared__ float s_red[2];
   __shared__ int2 s_pix[8][kRowsMaxPixPerWarp];  // per pixel: (row << 16 | column), destination pixel (-1: none)
   const int n = blockIdx.y;
-  if (kI8) slab_multipliers(p, n, s_mult, s_red);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int npix = p.hp * p.wp;
   const int item = blockIdx.x * 8 + warp;
   const int pg = item / groups;
   const int pix0 = pg * pw;
-  if (pix0 >= npix) return;  // no barrier follows
+  // a warp past the last pixel group still joins the block's multiplier pass (it has barriers)
+  const bool active = pix0 < npix;
   int g = item - pg * groups;
-  if (!kLinear || p.split) {
+  if (active && (!kLinear || p.split)) {
     for (int j = 0; j < pw / 32; ++j) {
       const int pix = pix0 + j * 32 + lane;
       const int h = pix / p.wp, w = pix - (pix / p.wp) * p.wp;
@@ -406,10 +406,11 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p,
   const int cidx = j0 + cl;  // chunk of this lane within the source
   const bool cact = cidx < nchunks;
   const int slab = kI8 ? (chunk_base + cidx) >> 1 : chunk_base + cidx;
-  const float mult = kI8 && cact ? s_mult[slab] : 0.0f;
   uint8_t* dst = out + static_cast<size_t>(slab) * plane * 16;
-  for (int b = 0; b < batches; ++b) {
-    uint4 v[8];
+  uint4 v[8];
+  // the loads of one batch (8 per lane); the first batch is issued before the block computes the
+  // slab multipliers, so their latency overlaps the amax reads and the block reduction
+  auto load_batch = [&](int b) {
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
       v[it] = make_uint4(0u, 0u, 0u, 0u);
@@ -426,6 +427,13 @@ __global__ void __launch_bounds__(256, 4) quant_rows_kernel(const QuantParams p,
               base + (static_cast<size_t>(h >> ush) * s.src_w + (w >> ush)) * s.ldc + cidx * 8);
       }
     }
+  };
+  if (active) load_batch(0);
+  if (kI8) slab_multipliers(p, n, s_mult, s_red);
+  if (!active) return;  // no barrier follows
+  const float mult = kI8 && cact ? s_mult[slab] : 0.0f;
+  for (int b = 0; b < batches; ++b) {
+    if (b > 0) load_batch(b);
     // rounding by the 1.5*2^23 addend (see quantize_nchw_kernel) when every lane's inputs stay in
     // its exact range, else float-to-int; the choice is warp-uniform
     bool magic = true;
