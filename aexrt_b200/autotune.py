@@ -211,6 +211,7 @@ class Tuner:
         cands = [bn for bn in bns] + [2 << 20, 1 << 20]
         if k == 3 and s == 1:
             cands.append(1 << 24)  # no stacked M blocks
+        cands.append(1 << 29)  # staged epilogue: tiles written by TMA tensor stores (bit-identical)
         return cands
 
     def _tune_variants(self):

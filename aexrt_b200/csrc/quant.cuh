@@ -325,7 +325,9 @@ __device__ __forceinline__ void slab_multipliers(const QuantParams& p, int n, fl
 // row; fp16: each chunk is one slab row.  Pixel coordinates come from a
 // per-warp table computed once (no divisions in the copy loops).  A warp's
 // pixel count pw = 32 * 8 / (widest source's L), so the widest source keeps
-// 8 loads per lane in flight in one batch and narrower ones as many or more.
+// 8 loads per lane in flight in one batch and narrower ones as many or more;
+// maps of at least 16 such groups take two batches per warp (up to 256
+// pixels), so that each block's multiplier pass serves twice the data.
 constexpr int kRowsMaxPixPerWarp = 256;
 
 // Lanes sharing one pixel in a load of source `ch` channels (see quant_rows_kernel).
@@ -338,7 +340,8 @@ __host__ __device__ inline int rows_lanes_per_pixel(int ch, bool i8) {
 inline int rows_pixels_per_warp(const QuantParams& q, bool i8) {
   int lmax = 1;
   for (int i = 0; i < q.nsrc; ++i) lmax = std::max(lmax, rows_lanes_per_pixel(q.src[i].ch, i8));
-  return 32 * 8 / lmax;
+  const int base = 32 * 8 / lmax;
+  return (q.hp * q.wp >= 16 * base && 2 * base <= kRowsMaxPixPerWarp) ? 2 * base : base;
 }
 
 // Channel groups of all sources: a group is the L_k chunks one load instruction covers.

@@ -1092,7 +1092,12 @@ bool prepare(AexrtYoloModel* m) {
   if (!cuda_ok(cudaStreamSynchronize(st), "warm-up forward", &m->error)) return false;
   cudaGraph_t g = nullptr;
   if (!cuda_ok(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture", &m->error)) return false;
+  // one image per run (the reference's aexrt_yolo_run): every kernel of the graph is launched with
+  // programmatic dependent launch, so its launch and set-up overlap the kernel before it (launch.cuh)
+  const uint32_t prev_flags = aexrt_b200_get_launch_flags();
+  aexrt_b200_set_launch_flags(m->batch == 1 ? AEXRT_B200_LAUNCH_PROGRAMMATIC : 0u);
   const bool ok = launch_forward(m, st, nullptr);
+  aexrt_b200_set_launch_flags(prev_flags);
   const cudaError_t ce = cudaStreamEndCapture(st, &g);
   if (!ok || !cuda_ok(ce, "end capture", &m->error)) {
     if (g) cudaGraphDestroy(g);

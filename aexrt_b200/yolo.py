@@ -222,11 +222,13 @@ class _Builder:
         self.conv(name + ".cv2", [Part(cat, 0, 4 * c_)], (out, 0), c2, 1, 1)
         return out
 
-    def detect(self, name: str, feats: List[str], strides: List[float]):
+    def detect(self, name: str, feats: List[str], strides: List[float], fused: bool = True):
         nc, reg_max = self.p.nc, self.p.reg_max
         chs = [self.p.values[f].channels for f in feats]
         c2 = max(16, chs[0] // 4, reg_max * 4)
         c3 = max(chs[0], min(nc, 100))
+        if not fused:
+            return self._detect_branches(name, feats, strides, c2, c3)
         levels = []
         for i, (f, st) in enumerate(zip(feats, strides)):
             v = self.p.values[f]
@@ -239,6 +241,30 @@ class _Builder:
             self.conv(f"{name}.{i}.cv2_1", [Part(h0, 0, c2)], (h1, 0), c2, 3, 1, precision="fp16")
             self.conv(f"{name}.{i}.cv3_1", [Part(h0, c2, c3)], (h1, c2), c3, 3, 1, precision="fp16")
             levels.append(self._head_logits(f"{name}.{i}", h1, o, c2, c3, st))
+        self.p.commands.append(DecodeCmd(name + ".decode", levels, nc, reg_max))
+
+    def _detect_branches(self, name: str, feats: List[str], strides: List[float], c2: int, c3: int):
+        """The Detect head in its model form: per level a box branch (3x3, 3x3, 1x1 to 4 * reg_max) and
+        a class branch (3x3, 3x3, 1x1 to nc), each conv its own command; the two 1x1s write the box and
+        class logits side by side in the level's output buffer."""
+        nc, reg_max = self.p.nc, self.p.reg_max
+        levels = []
+        for i, (f, st) in enumerate(zip(feats, strides)):
+            v = self.p.values[f]
+            ch = self.p.values[f].channels
+            pre = f"{name}.{i}"
+            o = self.value(pre + ".out", 4 * reg_max + nc, v.h, v.w)
+            for br, cm, oc in (("cv2", c2, 4 * reg_max), ("cv3", c3, nc)):
+                a = self.value(f"{pre}.{br}.0", cm, v.h, v.w)
+                b = self.value(f"{pre}.{br}.1", cm, v.h, v.w)
+                self.conv(f"{pre}.{br}_0", [Part(f, 0, ch)], (a, 0), cm, 3, 1, precision="fp16")
+                self.conv(f"{pre}.{br}_1", [Part(a, 0, cm)], (b, 0), cm, 3, 1, precision="fp16")
+                w, bias = self._weights(oc, cm, 1)
+                if br == "cv3":
+                    w, bias = w * np.float32(self.cls_gain), bias + np.float32(self.cls_bias)
+                self.p.commands.append(ConvCmd(f"{pre}.{br}_2", [Part(b, 0, cm)], (o, 0 if br == "cv2" else 4 * reg_max),
+                                               cm, oc, 1, 1, False, w, bias, "fp16"))
+            levels.append((Part(o, 0, 4 * reg_max), Part(o, 4 * reg_max, nc), float(st)))
         self.p.commands.append(DecodeCmd(name + ".decode", levels, nc, reg_max))
 
     def _head_logits(self, name: str, h1: str, o: str, c2: int, c3: int, stride: float):
@@ -374,13 +400,15 @@ class _Builder:
 
 def build_yolov8(width: float = 0.25, depth: float = 0.33, nc: int = 4, imgsz: int = 320, seed: int = 0,
                  max_channels: int = 1024, name: Optional[str] = None, gain: float = 1.0,
-                 cls_gain: float = 1.0, cls_bias: float = 0.0) -> YoloProgram:
+                 cls_gain: float = 1.0, cls_bias: float = 0.0, fused_head: bool = True) -> YoloProgram:
     """YOLOv8 command stream (n: width 0.25 depth 0.33; s: width 0.5 depth 0.33).
 
     ``gain`` scales the random weights' standard deviation (1.0: N(0, 1/sqrt(fan_in)), under which
     activations shrink through the SiLU layers); ``cls_gain`` scales the class-logit weights and
     ``cls_bias`` is added to the class-logit biases, which spreads the class scores and moves them
-    away from 0.5 so that only some anchors pass a confidence threshold."""
+    away from 0.5 so that only some anchors pass a confidence threshold.  ``fused_head=False`` keeps
+    the Detect head's box and class branches as separate convs (the model's own form, as an ONNX
+    export has it) instead of this backend's merged launches."""
     def ch(c):
         return _make_divisible(min(c, max_channels) * width, 8)
 
@@ -407,7 +435,7 @@ def build_yolov8(width: float = 0.25, depth: float = 0.33, nc: int = 4, imgsz: i
     h18 = b.c2f("l18", [Part(x, 0, ch(256)), Part(h12, 0, ch(512))], ch(512), dep(3), False)
     x = b.conv_block("l19", [Part(h18, 0, ch(512))], ch(512), 3, 2)
     h21 = b.c2f("l21", [Part(x, 0, ch(512)), Part(p5, 0, ch(1024))], ch(1024), dep(3), False)
-    b.detect("l22", [h15, h18, h21], [8.0, 16.0, 32.0])
+    b.detect("l22", [h15, h18, h21], [8.0, 16.0, 32.0], fused=fused_head)
     return b.p
 
 

@@ -64,6 +64,8 @@ def parse_args():
                          "64 for the layer workloads)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--onnx", default=None,
+                    help="model workloads: the program comes from this ONNX YOLO graph (imported without onnx)")
     ap.add_argument("--programmatic", default="auto", choices=["auto", "on", "off"],
                     help="model workloads: programmatic dependent launch (auto: the engine's choice by batch)")
     ap.add_argument("--quant-on-load", action="store_true",
@@ -395,6 +397,12 @@ def run_ours(args):
 
     builder, metric, workload, imgsz, nc, global_batch, scaling = MODELS[args.workload]
     program = getattr(yolo, builder)(nc=nc, imgsz=imgsz, seed=0)
+    if args.onnx:
+        from aexrt_b200 import onnx_yolo
+
+        program = onnx_yolo.import_onnx(args.onnx)
+        imgsz, nc = program.imgsz, program.nc
+        workload = f"{args.onnx} (ONNX import): " + workload
     if args.batch is None and global_batch:
         # strong scaling: this rank's shard of the global batch (image k is drawn from seed 1000 + k)
         start, B = shard_range(global_batch, world, rank)
