@@ -400,7 +400,8 @@ class _Builder:
 
 def build_yolov8(width: float = 0.25, depth: float = 0.33, nc: int = 4, imgsz: int = 320, seed: int = 0,
                  max_channels: int = 1024, name: Optional[str] = None, gain: float = 1.0,
-                 cls_gain: float = 1.0, cls_bias: float = 0.0, fused_head: bool = True) -> YoloProgram:
+                 cls_gain: float = 1.0, cls_bias: float = 0.0, fused_head: bool = True,
+                 v11_head: bool = False) -> YoloProgram:
     """YOLOv8 command stream (n: width 0.25 depth 0.33; s: width 0.5 depth 0.33).
 
     ``gain`` scales the random weights' standard deviation (1.0: N(0, 1/sqrt(fan_in)), under which
@@ -408,7 +409,8 @@ def build_yolov8(width: float = 0.25, depth: float = 0.33, nc: int = 4, imgsz: i
     ``cls_bias`` is added to the class-logit biases, which spreads the class scores and moves them
     away from 0.5 so that only some anchors pass a confidence threshold.  ``fused_head=False`` keeps
     the Detect head's box and class branches as separate convs (the model's own form, as an ONNX
-    export has it) instead of this backend's merged launches."""
+    export has it) instead of this backend's merged launches; ``v11_head=True`` puts the YOLOv11 Detect
+    head (depthwise class branch) on the YOLOv8 backbone."""
     def ch(c):
         return _make_divisible(min(c, max_channels) * width, 8)
 
@@ -435,7 +437,10 @@ def build_yolov8(width: float = 0.25, depth: float = 0.33, nc: int = 4, imgsz: i
     h18 = b.c2f("l18", [Part(x, 0, ch(256)), Part(h12, 0, ch(512))], ch(512), dep(3), False)
     x = b.conv_block("l19", [Part(h18, 0, ch(512))], ch(512), 3, 2)
     h21 = b.c2f("l21", [Part(x, 0, ch(512)), Part(p5, 0, ch(1024))], ch(1024), dep(3), False)
-    b.detect("l22", [h15, h18, h21], [8.0, 16.0, 32.0], fused=fused_head)
+    if v11_head:
+        b.detect_v11("l22", [h15, h18, h21], [8.0, 16.0, 32.0])
+    else:
+        b.detect("l22", [h15, h18, h21], [8.0, 16.0, 32.0], fused=fused_head)
     return b.p
 
 

@@ -59,9 +59,14 @@ def test_exported_graph_evaluates_to_the_oracle_output():
     assert np.abs(got[:, :4] - ref[:, :4]).max() < 0.25
 
 
-@pytest.mark.parametrize("builder", ["v8n", "v8s"])
+@pytest.mark.parametrize("builder", ["v8n", "v8s", "v11-head"])
 def test_import_gives_back_the_program(tmp_path, builder):
-    p = _program() if builder == "v8n" else yolo.build_yolov8(0.5, 0.33, 80, 64, 1, fused_head=False)
+    if builder == "v8n":
+        p = _program()
+    elif builder == "v8s":
+        p = yolo.build_yolov8(0.5, 0.33, 80, 64, 1, fused_head=False)
+    else:  # the YOLOv11 Detect head (depthwise convs in the class branch) on the YOLOv8n backbone
+        p = yolo.build_yolov8(0.25, 0.33, 80, 64, 2, v11_head=True)
     path = str(tmp_path / "model.onnx")
     onnx_yolo.export_onnx(p, path)
     q = onnx_yolo.import_onnx(path)
