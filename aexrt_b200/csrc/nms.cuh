@@ -16,9 +16,13 @@
 //      ascending: exactly the shaders' "higher" relation), then the candidates
 //      are permuted into rank order;
 //   3. suppress: for rank r < rank j, same class, IoU > threshold, r suppresses
-//      j.  A warp owns a row r and lane l tests column 32w + l, so one ballot is
-//      one 32-bit word of row r and the lanes read consecutive boxes (no bank
-//      conflicts).  Mode 0 (the reference's GPU "mark" rule) drops j if ANY
+//      j.  Only same-class pairs can suppress, so the candidates are put in
+//      (class, rank) order by a second sort of 32-bit keys: each class is one
+//      contiguous block and a row only tests the columns after it in its own
+//      block (with 4 classes a quarter of the pairs of the full triangle).  A
+//      warp owns a row and lane l tests column 32w + l, so one ballot is one
+//      32-bit word of the row.  The suppressed bits found in class order are
+//      moved back to rank order for step 4.  Mode 0 (the reference's GPU "mark" rule) drops j if ANY
 //      higher-ranked box suppresses it: the words are OR-ed per column word in
 //      shared memory, no matrix is stored.  Mode 1 (the greedy rule of
 //      yolo_postprocess, src/aexrt/yolo.py:996-1007) keeps the suppression
@@ -59,7 +63,9 @@ struct NmsParams {
 __host__ __device__ inline size_t nms_smem_bytes(int max_cand, int pow2, int mode) {
   const int words = (max_cand + 31) / 32;
   const size_t even = static_cast<size_t>((max_cand + 1) & ~1);
-  size_t b = even * (16 + 4 + 4 + 4) + static_cast<size_t>(pow2) * 8 + 64 * 4 + 32 * 4;
+  // box, score, class, area, then the class-order permutation and block ends; sort keys; two 32-word
+  // suppression sets (rank order and class order); scan words
+  size_t b = even * (16 + 4 + 4 + 4 + 4 + 4) + static_cast<size_t>(pow2) * 8 + 64 * 4 + 2 * 32 * 4;
   if (mode == 1) b += static_cast<size_t>(max_cand) * words * 4;
   return b;
 }
@@ -100,10 +106,13 @@ __global__ void __launch_bounds__(kNmsThreads) yolo_nms_kernel(const NmsParams p
   float* score = reinterpret_cast<float*>(box + MCe);
   float* cls = score + MCe;
   float* area = cls + MCe;
-  uint64_t* key = reinterpret_cast<uint64_t*>(area + MCe);  // 28 * MCe bytes before it: a multiple of 8
-  uint32_t* supp = reinterpret_cast<uint32_t*>(key + p.pow2);  // 32 words: suppressed / removed bits
-  int* scan = reinterpret_cast<int*>(supp + 32);               // warp totals + running count
-  uint32_t* mask = reinterpret_cast<uint32_t*>(scan + 64);     // mode 1: [MC][W]
+  int* perm = reinterpret_cast<int*>(area + MCe);   // class order position -> rank
+  int* bend = perm + MCe;                          // class order position -> end of its class block
+  uint64_t* key = reinterpret_cast<uint64_t*>(bend + MCe);  // 36 * MCe bytes before it: a multiple of 8
+  uint32_t* supp = reinterpret_cast<uint32_t*>(key + p.pow2);  // 32 words: suppressed / removed bits (rank order)
+  uint32_t* suppc = supp + 32;                                 // the same in class order
+  int* scan = reinterpret_cast<int*>(suppc + 32);              // warp totals + running count
+  uint32_t* mask = reinterpret_cast<uint32_t*>(scan + 64);     // mode 1: [MC][W], class order
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int img = blockIdx.x;
@@ -116,7 +125,7 @@ __global__ void __launch_bounds__(kNmsThreads) yolo_nms_kernel(const NmsParams p
 
   // ---- 1. filter + compaction in anchor order
   if (tid == 0) scan[32] = 0;
-  if (tid < 32) supp[tid] = 0;
+  if (tid < 32) supp[tid] = suppc[tid] = 0u;
   __syncthreads();
   for (int base = 0; base < p.anchors; base += kNmsThreads) {
     const int running = scan[32];
@@ -212,39 +221,84 @@ __global__ void __launch_bounds__(kNmsThreads) yolo_nms_kernel(const NmsParams p
   }
   __syncthreads();
 
-  // ---- 3. suppression words: bit j of word (r, w) = rank r suppresses rank j = 32w + bit
+  // ---- 3a. class order: sort (class << 10 | rank) keys; perm[k] = rank at class position k, bend[k] =
+  // end of k's class block
+  uint32_t* ckey = reinterpret_cast<uint32_t*>(key);
+  for (int i = tid; i < p.pow2; i += kNmsThreads)
+    ckey[i] = i < count ? (static_cast<uint32_t>(cls[i]) << 10) | static_cast<uint32_t>(i) : 0xFFFFFFFFu;
+  __syncthreads();
+  for (int k = 2; k <= p.pow2; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < p.pow2; i += kNmsThreads) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint32_t ka = ckey[i], kb = ckey[ixj];
+          const bool up = (i & k) == 0;
+          if ((ka > kb) == up) {
+            ckey[i] = kb;
+            ckey[ixj] = ka;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int k = tid; k < count; k += kNmsThreads) {
+    perm[k] = static_cast<int>(ckey[k] & 1023u);
+    // first position past k's class: binary search over the sorted keys
+    const uint32_t lim = ((ckey[k] >> 10) + 1) << 10;
+    int lo = k + 1, hi = count;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (ckey[mid] < lim) lo = mid + 1; else hi = mid;
+    }
+    bend[k] = lo;
+  }
+  __syncthreads();
+
+  // ---- 3b. suppression words in class order: bit j of word (k, w) = position k suppresses position
+  // j = 32w + bit (same class block, k before j, so rank(k) < rank(j))
   const int wc = (count + 31) / 32;
   const bool fast = p.iou >= 1e-20f && p.iou <= 1e20f;
   const float thr_hi = __fmul_rn(p.iou, 1.0f + 0x1p-20f), thr_lo = __fmul_rn(p.iou, 1.0f - 0x1p-20f);
-  for (int r = warp; r < count; r += kNmsThreads / 32) {  // rows round-robin over the warps
+  for (int k = warp; k < count; k += kNmsThreads / 32) {  // rows round-robin over the warps
+    const int r = perm[k];
     const float4 br = box[r];
-    const float cr = cls[r], ar = area[r];
-    const int w0 = (r + 1) >> 5;  // first word holding a column > r
+    const float ar = area[r];
+    const int e = bend[k];
+    const int w0 = (k + 1) >> 5, w1 = (e + 31) >> 5;  // words holding columns in (k, e)
     if (p.mode == 1)
-      for (int w = lane; w < w0; w += 32) mask[r * W + w] = 0u;
-    for (int w = w0; w < wc; ++w) {
+      for (int w = lane; w < W; w += 32)
+        if (w < w0 || w >= w1) mask[k * W + w] = 0u;
+    for (int w = w0; w < w1; ++w) {
       const int j = w * 32 + lane;
-      const bool s = j > r && j < count && cls[j] == cr &&
-                     nms_suppresses(br, ar, box[j], area[j], p.iou, thr_lo, thr_hi, fast);
+      const bool s = j > k && j < e &&
+                     nms_suppresses(br, ar, box[perm[min(j, count - 1)]], area[perm[min(j, count - 1)]], p.iou,
+                                    thr_lo, thr_hi, fast);
       const uint32_t bits = __ballot_sync(0xffffffffu, s);
       if (lane == 0) {
         if (p.mode == 1)
-          mask[r * W + w] = bits;
+          mask[k * W + w] = bits;
         else if (bits)
-          atomicOr(&supp[w], bits);
+          atomicOr(&suppc[w], bits);
       }
     }
   }
   __syncthreads();
   if (p.mode == 1 && warp == 0) {
-    // greedy: rows in rank order; a row that is still standing removes what it suppresses
+    // greedy: rows in class order (each class in rank order); a row that is still standing removes
+    // what it suppresses
     uint32_t removed = 0;  // word `lane`
-    for (int r = 0; r < count; ++r) {
-      const uint32_t word = __shfl_sync(0xffffffffu, removed, r >> 5);
-      if (!((word >> (r & 31)) & 1u) && lane < wc) removed |= mask[r * W + lane];
+    for (int k = 0; k < count; ++k) {
+      const uint32_t word = __shfl_sync(0xffffffffu, removed, k >> 5);
+      if (!((word >> (k & 31)) & 1u) && lane < wc) removed |= mask[k * W + lane];
     }
-    supp[lane] = removed;
+    suppc[lane] = removed;
   }
+  __syncthreads();
+  // ---- 3c. back to rank order
+  for (int k = tid; k < count; k += kNmsThreads)
+    if ((suppc[k >> 5] >> (k & 31)) & 1u) atomicOr(&supp[perm[k] >> 5], 1u << (perm[k] & 31));
   __syncthreads();
 
   // ---- 4. top-k: kept = not suppressed; slot = kept ranks before this one

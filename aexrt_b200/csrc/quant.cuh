@@ -326,8 +326,9 @@ __device__ __forceinline__ void slab_multipliers(const QuantParams& p, int n, fl
 // per-warp table computed once (no divisions in the copy loops).  A warp's
 // pixel count pw = 32 * 8 / (widest source's L), so the widest source keeps
 // 8 loads per lane in flight in one batch and narrower ones as many or more;
-// maps of at least 16 such groups take two batches per warp (up to 256
-// pixels), so that each block's multiplier pass serves twice the data.
+// when the launch still has at least 8 blocks per SM that way, warps take two
+// batches (up to 256 pixels), so that each block's multiplier pass serves
+// twice the data (small batches keep one batch per warp and more blocks).
 constexpr int kRowsMaxPixPerWarp = 256;
 
 // Lanes sharing one pixel in a load of source `ch` channels (see quant_rows_kernel).
@@ -341,7 +342,8 @@ inline int rows_pixels_per_warp(const QuantParams& q, bool i8) {
   int lmax = 1;
   for (int i = 0; i < q.nsrc; ++i) lmax = std::max(lmax, rows_lanes_per_pixel(q.src[i].ch, i8));
   const int base = 32 * 8 / lmax;
-  return (q.hp * q.wp >= 16 * base && 2 * base <= kRowsMaxPixPerWarp) ? 2 * base : base;
+  const long blocks2 = static_cast<long>(q.n) * ((q.hp * q.wp + 2 * base - 1) / (2 * base)) / 8;
+  return (blocks2 >= 8L * 148 && 2 * base <= kRowsMaxPixPerWarp) ? 2 * base : base;
 }
 
 // Channel groups of all sources: a group is the L_k chunks one load instruction covers.
