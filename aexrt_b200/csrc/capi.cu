@@ -378,7 +378,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
       // pipeline keeps min(st, max(4, 2 * pairs)) stages; the TMA box holds <= 256 rows
       if (st >= 2 && mblocks * th <= 256 && !direct_store) {
         const HaloSmemPlan one = halo_smem_plan(halo_h * pitch, boxes, 1, w_tile, oc_alloc, 0, 0, p->pg);
-        const int gbytes = halo_out_gbytes(bn, mblocks * th * tw);
+        const int gbytes = halo_out_gbytes(bn, p->pg, mblocks * th * tw);
         const int keep = std::min(st, std::max(4, 2 * pairs));
         for (int nb = 2; nb >= 1; --nb) {
           const int total = one.total_bytes + raw_slots * raw_bytes + 4 * nb * gbytes + 2048;  // + alignment
@@ -718,7 +718,7 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     if (p->out_nbuf > 0 && out_vec) {
       // staged output: the output slice as (channel, x, y, image), one box per epilogue group's
       // column block of a (super-)tile, swizzled by its row width (conv_halo.cuh halo_stage_off)
-      const int cols = halo_out_cols(p->bn);
+      const int cols = halo_out_cols(p->bn, p->pg);
       const uint64_t ldc = out_ldc, ow = p->desc.out_w, oh = p->desc.out_h;
       const uint64_t dims[4] = {oc, ow, oh, p->desc.batch};
       const uint64_t strides[3] = {2 * ldc, 2 * ldc * ow, 2 * ldc * ow * oh};
