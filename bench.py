@@ -243,7 +243,9 @@ class ClockSampler:
               "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+        # nvidia-smi numbers the GPUs physically: map this process's device through CUDA_VISIBLE_DEVICES
+        vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+        self.gpu = vis[gpu_index] if gpu_index < len(vis) else str(gpu_index)
         self.proc = None
         self.path = None
 
@@ -256,6 +258,11 @@ class ClockSampler:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            # the sampler takes a moment to start (longer when every rank starts one): wait for its
+            # first sample, so that the timed region is covered
+            t0 = time.time()
+            while time.time() - t0 < 5.0 and os.path.getsize(self.path) == 0 and self.proc.poll() is None:
+                time.sleep(0.05)
         except Exception:
             self.proc = None
         return self
