@@ -1164,6 +1164,28 @@ int amax_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t h, uint32_
                                      group_offset, mode, 1, q_out, scale_rec, stream);
 }
 
+// Whether a cluster of csize post-process CTAs with smem bytes each can be scheduled on the current
+// device (asked once per device, cluster size and the largest size seen; the kernel's shared-memory
+// attribute is raised before).
+bool nms_cluster_fits(int csize, size_t smem) {
+  static std::mutex mu;
+  static size_t ok_upto[128][9] = {};  // per device and cluster size: largest smem known schedulable
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128 || csize > 8) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (smem <= ok_upto[dev][csize]) return true;
+  cudaLaunchAttribute attr[2];
+  const cudaLaunchConfig_t cfg = launch_config(dim3(csize), dim3(aexrt::kNmsThreads), smem, nullptr,
+                                               static_cast<unsigned>(csize), attr);
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, aexrt::yolo_nms_kernel, &cfg) != cudaSuccess || clusters <= 0) {
+    cudaGetLastError();  // a refused query leaves no sticky error: the launch takes one CTA per image
+    return false;
+  }
+  ok_upto[dev][csize] = smem;
+  return true;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1645,7 +1667,9 @@ int aexrt_b200_yolo_nms_topk(const float* output0, uint32_t n, uint32_t channels
   if (nc == 0 || channels != (has_objectness ? 5u : 4u) + nc)
     return fail("yolo_nms_topk: channels %u do not match nc %u (objectness %u)", channels, nc, has_objectness);
   if (layout > 2) return fail("yolo_nms_topk: bad layout %u", layout);
-  if (mode > 1) return fail("yolo_nms_topk: bad mode %u", mode);
+  const uint32_t rule = mode & 0xFFu, ctas = (mode >> AEXRT_B200_NMS_CTAS_SHIFT) & 0xFu;
+  if (rule > 1 || (mode >> 12) != 0 || (ctas != 0 && ctas != 1 && ctas != 2 && ctas != 4 && ctas != 8))
+    return fail("yolo_nms_topk: bad mode 0x%x (rule 0 or 1, CTAs per image 0, 1, 2, 4 or 8)", mode);
   if (max_candidates == 0 || max_candidates > aexrt::kNmsMaxCandidates)
     return fail("yolo_nms_topk: max_candidates %u outside 1..%d", max_candidates, aexrt::kNmsMaxCandidates);
   if (max_detections == 0) return fail("yolo_nms_topk: max_detections must be >= 1");
@@ -1662,7 +1686,7 @@ int aexrt_b200_yolo_nms_topk(const float* output0, uint32_t n, uint32_t channels
   p.iou = iou_threshold;
   p.max_cand = static_cast<int>(max_candidates);
   p.max_det = static_cast<int>(max_detections);
-  p.mode = static_cast<int>(mode);
+  p.mode = static_cast<int>(rule);
   p.pow2 = 1;
   while (p.pow2 < p.max_cand) p.pow2 <<= 1;
   p.dets = reinterpret_cast<float*>(detections);
@@ -1685,7 +1709,22 @@ int aexrt_b200_yolo_nms_topk(const float* output0, uint32_t n, uint32_t channels
       raised[dev] = smem;
     }
   }
-  launch_kernel(aexrt::yolo_nms_kernel, dim3(n), dim3(aexrt::kNmsThreads), smem, static_cast<cudaStream_t>(stream), p);
+  // CTAs per image: automatic = the widest cluster (at most 8) whose grid still fits two CTAs per SM
+  int sms = 148;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  int csize = static_cast<int>(ctas);
+  if (csize == 0) {
+    csize = 8;
+    while (csize > 1 && static_cast<long>(n) * csize > 2L * sms) csize /= 2;
+  }
+  if (static_cast<uint64_t>(n) * csize > 0x7FFFFFFFull) return fail("yolo_nms_topk: too many images");
+  if (csize > 1 && !nms_cluster_fits(csize, smem)) csize = 1;
+  p.csize = csize;
+  launch_kernel_cluster(aexrt::yolo_nms_kernel, dim3(n * csize), dim3(aexrt::kNmsThreads), smem,
+                        static_cast<cudaStream_t>(stream), static_cast<unsigned>(csize), p);
   return cuda_ok(cudaGetLastError(), "nms launch") ? 1 : 0;
 }
 

@@ -17,21 +17,44 @@ constexpr uint32_t kLaunchProgrammatic = 1u;  // AEXRT_B200_LAUNCH_PROGRAMMATIC
 
 uint32_t launch_flags();  // this thread's flags (capi.cu)
 
-template <typename... KArgs, typename... Args>
-cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                          Args&&... args) {
+// The launch configuration of launch_kernel / launch_kernel_cluster (attr: room for two attributes).
+inline cudaLaunchConfig_t launch_config(dim3 grid, dim3 block, size_t smem, cudaStream_t stream, unsigned cluster_x,
+                                        cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cfg.attrs = attr;
   if (launch_flags() & kLaunchProgrammatic) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+    ++cfg.numAttrs;
   }
+  if (cluster_x > 1) {
+    attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+    attr[cfg.numAttrs].val.clusterDim.x = cluster_x;
+    attr[cfg.numAttrs].val.clusterDim.y = 1;
+    attr[cfg.numAttrs].val.clusterDim.z = 1;
+    ++cfg.numAttrs;
+  }
+  return cfg;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+  cudaLaunchAttribute attr[2];
+  const cudaLaunchConfig_t cfg = launch_config(grid, block, smem, stream, 1, attr);
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// launch_kernel with thread-block clusters of cluster_x CTAs along x (grid.x a multiple of it).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                  unsigned cluster_x, Args&&... args) {
+  cudaLaunchAttribute attr[2];
+  const cudaLaunchConfig_t cfg = launch_config(grid, block, smem, stream, cluster_x, attr);
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

@@ -4,9 +4,14 @@
 // (native/aexrt_d3d12_runtime.cpp:27104-27219): a decode-filter shader that
 // appends candidates with an atomic counter (:15300-15355), an O(count^2)
 // "mark" shader (:15637-15691) and a rank-by-counting top-k shader
-// (:15693-15733).  Here one CTA owns one image and does all three in shared
-// memory, so a batch is one launch and nothing but the detections and their
-// count reaches HBM:
+// (:15693-15733).  Here one thread-block cluster of 1-8 CTAs owns one image and
+// does all three in shared memory, so a batch is one launch and nothing but
+// the detections and their count reaches HBM.  Every CTA of the cluster runs
+// steps 1-2 on the same data (they come out identical); the rows of step 3
+// are spread over the cluster's warps, and CTA 0 gathers the suppressed bits
+// (mode 0) or the matrix rows (mode 1) through distributed shared memory and
+// runs step 4.  Small batches take 8 CTAs per image, so that the O(count^2)
+// pair tests of one image spread over eight SMs:
 //
 //   1. filter: the CTA walks the anchors in blocks of blockDim; a ballot +
 //      warp-total scan compacts the passing anchors in ASCENDING ANCHOR ORDER
@@ -16,13 +21,9 @@
 //      ascending: exactly the shaders' "higher" relation), then the candidates
 //      are permuted into rank order;
 //   3. suppress: for rank r < rank j, same class, IoU > threshold, r suppresses
-//      j.  Only same-class pairs can suppress, so the candidates are put in
-//      (class, rank) order by a second sort of 32-bit keys: each class is one
-//      contiguous block and a row only tests the columns after it in its own
-//      block (with 4 classes a quarter of the pairs of the full triangle).  A
-//      warp owns a row and lane l tests column 32w + l, so one ballot is one
-//      32-bit word of the row.  The suppressed bits found in class order are
-//      moved back to rank order for step 4.  Mode 0 (the reference's GPU "mark" rule) drops j if ANY
+//      j.  A warp owns a row r and lane l tests column 32w + l, so one ballot is
+//      one 32-bit word of row r and the lanes read consecutive boxes (no bank
+//      conflicts).  Mode 0 (the reference's GPU "mark" rule) drops j if ANY
 //      higher-ranked box suppresses it: the words are OR-ed per column word in
 //      shared memory, no matrix is stored.  Mode 1 (the greedy rule of
 //      yolo_postprocess, src/aexrt/yolo.py:996-1007) keeps the suppression
@@ -54,6 +55,7 @@ struct NmsParams {
   int anchors, channels, nc, has_obj, channels_last;
   float conf, iou;
   int max_cand, max_det, mode, pow2;  // pow2 = sort width >= max_cand
+  int csize;             // CTAs per image: one thread-block cluster of csize CTAs (1, 2, 4 or 8)
   float* dets;           // [n][max_det][6]: x1, y1, x2, y2, score, class
   uint32_t* counts;      // [n]
 };
@@ -63,9 +65,7 @@ struct NmsParams {
 __host__ __device__ inline size_t nms_smem_bytes(int max_cand, int pow2, int mode) {
   const int words = (max_cand + 31) / 32;
   const size_t even = static_cast<size_t>((max_cand + 1) & ~1);
-  // box, score, class, area, then the class-order permutation and block ends; sort keys; two 32-word
-  // suppression sets (rank order and class order); scan words
-  size_t b = even * (16 + 4 + 4 + 4 + 4 + 4) + static_cast<size_t>(pow2) * 8 + 64 * 4 + 2 * 32 * 4;
+  size_t b = even * (16 + 4 + 4 + 4) + static_cast<size_t>(pow2) * 8 + 64 * 4 + 32 * 4;
   if (mode == 1) b += static_cast<size_t>(max_cand) * words * 4;
   return b;
 }
@@ -106,16 +106,16 @@ __global__ void __launch_bounds__(kNmsThreads) yolo_nms_kernel(const NmsParams p
   float* score = reinterpret_cast<float*>(box + MCe);
   float* cls = score + MCe;
   float* area = cls + MCe;
-  int* perm = reinterpret_cast<int*>(area + MCe);   // class order position -> rank
-  int* bend = perm + MCe;                          // class order position -> end of its class block
-  uint64_t* key = reinterpret_cast<uint64_t*>(bend + MCe);  // 36 * MCe bytes before it: a multiple of 8
-  uint32_t* supp = reinterpret_cast<uint32_t*>(key + p.pow2);  // 32 words: suppressed / removed bits (rank order)
-  uint32_t* suppc = supp + 32;                                 // the same in class order
-  int* scan = reinterpret_cast<int*>(suppc + 32);              // warp totals + running count
-  uint32_t* mask = reinterpret_cast<uint32_t*>(scan + 64);     // mode 1: [MC][W], class order
+  uint64_t* key = reinterpret_cast<uint64_t*>(area + MCe);  // 28 * MCe bytes before it: a multiple of 8
+  uint32_t* supp = reinterpret_cast<uint32_t*>(key + p.pow2);  // 32 words: suppressed / removed bits
+  int* scan = reinterpret_cast<int*>(supp + 32);               // warp totals + running count
+  uint32_t* mask = reinterpret_cast<uint32_t*>(scan + 64);     // mode 1: [MC][W]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int img = blockIdx.x;
+  const int img = blockIdx.x / p.csize;
+  // the cluster's CTAs run steps 1-2 alike on the same data and share step 3's rows; CTA 0 of the
+  // cluster collects the suppressed bits and writes the detections
+  const uint32_t crank = p.csize > 1 ? cluster_rank() : 0u;
   const float* y = p.y + static_cast<long>(img) * p.channels * p.anchors;
   const int off = p.has_obj ? 5 : 4;
   // element (ch, a) of this image's output0
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(kNmsThreads) yolo_nms_kernel(const NmsParams p
 
   // ---- 1. filter + compaction in anchor order
   if (tid == 0) scan[32] = 0;
-  if (tid < 32) supp[tid] = suppc[tid] = 0u;
+  if (tid < 32) supp[tid] = 0;
   __syncthreads();
   for (int base = 0; base < p.anchors; base += kNmsThreads) {
     const int running = scan[32];
@@ -221,84 +221,62 @@ __global__ void __launch_bounds__(kNmsThreads) yolo_nms_kernel(const NmsParams p
   }
   __syncthreads();
 
-  // ---- 3a. class order: sort (class << 10 | rank) keys; perm[k] = rank at class position k, bend[k] =
-  // end of k's class block
-  uint32_t* ckey = reinterpret_cast<uint32_t*>(key);
-  for (int i = tid; i < p.pow2; i += kNmsThreads)
-    ckey[i] = i < count ? (static_cast<uint32_t>(cls[i]) << 10) | static_cast<uint32_t>(i) : 0xFFFFFFFFu;
-  __syncthreads();
-  for (int k = 2; k <= p.pow2; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < p.pow2; i += kNmsThreads) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint32_t ka = ckey[i], kb = ckey[ixj];
-          const bool up = (i & k) == 0;
-          if ((ka > kb) == up) {
-            ckey[i] = kb;
-            ckey[ixj] = ka;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-  for (int k = tid; k < count; k += kNmsThreads) {
-    perm[k] = static_cast<int>(ckey[k] & 1023u);
-    // first position past k's class: binary search over the sorted keys
-    const uint32_t lim = ((ckey[k] >> 10) + 1) << 10;
-    int lo = k + 1, hi = count;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if (ckey[mid] < lim) lo = mid + 1; else hi = mid;
-    }
-    bend[k] = lo;
-  }
-  __syncthreads();
-
-  // ---- 3b. suppression words in class order: bit j of word (k, w) = position k suppresses position
-  // j = 32w + bit (same class block, k before j, so rank(k) < rank(j))
+  // ---- 3. suppression words: bit j of word (r, w) = rank r suppresses rank j = 32w + bit
   const int wc = (count + 31) / 32;
   const bool fast = p.iou >= 1e-20f && p.iou <= 1e20f;
   const float thr_hi = __fmul_rn(p.iou, 1.0f + 0x1p-20f), thr_lo = __fmul_rn(p.iou, 1.0f - 0x1p-20f);
-  for (int k = warp; k < count; k += kNmsThreads / 32) {  // rows round-robin over the warps
-    const int r = perm[k];
+  // rows round-robin over the warps of the cluster; the greedy rule's matrix rows go to CTA 0
+  constexpr int kWarps = kNmsThreads / 32;
+  for (int r = warp + kWarps * static_cast<int>(crank); r < count; r += kWarps * p.csize) {
     const float4 br = box[r];
-    const float ar = area[r];
-    const int e = bend[k];
-    const int w0 = (k + 1) >> 5, w1 = (e + 31) >> 5;  // words holding columns in (k, e)
+    const float cr = cls[r], ar = area[r];
+    const int w0 = (r + 1) >> 5;  // first word holding a column > r
     if (p.mode == 1)
-      for (int w = lane; w < W; w += 32)
-        if (w < w0 || w >= w1) mask[k * W + w] = 0u;
-    for (int w = w0; w < w1; ++w) {
+      for (int w = lane; w < w0; w += 32) {
+        if (crank == 0)
+          mask[r * W + w] = 0u;
+        else
+          st_peer_u32(&mask[r * W + w], 0, 0u);
+      }
+    for (int w = w0; w < wc; ++w) {
       const int j = w * 32 + lane;
-      const bool s = j > k && j < e &&
-                     nms_suppresses(br, ar, box[perm[min(j, count - 1)]], area[perm[min(j, count - 1)]], p.iou,
-                                    thr_lo, thr_hi, fast);
+      const bool s = j > r && j < count && cls[j] == cr &&
+                     nms_suppresses(br, ar, box[j], area[j], p.iou, thr_lo, thr_hi, fast);
       const uint32_t bits = __ballot_sync(0xffffffffu, s);
       if (lane == 0) {
-        if (p.mode == 1)
-          mask[k * W + w] = bits;
-        else if (bits)
-          atomicOr(&suppc[w], bits);
+        if (p.mode == 1) {
+          if (crank == 0)
+            mask[r * W + w] = bits;
+          else
+            st_peer_u32(&mask[r * W + w], 0, bits);
+        } else if (bits) {
+          atomicOr(&supp[w], bits);
+        }
       }
     }
   }
   __syncthreads();
-  if (p.mode == 1 && warp == 0) {
-    // greedy: rows in class order (each class in rank order); a row that is still standing removes
-    // what it suppresses
-    uint32_t removed = 0;  // word `lane`
-    for (int k = 0; k < count; ++k) {
-      const uint32_t word = __shfl_sync(0xffffffffu, removed, k >> 5);
-      if (!((word >> (k & 31)) & 1u) && lane < wc) removed |= mask[k * W + lane];
+  if (p.csize > 1) {
+    // every CTA's rows are in (mode 1: CTA 0's matrix; mode 0: each CTA's own words); CTA 0 ORs the
+    // words of the others, which stay resident until it has read them (second barrier)
+    cluster_sync_all();
+    if (p.mode == 0 && crank == 0 && tid < wc) {
+      uint32_t v = supp[tid];
+      for (int r = 1; r < p.csize; ++r) v |= ld_peer_u32(&supp[tid], static_cast<uint32_t>(r));
+      supp[tid] = v;
     }
-    suppc[lane] = removed;
+    cluster_sync_all();
+    if (crank != 0) return;
   }
-  __syncthreads();
-  // ---- 3c. back to rank order
-  for (int k = tid; k < count; k += kNmsThreads)
-    if ((suppc[k >> 5] >> (k & 31)) & 1u) atomicOr(&supp[perm[k] >> 5], 1u << (perm[k] & 31));
+  if (p.mode == 1 && warp == 0) {
+    // greedy: rows in rank order; a row that is still standing removes what it suppresses
+    uint32_t removed = 0;  // word `lane`
+    for (int r = 0; r < count; ++r) {
+      const uint32_t word = __shfl_sync(0xffffffffu, removed, r >> 5);
+      if (!((word >> (r & 31)) & 1u) && lane < wc) removed |= mask[r * W + lane];
+    }
+    supp[lane] = removed;
+  }
   __syncthreads();
 
   // ---- 4. top-k: kept = not suppressed; slot = kept ranks before this one

@@ -36,18 +36,6 @@ constexpr int kClusterQuantMaxCtas = 8;     // portable cluster size
 constexpr int kClusterQuantMaxSliceBytes = 112 * 1024;
 constexpr uint32_t kSliceFailed = 0x80000000u;
 
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// 32-bit load from the shared memory of CTA `rank` of this cluster, at the address of `p` in ours.
-__device__ __forceinline__ uint32_t ld_peer_u32(const void* p, uint32_t rank) {
-  uint32_t remote, v;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(p)), "r"(rank));
-  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(remote) : "memory");
-  return v;
-}
-
 // Codes of one channel for two pixels: low byte of round_half_even(fl32(x * mult)) by the
 // 1.5 * 2^23 addend, exact because |x * mult| <= 127 here (x is bounded by the amax that mult
 // comes from).  The product is rounded on its own (packed multiply, then separate adds).

@@ -50,6 +50,7 @@ class NmsConfig:
     max_candidates: int = 512
     max_detections: int = 100
     mode: int = ops.NMS_MARK  # the reference GPU path's rule; ops.NMS_GREEDY = yolo_postprocess's
+    ctas_per_image: int = 0   # 0 automatic (8 for small batches), else 1, 2, 4 or 8
 
 
 class CompiledYolo:
@@ -334,7 +335,8 @@ class CompiledYolo:
                 counts, dets = self.split_detections(self.det_buf)
                 check(lib.aexrt_b200_yolo_nms_topk(self.output.data_ptr(), n, 4 + c.nc, self.program.anchors, c.nc, 0,
                                                    1, cfg.conf, cfg.iou, cfg.max_candidates, cfg.max_detections,
-                                                   cfg.mode, dets.data_ptr(), counts.data_ptr(), stream), "nms")
+                                                   cfg.mode | (cfg.ctas_per_image << ops.NMS_CTAS_SHIFT),
+                                                   dets.data_ptr(), counts.data_ptr(), stream), "nms")
 
     def capture(self) -> None:
         """Records one forward into a CUDA graph (warm-up run first, as graph capture requires)."""

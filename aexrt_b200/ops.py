@@ -35,6 +35,7 @@ SCALE_PER_TENSOR = 0
 SCALE_PG16 = 1
 NMS_MARK = 0
 NMS_GREEDY = 1
+NMS_CTAS_SHIFT = 8  # AEXRT_B200_NMS_CTAS_SHIFT: mode bits 8-11 = CTAs per image
 
 
 def _torch():
@@ -356,13 +357,15 @@ def conv_w8a8_layer(plan: ConvPlan, x_nhwc, mode: int = SCALE_PER_TENSOR, residu
 
 def yolo_nms_topk(output0, nc: int, conf: float = 0.25, iou: float = 0.45, max_candidates: int = 512,
                   max_detections: int = 100, mode: int = NMS_MARK, has_objectness: bool = False,
-                  channels_last: bool = False, dets=None, counts=None, stream=None):
+                  channels_last: bool = False, dets=None, counts=None, stream=None, ctas_per_image: int = 0):
     """Detections of a batch of fp32 output0 tensors ([n, 4 + nc, anchors], or [n, anchors, 4 + nc]
     when `channels_last`): returns (dets [n, max_detections, 6] fp32 rows x1, y1, x2, y2, score,
     class; counts [n] int32).  Rows at and beyond counts[i] are zero.
 
     Defaults are the reference model's (runtime.cpp:551-561): 512 candidates, 100 detections,
-    conf 0.25, IoU 0.45, the GPU path's NMS rule; ``mode=NMS_GREEDY`` gives yolo_postprocess's."""
+    conf 0.25, IoU 0.45, the GPU path's NMS rule; ``mode=NMS_GREEDY`` gives yolo_postprocess's.
+    ``ctas_per_image`` (0 automatic, else 1, 2, 4 or 8): the thread-block cluster that shares one
+    image's pair tests; the detections do not depend on it."""
     torch = _torch()
     n = output0.shape[0]
     channels = output0.shape[2] if channels_last else output0.shape[1]
@@ -373,5 +376,6 @@ def yolo_nms_topk(output0, nc: int, conf: float = 0.25, iou: float = 0.45, max_c
         counts = torch.zeros((n,), dtype=torch.int32, device=output0.device)
     check(_native.load().aexrt_b200_yolo_nms_topk(
         output0.data_ptr(), n, channels, anchors, nc, int(has_objectness), 2 if channels_last else 1, conf, iou,
-        max_candidates, max_detections, mode, dets.data_ptr(), counts.data_ptr(), _stream(stream)), "yolo_nms_topk")
+        max_candidates, max_detections, mode | (ctas_per_image << NMS_CTAS_SHIFT), dets.data_ptr(), counts.data_ptr(),
+        _stream(stream)), "yolo_nms_topk")
     return dets, counts

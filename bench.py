@@ -84,6 +84,9 @@ def parse_args():
                     help="extra plan tuning bits for every conv (block_n bits 16-31, e.g. 0x10000000 direct stores)")
     ap.add_argument("--amax-out", action="store_true",
                     help="layer workloads: the conv also maxes |y| per 16-channel group for the next layer")
+    ap.add_argument("--chain", type=int, default=0,
+                    help="layer workloads: time N back-to-back conv launches in one CUDA graph (programmatic "
+                         "dependent launch, as inside a batch-1 model graph) and report the time per launch")
     ap.add_argument("--engine", default=None,
                     help="time an .aexrt engine compiled by the reference (e.g. tests/golden/yolov8n_w8a8.aexrt) "
                          "through the reference runtime ABI (libaexrt_b200.so aexrt_yolo_*), batch --batch (256)")
@@ -166,6 +169,27 @@ def run_layer(args):
         desc = (f"conv {ic}->{oc} k{k} s{s} @{h}x{w}, batch {n}, {'pg16' if args.mode else 'per-tensor'}"
                 f"{', amax out' if args.amax_out else ''}{f', order {args.order}' if args.order else ''}"
                 " (BASELINE configs 1-2)")
+    per = 1
+    if args.chain > 0 and args.workload in LAYERS:
+        # N launches of the conv in one graph, each a programmatic dependent of the one before (the
+        # form a batch-1 model graph takes): the time per launch is the conv's cost inside a forward
+        from aexrt_b200 import _native
+
+        lib = _native.load()
+        _native.check(lib.aexrt_b200_set_launch_flags(_native.LAUNCH_PROGRAMMATIC), "launch flags")
+        step()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(args.chain):
+                    step()
+        torch.cuda.current_stream().wait_stream(s)
+        lib.aexrt_b200_set_launch_flags(0)
+        step = g.replay
+        per = args.chain
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
@@ -179,10 +203,12 @@ def run_layer(args):
         e1.record()
         torch.cuda.synchronize()
         ts.append(e0.elapsed_time(e1) / 1e3)
-    t = statistics.median(ts)
+    t = statistics.median(ts) / per
     int8_peak = 2.0 * bf16
     line = {"metric": f"{args.workload} kernel time", "value": t * 1e3, "unit": "ms", "higher_is_better": False,
-            "steps": args.steps, "warmup": args.warmup, "config": {"workload": desc, "l2": "flushed between steps"},
+            "steps": args.steps, "warmup": args.warmup,
+            "config": {"workload": desc + (f", {per} launches per graph (programmatic)" if per > 1 else ""),
+                       "l2": "flushed between steps"},
             "achieved_gbs": byts / t / 1e9, "hbm_frac": byts / t / 1e9 / hbm}
     if ops_:
         line.update({"achieved_tops": ops_ / t / 1e12, "tensor_frac": ops_ / t / 1e12 / int8_peak,

@@ -371,7 +371,12 @@ typedef struct AexrtYoloDetection {
  *   are the candidates; NMS per class with IoU > iou_threshold; the kept boxes by
  *   (score desc, anchor order) fill detections[img * max_detections ...] and
  *   counts[img] = min(kept, max_detections); the rows after the count are zeroed.
- *   max_candidates <= AEXRT_B200_NMS_MAX_CANDIDATES (the reference default is 512). */
+ *   max_candidates <= AEXRT_B200_NMS_MAX_CANDIDATES (the reference default is 512).
+ *   mode: the rule (AEXRT_B200_NMS_MARK / _GREEDY) in bits 0-7; bits 8-11 the CTAs
+ *   per image (0 automatic: 8 for small batches down to 1 for large ones; else 1, 2,
+ *   4 or 8), one thread-block cluster per image that shares the pair tests.  The
+ *   detections do not depend on it. */
+#define AEXRT_B200_NMS_CTAS_SHIFT 8u
 int aexrt_b200_yolo_nms_topk(const float* output0, uint32_t n, uint32_t channels, uint32_t anchors, uint32_t nc,
                              uint32_t has_objectness, uint32_t layout, float conf_threshold, float iou_threshold,
                              uint32_t max_candidates, uint32_t max_detections, uint32_t mode,

@@ -11,20 +11,20 @@ from oracle import yolo_post as op
 pytestmark = pytest.mark.gpu
 
 
-def _run(y, nc, conf, iou, mc, md, mode, has_obj=False, channels_last=False):
+def _run(y, nc, conf, iou, mc, md, mode, has_obj=False, channels_last=False, ctas=0):
     import torch
 
     from aexrt_b200 import ops
 
     t = torch.from_numpy(np.ascontiguousarray(y, dtype=np.float32)).cuda()
     dets, counts = ops.yolo_nms_topk(t, nc, conf, iou, mc, md, mode, has_objectness=has_obj,
-                                     channels_last=channels_last)
+                                     channels_last=channels_last, ctas_per_image=ctas)
     torch.cuda.synchronize()
     return dets.cpu().numpy(), counts.cpu().numpy()
 
 
-def _check(y, nc, conf, iou, mc, md, mode, has_obj=False, channels_last=False):
-    dets, counts = _run(y, nc, conf, iou, mc, md, mode, has_obj, channels_last)
+def _check(y, nc, conf, iou, mc, md, mode, has_obj=False, channels_last=False, ctas=0):
+    dets, counts = _run(y, nc, conf, iou, mc, md, mode, has_obj, channels_last, ctas)
     for i in range(y.shape[0]):
         ref, cnt = op.postprocess(y[i], nc, conf, iou, mc, md, mode, has_obj, channels_last)
         assert counts[i] == cnt, (i, counts[i], cnt)
@@ -62,6 +62,36 @@ def test_batch_matches_oracle(mode):
     y = _clustered(rng, 5, 4, 2100, 25)  # YOLOv8n-320: 2100 anchors
     counts = _check(y, 4, 0.25, 0.45, 512, 100, mode)
     assert counts.max() > 0
+
+
+@pytest.mark.parametrize("ctas", [1, 2, 4, 8])
+@pytest.mark.parametrize("mode", [op.MODE_MARK, op.MODE_GREEDY])
+def test_cluster_sizes_give_the_same_detections(mode, ctas):
+    # one image's pair tests shared by a cluster of 1-8 CTAs; the full candidate cap (the greedy
+    # matrix at its largest) and a small one that leaves most CTAs without rows
+    rng = np.random.default_rng(70 + mode)
+    y = _clustered(rng, 3, 4, 8400, 120)
+    _check(y, 4, 0.05, 0.45, 1024, 300, mode, ctas=ctas)
+    _check(y[:1], 4, 0.25, 0.45, 40, 10, mode, ctas=ctas)
+
+
+def test_automatic_cluster_size_across_batches():
+    # automatic CTAs per image: 8 (batch 1-37), 4, 2, then 1 from batch 149 on
+    rng = np.random.default_rng(77)
+    base = _clustered(rng, 4, 4, 2100, 25)
+    for n in (1, 40, 100, 160):
+        y = base[np.arange(n) % 4]
+        _check(y, 4, 0.25, 0.45, 512, 100, op.MODE_MARK)
+
+
+def test_bad_cluster_size_is_refused():
+    import torch
+
+    from aexrt_b200 import ops
+
+    t = torch.zeros((1, 8, 64), dtype=torch.float32, device="cuda")
+    with pytest.raises(RuntimeError, match="mode"):
+        ops.yolo_nms_topk(t, 4, ctas_per_image=3)
 
 
 @pytest.mark.parametrize("mc,md", [(512, 100), (300, 1000), (1024, 1024), (1, 1), (37, 5)])
