@@ -196,6 +196,9 @@ def run_layer(args):
     ts = []
     for _ in range(args.steps):
         flush.zero_()  # inputs of some layers fit in L2: flush it between timed iterations
+        # the stream waits ~0.5 ms while the host enqueues the events and the launch, so the event
+        # pair brackets the kernel, not the host's launch latency
+        torch.cuda._sleep(1_000_000)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -342,6 +345,10 @@ def conv_roofline(eng, torch, stream):
     lib = eng.lib
     n = eng.batch
     recs = []
+    torch.cuda.synchronize()
+    # hold the stream for ~0.1 s so that the host enqueues every launch below before the first one
+    # runs: an event pair then brackets its kernel alone, not the host's launch latency
+    torch.cuda._sleep(200_000_000)
     check(lib.aexrt_b200_zero(eng.amax_arena.data_ptr(), eng.amax_arena.numel() * 4, stream), "zero")
     for st in eng.steps:
         if st[0] not in ("conv", "conv_ql") or st[1].precision != "int8":
