@@ -292,9 +292,115 @@ def apply(model, algo_map: Optional[str] = None, variants: Optional[str] = None)
             model.override_conv_variant(int(cmd), int(bits))
 
 
+# built-in programs: builder, image size, classes (the bench's workloads)
+PROGRAMS = {"yolov8n-320": ("build_yolov8n", 320, 4), "yolov8s-640": ("build_yolov8s", 640, 80),
+            "yolov11s-320": ("build_yolov11s", 320, 80)}
+
+
+def program_tile_candidates(c, bn_default: int) -> List[int]:
+    """Tile choices of one int8 conv of a program: every output-channel tile the halo kernel has
+    (16-256, at most twice the channels), then, around the best of those, strided and contiguous tile
+    order, one or two stacked M blocks (3x3 stride 1) and the staged epilogue."""
+    bns = [b for b in (16, 32, 64, 128, 256) if b <= max(32, 2 * c.oc) and (not c.pg16 or b in (64, 128))]
+    return [b for b in bns if b != bn_default]
+
+
+def tune_program(program, batch: int, runs: int = 10, log=print, seed: int = 0) -> Dict[str, int]:
+    """Per-conv tile choice for a program compiled by :class:`aexrt_b200.engine.CompiledYolo` (the
+    streaming engine the bench runs), on the current GPU.
+
+    After one forward on seeded images every int8 conv's own inputs (codes and scale record) are in
+    its scratch.  Each conv is then timed alone, ``runs`` back-to-back launches between one CUDA-event
+    pair, with its default plan and with every candidate tile (:func:`program_tile_candidates`, then
+    order / stacked-M / staged bits on the best tile).  A candidate must write the default plan's
+    output bit for bit (integer accumulation makes every int8 tile exact, so the gate only rejects a
+    broken plan) and is kept only when more than 5 % faster (the reference tuner's rule,
+    ``conv_autotune.cpp:336-345``).  Returns ``{conv name: block_n bits}`` for
+    ``CompiledYolo(block_n=...)``; convs whose default stays best are left out."""
+    import torch
+
+    from . import engine, ops
+
+    eng = engine.CompiledYolo(program, batch)
+    rng = np.random.default_rng(seed)
+    imgs = torch.from_numpy(rng.uniform(0, 1, (batch, program.in_channels, program.imgsz, program.imgsz))
+                            .astype(np.float16)).cuda()
+    eng.forward(imgs)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+
+    def timed(plan, q, rec, c, out, res, amax_out):
+        def once():
+            plan.run(q, rec, out=out, out_coff=c.out[1], residual=res,
+                     res_coff=c.residual[1] if c.residual is not None else 0, amax_out=amax_out,
+                     amax_goff=c.out[1] // 16, stream=stream.cuda_stream)
+        once()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(20_000_000)  # the host enqueues every launch before the first one runs
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(runs):
+            once()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / runs
+
+    chosen: Dict[str, int] = {}
+    for st in eng.steps:
+        if st[0] != "conv" or st[1].precision != "int8":
+            continue
+        _, c, plan0, _, (q, rec), (h, w) = st
+        out = eng.values[c.out[0]]
+        res = eng.values[c.residual[0]] if c.residual is not None else None
+        amax_out = eng._amax_view(c.out[0]) if c.out[0] in eng.needs_amax else None
+        t0 = timed(plan0, q, rec, c, out, res, amax_out)
+        ref = out[..., c.out[1]:c.out[1] + c.oc].clone()
+        codes, scale = ops.quantize_conv_weight_int8(c.weight)
+
+        def trial(bits):
+            try:
+                plan = ops.ConvPlan.int8(batch, c.ic, h, w, c.oc, c.k, c.s, codes, scale, c.bias, silu=c.silu,
+                                         pg16=c.pg16, block_n=bits)
+            except RuntimeError:
+                return None  # this tile does not fit the conv: the plan is refused
+            out[..., c.out[1]:c.out[1] + c.oc].fill_(0.0)
+            t = timed(plan, q, rec, c, out, res, amax_out)
+            if plan.status() != 0 or not torch.equal(out[..., c.out[1]:c.out[1] + c.oc], ref):
+                log(f"  {c.name} bits {bits:#x}: output differs, rejected")
+                return None
+            return t
+
+        bn0 = plan0.info.block_n
+        best_t, best_bits = t0, 0
+        for bn in program_tile_candidates(c, bn0):
+            t = trial(bn)
+            if t is not None and t < best_t:
+                best_t, best_bits = t, bn
+        base = best_bits or bn0
+        extra = [base | (1 << 20), base | (2 << 20), base | (1 << 29)]
+        if c.k == 3 and c.s == 1 and base <= 64:
+            extra += [base | (1 << 24), base | (2 << 24)]
+        for bits in extra:
+            t = trial(bits)
+            if t is not None and t < best_t:
+                best_t, best_bits = t, bits
+        out[..., c.out[1]:c.out[1] + c.oc].copy_(ref)
+        if best_bits and best_t < t0 * SIGNIFICANCE:
+            chosen[c.name] = best_bits
+            log(f"{c.name}: {t0 * 1e3:.1f} -> {best_t * 1e3:.1f} us with bits {best_bits:#x}")
+        else:
+            log(f"{c.name}: {t0 * 1e3:.1f} us, default kept")
+    return chosen
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("engine")
+    ap.add_argument("engine", nargs="?", default=None)
+    ap.add_argument("--program", default=None,
+                    help="instead of an engine: tune the tiles of a built-in program (yolov8n-320, yolov8s-640, "
+                         "yolov11s-320) compiled for --batch by the streaming engine; writes --tiles-out")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--tiles-out", default=None, help="--program: JSON {conv name: block_n bits}")
     ap.add_argument("--images", type=int, default=1)
     ap.add_argument("--runs", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
@@ -304,6 +410,18 @@ def main(argv=None) -> int:
     ap.add_argument("--variants", default=None, help="JSON {command: tile bits} of this backend")
     ap.add_argument("--report", default=None)
     a = ap.parse_args(argv)
+    if a.program:
+        from . import yolo
+
+        builder, imgsz, nc = PROGRAMS[a.program]
+        tiles = tune_program(getattr(yolo, builder)(nc=nc, imgsz=imgsz, seed=0), a.batch, runs=a.runs)
+        if a.tiles_out:
+            with open(a.tiles_out, "w") as f:
+                json.dump(tiles, f, indent=1, sort_keys=True)
+        print(json.dumps(tiles))
+        return 0
+    if a.engine is None:
+        ap.error("an engine file or --program is required")
     t = Tuner(a.engine, a.images, a.runs, a.warmup)
     ok = t.tune(a.shape_limit, variants=not a.no_variants)
     t.write(a.report, a.emit_map, a.variants)

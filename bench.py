@@ -64,6 +64,9 @@ def parse_args():
                          "64 for the layer workloads)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--conv-table", action="store_true",
+                    help="model workloads: print every W8A8 conv launch of the roofline pass (time, GB/s, TOPS) "
+                         "to stderr")
     ap.add_argument("--onnx", default=None,
                     help="model workloads: the program comes from this ONNX YOLO graph (imported without onnx)")
     ap.add_argument("--programmatic", default="auto", choices=["auto", "on", "off"],
@@ -91,6 +94,10 @@ def parse_args():
                     help="time an .aexrt engine compiled by the reference (e.g. tests/golden/yolov8n_w8a8.aexrt) "
                          "through the reference runtime ABI (libaexrt_b200.so aexrt_yolo_*), batch --batch (256)")
     ap.add_argument("--algo-map", default=None, help="--engine: a tuned {command: algorithm} map to apply")
+    ap.add_argument("--tiles", default=None,
+                    help="model workloads: a tuned {conv name: tile bits} map (python -m aexrt_b200.autotune "
+                         "--program ... --tiles-out FILE) applied at compile time; default "
+                         "aexrt_b200/tuned/<workload>_b<batch>.json when it exists, 'none' for the heuristics")
     ap.add_argument("--variants", default=None, help="--engine: a tuned {command: tile bits} sidecar to apply")
     return ap.parse_args()
 
@@ -380,12 +387,15 @@ def conv_roofline(eng, torch, stream):
         d = eng.program.values[c.out[0]]
         ops = 2.0 * n * d.h * d.w * c.oc * c.ic * c.k * c.k
         byts = n * (in_bytes * c.ic * h * w + 2 * c.oc * d.h * d.w) + c.oc * c.ic * c.k * c.k
-        recs.append((e0, e1, ops, byts))
+        name = f"{c.name} {c.ic}->{c.oc} k{c.k} s{c.s} @{h}x{w}{' pg16' if c.pg16 else ''}"
+        recs.append((e0, e1, ops, byts, name))
     torch.cuda.synchronize()
-    t = sum(e0.elapsed_time(e1) for e0, e1, _, _ in recs) / 1e3
+    t = sum(r[0].elapsed_time(r[1]) for r in recs) / 1e3
     ops = sum(r[2] for r in recs)
     byts = sum(r[3] for r in recs)
-    return {"time_s": t, "ops": ops, "bytes": byts, "launches": len(recs)}
+    table = [{"conv": r[4], "us": r[0].elapsed_time(r[1]) * 1e3, "gbs": r[3] / (r[0].elapsed_time(r[1]) / 1e3) / 1e9,
+              "tops": r[2] / (r[0].elapsed_time(r[1]) / 1e3) / 1e12} for r in recs]
+    return {"time_s": t, "ops": ops, "bytes": byts, "launches": len(recs), "table": table}
 
 
 def run_reference(args):
@@ -454,8 +464,17 @@ def run_ours(args):
         tb = torch.tensor([B], device="cuda")
         dist.all_reduce(tb)
         total = int(tb.item())  # images of one step over all ranks
+    # the autotuner's tile plan for this workload and batch (aexrt_b200/tuned/), unless --tiles names
+    # another map or "none"
+    tiles_path = args.tiles
+    if tiles_path is None:
+        cand = os.path.join(ROOT, "aexrt_b200", "tuned", f"{args.workload}_b{B}.json")
+        tiles_path = cand if os.path.exists(cand) and not args.onnx else None
+    elif tiles_path == "none":
+        tiles_path = None
+    tiles = json.load(open(tiles_path)) if tiles_path else None
     eng = engine.CompiledYolo(program, B, nms=engine.NmsConfig(), quant_on_load=args.quant_on_load,
-                              plan_bits=args.plan_bits,
+                              plan_bits=args.plan_bits, block_n=tiles,
                               programmatic=None if args.programmatic == "auto" else args.programmatic == "on")
     # fp16 images, as BASELINE's config feeds them (uniform[0,1]); image k of the job from seed 1000 + k
     host_in = torch.from_numpy(np.stack([np.random.default_rng(1000 + start + k).uniform(0, 1, (3, imgsz, imgsz))
@@ -539,6 +558,9 @@ def run_ours(args):
     status = eng.status()
     # roofline of the dominant kernel (W8A8 conv), measured per launch with CUDA events
     rf = conv_roofline(eng, torch, stream.cuda_stream)
+    if args.conv_table and rank == 0:
+        for r in sorted(rf["table"], key=lambda r: -r["us"]):
+            print(f"{r['conv']:48s} {r['us']:8.1f} us {r['gbs']:7.0f} GB/s {r['tops']:6.0f} TOPS", file=sys.stderr)
     hbm, bf16, src = measured_peaks()
     int8_peak = 2.0 * bf16  # dense int8 tensor throughput is twice bf16 on B200
     achieved = rf["ops"] / rf["time_s"] / 1e12
@@ -563,7 +585,9 @@ def run_ours(args):
                              "per step)",
                        **({"quant_on_load": True} if args.quant_on_load else {}),
                        "programmatic_launch": eng.programmatic,
-                       **({"plan_bits": hex(args.plan_bits)} if args.plan_bits else {})},
+                       **({"plan_bits": hex(args.plan_bits)} if args.plan_bits else {}),
+                       "tiles": (f"autotuned: {os.path.relpath(tiles_path, ROOT)} ({len(tiles)} of the int8 convs "
+                                 "off the default tile)" if tiles_path else "default heuristics")},
             "e2e": e2e,
             "gpu_launches": eng.launches_per_run * args.steps,
             "roofline": {"bound": "hbm", "achieved": rf["bytes"] / rf["time_s"] / 1e9, "peak": hbm, "unit": "GB/s",

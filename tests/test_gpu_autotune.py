@@ -34,3 +34,29 @@ def test_autotune_gate_map_and_replay(tmp_path):
     assert np.array_equal(m.output0(), tuned_out)
     assert m.status() == 0
     m.close()
+
+
+def test_program_tile_tuning_replays_bit_identically():
+    """The tile stage for the streaming engine's programs (autotune.tune_program): every choice it
+    returns is a tile the int8 kernels accept, and a model compiled with the tuned tiles gives the
+    default model's output0 and detections bit for bit."""
+    import torch
+
+    from aexrt_b200 import autotune, engine, yolo
+
+    program = yolo.build_yolov8n(nc=4, imgsz=96, seed=3)
+    logs = []
+    tiles = autotune.tune_program(program, 2, runs=2, log=logs.append)
+    names = {c.name for c in program.commands if getattr(c, "precision", None) == "int8"}
+    assert set(tiles) <= names
+    assert len(logs) == len(names)
+    imgs = torch.from_numpy(np.random.default_rng(5).uniform(0, 1, (2, 3, 96, 96)).astype(np.float16)).cuda()
+    outs = []
+    for bn in (None, tiles):
+        eng = engine.CompiledYolo(program, 2, block_n=bn, nms=engine.NmsConfig())
+        eng.forward(imgs)
+        torch.cuda.synchronize()
+        assert eng.status() == 0
+        outs.append((eng.output.cpu().numpy(), eng.det_buf.cpu().numpy()))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert np.array_equal(outs[0][1], outs[1][1])
