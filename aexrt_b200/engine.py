@@ -453,13 +453,21 @@ def main(argv=None) -> int:
     ap.add_argument("--no-nms", action="store_true", help="stop at output0 (no GPU filter + NMS + top-k)")
     ap.add_argument("--model", default="yolov8n", choices=["yolov8n", "yolov8s", "yolov11s"])
     ap.add_argument("--programmatic", default="auto", choices=["auto", "on", "off"])
+    ap.add_argument("--tiles", default=None, help="a tuned {conv name: tile bits} map (python -m "
+                    "aexrt_b200.autotune --program ... --tiles-out FILE)")
     a = ap.parse_args(argv)
     torch = _torch()
     if a.model == "yolov8n":
         program = yolo.build_yolov8n(nc=4, imgsz=a.imgsz, seed=0)
     else:
         program = getattr(yolo, f"build_{a.model}")(nc=80, imgsz=a.imgsz, seed=0)
-    eng = CompiledYolo(program, a.batch, nms=None if a.no_nms else NmsConfig(),
+    tiles = None
+    if a.tiles:
+        import json
+
+        with open(a.tiles) as f:
+            tiles = json.load(f)
+    eng = CompiledYolo(program, a.batch, nms=None if a.no_nms else NmsConfig(), block_n=tiles,
                        programmatic=None if a.programmatic == "auto" else a.programmatic == "on")
     x = torch.from_numpy(np.random.default_rng(0).uniform(0, 1, (a.batch, 3, a.imgsz, a.imgsz)).astype(np.float16))
     x = x.to(eng.device)
