@@ -315,7 +315,8 @@ def tune_program(program, batch: int, runs: int = 10, log=print, seed: int = 0) 
     order / stacked-M / staged bits on the best tile).  A candidate must write the default plan's
     output bit for bit (integer accumulation makes every int8 tile exact, so the gate only rejects a
     broken plan) and is kept only when more than 5 % faster (the reference tuner's rule,
-    ``conv_autotune.cpp:336-345``).  Returns ``{conv name: block_n bits}`` for
+    ``conv_autotune.cpp:336-345``).  The fp16 convs that read their NHWC input directly (the detect
+    head) are swept the same way, halo tiles only.  Returns ``{conv name: block_n bits}`` for
     ``CompiledYolo(block_n=...)``; convs whose default stays best are left out."""
     import torch
 
@@ -331,9 +332,15 @@ def tune_program(program, batch: int, runs: int = 10, log=print, seed: int = 0) 
 
     def timed(plan, q, rec, c, out, res, amax_out):
         def once():
-            plan.run(q, rec, out=out, out_coff=c.out[1], residual=res,
-                     res_coff=c.residual[1] if c.residual is not None else 0, amax_out=amax_out,
-                     amax_goff=c.out[1] // 16, stream=stream.cuda_stream)
+            if plan.is_f16:
+                # fp16 head convs read the NHWC activation itself (q is that tensor)
+                plan.run_nhwc(q, x_coff=c.inputs[0].coff, out=out, out_coff=c.out[1], residual=res,
+                              res_coff=c.residual[1] if c.residual is not None else 0, amax_out=amax_out,
+                              amax_goff=c.out[1] // 16, stream=stream.cuda_stream)
+            else:
+                plan.run(q, rec, out=out, out_coff=c.out[1], residual=res,
+                         res_coff=c.residual[1] if c.residual is not None else 0, amax_out=amax_out,
+                         amax_goff=c.out[1] // 16, stream=stream.cuda_stream)
         once()
         torch.cuda.synchronize()
         torch.cuda._sleep(20_000_000)  # the host enqueues every launch before the first one runs
@@ -347,20 +354,33 @@ def tune_program(program, batch: int, runs: int = 10, log=print, seed: int = 0) 
 
     chosen: Dict[str, int] = {}
     for st in eng.steps:
-        if st[0] != "conv" or st[1].precision != "int8":
+        if st[0] == "conv" and st[1].precision == "int8":
+            _, c, plan0, _, (q, rec), (h, w) = st
+        elif st[0] == "conv_nhwc":
+            # fp16 stride-1 convs reading the NHWC activation: within the halo kernel every tile sums
+            # K in the same order, so these are exact too (the gate still checks)
+            _, c, plan0 = st
+            q, rec = eng.values[c.inputs[0].value], None
+            h, w = eng._spatial(c.inputs[0])
+        else:
             continue
-        _, c, plan0, _, (q, rec), (h, w) = st
         out = eng.values[c.out[0]]
         res = eng.values[c.residual[0]] if c.residual is not None else None
         amax_out = eng._amax_view(c.out[0]) if c.out[0] in eng.needs_amax else None
         t0 = timed(plan0, q, rec, c, out, res, amax_out)
         ref = out[..., c.out[1]:c.out[1] + c.oc].clone()
-        codes, scale = ops.quantize_conv_weight_int8(c.weight)
+        codes, scale = (None, None) if plan0.is_f16 else ops.quantize_conv_weight_int8(c.weight)
 
         def trial(bits):
             try:
-                plan = ops.ConvPlan.int8(batch, c.ic, h, w, c.oc, c.k, c.s, codes, scale, c.bias, silu=c.silu,
-                                         pg16=c.pg16, block_n=bits)
+                if plan0.is_f16:
+                    plan = ops.ConvPlan.fp16(batch, c.ic, h, w, c.oc, c.k, c.s, c.weight, c.bias, silu=c.silu,
+                                             block_n=bits)
+                    if plan.info.variant != 2:
+                        return None  # the slot kernel cannot read NHWC (and sums K in another order)
+                else:
+                    plan = ops.ConvPlan.int8(batch, c.ic, h, w, c.oc, c.k, c.s, codes, scale, c.bias,
+                                             silu=c.silu, pg16=c.pg16, block_n=bits)
             except RuntimeError:
                 return None  # this tile does not fit the conv: the plan is refused
             out[..., c.out[1]:c.out[1] + c.oc].fill_(0.0)
