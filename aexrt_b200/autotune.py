@@ -315,12 +315,16 @@ def tune_program(program, batch: int, runs: int = 10, log=print, seed: int = 0) 
     order / stacked-M / staged bits on the best tile).  A candidate must write the default plan's
     output bit for bit (integer accumulation makes every int8 tile exact, so the gate only rejects a
     broken plan) and is kept only when more than 5 % faster (the reference tuner's rule,
-    ``conv_autotune.cpp:336-345``).  The fp16 convs that read their NHWC input directly (the detect
+    ``conv_autotune.cpp:336-345``).  An int8 conv that can quantize its fp16 sources itself is then
+    also timed that way against its best tile plus the separate quantize launch it replaces, and
+    marked with ``engine.TILE_QUANT_ON_LOAD`` when that is more than 5 % faster (same codes, so the
+    same output).  The fp16 convs that read their NHWC input directly (the detect
     head) are swept the same way, halo tiles only.  Returns ``{conv name: block_n bits}`` for
     ``CompiledYolo(block_n=...)``; convs whose default stays best are left out."""
     import torch
 
     from . import engine, ops
+    from ._native import check
 
     eng = engine.CompiledYolo(program, batch)
     rng = np.random.default_rng(seed)
@@ -329,6 +333,18 @@ def tune_program(program, batch: int, runs: int = 10, log=print, seed: int = 0) 
     eng.forward(imgs)
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
+
+    def timed_fn(fn):
+        fn()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(20_000_000)  # the host enqueues every launch before the first one runs
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(runs):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / runs
 
     def timed(plan, q, rec, c, out, res, amax_out):
         def once():
@@ -404,10 +420,41 @@ def tune_program(program, batch: int, runs: int = 10, log=print, seed: int = 0) 
             t = trial(bits)
             if t is not None and t < best_t:
                 best_t, best_bits = t, bits
+        if not (best_bits and best_t < t0 * SIGNIFICANCE):
+            best_t, best_bits = t0, 0
+        note = ""
+        if not plan0.is_f16 and engine.ql_eligible(c):
+            # quantize on load: the conv quantizes its fp16 sources itself and the quantize launch
+            # before it goes away, so it competes with that launch and the conv together
+            srcs = st[3]
+            lib = eng.lib
+
+            def quantize():
+                check(lib.aexrt_b200_act_quantize_concat(srcs, len(srcs), batch, h, w, int(c.pg16), c.s, q.data_ptr(),
+                                                         rec.data_ptr(), stream.cuda_stream), "quantize")
+
+            tq = timed_fn(quantize)
+            ql_bits = best_bits | engine.TILE_QUANT_ON_LOAD
+            try:
+                plan = ops.ConvPlan.int8(batch, c.ic, h, w, c.oc, c.k, c.s, codes, scale, c.bias, silu=c.silu,
+                                         pg16=c.pg16, block_n=best_bits, quant_on_load=True)
+            except RuntimeError:
+                plan = None
+            if plan is not None and plan.info.quant_on_load:
+                out[..., c.out[1]:c.out[1] + c.oc].fill_(0.0)
+                t = timed_fn(lambda: plan.run_sources(
+                    srcs, out=out, out_coff=c.out[1], residual=res,
+                    res_coff=c.residual[1] if c.residual is not None else 0, amax_out=amax_out,
+                    amax_goff=c.out[1] // 16, stream=stream.cuda_stream))
+                if plan.status() != 0 or not torch.equal(out[..., c.out[1]:c.out[1] + c.oc], ref):
+                    log(f"  {c.name} quantize on load: output differs, rejected")
+                elif t < (best_t + tq) * SIGNIFICANCE:
+                    note = f" (quantize on load: {(best_t + tq) * 1e3:.1f} -> {t * 1e3:.1f} us with the quantize)"
+                    best_bits = ql_bits
         out[..., c.out[1]:c.out[1] + c.oc].copy_(ref)
-        if best_bits and best_t < t0 * SIGNIFICANCE:
+        if best_bits:
             chosen[c.name] = best_bits
-            log(f"{c.name}: {t0 * 1e3:.1f} -> {best_t * 1e3:.1f} us with bits {best_bits:#x}")
+            log(f"{c.name}: {t0 * 1e3:.1f} -> {best_t * 1e3:.1f} us with bits {best_bits:#x}{note}")
         else:
             log(f"{c.name}: {t0 * 1e3:.1f} us, default kept")
     return chosen

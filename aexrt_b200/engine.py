@@ -53,6 +53,21 @@ class NmsConfig:
     ctas_per_image: int = 0   # 0 automatic (8 for small batches), else 1, 2, 4 or 8
 
 
+# A tuned tile map's bit for "this int8 conv quantizes its fp16 sources itself" (above the plan's
+# tuning bits, which end at bit 30; stripped before the plan is created)
+TILE_QUANT_ON_LOAD = 1 << 31
+
+
+def ql_eligible(c: ConvCmd) -> bool:
+    """Whether an int8 conv can quantize on load: every input part fits the rules of
+    conv_w8a8_sources; SiLU convs only (the linear ones, with or without a residual, have no instance
+    of every tile)."""
+    return c.silu and all(
+        pt.value != "images" and pt.coff % 16 == 0 and pt.channels >= 16
+        and (pt.channels % 16 == 0 or i == len(c.inputs) - 1) and (pt.upsample == 1 or c.s == 1)
+        for i, pt in enumerate(c.inputs)) and len(c.inputs) <= 4
+
+
 class CompiledYolo:
     """One program compiled for one batch size on the current CUDA device."""
 
@@ -161,14 +176,11 @@ class CompiledYolo:
         if c.precision == "int8":
             codes, scale = ops.quantize_conv_weight_int8(c.weight)
             # quantize on load: the conv reads the producers' fp16 slices and quantizes them itself,
-            # when the plan supports it and every part fits its rules (see conv_w8a8_sources); SiLU
-            # convs only (the linear ones, with or without a residual, have no instance of every tile)
-            ql = self.quant_on_load and c.silu and all(
-                pt.value != "images" and pt.coff % 16 == 0 and pt.channels >= 16
-                and (pt.channels % 16 == 0 or i == len(c.inputs) - 1) and (pt.upsample == 1 or c.s == 1)
-                for i, pt in enumerate(c.inputs)) and len(c.inputs) <= 4
+            # for every eligible conv with the engine's quant_on_load, or for the convs a tuned tile map
+            # marks with TILE_QUANT_ON_LOAD
+            ql = (self.quant_on_load or bool(block_n & TILE_QUANT_ON_LOAD)) and ql_eligible(c)
             plan = ops.ConvPlan.int8(n, c.ic, h, w, c.oc, c.k, c.s, codes, scale, c.bias, silu=c.silu, pg16=c.pg16,
-                                     block_n=block_n, quant_on_load=ql)
+                                     block_n=block_n & ~TILE_QUANT_ON_LOAD, quant_on_load=ql)
             if ql and plan.info.quant_on_load:
                 self.plans[c.name] = plan
                 self.steps.append(("conv_ql", c, plan, self._sources(c.inputs, True), (h, w)))
