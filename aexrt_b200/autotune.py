@@ -312,8 +312,8 @@ def tune_program(program, batch: int, runs: int = 10, log=print, seed: int = 0) 
     After one forward on seeded images every int8 conv's own inputs (codes and scale record) are in
     its scratch.  Each conv is then timed alone, ``runs`` back-to-back launches between one CUDA-event
     pair, with its default plan and with every candidate tile (:func:`program_tile_candidates`, then
-    order / stacked-M / staged bits on the best tile).  A candidate must write the default plan's
-    output bit for bit (integer accumulation makes every int8 tile exact, so the gate only rejects a
+    order / stacked-M / staged / two-issuer bits on the best tile).  A candidate must write the default
+    plan's output bit for bit (integer accumulation makes every int8 tile exact, so the gate only rejects a
     broken plan) and is kept only when more than 5 % faster (the reference tuner's rule,
     ``conv_autotune.cpp:336-345``).  An int8 conv that can quantize its fp16 sources itself is then
     also timed that way against its best tile plus the separate quantize launch it replaces, and
@@ -413,7 +413,7 @@ def tune_program(program, batch: int, runs: int = 10, log=print, seed: int = 0) 
             if t is not None and t < best_t:
                 best_t, best_bits = t, bn
         base = best_bits or bn0
-        extra = [base | (1 << 20), base | (2 << 20), base | (1 << 29)]
+        extra = [base | (1 << 20), base | (2 << 20), base | (1 << 29), base | (1 << 30)]
         if c.k == 3 and c.s == 1 and base <= 64:
             extra += [base | (1 << 24), base | (2 << 24)]
         for bits in extra:

@@ -141,6 +141,8 @@ struct AexrtB200ConvPlan {
   // pg16 halo: K steps pair two taps of one slab, ordered by their shared-memory offset
   int tap_pairs = 0, tap_a[5] = {0, 0, 0, 0, 0}, tap_b[5] = {-1, -1, -1, -1, -1};
   int mblocks = 1, nacc = 4, tmem_cols = 512;  // super-tile M blocks, TMEM buffers and columns
+  // two MMA issuers even when half the stage ring holds less than a tile (plan bit 30, per tensor)
+  bool two_issuers = false;
   // staged output (conv_halo.cuh): buffers per epilogue group (0: direct stores) and their bytes
   int out_nbuf = 0, out_gbytes = 0;
   // every |int32 accumulator| <= 2^22 (bounded from the weight codes): exact fast conversion
@@ -282,6 +284,7 @@ AexrtB200ConvPlan* build_plan(const AexrtConv2DDesc& d, uint32_t kind, uint32_t 
   // slower staged (the per-tile barrier holds the four warps of a column block in step), and the
   // YOLOv8n-320 step at batch 256 was 1.3 % slower even with only its 1x1 convs staged
   const bool direct_store = ((block_n >> 28) & 1u) != 0 || ((block_n >> 29) & 1u) == 0;
+  p->two_issuers = !p->pg && ((block_n >> 30) & 1u) != 0;
   int sms = 148;
   {
     int dev = 0;
@@ -698,8 +701,9 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     // one, where the strided walk reloads weights at every n-tile), strided otherwise
     // (neighbouring tiles run together)
     h.contiguous = (p->order == 2 || (p->order == 0 && (amax_out != nullptr || p->n_tiles > 1))) ? 1 : 0;
-    // two MMA issuers when each half of the stage ring holds a whole tile's stages
-    h.issuers = 2 * p->slab_pairs <= p->stages ? 2 : 1;
+    // two MMA issuers when each half of the stage ring holds a whole tile's stages (or when the plan
+    // asks for them: each issuer then walks its half ring through its tiles' stages)
+    h.issuers = (2 * p->slab_pairs <= p->stages || (p->two_issuers && p->stages >= 4)) ? 2 : 1;
     h.w_tile_bytes = p->w_tile_bytes;
     h.oc_alloc = p->oc_alloc;
     h.scale_rec = scale_rec;

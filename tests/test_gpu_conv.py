@@ -580,3 +580,36 @@ def test_fp16_staged_epilogue_equals_direct_stores(n, ic, h, w, oc, k, silu, blo
         outs.append((plan.info.staged_out, out, am))
     assert outs[0][0] > 0 and outs[1][0] == 0
     assert torch.equal(outs[0][1], outs[1][1]) and torch.equal(outs[0][2], outs[1][2])
+
+
+@pytest.mark.parametrize("n,ic,h,w,oc,k,s,f16", [
+    (4, 256, 10, 10, 128, 3, 1, False),   # 16 slab pairs a tile: one issuer by default
+    (2, 512, 10, 10, 64, 1, 1, False),
+    (4, 256, 10, 10, 128, 3, 1, True),    # the fp16 detect head's P5 shape (NHWC input)
+])
+def test_two_issuers_equal_one(n, ic, h, w, oc, k, s, f16):
+    """Plan bit 30 runs two MMA issuers on plans whose tiles have more stages than half the ring
+    holds; every tile is still accumulated by one issuer in the same order, so the outputs (and, for
+    int8, the accumulators and the oracle's results) are identical."""
+    torch = _torch()
+    from aexrt_b200 import ops
+
+    rng = np.random.default_rng(77 + ic + oc)
+    x = seeded_act(rng, (n, ic, h, w))
+    wt = rng.normal(0, 0.05, (oc, ic, k, k)).astype(np.float32)
+    b = rng.normal(0, 0.1, oc).astype(np.float32)
+    if not f16:
+        g, _, _ = check_against_oracle(x, wt, b, k, s, 0)
+        g2, _, _ = check_against_oracle(x, wt, b, k, s, 0, block_n=1 << 30)
+        assert np.array_equal(g["acc"], g2["acc"]) and np.array_equal(g["y"], g2["y"])
+        return
+    xt = torch.from_numpy(nchw_to_nhwc(x)).cuda()
+    outs = []
+    for bits in (0, 1 << 30):
+        plan = ops.ConvPlan.fp16(n, ic, h, w, oc, k, s, wt, b, silu=True, block_n=bits)
+        out = torch.zeros((n, h, w, oc), dtype=torch.float16, device="cuda")
+        plan.run_nhwc(xt, out=out)
+        torch.cuda.synchronize()
+        assert plan.status() == 0
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
