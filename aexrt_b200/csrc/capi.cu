@@ -141,7 +141,8 @@ struct AexrtB200ConvPlan {
   // pg16 halo: K steps pair two taps of one slab, ordered by their shared-memory offset
   int tap_pairs = 0, tap_a[5] = {0, 0, 0, 0, 0}, tap_b[5] = {-1, -1, -1, -1, -1};
   int mblocks = 1, nacc = 4, tmem_cols = 512;  // super-tile M blocks, TMEM buffers and columns
-  // two MMA issuers even when half the stage ring holds less than a tile (plan bit 30, per tensor)
+  // plan bit 30: two MMA issuers even when half the stage ring holds less than a tile (the default
+  // for per-tensor plans since it was measured faster; the bit is kept for tuned maps)
   bool two_issuers = false;
   // staged output (conv_halo.cuh): buffers per epilogue group (0: direct stores) and their bytes
   int out_nbuf = 0, out_gbytes = 0;
@@ -701,9 +702,12 @@ int launch_conv(const AexrtB200ConvPlan* p, const void* x, const float* scale_re
     // one, where the strided walk reloads weights at every n-tile), strided otherwise
     // (neighbouring tiles run together)
     h.contiguous = (p->order == 2 || (p->order == 0 && (amax_out != nullptr || p->n_tiles > 1))) ? 1 : 0;
-    // two MMA issuers when each half of the stage ring holds a whole tile's stages (or when the plan
-    // asks for them: each issuer then walks its half ring through its tiles' stages)
-    h.issuers = (2 * p->slab_pairs <= p->stages || (p->two_issuers && p->stages >= 4)) ? 2 : 1;
+    // two MMA issuers when each half of the stage ring holds a whole tile's stages, and for every
+    // per-tensor plan with >= 4 stages (each issuer then walks its half ring through its own tiles'
+    // stages).  Measured with the default tiles: YOLOv8n-320 2.564 against 2.600 ms per step at
+    // batch 256, 1.074 against 1.083 at 64, 0.500 against 0.501 at 1; YOLOv11s-320 batch 64 2.167
+    // against 2.194 (one issuer where a half ring held less than a tile).  pg16 keeps the first rule
+    h.issuers = (2 * p->slab_pairs <= p->stages || ((!p->pg || p->two_issuers) && p->stages >= 4)) ? 2 : 1;
     h.w_tile_bytes = p->w_tile_bytes;
     h.oc_alloc = p->oc_alloc;
     h.scale_rec = scale_rec;

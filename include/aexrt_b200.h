@@ -168,9 +168,10 @@ int aexrt_b200_act_quantize_f16(const void* x, uint32_t n, uint32_t c, uint32_t 
  * 2 one contiguous run per CTA), bits 24-27 the most M blocks stacked in one
  * halo super-tile (0 auto, 1 none), bit 29 halo epilogue stages each tile in
  * shared memory and writes it with one TMA tensor store per column block,
- * bit 28 it stores each output pixel directly (the default), bit 30 runs two
- * MMA issuers even when half the stage ring holds less than one tile's stages
- * (per-tensor halo plans; by default one issuer runs then).  Small grids (one
+ * bit 28 it stores each output pixel directly (the default), bit 30 asks for
+ * two MMA issuers even when half the stage ring holds less than one tile's
+ * stages (per-tensor halo plans with at least 4 stages have two anyway; the
+ * bit changes nothing there).  Small grids (one
  * or a few images) pick narrower automatic tiles so that the conv spreads over
  * more SMs.  For int8 plans the results are identical
  * for every choice (integer accumulation); an fp16 plan whose choice moves it

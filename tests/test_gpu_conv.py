@@ -588,9 +588,9 @@ def test_fp16_staged_epilogue_equals_direct_stores(n, ic, h, w, oc, k, silu, blo
     (4, 256, 10, 10, 128, 3, 1, True),    # the fp16 detect head's P5 shape (NHWC input)
 ])
 def test_two_issuers_equal_one(n, ic, h, w, oc, k, s, f16):
-    """Plan bit 30 runs two MMA issuers on plans whose tiles have more stages than half the ring
-    holds; every tile is still accumulated by one issuer in the same order, so the outputs (and, for
-    int8, the accumulators and the oracle's results) are identical."""
+    """Per-tensor plans whose tiles have more stages than half the stage ring holds run two MMA
+    issuers (each walks its half ring through its own tiles); int8 results equal the oracle's, and
+    plan bit 30 (which asks for two issuers explicitly) changes nothing."""
     torch = _torch()
     from aexrt_b200 import ops
 
