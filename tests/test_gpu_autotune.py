@@ -62,3 +62,30 @@ def test_program_tile_tuning_replays_bit_identically():
         outs.append((eng.output.cpu().numpy(), eng.det_buf.cpu().numpy()))
     assert np.array_equal(outs[0][0], outs[1][0])
     assert np.array_equal(outs[0][1], outs[1][1])
+
+
+def test_tile_map_quantize_on_load_bit():
+    """A tile map can mark single int8 convs to quantize their fp16 sources themselves
+    (engine.TILE_QUANT_ON_LOAD); those convs then run as quantize-on-load steps and the model's
+    output0 and detections equal the default model's bit for bit."""
+    import torch
+
+    from aexrt_b200 import engine, yolo
+
+    program = yolo.build_yolov8n(nc=4, imgsz=96, seed=4)
+    names = [c.name for c in program.commands if getattr(c, "precision", None) == "int8" and engine.ql_eligible(c)]
+    assert names
+    tiles = {names[0]: engine.TILE_QUANT_ON_LOAD, names[-1]: engine.TILE_QUANT_ON_LOAD | 32}
+    imgs = torch.from_numpy(np.random.default_rng(6).uniform(0, 1, (2, 3, 96, 96)).astype(np.float16)).cuda()
+    outs = []
+    for bn in (None, tiles):
+        eng = engine.CompiledYolo(program, 2, block_n=bn, nms=engine.NmsConfig())
+        if bn:
+            ql = {st[1].name for st in eng.steps if st[0] == "conv_ql"}
+            assert ql <= set(tiles) and ql, ql
+        eng.forward(imgs)
+        torch.cuda.synchronize()
+        assert eng.status() == 0
+        outs.append((eng.output.cpu().numpy(), eng.det_buf.cpu().numpy()))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert np.array_equal(outs[0][1], outs[1][1])
