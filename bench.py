@@ -440,7 +440,10 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
         "scaling": scaling, "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": workload + " on the host CPU", "global_batch": per_step, "imgsz": imgsz, "nc": nc,
-                   "parallelism": "host cores"},
+                   "parallelism": "host cores",
+                   "batch_note": ("a bounded sample of 4 images per step, where the GPU arm runs 256: every image has "
+                                  "its own activation scales, so an image's work and result do not depend on the "
+                                  "batch it runs in, and images/s compare directly")},
         "cpu_baseline": {"value": ips, "unit": "images/s", "cores": cores, "kind": "port",
                          "sample": f"{per_step} images per step x {args.steps} steps through the CPU restatement "
                                    "of the reference's W8A8 arithmetic (oracle/), C/OpenMP int32 convolutions"},
