@@ -313,13 +313,13 @@ def tune_program(program, batch: int, runs: int = 10, log=print, seed: int = 0) 
     its scratch.  Each conv is then timed alone, ``runs`` back-to-back launches between one CUDA-event
     pair, with its default plan and with every candidate tile (:func:`program_tile_candidates`, then
     order / stacked-M / staged / two-issuer bits on the best tile).  A candidate must write the default
-    plan's output bit for bit (integer accumulation makes every int8 tile exact, so the gate only rejects a
-    broken plan) and is kept only when more than 5 % faster (the reference tuner's rule,
+    plan's output bit for bit (integer accumulation makes every int8 tile exact, so the gate only
+    rejects a broken plan) and is kept only when more than 5 % faster (the reference tuner's rule,
     ``conv_autotune.cpp:336-345``).  An int8 conv that can quantize its fp16 sources itself is then
     also timed that way against its best tile plus the separate quantize launch it replaces, and
     marked with ``engine.TILE_QUANT_ON_LOAD`` when that is more than 5 % faster (same codes, so the
-    same output).  The fp16 convs that read their NHWC input directly (the detect
-    head) are swept the same way, halo tiles only.  Returns ``{conv name: block_n bits}`` for
+    same output).  The fp16 convs that read their NHWC input directly (the detect head) are swept
+    the same way, halo tiles only.  Returns ``{conv name: block_n bits}`` for
     ``CompiledYolo(block_n=...)``; convs whose default stays best are left out."""
     import torch
 
@@ -357,16 +357,7 @@ def tune_program(program, batch: int, runs: int = 10, log=print, seed: int = 0) 
                 plan.run(q, rec, out=out, out_coff=c.out[1], residual=res,
                          res_coff=c.residual[1] if c.residual is not None else 0, amax_out=amax_out,
                          amax_goff=c.out[1] // 16, stream=stream.cuda_stream)
-        once()
-        torch.cuda.synchronize()
-        torch.cuda._sleep(20_000_000)  # the host enqueues every launch before the first one runs
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(runs):
-            once()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / runs
+        return timed_fn(once)
 
     chosen: Dict[str, int] = {}
     for st in eng.steps:
